@@ -1,0 +1,180 @@
+/* laya_b200 — C ABI of the B200 (sm_100a) execution library for Laya decision models.
+ *
+ * This library is the device half of the Laya encoder + decision-head forward pass.  It
+ * replaces, in the reference project (laya-cuda):
+ *   - laya_cuda/runtime.py:136-197  Runtime: weight residency, shape classes, CUDA-graph LRU
+ *   - laya_cuda/runtime.py:28-133   Slot: packed inputs, activations, encoder schedule, graphs
+ *   - laya_cuda/laya.py:195-245     Laya.allocate_head / read_outputs / forward_head
+ *   - laya_cuda/ops.py:20-71        Ops: NVRTC kernels + cuBLAS GemmEx
+ *   - laya_cuda/kernels.cu:1-183    every device kernel
+ * Python keeps the request contract (tokenisation, packing order, decoding) and calls this
+ * library through ctypes.  Plain C types only; every function returns 0 on success or a
+ * LAYA_ERR_* code, with a message available from laya_last_error().
+ *
+ * Threading: one engine handle per host thread at a time (the reference's Engine is not
+ * thread-safe either, docs/guide.md:17).  Different handles may run concurrently, e.g. one
+ * host thread per GPU.
+ */
+#ifndef LAYA_B200_H
+#define LAYA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LAYA_OK 0
+#define LAYA_ERR_INVALID 1     /* bad argument, configuration, tensor name or shape -> ValueError */
+#define LAYA_ERR_CUDA 2        /* CUDA runtime/driver failure                       -> RuntimeError */
+#define LAYA_ERR_DEVICE 3      /* a kernel reported an error (bad index, pipeline wait timeout) */
+#define LAYA_ERR_STATE 4       /* call in the wrong state (not finalised, closed)   -> RuntimeError */
+#define LAYA_ERR_NO_DEVICE 5   /* no usable sm_100 device                           -> RuntimeError */
+
+#define LAYA_DTYPE_F32 0
+#define LAYA_DTYPE_F16 1
+#define LAYA_DTYPE_BF16 2
+
+#define LAYA_PRECISION_BF16 0  /* 16-bit GEMM/attention operands: bfloat16 (fp32 accumulate) */
+#define LAYA_PRECISION_F16 1   /* 16-bit operands: float16, as the reference (runtime.py:157-158) */
+
+/* Model geometry, from encoder/config.json and rl_agent_config.json (laya.py:55-99). */
+typedef struct laya_config {
+  int32_t vocab;            /* encoder vocab_size */
+  int32_t width;            /* hidden_size, a multiple of 64, <= 1024 */
+  int32_t heads;            /* num_attention_heads; width / heads must be 64 */
+  int32_t layers;           /* num_hidden_layers */
+  int32_t intermediate;     /* intermediate_size F (GeGLU: Wi is 2F x width) */
+  int32_t global_every;     /* global_attn_every_n_layers */
+  int32_t window;           /* local_attention // 2 (keys within +-window) */
+  float theta_global;       /* RoPE theta of full-attention layers */
+  float theta_local;        /* RoPE theta of sliding-window layers */
+  float eps;                /* encoder norm_eps */
+  int32_t max_len;          /* rl_agent_config max_len (<= 1024) */
+  int32_t head_layers;      /* decision-head transformer layers (>= 1) */
+  int32_t n_act;            /* action-head outputs: len(act_costs) + 1 */
+  int32_t precision;        /* LAYA_PRECISION_* */
+} laya_config;
+
+typedef struct laya_metrics {
+  float gpu_ms;             /* CUDA-event time of the forward pass (graph or eager) */
+  int32_t rows;             /* shape class: packed token rows */
+  int32_t batch;            /* shape class: questions (power of two) */
+  int32_t options;          /* shape class: options (power of two >= 8) */
+  int32_t cache_miss;       /* the shape class had no cached slot */
+  int32_t graph_capture;    /* this call captured the class's CUDA graph */
+  int32_t graph_replay;     /* this call ran a captured graph */
+  int32_t kernel_launches;  /* kernels launched by this forward pass */
+  uint64_t owned_gpu_bytes; /* device bytes held by the engine after the call */
+} laya_metrics;
+
+typedef struct laya_engine laya_engine;
+
+/* Replaces Runtime.__init__ (runtime.py:137-146): selects `device`, creates the stream.
+ * max_cached_shapes bounds the shape-class LRU (engine.py:12-13: 1..64). */
+int laya_create(const laya_config* cfg, int device, int max_cached_shapes, laya_engine** out);
+
+/* Replaces the per-tensor validation and upload of runtime.py:147-158.  `name` must be one of
+ * Laya.weight_shapes() (laya.py:167-190) and `shape` must match it exactly; "temperature" is
+ * accepted and ignored, as the reference does.  `host` holds the values in `dtype`. */
+int laya_load_tensor(laya_engine* e, const char* name, int dtype, const int64_t* shape, int ndim,
+                     const void* host);
+
+/* After all tensors are loaded: checks completeness and builds the RoPE tables
+ * (runtime.py:159-165) and the device-side weight layouts. */
+int laya_finalize(laya_engine* e);
+
+/* Replaces Runtime.predict (runtime.py:171-186) + Slot.fill/run (runtime.py:52-68, 115-133) +
+ * Laya.read_outputs (laya.py:206-208).  Items are the adapter's (ids, markers, kind) triples
+ * flattened: tokens = concat(ids), lengths[i] = len(ids_i), markers = concat(markers),
+ * marker_counts[i] = len(markers_i), kinds[i] = question type.  The call packs the rows,
+ * uploads them, runs the class's CUDA graph (capturing it on first use) or the eager pass,
+ * and writes logits_out[i * options + j] (option logits, fp32, options = the class's option
+ * count reported in metrics->options; the caller sizes the buffer with laya_shape_class) and
+ * acts_out[i * n_act + a]. */
+int laya_predict(laya_engine* e, const int32_t* tokens, const int32_t* lengths, const int32_t* markers,
+                 const int32_t* marker_counts, const int32_t* kinds, int n_items, int capture,
+                 float* logits_out, float* acts_out, laya_metrics* metrics);
+
+/* Shape class of a request (runtime.py:20-25): packed rows, batch and option counts. */
+int laya_shape_class(const int32_t* lengths, const int32_t* marker_counts, int n_items, int32_t* rows,
+                     int32_t* batch, int32_t* options);
+
+/* Device-resident variant for throughput runs: `packed` (device memory, laya_packed_ints()
+ * int32 values laid out by laya_pack()) is copied into the class's input buffer and the
+ * forward pass is enqueued on the engine's stream; outputs stay on the device
+ * (logits [batch][options+1] including the CLS column, acts [batch][n_act]).  No host sync. */
+int laya_forward_device(laya_engine* e, const int32_t* packed, int rows, int batch, int options,
+                        int capture, float* logits_dev, float* acts_dev);
+
+/* Host-side packing used by laya_predict, exposed for laya_forward_device callers. */
+int64_t laya_packed_ints(int rows, int batch, int options);
+int laya_pack(const int32_t* tokens, const int32_t* lengths, const int32_t* markers, const int32_t* marker_counts,
+              const int32_t* kinds, int n_items, int pad_id, int rows, int batch, int options, int32_t* packed);
+
+/* The engine's CUDA stream (cudaStream_t), for callers that time laya_forward_device. */
+void* laya_stream(laya_engine* e);
+
+/* Per-kernel-family device time accumulated over forward passes run with profiling on
+ * (CUDA events on the engine stream around each launch of the family).  family: 0 GEMM,
+ * 1 attention, 2 row kernels (embedding, norms, gather), 3 head tail.  Eager passes only. */
+int laya_set_profiling(laya_engine* e, int enabled);
+int laya_profile_read(laya_engine* e, int family, double* total_ms, int64_t* launches, double* flops);
+
+/* Reads a loaded tensor back as fp32 (tests; runtime.weights[name].get()). */
+int laya_read_tensor(laya_engine* e, const char* name, float* out, int64_t count);
+
+/* Number of cached shape-class slots (len(runtime.slots)). */
+int laya_cached_shapes(laya_engine* e, int32_t* count);
+
+/* Device bytes owned by the engine (runtime.pool.used_bytes()/total_bytes()). */
+int laya_pool_bytes(laya_engine* e, uint64_t* used, uint64_t* total);
+
+/* Replaces Runtime.close (runtime.py:188-197).  Frees every device allocation and the handle. */
+int laya_destroy(laya_engine* e);
+
+/* Message of the last failing call on `e` (or of the last failing laya_create when e is NULL). */
+const char* laya_last_error(laya_engine* e);
+
+/* ------------------------------------------------------------------------------------------
+ * Kernel-level entry points (device pointers, enqueued on `stream`), used by the parity tests
+ * the way the reference's tests drive Ops directly (tests/test_gpu.py, tests/test_attention.py).
+ * `precision` selects the 16-bit operand type (LAYA_PRECISION_*).
+ * ------------------------------------------------------------------------------------------ */
+
+/* out/residual = epilogue(x[M][K] @ w[N][K]^T).  epi: 0 store, 1 relu, 2 gelu, 3 geglu (w rows
+ * pre-interleaved by laya_interleave_geglu; out is [M][N/2]), 4 qkv (RoPE when cos/sin given;
+ * out is [3][heads][M][64]), 5 residual += (fp32), 6 split-K partials.  bias: fp32 [N] or NULL.
+ * Replaces cublasGemmEx + bias/activate/layout (ops.py:58-66; kernels.cu:50-82). */
+int laya_op_gemm(int precision, int epi, const void* x, const void* w, int M, int N, int K, void* out, int ldo,
+                 float* residual, int ldr, const float* bias, int heads, const float* cos_tab, const float* sin_tab,
+                 const int32_t* positions, int splits, int block_n, int* err, void* stream);
+
+/* Reorders Wi [2F][K] (gate rows then up rows) into 64-row blocks [gate_i, up_i] (host memory). */
+int laya_interleave_geglu(const uint16_t* src, uint16_t* dst, int F, int K);
+
+/* Packed attention (kernels.cu:90-154).  qkv [3][heads][M][64], out [M][heads*64], tiles from
+ * laya_attention_tiles. */
+int laya_op_attention(int precision, const void* qkv, void* out, const int32_t* tiles, int n_tiles,
+                      const int32_t* starts, const int32_t* lengths, int M, int heads, int window, int split_p,
+                      void* stream);
+
+/* Builds the attention tile table for rows packed at `starts` with `lengths` into M tokens.
+ * Returns the number of tiles written (<= capacity) or -1. */
+int laya_attention_tiles(const int32_t* starts, const int32_t* lengths, int n_rows, int M, int32_t* tiles,
+                         int capacity);
+
+/* residual = LN(E[ids]); x = residual (16-bit).  (kernels.cu:16-19 + runtime.py:93-95) */
+int laya_op_embed_norm(int precision, const int32_t* ids, const float* table, const float* gamma, float eps, int rows,
+                       int width, int vocab, float* residual, void* x, int* err, void* stream);
+
+/* residual += sum(partials[0..splits)); x = LN(residual; gamma, beta).  (kernels.cu:20-49) */
+int laya_op_norm(int precision, float* residual, const float* partials, int splits, const float* gamma,
+                 const float* beta, float eps, void* x, int rows, int width, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LAYA_B200_H */

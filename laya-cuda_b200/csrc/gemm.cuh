@@ -1,0 +1,327 @@
+// Persistent, warp-specialised tcgen05 GEMM for the encoder and head linears:
+//
+//   D[M, N] = A[M, K] * W[N, K]^T       (A: activations, W: PyTorch Linear weight; both K-major)
+//
+// with the consumer of D fused into the epilogue (RoPE + head-major layout for QKV, GeGLU for
+// the FFN up-projection, residual accumulation for the attention-out and FFN down projections,
+// bias + ReLU / GELU for the decision head, split-K partials for small row counts).
+//
+// One CTA per SM, 6 warps:
+//   warp 0      TMA producer: A/W tiles (BK = 64 16-bit elements, 128-byte swizzle) into a
+//               ring of shared-memory stages (no multicast).
+//   warp 1      TMEM allocator + MMA issuer: one elected thread issues tcgen05.mma
+//               (M = 128, N = BN, K = 16) into one of two TMEM accumulators.
+//   warps 2..5  epilogue: tcgen05.ld of the finished accumulator (warp w reads TMEM lanes
+//               32*(w%4) .. +31, i.e. tile rows), fused transform, global stores.
+// The two accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
+//
+// Replaces the reference's cuBLAS GemmEx calls (laya_cuda/ops.py:58-66 called from
+// laya_cuda/runtime.py:77-80) and the elementwise kernels that followed them
+// (kernels.cu:50-82 bias/add/activate/layout).
+#pragma once
+#include "common.cuh"
+
+namespace laya {
+
+enum EpiKind : int {
+  EPI_STORE = 0,    // out = acc + bias
+  EPI_RELU = 1,     // out = relu(acc + bias)
+  EPI_GELU = 2,     // out = gelu(acc + bias)
+  EPI_GEGLU = 3,    // W rows interleaved in 64-row blocks [gate_i, up_i]: out = gelu(gate) * up
+  EPI_QKV = 4,      // (+bias) RoPE on q/k, scatter into [3][heads][M][64]
+  EPI_RESIDUAL = 5, // residual(fp32) += acc + bias
+  EPI_PARTIAL = 6,  // partial[split](fp32) = acc          (split-K)
+};
+
+struct GemmArgs {
+  int M, N, K;
+  int splits;             // split-K factor (EPI_PARTIAL only; 1 otherwise)
+  void* out;              // 16-bit output
+  int ldo;                // elements
+  float* residual;        // EPI_RESIDUAL target, or EPI_PARTIAL base ([splits][M][ldr])
+  int ldr;
+  const float* bias;      // fp32 [N] (GeGLU: unused) or nullptr
+  // EPI_QKV
+  int heads;
+  const float* cos_tab;   // [positions][32] or nullptr (no rotary embedding)
+  const float* sin_tab;
+  const int* positions;   // [M]
+  int* err;               // device error word
+};
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kGemmThreads = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kStageA = kBM * kBK * 2;
+  static constexpr int kStageB = BN * kBK * 2;
+  static constexpr int kStageBytes = kStageA + kStageB;
+  static constexpr int kStages = (192 * 1024) / kStageBytes;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <typename T, int EPI>
+__device__ __forceinline__ void epi_store_chunk(const GemmArgs& a, int row, int col, const float (&v)[32]) {
+  T* out = reinterpret_cast<T*>(a.out) + (size_t)row * a.ldo + col;
+  float b[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) b[i] = 0.f;
+  if (a.bias) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      float4 t = *reinterpret_cast<const float4*>(a.bias + col + i);
+      b[i] = t.x; b[i + 1] = t.y; b[i + 2] = t.z; b[i + 3] = t.w;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    float x[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float t = v[i + j] + b[i + j];
+      if (EPI == EPI_RELU) t = fmaxf(t, 0.f);
+      if (EPI == EPI_GELU) t = gelu_erf(t);
+      x[j] = t;
+    }
+    uint4 w;
+    w.x = pack2<T>(x[0], x[1]); w.y = pack2<T>(x[2], x[3]);
+    w.z = pack2<T>(x[4], x[5]); w.w = pack2<T>(x[6], x[7]);
+    *reinterpret_cast<uint4*>(out + i) = w;
+  }
+}
+
+__device__ __forceinline__ void epi_residual_chunk(const GemmArgs& a, int row, int col, const float (&v)[32]) {
+  float* r = a.residual + (size_t)row * a.ldr + col;
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    float4 t = *reinterpret_cast<float4*>(r + i);
+    float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (a.bias) bb = *reinterpret_cast<const float4*>(a.bias + col + i);
+    t.x += v[i] + bb.x; t.y += v[i + 1] + bb.y; t.z += v[i + 2] + bb.z; t.w += v[i + 3] + bb.w;
+    *reinterpret_cast<float4*>(r + i) = t;
+  }
+}
+
+__device__ __forceinline__ void epi_partial_chunk(const GemmArgs& a, int split, int row, int col,
+                                                  const float (&v)[32]) {
+  float* r = a.residual + ((size_t)split * a.M + row) * a.ldr + col;
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(r + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+}
+
+template <int BN, int EPI, typename T>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const GemmArgs args) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * Cfg::kStageA;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tfull = bars + 2 * S;
+  uint64_t* tempty = bars + 2 * S + 2;
+  uint64_t* drain = bars + 2 * S + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int m_blocks = (args.M + kBM - 1) / kBM;
+  const int n_blocks = args.N / BN;
+  const int splits = args.splits;
+  const int k_blocks_total = args.K / kBK;
+  const int k_blocks = k_blocks_total / splits;
+  const int tiles = m_blocks * n_blocks * splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 4); }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) { tma_prefetch_desc(&tmA); tma_prefetch_desc(&tmB); }
+  if (warp == 1) { tmem_alloc(tmem_slot, Cfg::kTmemCols); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  // Tile order: split outermost, then row block, then column block, so CTAs running together
+  // share an A row block (it stays in L2 while all its column blocks are computed).
+  auto decode = [&](int t, int& split, int& mb, int& nb) {
+    split = t / (m_blocks * n_blocks);
+    int r = t - split * m_blocks * n_blocks;
+    mb = r / n_blocks;
+    nb = r - mb * n_blocks;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0; uint32_t phase = 0;
+      uint32_t issued = 0, last_par = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        int split, mb, nb; decode(t, split, mb, nb);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrGemmProducerWait, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+          const int kx = (split * k_blocks + kb) * kBK;
+          tma_load_2d(sA + stage * Cfg::kStageA, &tmA, &full[stage], kx, mb * kBM);
+          tma_load_2d(sB + stage * Cfg::kStageB, &tmB, &full[stage], kx, nb * BN);
+          issued |= 1u << stage;
+          last_par = (last_par & ~(1u << stage)) | (phase << stage);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {
+        // Let copies already in flight land before the CTA exits.
+        for (int s = 0; s < S; ++s)
+          if (issued & (1u << s)) mbar_wait(&full[s], (last_par >> s) & 1, nullptr, 0, abort_flag);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = mma_idesc<std::is_same<T, __nv_bfloat16>::value>(kBM, BN);
+      int stage = 0; uint32_t phase = 0;
+      int acc = 0; uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, args.err, kErrGemmMmaWait, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, args.err, kErrGemmMmaWait, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * Cfg::kStageA);
+          const uint32_t b0 = smem_u32(sB + stage * Cfg::kStageB);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            tc_mma_f16(d_tmem, smem_desc_sw128(a0 + k * 32), smem_desc_sw128(b0 + k * 32), idesc,
+                       (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+      // Drain: make sure no MMA is still writing TMEM when it is released.
+      tc_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0, abort_flag);
+    }
+  } else {
+    // Epilogue warps 2..5 -> TMEM lane quarter (warp % 4).
+    const int quarter = warp & 3;
+    int acc = 0; uint32_t acc_phase = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+      int split, mb, nb; decode(t, split, mb, nb);
+      if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag)) break;
+      tc_fence_after();
+      const int row = mb * kBM + quarter * 32 + lane;
+      const bool live = row < args.M;
+      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      const int n0 = nb * BN;
+      if (EPI == EPI_GEGLU) {
+        // Tile columns: [gate 64 | up 64] x (BN / 128); output column = n0/2 + 64*c + j.
+#pragma unroll 1
+        for (int c = 0; c < BN / 128; ++c) {
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            float g[32], u[32];
+            tmem_ld32(tbase + c * 128 + h * 32, g);
+            tmem_ld32(tbase + c * 128 + 64 + h * 32, u);
+            if (live) {
+              T* out = reinterpret_cast<T*>(args.out) + (size_t)row * args.ldo + n0 / 2 + c * 64 + h * 32;
+#pragma unroll
+              for (int i = 0; i < 32; i += 8) {
+                uint4 w;
+                w.x = pack2<T>(gelu_erf(g[i + 0]) * u[i + 0], gelu_erf(g[i + 1]) * u[i + 1]);
+                w.y = pack2<T>(gelu_erf(g[i + 2]) * u[i + 2], gelu_erf(g[i + 3]) * u[i + 3]);
+                w.z = pack2<T>(gelu_erf(g[i + 4]) * u[i + 4], gelu_erf(g[i + 5]) * u[i + 5]);
+                w.w = pack2<T>(gelu_erf(g[i + 6]) * u[i + 6], gelu_erf(g[i + 7]) * u[i + 7]);
+                *reinterpret_cast<uint4*>(out + i) = w;
+              }
+            }
+          }
+        }
+      } else if (EPI == EPI_QKV) {
+        const int width = args.heads * 64;
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          float x[64];
+          {
+            float lo[32], hi[32];
+            tmem_ld32(tbase + c * 64, lo);
+            tmem_ld32(tbase + c * 64 + 32, hi);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) { x[i] = lo[i]; x[32 + i] = hi[i]; }
+          }
+          if (live) {
+            const int n = n0 + c * 64;
+            const int part = n / width;
+            const int head = (n - part * width) >> 6;
+            if (args.bias) {
+#pragma unroll
+              for (int i = 0; i < 64; ++i) x[i] += args.bias[n + i];
+            }
+            if (part < 2 && args.cos_tab) {
+              // Rotate-half RoPE: out[d] = x[d] cos - x[d+32] sin (d < 32),
+              //                   out[d] = x[d] cos + x[d-32] sin (d >= 32).
+              const int pos = args.positions[row];
+              const float* cs = args.cos_tab + (size_t)pos * 32;
+              const float* sn = args.sin_tab + (size_t)pos * 32;
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const float c0 = cs[i], s0 = sn[i];
+                const float a = x[i], b = x[i + 32];
+                x[i] = a * c0 - b * s0;
+                x[i + 32] = b * c0 + a * s0;
+              }
+            }
+            T* out = reinterpret_cast<T*>(args.out) + (((size_t)part * args.heads + head) * args.M + row) * 64;
+#pragma unroll
+            for (int i = 0; i < 64; i += 8) {
+              uint4 w;
+              w.x = pack2<T>(x[i + 0], x[i + 1]); w.y = pack2<T>(x[i + 2], x[i + 3]);
+              w.z = pack2<T>(x[i + 4], x[i + 5]); w.w = pack2<T>(x[i + 6], x[i + 7]);
+              *reinterpret_cast<uint4*>(out + i) = w;
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(tbase + c * 32, v);
+          if (live) {
+            const int col = n0 + c * 32;
+            if (EPI == EPI_RESIDUAL) epi_residual_chunk(args, row, col, v);
+            else if (EPI == EPI_PARTIAL) epi_partial_chunk(args, split, row, col, v);
+            else epi_store_chunk<T, EPI>(args, row, col, v);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+}
+
+}  // namespace laya

@@ -1,0 +1,1239 @@
+// laya_b200: host runtime + C ABI (see include/laya_b200.h).
+//
+// The engine owns the resident weights, one device workspace shared by every shape class,
+// pinned staging buffers, and an LRU of shape-class slots, each holding the class's tensor
+// maps and (once captured) its CUDA graph.  Only one forward pass runs at a time on the
+// engine's stream, so all classes can share the workspace: a class whose layout does not fit
+// grows it, which drops the graphs that pointed into the old one.
+//
+// Reference counterparts: laya_cuda/runtime.py (Runtime, Slot), laya_cuda/laya.py:195-245
+// (head buffers and forward), laya_cuda/ops.py (launch glue).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <exception>
+#include <list>
+#include <map>
+#include <memory>
+#include <string>
+#include <tuple>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/laya_b200.h"
+#include "attention.cuh"
+#include "gemm.cuh"
+#include "rowops.cuh"
+
+using namespace laya;
+
+namespace {
+
+// ---------------------------------------------------------------------------------------------
+// Errors
+// ---------------------------------------------------------------------------------------------
+thread_local std::string g_create_error;
+
+struct Failure {
+  int code;
+  std::string msg;
+};
+
+[[noreturn]] void fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  throw Failure{code, buf};
+}
+
+#define CK(call)                                                                                    \
+  do {                                                                                              \
+    cudaError_t e_ = (call);                                                                        \
+    if (e_ != cudaSuccess) fail(LAYA_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_));     \
+  } while (0)
+
+// ---------------------------------------------------------------------------------------------
+// Driver entry point for tensor-map encoding (no link-time dependency on libcuda).
+// ---------------------------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    CK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    if (!p || q != cudaDriverEntryPointSuccess) fail(LAYA_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D K-major operand [rows][cols] of 16-bit elements, box {64, box_rows}, 128-byte swizzle.
+CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int box_rows, bool bf16) {
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0 || (cols * 2) % 16 != 0)
+    fail(LAYA_ERR_INVALID, "TMA operand must be 16-byte aligned with rows a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                           const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail(LAYA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return m;
+}
+
+int sm_count(int device) {
+  static std::map<int, int> cache;
+  auto it = cache.find(device);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  CK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device));
+  cache[device] = n;
+  return n;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Kernel dispatch
+// ---------------------------------------------------------------------------------------------
+template <typename T, int BN, int EPI>
+void launch_gemm_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t st) {
+  static uint64_t configured = 0;  // one bit per device
+  auto kern = gemm_kernel<BN, EPI, T>;
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  if (!(configured & (1ull << dev))) {
+    CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::kSmemBytes));
+    configured |= 1ull << dev;
+  }
+  kern<<<grid, kGemmThreads, GemmCfg<BN>::kSmemBytes, st>>>(ta, tb, a);
+  CK(cudaGetLastError());
+}
+
+template <typename T, int BN>
+void launch_gemm_bn(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t st) {
+  switch (epi) {
+    case EPI_STORE: launch_gemm_inst<T, BN, EPI_STORE>(ta, tb, a, grid, st); break;
+    case EPI_RELU: launch_gemm_inst<T, BN, EPI_RELU>(ta, tb, a, grid, st); break;
+    case EPI_GELU: launch_gemm_inst<T, BN, EPI_GELU>(ta, tb, a, grid, st); break;
+    case EPI_GEGLU:
+      if (BN < 128) fail(LAYA_ERR_INVALID, "GeGLU epilogue needs a column tile of at least 128");
+      launch_gemm_inst<T, BN, EPI_GEGLU>(ta, tb, a, grid, st);
+      break;
+    case EPI_QKV: launch_gemm_inst<T, BN, EPI_QKV>(ta, tb, a, grid, st); break;
+    case EPI_RESIDUAL: launch_gemm_inst<T, BN, EPI_RESIDUAL>(ta, tb, a, grid, st); break;
+    case EPI_PARTIAL: launch_gemm_inst<T, BN, EPI_PARTIAL>(ta, tb, a, grid, st); break;
+    default: fail(LAYA_ERR_INVALID, "unknown epilogue %d", epi);
+  }
+}
+
+template <typename T>
+void launch_gemm(int epi, int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int sms,
+                 cudaStream_t st) {
+  if (a.K % kBK != 0 || a.N % bn != 0 || a.M <= 0) fail(LAYA_ERR_INVALID, "GEMM shape %dx%dx%d not tileable", a.M, a.N, a.K);
+  if ((a.K / kBK) % a.splits != 0) fail(LAYA_ERR_INVALID, "split-K %d does not divide %d k-blocks", a.splits, a.K / kBK);
+  const int tiles = ((a.M + kBM - 1) / kBM) * (a.N / bn) * a.splits;
+  const int grid = std::min(tiles, sms);
+  switch (bn) {
+    case 64: launch_gemm_bn<T, 64>(epi, ta, tb, a, grid, st); break;
+    case 128: launch_gemm_bn<T, 128>(epi, ta, tb, a, grid, st); break;
+    case 256: launch_gemm_bn<T, 256>(epi, ta, tb, a, grid, st); break;
+    default: fail(LAYA_ERR_INVALID, "unsupported column tile %d", bn);
+  }
+}
+
+// Column tile: the largest tile that still keeps the SMs busy.
+int pick_bn(int M, int N, int epi, int sms) {
+  const int mb = (M + kBM - 1) / kBM;
+  int best = 0;
+  double best_score = -1;
+  for (int bn : {256, 128, 64}) {
+    if (N % bn) continue;
+    if (epi == EPI_GEGLU && bn < 128) continue;
+    const int tiles = mb * (N / bn);
+    const int waves = (tiles + sms - 1) / sms;
+    const double util = (double)tiles / ((double)waves * sms);
+    const double eff = bn == 256 ? 1.0 : bn == 128 ? 0.92 : 0.8;
+    const double score = util * eff;
+    if (score > best_score + 1e-9) { best_score = score; best = bn; }
+  }
+  if (!best) fail(LAYA_ERR_INVALID, "no column tile divides N=%d", N);
+  return best;
+}
+
+template <typename T>
+void launch_attention(const AttnArgs& a, int n_tiles, bool split_p, cudaStream_t st) {
+  dim3 grid(n_tiles, a.heads);
+  if (split_p) attention_kernel<T, true><<<grid, kAttnThreads, 0, st>>>(a);
+  else attention_kernel<T, false><<<grid, kAttnThreads, 0, st>>>(a);
+  CK(cudaGetLastError());
+}
+
+template <typename T>
+void launch_embed(const int* ids, const float* table, const float* gamma, float eps, int rows, int d, int vocab,
+                  float* residual, T* x, int* err, cudaStream_t st) {
+  const int grid = (rows + kRowWarps - 1) / kRowWarps;
+  if (d % 128 == 0) embed_norm_kernel<4, T><<<grid, kRowWarps * 32, 0, st>>>(ids, table, gamma, eps, rows, d, vocab, residual, x, err);
+  else embed_norm_kernel<2, T><<<grid, kRowWarps * 32, 0, st>>>(ids, table, gamma, eps, rows, d, vocab, residual, x, err);
+  CK(cudaGetLastError());
+}
+
+template <typename T>
+void launch_norm(const NormArgs& a, cudaStream_t st) {
+  const int grid = (a.rows + kRowWarps - 1) / kRowWarps;
+  if (a.d % 128 == 0) norm_kernel<4, T><<<grid, kRowWarps * 32, 0, st>>>(a);
+  else norm_kernel<2, T><<<grid, kRowWarps * 32, 0, st>>>(a);
+  CK(cudaGetLastError());
+}
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+int span16(int n) { return (n + 15) / 16 * 16; }
+
+// ---------------------------------------------------------------------------------------------
+// Packing (runtime.py:15-25, 52-68)
+// ---------------------------------------------------------------------------------------------
+void shape_class(const int32_t* lengths, const int32_t* marker_counts, int n, int& rows, int& batch, int& options) {
+  if (n <= 0) fail(LAYA_ERR_INVALID, "no items");
+  int64_t total = 0;
+  int kmax = 0;
+  for (int i = 0; i < n; ++i) {
+    if (lengths[i] <= 0) fail(LAYA_ERR_INVALID, "item %d is empty", i);
+    total += span16(lengths[i]);
+    kmax = std::max(kmax, (int)marker_counts[i]);
+  }
+  const int step = total <= 256 ? 32 : total <= 512 ? 64 : 128;
+  if (total > (1 << 30)) fail(LAYA_ERR_INVALID, "request too large");
+  rows = (int)((total + step - 1) / step * step);
+  auto pow2 = [](int v, int low) { int p = 1; while (p < v) p <<= 1; return std::max(low, p); };
+  batch = pow2(n, 1);
+  options = pow2(std::max(kmax, 1), 8);
+}
+
+int tiles_capacity(int rows, int batch) { return (rows + 48 * batch + 63) / 64 + 1; }
+
+struct PackLayout {
+  int64_t ids, positions, rows_, kinds, starts, lengths, counts, indices, tiles, total;
+};
+PackLayout pack_layout(int m, int b, int k) {
+  PackLayout p;
+  int64_t o = 0;
+  p.ids = o; o += m;
+  p.positions = o; o += m;
+  p.rows_ = o; o += m;
+  p.kinds = o; o += m;
+  p.starts = o; o += b;
+  p.lengths = o; o += b;
+  p.counts = o; o += b;
+  p.indices = o; o += (int64_t)b * (k + 1);
+  o = (o + 3) / 4 * 4;  // int4 alignment of the tile table
+  p.tiles = o; o += 4LL * tiles_capacity(m, b);
+  p.total = o;
+  return p;
+}
+
+int build_tiles(const int32_t* starts, const int32_t* lengths, int n_rows, int M, int32_t* tiles, int capacity) {
+  int t = 0, end = 0;
+  auto put = [&](int a, int b, int r) {
+    if (t >= capacity) return false;
+    tiles[4 * t] = a; tiles[4 * t + 1] = b; tiles[4 * t + 2] = r; tiles[4 * t + 3] = 0;
+    ++t;
+    return true;
+  };
+  for (int r = 0; r < n_rows; ++r) {
+    const int s = starts[r], sp = span16(lengths[r]);
+    for (int q = 0; q < sp; q += kAttnQ)
+      if (!put(s + q, std::min(s + q + kAttnQ, s + sp), r)) return -1;
+    end = std::max(end, s + sp);
+  }
+  for (int q = end; q < M; q += kAttnQ)
+    if (!put(q, std::min(q + kAttnQ, M), -1)) return -1;
+  const int used = t;
+  while (t < capacity) put(0, 0, -2);
+  return used;
+}
+
+void pack(const int32_t* tokens, const int32_t* lengths, const int32_t* markers, const int32_t* marker_counts,
+          const int32_t* kinds, int n, int pad, int m, int b, int k, int max_len, int32_t* out) {
+  const PackLayout L = pack_layout(m, b, k);
+  int32_t* ids = out + L.ids;
+  std::fill(out, out + L.total, 0);
+  std::fill(ids, ids + m, pad);
+  std::fill(out + L.rows_, out + L.rows_ + m, -1);
+  int offset = 0;
+  int64_t tok = 0, mk = 0;
+  for (int r = 0; r < n; ++r) {
+    const int len = lengths[r], cnt = marker_counts[r];
+    if (len <= 0 || len > max_len) fail(LAYA_ERR_INVALID, "item %d has %d tokens (max_len %d)", r, len, max_len);
+    if (cnt < 0 || cnt > k) fail(LAYA_ERR_INVALID, "item %d has %d options (class %d)", r, cnt, k);
+    if (kinds[r] < 0 || kinds[r] > 2) fail(LAYA_ERR_INVALID, "item %d has question type %d", r, kinds[r]);
+    const int end = offset + span16(len);
+    if (end > m) fail(LAYA_ERR_INVALID, "items exceed %d packed rows", m);
+    std::copy(tokens + tok, tokens + tok + len, ids + offset);
+    for (int t = offset; t < end; ++t) {
+      out[L.positions + t] = t - offset;
+      out[L.rows_ + t] = r;
+      out[L.kinds + t] = kinds[r];
+    }
+    out[L.starts + r] = offset;
+    out[L.lengths + r] = len;
+    out[L.counts + r] = cnt;
+    int32_t* ind = out + L.indices + (int64_t)r * (k + 1);
+    for (int j = 0; j <= k; ++j) ind[j] = offset;
+    for (int j = 0; j < cnt; ++j) {
+      const int pos = markers[mk + j];
+      if (pos < 0 || pos >= len) fail(LAYA_ERR_INVALID, "item %d marker %d out of range", r, pos);
+      ind[j + 1] = offset + pos;
+    }
+    tok += len;
+    mk += cnt;
+    offset = end;
+  }
+  if (build_tiles(out + L.starts, out + L.lengths, n, m, out + L.tiles, tiles_capacity(m, b)) < 0)
+    fail(LAYA_ERR_INVALID, "attention tile table overflow");
+}
+
+// ---------------------------------------------------------------------------------------------
+// Engine
+// ---------------------------------------------------------------------------------------------
+struct Tensor {
+  void* ptr = nullptr;
+  int dtype = LAYA_DTYPE_F32;  // storage dtype
+  std::vector<int64_t> shape;
+  size_t bytes = 0;
+};
+
+struct ClassLayout {
+  int m = 0, b = 0, k = 0, count = 0, tiles_cap = 0;
+  PackLayout pack{};
+  size_t packed, residual, x, qkv, attn, ff, sel, selx, scored, ffsel, out, total;
+  size_t n_out_floats;  // logits b*(k+1) + acts b*n_act + 1 error word
+};
+
+struct Slot {
+  int m, b, k;
+  ClassLayout L;
+  cudaGraphExec_t graph = nullptr;
+  bool maps_ready = false;
+  size_t maps_ws = 0;  // workspace generation the maps point into
+  CUtensorMap map_x, map_attn, map_ff, map_selx, map_scored, map_ffsel;
+  int launches = 0;
+};
+
+struct ProfEvent {
+  int family;
+  cudaEvent_t a, b;
+  double flops;
+};
+
+struct Engine {
+  laya_config cfg{};
+  int device = 0;
+  int limit = 16;
+  int sms = 148;
+  bool finalized = false;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev_start = nullptr, ev_end = nullptr;
+  std::unordered_map<std::string, Tensor> weights;
+  std::map<std::string, std::vector<int64_t>> expected;
+  float* rope_cos[2] = {nullptr, nullptr};
+  float* rope_sin[2] = {nullptr, nullptr};
+  int rope_rows = 0;
+  uint8_t* ws = nullptr;
+  size_t ws_bytes = 0;
+  size_t ws_generation = 0;
+  int32_t* h_packed = nullptr;
+  size_t h_packed_cap = 0;
+  float* h_out = nullptr;
+  size_t h_out_cap = 0;
+  std::list<std::tuple<int, int, int>> lru;  // front = least recently used
+  std::map<std::tuple<int, int, int>, std::unique_ptr<Slot>> slots;
+  std::map<std::tuple<const void*, int>, CUtensorMap> wmaps;
+  std::string error;
+  bool profiling = false;
+  std::vector<ProfEvent> prof_pending;
+  std::vector<cudaEvent_t> prof_pool;
+  double prof_ms[4] = {0, 0, 0, 0};
+  double prof_flops[4] = {0, 0, 0, 0};
+  int64_t prof_launches[4] = {0, 0, 0, 0};
+  int launches = 0;
+
+  bool bf16() const { return cfg.precision == LAYA_PRECISION_BF16; }
+  int d() const { return cfg.width; }
+  int F() const { return cfg.intermediate; }
+  int ffw() const { return std::max(cfg.intermediate, 4 * cfg.width); }
+  size_t owned() const {
+    size_t s = ws_bytes;
+    for (auto& kv : weights) s += kv.second.bytes;
+    for (int i = 0; i < 2; ++i) if (rope_cos[i]) s += 2 * (size_t)rope_rows * 32 * sizeof(float);
+    return s;
+  }
+};
+
+void build_expected(Engine& e) {
+  const laya_config& c = e.cfg;
+  const int64_t w = c.width, f = c.intermediate;
+  auto& s = e.expected;
+  s["encoder.embeddings.tok_embeddings.weight"] = {c.vocab, w};
+  s["encoder.embeddings.norm.weight"] = {w};
+  s["encoder.final_norm.weight"] = {w};
+  s["type_emb.weight"] = {3, w};
+  s["temperature"] = {3};
+  s["scorer.0.weight"] = {w};
+  s["scorer.0.bias"] = {w};
+  s["scorer.1.weight"] = {w, w};
+  s["scorer.1.bias"] = {w};
+  s["scorer.3.weight"] = {1, w};
+  s["scorer.3.bias"] = {1};
+  s["act_head.0.weight"] = {256, w + 4};
+  s["act_head.0.bias"] = {256};
+  s["act_head.2.weight"] = {c.n_act, 256};
+  s["act_head.2.bias"] = {c.n_act};
+  for (int i = 0; i < c.layers; ++i) {
+    const std::string p = "encoder.layers." + std::to_string(i) + ".";
+    s[p + "attn.Wqkv.weight"] = {3 * w, w};
+    s[p + "attn.Wo.weight"] = {w, w};
+    s[p + "mlp.Wi.weight"] = {2 * f, w};
+    s[p + "mlp.Wo.weight"] = {w, f};
+    s[p + "mlp_norm.weight"] = {w};
+    if (i) s[p + "attn_norm.weight"] = {w};
+  }
+  for (int i = 0; i < c.head_layers; ++i) {
+    const std::string p = "head.layers." + std::to_string(i) + ".";
+    s[p + "self_attn.in_proj_weight"] = {3 * w, w};
+    s[p + "self_attn.in_proj_bias"] = {3 * w};
+    s[p + "self_attn.out_proj.weight"] = {w, w};
+    s[p + "self_attn.out_proj.bias"] = {w};
+    s[p + "linear1.weight"] = {4 * w, w};
+    s[p + "linear1.bias"] = {4 * w};
+    s[p + "linear2.weight"] = {w, 4 * w};
+    s[p + "linear2.bias"] = {w};
+    s[p + "norm1.weight"] = {w};
+    s[p + "norm1.bias"] = {w};
+    s[p + "norm2.weight"] = {w};
+    s[p + "norm2.bias"] = {w};
+  }
+}
+
+// 16-bit GEMM operands; everything else (norms, embeddings, biases, the head tail) stays fp32.
+bool stored_16bit(const std::string& name) {
+  if (name.find("norm") != std::string::npos) return false;
+  if (name.size() >= 5 && name.compare(name.size() - 5, 5, ".bias") == 0) return false;
+  if (name.size() >= 5 && name.compare(name.size() - 5, 5, "_bias") == 0) return false;
+  if (name == "type_emb.weight" || name == "encoder.embeddings.tok_embeddings.weight") return false;
+  if (name.rfind("scorer.0.", 0) == 0 || name.rfind("scorer.3.", 0) == 0 || name.rfind("act_head.", 0) == 0) return false;
+  return true;
+}
+
+float half_bits_to_float(uint16_t h, bool bf16) {
+  if (bf16) {
+    uint32_t u = (uint32_t)h << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+  }
+  // IEEE binary16 -> binary32
+  const uint32_t sign = (uint32_t)(h & 0x8000) << 16;
+  uint32_t exp = (h >> 10) & 0x1F, man = h & 0x3FF, u;
+  if (exp == 0) {
+    if (man == 0) u = sign;
+    else {
+      int e = -1;
+      do { man <<= 1; ++e; } while (!(man & 0x400));
+      u = sign | ((uint32_t)(127 - 15 - e) << 23) | ((man & 0x3FF) << 13);
+    }
+  } else if (exp == 31) u = sign | 0x7F800000 | (man << 13);
+  else u = sign | ((exp + 112) << 23) | (man << 13);
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+uint16_t float_to_half_bits(float f, bool bf16) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if (bf16) {
+    if ((u & 0x7FFFFFFF) > 0x7F800000) return 0x7FC0;  // NaN
+    const uint32_t lsb = (u >> 16) & 1;
+    return (uint16_t)((u + 0x7FFF + lsb) >> 16);       // round to nearest even
+  }
+  const uint32_t sign = (u >> 16) & 0x8000;
+  const uint32_t a = u & 0x7FFFFFFF;
+  if (a > 0x7F800000) return (uint16_t)(sign | 0x7E00);
+  if (a >= 0x477FF000) return (uint16_t)(sign | 0x7C00);  // overflow -> inf (ties above max)
+  if (a < 0x38800000) {                                    // subnormal or zero
+    if (a < 0x33000000) return (uint16_t)sign;
+    const uint32_t e = a >> 23;
+    const uint32_t m = (a & 0x7FFFFF) | 0x800000;
+    const int shift = 126 - (int)e;  // 14 + (113 - e)
+    uint32_t v = m >> (shift);
+    const uint32_t rem = m & ((1u << shift) - 1), half = 1u << (shift - 1);
+    if (rem > half || (rem == half && (v & 1))) ++v;
+    return (uint16_t)(sign | v);
+  }
+  uint32_t v = ((a - 0x38000000) >> 13);
+  const uint32_t rem = a & 0x1FFF;
+  if (rem > 0x1000 || (rem == 0x1000 && (v & 1))) ++v;
+  return (uint16_t)(sign | v);
+}
+
+void* dev_alloc(size_t bytes) {
+  void* p = nullptr;
+  CK(cudaMalloc(&p, std::max<size_t>(bytes, 256)));
+  return p;
+}
+
+void drop_graphs(Engine& e) {
+  for (auto& kv : e.slots) {
+    if (kv.second->graph) cudaGraphExecDestroy(kv.second->graph);
+    kv.second->graph = nullptr;
+    kv.second->maps_ready = false;
+  }
+}
+
+ClassLayout make_layout(const Engine& e, int m, int b, int k) {
+  ClassLayout L;
+  L.m = m; L.b = b; L.k = k;
+  L.count = b * (k + 1);
+  L.tiles_cap = tiles_capacity(m, b);
+  L.pack = pack_layout(m, b, k);
+  const size_t d = e.d(), es = 2, A = 256;
+  size_t o = 0;
+  auto take = [&](size_t bytes) { size_t at = o; o = align_up(o + bytes, A); return at; };
+  L.packed = take(L.pack.total * 4);
+  L.residual = take((size_t)m * d * 4);
+  L.x = take((size_t)m * d * es);
+  L.qkv = take((size_t)3 * m * d * es);
+  L.attn = take((size_t)m * d * es);
+  L.ff = take((size_t)m * e.ffw() * es);
+  L.sel = take((size_t)L.count * d * 4);
+  L.selx = take((size_t)L.count * d * es);
+  L.scored = take((size_t)L.count * d * es);
+  L.ffsel = take((size_t)L.count * 4 * d * es);
+  L.n_out_floats = (size_t)b * (k + 1) + (size_t)b * e.cfg.n_act + 1;
+  L.out = take(L.n_out_floats * 4);
+  L.total = o;
+  return L;
+}
+
+void ensure_workspace(Engine& e, size_t bytes) {
+  if (bytes <= e.ws_bytes) return;
+  CK(cudaStreamSynchronize(e.stream));
+  drop_graphs(e);
+  if (e.ws) CK(cudaFree(e.ws));
+  e.ws = nullptr;
+  e.ws_bytes = 0;
+  const size_t want = align_up(bytes + bytes / 8, 1 << 20);
+  e.ws = static_cast<uint8_t*>(dev_alloc(want));
+  e.ws_bytes = want;
+  ++e.ws_generation;
+}
+
+void ensure_host(Engine& e, size_t ints, size_t floats) {
+  if (ints > e.h_packed_cap) {
+    if (e.h_packed) CK(cudaFreeHost(e.h_packed));
+    e.h_packed = nullptr;
+    CK(cudaHostAlloc(reinterpret_cast<void**>(&e.h_packed), ints * 4, cudaHostAllocDefault));
+    e.h_packed_cap = ints;
+  }
+  if (floats > e.h_out_cap) {
+    if (e.h_out) CK(cudaFreeHost(e.h_out));
+    e.h_out = nullptr;
+    CK(cudaHostAlloc(reinterpret_cast<void**>(&e.h_out), floats * 4, cudaHostAllocDefault));
+    e.h_out_cap = floats;
+  }
+}
+
+const Tensor& W(const Engine& e, const std::string& name) {
+  auto it = e.weights.find(name);
+  if (it == e.weights.end() || !it->second.ptr) fail(LAYA_ERR_STATE, "tensor %s not loaded", name.c_str());
+  return it->second;
+}
+const float* Wf(const Engine& e, const std::string& name) {
+  const Tensor& t = W(e, name);
+  return static_cast<const float*>(t.ptr);
+}
+
+const CUtensorMap& weight_map(Engine& e, const std::string& name, int bn) {
+  const Tensor& t = W(e, name);
+  auto key = std::make_tuple((const void*)t.ptr, bn);
+  auto it = e.wmaps.find(key);
+  if (it != e.wmaps.end()) return it->second;
+  CUtensorMap m = make_map(t.ptr, t.shape[0], t.shape[1], bn, e.bf16());
+  return e.wmaps.emplace(key, m).first->second;
+}
+
+void prepare_maps(Engine& e, Slot& s) {
+  if (s.maps_ready && s.maps_ws == e.ws_generation) return;
+  const ClassLayout& L = s.L;
+  const bool bf = e.bf16();
+  const int d = e.d();
+  s.map_x = make_map(e.ws + L.x, L.m, d, kBM, bf);
+  s.map_attn = make_map(e.ws + L.attn, L.m, d, kBM, bf);
+  s.map_ff = make_map(e.ws + L.ff, L.m, e.F(), kBM, bf);
+  s.map_selx = make_map(e.ws + L.selx, L.count, d, kBM, bf);
+  s.map_scored = make_map(e.ws + L.scored, L.count, d, kBM, bf);
+  s.map_ffsel = make_map(e.ws + L.ffsel, L.count, 4 * d, kBM, bf);
+  s.maps_ready = true;
+  s.maps_ws = e.ws_generation;
+}
+
+cudaEvent_t prof_event(Engine& e) {
+  if (!e.prof_pool.empty()) {
+    cudaEvent_t ev = e.prof_pool.back();
+    e.prof_pool.pop_back();
+    return ev;
+  }
+  cudaEvent_t ev;
+  CK(cudaEventCreate(&ev));
+  return ev;
+}
+
+// Wraps one launch: counts it and, when profiling an eager pass, brackets it with events.
+template <typename F>
+void launch(Engine& e, bool prof, int family, double flops, F&& f) {
+  ProfEvent pe{family, nullptr, nullptr, flops};
+  if (prof) {
+    pe.a = prof_event(e);
+    pe.b = prof_event(e);
+    CK(cudaEventRecord(pe.a, e.stream));
+  }
+  f();
+  ++e.launches;
+  if (prof) {
+    CK(cudaEventRecord(pe.b, e.stream));
+    e.prof_pending.push_back(pe);
+  }
+}
+
+void prof_resolve(Engine& e) {
+  if (e.prof_pending.empty()) return;
+  CK(cudaStreamSynchronize(e.stream));
+  for (auto& p : e.prof_pending) {
+    float ms = 0;
+    CK(cudaEventElapsedTime(&ms, p.a, p.b));
+    e.prof_ms[p.family] += ms;
+    e.prof_flops[p.family] += p.flops;
+    e.prof_launches[p.family] += 1;
+    e.prof_pool.push_back(p.a);
+    e.prof_pool.push_back(p.b);
+  }
+  e.prof_pending.clear();
+}
+
+template <typename T>
+void gemm(Engine& e, bool prof, int epi, const CUtensorMap& ta, const std::string& wname, int M, void* out, int ldo,
+          float* residual, int ldr, const float* bias, int* err, int rope = -1, const int* positions = nullptr) {
+  const Tensor& w = W(e, wname);
+  const int N = (int)w.shape[0], K = (int)w.shape[1];
+  const int bn = pick_bn(M, N, epi, e.sms);
+  GemmArgs a{};
+  a.M = M; a.N = N; a.K = K; a.splits = 1;
+  a.out = out; a.ldo = ldo; a.residual = residual; a.ldr = ldr; a.bias = bias;
+  a.heads = e.cfg.heads;
+  if (rope >= 0) { a.cos_tab = e.rope_cos[rope]; a.sin_tab = e.rope_sin[rope]; }
+  a.positions = positions;
+  a.err = err;
+  const CUtensorMap& tb = weight_map(e, wname, bn);
+  launch(e, prof, 0, 2.0 * M * N * K, [&] { launch_gemm<T>(epi, bn, ta, tb, a, e.sms, e.stream); });
+}
+
+// The whole forward pass of one shape class (runtime.py:90-113 + laya.py:214-245), enqueued
+// on the engine stream.  Used eagerly and inside graph capture.
+template <typename T>
+void enqueue_forward(Engine& e, Slot& s, bool prof) {
+  const ClassLayout& L = s.L;
+  const laya_config& c = e.cfg;
+  const int m = L.m, d = c.width, count = L.count;
+  uint8_t* ws = e.ws;
+  const int32_t* in = reinterpret_cast<const int32_t*>(ws + L.packed);
+  const int* ids = in + L.pack.ids;
+  const int* positions = in + L.pack.positions;
+  const int* kinds = in + L.pack.kinds;
+  const int* starts = in + L.pack.starts;
+  const int* lengths = in + L.pack.lengths;
+  const int* counts = in + L.pack.counts;
+  const int* indices = in + L.pack.indices;
+  const int4* tiles = reinterpret_cast<const int4*>(in + L.pack.tiles);
+  float* residual = reinterpret_cast<float*>(ws + L.residual);
+  T* x = reinterpret_cast<T*>(ws + L.x);
+  T* qkv = reinterpret_cast<T*>(ws + L.qkv);
+  T* attn = reinterpret_cast<T*>(ws + L.attn);
+  T* ff = reinterpret_cast<T*>(ws + L.ff);
+  float* sel = reinterpret_cast<float*>(ws + L.sel);
+  T* selx = reinterpret_cast<T*>(ws + L.selx);
+  T* scored = reinterpret_cast<T*>(ws + L.scored);
+  T* ffsel = reinterpret_cast<T*>(ws + L.ffsel);
+  float* outf = reinterpret_cast<float*>(ws + L.out);
+  float* logits = outf;
+  float* acts = outf + (size_t)L.b * (L.k + 1);
+  int* err = reinterpret_cast<int*>(acts + (size_t)L.b * c.n_act);
+
+  CK(cudaMemsetAsync(err, 0, sizeof(int), e.stream));
+  const double rowbytes = (double)m * d;
+  launch(e, prof, 2, 0, [&] {
+    launch_embed<T>(ids, Wf(e, "encoder.embeddings.tok_embeddings.weight"), Wf(e, "encoder.embeddings.norm.weight"),
+                    c.eps, m, d, c.vocab, residual, x, err, e.stream);
+  });
+  (void)rowbytes;
+
+  auto attention = [&](int window) {
+    AttnArgs a{};
+    a.qkv = qkv; a.out = attn; a.tiles = tiles; a.starts = starts; a.lengths = lengths;
+    a.M = m; a.heads = c.heads; a.window = window;
+    launch(e, prof, 1, 0, [&] { launch_attention<T>(a, L.tiles_cap, false, e.stream); });
+  };
+  auto norm = [&](float* res, int rows, const float* g, const float* b, float eps, T* out) {
+    NormArgs a{};
+    a.residual = res; a.partials = nullptr; a.splits = 0;
+    a.gamma1 = g; a.beta1 = b; a.eps1 = eps; a.fused_final = 0;
+    a.x = out; a.rows = rows; a.d = d;
+    launch(e, prof, 2, 0, [&] { launch_norm<T>(a, e.stream); });
+  };
+
+  for (int i = 0; i < c.layers; ++i) {
+    const std::string p = "encoder.layers." + std::to_string(i) + ".";
+    const bool local = i % c.global_every != 0;
+    gemm<T>(e, prof, EPI_QKV, s.map_x, p + "attn.Wqkv.weight", m, qkv, 0, nullptr, 0, nullptr, err, local ? 1 : 0, positions);
+    attention(local ? c.window : -1);
+    gemm<T>(e, prof, EPI_RESIDUAL, s.map_attn, p + "attn.Wo.weight", m, nullptr, 0, residual, d, nullptr, err);
+    norm(residual, m, Wf(e, p + "mlp_norm.weight"), nullptr, c.eps, x);
+    gemm<T>(e, prof, EPI_GEGLU, s.map_x, p + "mlp.Wi.weight", m, ff, e.F(), nullptr, 0, nullptr, err);
+    gemm<T>(e, prof, EPI_RESIDUAL, s.map_ff, p + "mlp.Wo.weight", m, nullptr, 0, residual, d, nullptr, err);
+    if (i + 1 < c.layers) {
+      norm(residual, m, Wf(e, "encoder.layers." + std::to_string(i + 1) + ".attn_norm.weight"), nullptr, c.eps, x);
+    } else {
+      // encoder.final_norm -> residual; residual += type_emb[kind]; x = head.layers.0.norm1(residual)
+      NormArgs a{};
+      a.residual = residual; a.splits = 0;
+      a.gamma1 = Wf(e, "encoder.final_norm.weight"); a.beta1 = nullptr; a.eps1 = c.eps;
+      a.fused_final = 1; a.type_emb = Wf(e, "type_emb.weight"); a.kinds = kinds;
+      a.gamma2 = Wf(e, "head.layers.0.norm1.weight"); a.beta2 = Wf(e, "head.layers.0.norm1.bias"); a.eps2 = 1e-5f;
+      a.x = x; a.rows = m; a.d = d;
+      launch(e, prof, 2, 0, [&] { launch_norm<T>(a, e.stream); });
+    }
+  }
+
+  for (int i = 0; i < c.head_layers; ++i) {
+    const std::string p = "head.layers." + std::to_string(i) + ".";
+    if (i > 0) norm(residual, m, Wf(e, p + "norm1.weight"), Wf(e, p + "norm1.bias"), 1e-5f, x);
+    gemm<T>(e, prof, EPI_QKV, s.map_x, p + "self_attn.in_proj_weight", m, qkv, 0, nullptr, 0,
+            Wf(e, p + "self_attn.in_proj_bias"), err);
+    attention(-1);
+    if (i + 1 == c.head_layers) {
+      launch(e, prof, 2, 0, [&] {
+        gather_rows_kernel<T><<<count, 256, 0, e.stream>>>(residual, attn, indices, count, d, m, sel, scored, err);
+        CK(cudaGetLastError());
+      });
+      gemm<T>(e, prof, EPI_RESIDUAL, s.map_scored, p + "self_attn.out_proj.weight", count, nullptr, 0, sel, d,
+              Wf(e, p + "self_attn.out_proj.bias"), err);
+      norm(sel, count, Wf(e, p + "norm2.weight"), Wf(e, p + "norm2.bias"), 1e-5f, selx);
+      gemm<T>(e, prof, EPI_RELU, s.map_selx, p + "linear1.weight", count, ffsel, 4 * d, nullptr, 0,
+              Wf(e, p + "linear1.bias"), err);
+      gemm<T>(e, prof, EPI_RESIDUAL, s.map_ffsel, p + "linear2.weight", count, nullptr, 0, sel, d,
+              Wf(e, p + "linear2.bias"), err);
+    } else {
+      gemm<T>(e, prof, EPI_RESIDUAL, s.map_attn, p + "self_attn.out_proj.weight", m, nullptr, 0, residual, d,
+              Wf(e, p + "self_attn.out_proj.bias"), err);
+      norm(residual, m, Wf(e, p + "norm2.weight"), Wf(e, p + "norm2.bias"), 1e-5f, x);
+      gemm<T>(e, prof, EPI_RELU, s.map_x, p + "linear1.weight", m, ff, 4 * d, nullptr, 0, Wf(e, p + "linear1.bias"), err);
+      const CUtensorMap ffmap = make_map(ff, m, 4 * d, kBM, e.bf16());
+      gemm<T>(e, prof, EPI_RESIDUAL, ffmap, p + "linear2.weight", m, nullptr, 0, residual, d,
+              Wf(e, p + "linear2.bias"), err);
+    }
+  }
+  norm(sel, count, Wf(e, "scorer.0.weight"), Wf(e, "scorer.0.bias"), 1e-5f, selx);
+  gemm<T>(e, prof, EPI_GELU, s.map_selx, "scorer.1.weight", count, scored, d, nullptr, 0, Wf(e, "scorer.1.bias"), err);
+  TailArgs t{};
+  t.selected = sel; t.scored = scored; t.counts = counts;
+  t.w3 = Wf(e, "scorer.3.weight"); t.b3 = Wf(e, "scorer.3.bias");
+  t.wa0 = Wf(e, "act_head.0.weight"); t.ba0 = Wf(e, "act_head.0.bias");
+  t.wa2 = Wf(e, "act_head.2.weight"); t.ba2 = Wf(e, "act_head.2.bias");
+  t.logits = logits; t.acts = acts; t.k = L.k; t.d = d; t.n_act = c.n_act;
+  const size_t tail_smem = ((size_t)(L.k + 1) + d + 4 + kActHidden) * sizeof(float);
+  launch(e, prof, 3, 0, [&] {
+    head_tail_kernel<T><<<L.b, kTailThreads, tail_smem, e.stream>>>(t);
+    CK(cudaGetLastError());
+  });
+}
+
+void forward(Engine& e, Slot& s, bool prof) {
+  if (e.bf16()) enqueue_forward<__nv_bfloat16>(e, s, prof);
+  else enqueue_forward<__half>(e, s, prof);
+}
+
+Slot& get_slot(Engine& e, int m, int b, int k, bool& miss) {
+  auto key = std::make_tuple(m, b, k);
+  auto it = e.slots.find(key);
+  miss = it == e.slots.end();
+  if (miss) {
+    if ((int)e.slots.size() >= e.limit) {
+      CK(cudaStreamSynchronize(e.stream));
+      auto victim = e.lru.front();
+      e.lru.pop_front();
+      auto& vs = e.slots[victim];
+      if (vs->graph) cudaGraphExecDestroy(vs->graph);
+      e.slots.erase(victim);
+    }
+    auto s = std::make_unique<Slot>();
+    s->m = m; s->b = b; s->k = k;
+    s->L = make_layout(e, m, b, k);
+    it = e.slots.emplace(key, std::move(s)).first;
+  } else {
+    e.lru.remove(key);
+  }
+  e.lru.push_back(key);
+  return *it->second;
+}
+
+// Runs one pass of slot `s` whose inputs are already in the workspace.  Returns the launch count.
+int run_slot(Engine& e, Slot& s, bool capture, bool& captured) {
+  captured = false;
+  prepare_maps(e, s);
+  if (capture) {
+    if (!s.graph) {
+      cudaGraph_t g = nullptr;
+      const int before = e.launches;
+      CK(cudaStreamBeginCapture(e.stream, cudaStreamCaptureModeThreadLocal));
+      try {
+        forward(e, s, false);
+      } catch (...) {
+        cudaStreamEndCapture(e.stream, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+      }
+      CK(cudaStreamEndCapture(e.stream, &g));
+      cudaError_t r = cudaGraphInstantiate(&s.graph, g, 0);
+      cudaGraphDestroy(g);
+      if (r != cudaSuccess) { s.graph = nullptr; fail(LAYA_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(r)); }
+      s.launches = e.launches - before;
+      e.launches = before;
+      captured = true;
+    }
+    CK(cudaGraphLaunch(s.graph, e.stream));
+    return s.launches;
+  }
+  const int before = e.launches;
+  forward(e, s, e.profiling);
+  return e.launches - before;
+}
+
+}  // namespace
+
+struct laya_engine {
+  Engine impl;
+};
+
+namespace {
+int finish_error(laya_engine* h, const Failure& f) {
+  if (h) h->impl.error = f.msg;
+  else g_create_error = f.msg;
+  return f.code;
+}
+}  // namespace
+
+#define API_BEGIN try {
+#define API_END(h)                                                   \
+  }                                                                  \
+  catch (const Failure& f) { return finish_error(h, f); }            \
+  catch (const std::exception& x) { return finish_error(h, Failure{LAYA_ERR_CUDA, x.what()}); } \
+  return LAYA_OK;
+
+extern "C" {
+
+int laya_create(const laya_config* cfg, int device, int max_cached_shapes, laya_engine** out) {
+  API_BEGIN
+  if (!cfg || !out) fail(LAYA_ERR_INVALID, "null argument");
+  *out = nullptr;
+  const laya_config& c = *cfg;
+  if (c.width <= 0 || c.width % 64 || c.width > 1024 || c.heads * 64 != c.width)
+    fail(LAYA_ERR_INVALID, "width must be heads x 64 and at most 1024");
+  if (c.layers <= 0 || c.intermediate <= 0 || c.intermediate % 64 || c.global_every <= 0 || c.window < 0)
+    fail(LAYA_ERR_INVALID, "invalid encoder geometry");
+  if (c.max_len <= 0 || c.max_len > 1024 || c.head_layers < 1 || c.n_act < 1 || c.n_act > 64 || c.vocab <= 0)
+    fail(LAYA_ERR_INVALID, "invalid context budget or decision head");
+  if (c.precision != LAYA_PRECISION_BF16 && c.precision != LAYA_PRECISION_F16) fail(LAYA_ERR_INVALID, "bad precision");
+  if (max_cached_shapes < 1 || max_cached_shapes > 64) fail(LAYA_ERR_INVALID, "max_cached_shapes must be 1..64");
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) fail(LAYA_ERR_NO_DEVICE, "no CUDA device");
+  if (device < 0 || device >= n) fail(LAYA_ERR_NO_DEVICE, "device %d not present", device);
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10) fail(LAYA_ERR_NO_DEVICE, "%s is sm_%d%d; this build targets sm_100a (B200)", prop.name, prop.major, prop.minor);
+  CK(cudaSetDevice(device));
+  auto h = std::make_unique<laya_engine>();
+  Engine& e = h->impl;
+  e.cfg = c;
+  e.device = device;
+  e.limit = max_cached_shapes;
+  e.sms = sm_count(device);
+  build_expected(e);
+  CK(cudaStreamCreateWithFlags(&e.stream, cudaStreamNonBlocking));
+  CK(cudaEventCreate(&e.ev_start));
+  CK(cudaEventCreate(&e.ev_end));
+  *out = h.release();
+  API_END(nullptr)
+}
+
+int laya_load_tensor(laya_engine* h, const char* name, int dtype, const int64_t* shape, int ndim, const void* host) {
+  API_BEGIN
+  if (!h || !name || !host || (ndim > 0 && !shape)) fail(LAYA_ERR_INVALID, "null argument");
+  Engine& e = h->impl;
+  CK(cudaSetDevice(e.device));
+  auto it = e.expected.find(name);
+  if (it == e.expected.end()) fail(LAYA_ERR_INVALID, "Checkpoint tensor names do not match the Laya adapter: %s", name);
+  std::vector<int64_t> sh(shape, shape + ndim);
+  if (sh != it->second) fail(LAYA_ERR_INVALID, "Incompatible tensor shape: %s", name);
+  if (std::string(name) == "temperature") return LAYA_OK;
+  int64_t count = 1;
+  for (auto v : sh) count *= v;
+  std::vector<float> vals((size_t)count);
+  if (dtype == LAYA_DTYPE_F32) memcpy(vals.data(), host, (size_t)count * 4);
+  else if (dtype == LAYA_DTYPE_F16 || dtype == LAYA_DTYPE_BF16) {
+    const uint16_t* s = static_cast<const uint16_t*>(host);
+    for (int64_t i = 0; i < count; ++i) vals[i] = half_bits_to_float(s[i], dtype == LAYA_DTYPE_BF16);
+  } else fail(LAYA_ERR_INVALID, "unsupported dtype %d", dtype);
+  Tensor t;
+  t.shape = sh;
+  const std::string n(name);
+  const bool is16 = stored_16bit(n);
+  std::vector<uint16_t> packed;
+  const void* src = vals.data();
+  if (is16) {
+    packed.resize((size_t)count);
+    const bool geglu = n.find("mlp.Wi.weight") != std::string::npos;
+    if (geglu) {
+      // Interleave gate/up rows in 64-row blocks so one column tile holds matching pairs.
+      const int64_t F = sh[0] / 2, K = sh[1];
+      for (int64_t blk = 0; blk < F / 64; ++blk)
+        for (int half = 0; half < 2; ++half)
+          for (int64_t r = 0; r < 64; ++r) {
+            const int64_t src_row = half * F + blk * 64 + r, dst_row = blk * 128 + half * 64 + r;
+            for (int64_t c = 0; c < K; ++c) packed[dst_row * K + c] = float_to_half_bits(vals[src_row * K + c], e.bf16());
+          }
+    } else {
+      for (int64_t i = 0; i < count; ++i) packed[i] = float_to_half_bits(vals[i], e.bf16());
+    }
+    src = packed.data();
+    t.dtype = e.bf16() ? LAYA_DTYPE_BF16 : LAYA_DTYPE_F16;
+    t.bytes = (size_t)count * 2;
+  } else {
+    t.dtype = LAYA_DTYPE_F32;
+    t.bytes = (size_t)count * 4;
+  }
+  auto old = e.weights.find(n);
+  if (old != e.weights.end() && old->second.ptr) {
+    CK(cudaFree(old->second.ptr));
+    e.wmaps.clear();
+  }
+  t.ptr = dev_alloc(t.bytes);
+  CK(cudaMemcpy(t.ptr, src, t.bytes, cudaMemcpyHostToDevice));
+  e.weights[n] = t;
+  e.finalized = false;
+  API_END(h)
+}
+
+int laya_finalize(laya_engine* h) {
+  API_BEGIN
+  if (!h) fail(LAYA_ERR_INVALID, "null engine");
+  Engine& e = h->impl;
+  CK(cudaSetDevice(e.device));
+  for (auto& kv : e.expected)
+    if (kv.first != "temperature" && !e.weights.count(kv.first)) fail(LAYA_ERR_INVALID, "missing tensor %s", kv.first.c_str());
+  if (e.F() % 64) fail(LAYA_ERR_INVALID, "intermediate size must be a multiple of 64");
+  // RoPE tables cover every position a packed row can hold (runtime.py:159-165):
+  // freq_j = 1 / theta^(2j/64) in fp32, angle = pos * freq_j in fp32.
+  e.rope_rows = span16(e.cfg.max_len);
+  const float thetas[2] = {e.cfg.theta_global, e.cfg.theta_local};
+  for (int t = 0; t < 2; ++t) {
+    std::vector<float> cs((size_t)e.rope_rows * 32), sn((size_t)e.rope_rows * 32);
+    for (int j = 0; j < 32; ++j) {
+      const float expo = (float)(2 * j) / 64.0f;
+      const float freq = 1.0f / powf(thetas[t], expo);
+      for (int pos = 0; pos < e.rope_rows; ++pos) {
+        const float angle = (float)pos * freq;
+        cs[(size_t)pos * 32 + j] = (float)cos((double)angle);
+        sn[(size_t)pos * 32 + j] = (float)sin((double)angle);
+      }
+    }
+    if (e.rope_cos[t]) { cudaFree(e.rope_cos[t]); cudaFree(e.rope_sin[t]); }
+    e.rope_cos[t] = static_cast<float*>(dev_alloc(cs.size() * 4));
+    e.rope_sin[t] = static_cast<float*>(dev_alloc(sn.size() * 4));
+    CK(cudaMemcpy(e.rope_cos[t], cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(e.rope_sin[t], sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+  }
+  drop_graphs(e);
+  e.finalized = true;
+  API_END(h)
+}
+
+int laya_shape_class(const int32_t* lengths, const int32_t* marker_counts, int n_items, int32_t* rows, int32_t* batch,
+                     int32_t* options) {
+  API_BEGIN
+  int m, b, k;
+  shape_class(lengths, marker_counts, n_items, m, b, k);
+  *rows = m; *batch = b; *options = k;
+  API_END(nullptr)
+}
+
+int64_t laya_packed_ints(int rows, int batch, int options) { return pack_layout(rows, batch, options).total; }
+
+int laya_pack(const int32_t* tokens, const int32_t* lengths, const int32_t* markers, const int32_t* marker_counts,
+              const int32_t* kinds, int n_items, int pad_id, int rows, int batch, int options, int32_t* packed) {
+  API_BEGIN
+  if (n_items > batch) fail(LAYA_ERR_INVALID, "more items than the batch class");
+  pack(tokens, lengths, markers, marker_counts, kinds, n_items, pad_id, rows, batch, options, 1024, packed);
+  API_END(nullptr)
+}
+
+int laya_predict(laya_engine* h, const int32_t* tokens, const int32_t* lengths, const int32_t* markers,
+                 const int32_t* marker_counts, const int32_t* kinds, int n_items, int capture, float* logits_out,
+                 float* acts_out, laya_metrics* metrics) {
+  API_BEGIN
+  if (!h) fail(LAYA_ERR_INVALID, "null engine");
+  Engine& e = h->impl;
+  if (!e.finalized) fail(LAYA_ERR_STATE, "engine not finalised");
+  if (!tokens || !lengths || !marker_counts || !kinds || !logits_out || !acts_out) fail(LAYA_ERR_INVALID, "null argument");
+  CK(cudaSetDevice(e.device));
+  int m, b, k;
+  shape_class(lengths, marker_counts, n_items, m, b, k);
+  bool miss = false;
+  Slot& s = get_slot(e, m, b, k, miss);
+  ensure_workspace(e, s.L.total);
+  ensure_host(e, (size_t)s.L.pack.total, s.L.n_out_floats);
+  // The pad id is the tokenizer's [PAD]; padded positions are never attended by real tokens.
+  pack(tokens, lengths, markers, marker_counts, kinds, n_items, 0, m, b, k, e.cfg.max_len, e.h_packed);
+  CK(cudaMemcpyAsync(e.ws + s.L.packed, e.h_packed, (size_t)s.L.pack.total * 4, cudaMemcpyHostToDevice, e.stream));
+  bool captured = false;
+  CK(cudaEventRecord(e.ev_start, e.stream));
+  const int launches = run_slot(e, s, capture != 0, captured);
+  CK(cudaEventRecord(e.ev_end, e.stream));
+  CK(cudaMemcpyAsync(e.h_out, e.ws + s.L.out, s.L.n_out_floats * 4, cudaMemcpyDeviceToHost, e.stream));
+  CK(cudaStreamSynchronize(e.stream));
+  prof_resolve(e);
+  const float* outf = e.h_out;
+  const int errword = *reinterpret_cast<const int*>(outf + (size_t)b * (k + 1) + (size_t)b * e.cfg.n_act);
+  if (errword) fail(LAYA_ERR_DEVICE, "device error %d during the forward pass", errword);
+  for (int i = 0; i < n_items; ++i) {
+    memcpy(logits_out + (size_t)i * k, outf + (size_t)i * (k + 1) + 1, (size_t)k * 4);
+    memcpy(acts_out + (size_t)i * e.cfg.n_act, outf + (size_t)b * (k + 1) + (size_t)i * e.cfg.n_act,
+           (size_t)e.cfg.n_act * 4);
+  }
+  if (metrics) {
+    float ms = 0;
+    CK(cudaEventElapsedTime(&ms, e.ev_start, e.ev_end));
+    metrics->gpu_ms = ms;
+    metrics->rows = m; metrics->batch = b; metrics->options = k;
+    metrics->cache_miss = miss;
+    metrics->graph_capture = captured;
+    metrics->graph_replay = capture && s.graph != nullptr;
+    metrics->kernel_launches = launches;
+    metrics->owned_gpu_bytes = e.owned();
+  }
+  API_END(h)
+}
+
+int laya_forward_device(laya_engine* h, const int32_t* packed, int rows, int batch, int options, int capture,
+                        float* logits_dev, float* acts_dev) {
+  API_BEGIN
+  if (!h || !packed) fail(LAYA_ERR_INVALID, "null argument");
+  Engine& e = h->impl;
+  if (!e.finalized) fail(LAYA_ERR_STATE, "engine not finalised");
+  CK(cudaSetDevice(e.device));
+  bool miss = false;
+  Slot& s = get_slot(e, rows, batch, options, miss);
+  ensure_workspace(e, s.L.total);
+  CK(cudaMemcpyAsync(e.ws + s.L.packed, packed, (size_t)s.L.pack.total * 4, cudaMemcpyDeviceToDevice, e.stream));
+  bool captured = false;
+  run_slot(e, s, capture != 0, captured);
+  const float* outf = reinterpret_cast<const float*>(e.ws + s.L.out);
+  if (logits_dev)
+    CK(cudaMemcpyAsync(logits_dev, outf, (size_t)batch * (options + 1) * 4, cudaMemcpyDeviceToDevice, e.stream));
+  if (acts_dev)
+    CK(cudaMemcpyAsync(acts_dev, outf + (size_t)batch * (options + 1), (size_t)batch * e.cfg.n_act * 4,
+                       cudaMemcpyDeviceToDevice, e.stream));
+  API_END(h)
+}
+
+void* laya_stream(laya_engine* h) { return h ? (void*)h->impl.stream : nullptr; }
+
+int laya_set_profiling(laya_engine* h, int enabled) {
+  API_BEGIN
+  if (!h) fail(LAYA_ERR_INVALID, "null engine");
+  h->impl.profiling = enabled != 0;
+  API_END(h)
+}
+
+int laya_profile_read(laya_engine* h, int family, double* total_ms, int64_t* launches, double* flops) {
+  API_BEGIN
+  if (!h || family < 0 || family > 3) fail(LAYA_ERR_INVALID, "bad profile family");
+  Engine& e = h->impl;
+  CK(cudaSetDevice(e.device));
+  prof_resolve(e);
+  if (total_ms) *total_ms = e.prof_ms[family];
+  if (launches) *launches = e.prof_launches[family];
+  if (flops) *flops = e.prof_flops[family];
+  API_END(h)
+}
+
+int laya_read_tensor(laya_engine* h, const char* name, float* out, int64_t count) {
+  API_BEGIN
+  if (!h || !name || !out) fail(LAYA_ERR_INVALID, "null argument");
+  Engine& e = h->impl;
+  CK(cudaSetDevice(e.device));
+  auto it = e.weights.find(name);
+  if (it == e.weights.end()) fail(LAYA_ERR_INVALID, "tensor %s not loaded", name);
+  const Tensor& t = it->second;
+  int64_t n = 1;
+  for (auto v : t.shape) n *= v;
+  if (count != n) fail(LAYA_ERR_INVALID, "tensor %s has %lld values", name, (long long)n);
+  if (t.dtype == LAYA_DTYPE_F32) {
+    CK(cudaMemcpy(out, t.ptr, (size_t)n * 4, cudaMemcpyDeviceToHost));
+  } else {
+    std::vector<uint16_t> tmp((size_t)n);
+    CK(cudaMemcpy(tmp.data(), t.ptr, (size_t)n * 2, cudaMemcpyDeviceToHost));
+    const bool geglu = std::string(name).find("mlp.Wi.weight") != std::string::npos;
+    const int64_t K = t.shape.size() > 1 ? t.shape[1] : 1, F = t.shape[0] / 2;
+    for (int64_t i = 0; i < n; ++i) {
+      int64_t src = i;
+      if (geglu) {  // undo the gate/up interleave
+        const int64_t row = i / K, c = i % K, half = row / F, r = row % F;
+        src = ((r / 64) * 128 + half * 64 + r % 64) * K + c;
+      }
+      out[i] = half_bits_to_float(tmp[(size_t)src], t.dtype == LAYA_DTYPE_BF16);
+    }
+  }
+  API_END(h)
+}
+
+int laya_cached_shapes(laya_engine* h, int32_t* count) {
+  API_BEGIN
+  if (!h || !count) fail(LAYA_ERR_INVALID, "null argument");
+  *count = (int32_t)h->impl.slots.size();
+  API_END(h)
+}
+
+int laya_pool_bytes(laya_engine* h, uint64_t* used, uint64_t* total) {
+  API_BEGIN
+  if (!h) fail(LAYA_ERR_INVALID, "null engine");
+  const uint64_t v = h->impl.owned();
+  if (used) *used = v;
+  if (total) *total = v;
+  API_END(h)
+}
+
+int laya_destroy(laya_engine* h) {
+  if (!h) return LAYA_OK;
+  Engine& e = h->impl;
+  int rc = LAYA_OK;
+  if (cudaSetDevice(e.device) != cudaSuccess) rc = LAYA_ERR_CUDA;
+  if (e.stream) cudaStreamSynchronize(e.stream);
+  for (auto& kv : e.slots)
+    if (kv.second->graph) cudaGraphExecDestroy(kv.second->graph);
+  e.slots.clear();
+  for (auto& kv : e.weights)
+    if (kv.second.ptr) cudaFree(kv.second.ptr);
+  e.weights.clear();
+  for (int i = 0; i < 2; ++i) {
+    if (e.rope_cos[i]) cudaFree(e.rope_cos[i]);
+    if (e.rope_sin[i]) cudaFree(e.rope_sin[i]);
+  }
+  if (e.ws) cudaFree(e.ws);
+  if (e.h_packed) cudaFreeHost(e.h_packed);
+  if (e.h_out) cudaFreeHost(e.h_out);
+  for (auto& p : e.prof_pending) { cudaEventDestroy(p.a); cudaEventDestroy(p.b); }
+  for (auto ev : e.prof_pool) cudaEventDestroy(ev);
+  if (e.ev_start) cudaEventDestroy(e.ev_start);
+  if (e.ev_end) cudaEventDestroy(e.ev_end);
+  if (e.stream) cudaStreamDestroy(e.stream);
+  delete h;
+  return rc;
+}
+
+const char* laya_last_error(laya_engine* h) { return h ? h->impl.error.c_str() : g_create_error.c_str(); }
+
+// ---------------------------------------------------------------------------------------------
+// Kernel-level entry points
+// ---------------------------------------------------------------------------------------------
+int laya_op_gemm(int precision, int epi, const void* x, const void* w, int M, int N, int K, void* out, int ldo,
+                 float* residual, int ldr, const float* bias, int heads, const float* cos_tab, const float* sin_tab,
+                 const int32_t* positions, int splits, int block_n, int* err, void* stream) {
+  API_BEGIN
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  const int sms = sm_count(dev);
+  const bool bf = precision == LAYA_PRECISION_BF16;
+  if (splits < 1) splits = 1;
+  const int bn = block_n ? block_n : pick_bn(M, N, epi, sms);
+  GemmArgs a{};
+  a.M = M; a.N = N; a.K = K; a.splits = splits;
+  a.out = out; a.ldo = ldo; a.residual = residual; a.ldr = ldr; a.bias = bias;
+  a.heads = heads; a.cos_tab = cos_tab; a.sin_tab = sin_tab; a.positions = positions; a.err = err;
+  const CUtensorMap ta = make_map(x, M, K, kBM, bf);
+  const CUtensorMap tb = make_map(w, N, K, bn, bf);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (bf) launch_gemm<__nv_bfloat16>(epi, bn, ta, tb, a, sms, st);
+  else launch_gemm<__half>(epi, bn, ta, tb, a, sms, st);
+  API_END(nullptr)
+}
+
+int laya_interleave_geglu(const uint16_t* src, uint16_t* dst, int F, int K) {
+  API_BEGIN
+  if (F % 64) fail(LAYA_ERR_INVALID, "F must be a multiple of 64");
+  for (int blk = 0; blk < F / 64; ++blk)
+    for (int half = 0; half < 2; ++half)
+      for (int r = 0; r < 64; ++r)
+        memcpy(dst + ((size_t)blk * 128 + half * 64 + r) * K, src + ((size_t)half * F + blk * 64 + r) * K, (size_t)K * 2);
+  API_END(nullptr)
+}
+
+int laya_attention_tiles(const int32_t* starts, const int32_t* lengths, int n_rows, int M, int32_t* tiles, int capacity) {
+  return build_tiles(starts, lengths, n_rows, M, tiles, capacity);
+}
+
+int laya_op_attention(int precision, const void* qkv, void* out, const int32_t* tiles, int n_tiles, const int32_t* starts,
+                      const int32_t* lengths, int M, int heads, int window, int split_p, void* stream) {
+  API_BEGIN
+  AttnArgs a{};
+  a.qkv = qkv; a.out = out; a.tiles = reinterpret_cast<const int4*>(tiles); a.starts = starts; a.lengths = lengths;
+  a.M = M; a.heads = heads; a.window = window;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (precision == LAYA_PRECISION_BF16) launch_attention<__nv_bfloat16>(a, n_tiles, split_p != 0, st);
+  else launch_attention<__half>(a, n_tiles, split_p != 0, st);
+  API_END(nullptr)
+}
+
+int laya_op_embed_norm(int precision, const int32_t* ids, const float* table, const float* gamma, float eps, int rows,
+                       int width, int vocab, float* residual, void* x, int* err, void* stream) {
+  API_BEGIN
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (precision == LAYA_PRECISION_BF16)
+    launch_embed<__nv_bfloat16>(ids, table, gamma, eps, rows, width, vocab, residual, static_cast<__nv_bfloat16*>(x), err, st);
+  else launch_embed<__half>(ids, table, gamma, eps, rows, width, vocab, residual, static_cast<__half*>(x), err, st);
+  API_END(nullptr)
+}
+
+int laya_op_norm(int precision, float* residual, const float* partials, int splits, const float* gamma, const float* beta,
+                 float eps, void* x, int rows, int width, void* stream) {
+  API_BEGIN
+  NormArgs a{};
+  a.residual = residual; a.partials = partials; a.splits = partials ? splits : 0;
+  a.gamma1 = gamma; a.beta1 = beta; a.eps1 = eps; a.fused_final = 0; a.x = x; a.rows = rows; a.d = width;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (precision == LAYA_PRECISION_BF16) launch_norm<__nv_bfloat16>(a, st);
+  else launch_norm<__half>(a, st);
+  API_END(nullptr)
+}
+
+}  // extern "C"

@@ -1,0 +1,256 @@
+"""Kernel-level parity of the sm_100a library against float64 / fp32 references.
+
+Mirrors the reference's kernel tests (tests/test_gpu.py, tests/test_attention.py): GEMM with
+every fused epilogue, RoPE layout, LayerNorm, embedding gather, packed varlen attention with
+sliding windows and padding rows.  Device memory comes from torch (plumbing only); every kernel
+runs through the C ABI.
+"""
+import ctypes as ct
+import math
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+from laya_cuda import _lib  # noqa: E402
+from laya_cuda.runtime import span  # noqa: E402
+
+PRECISIONS = {"bf16": (_lib.PRECISION_BF16, torch.bfloat16), "f16": (_lib.PRECISION_F16, torch.float16)}
+# Output rounding of one 16-bit value (relative); bf16 keeps 8 mantissa bits, f16 11.
+ROUND = {"bf16": 2.0 ** -8, "f16": 2.0 ** -11}
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA device required")
+    return _lib.load()
+
+
+def ptr(t):
+    return ct.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def stream():
+    return ct.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def gemm(lib, prec, epi, x, w, out=None, ldo=0, residual=None, ldr=0, bias=None, heads=0, cos=None, sin=None,
+         positions=None, splits=1, block_n=0):
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    M, K = x.shape
+    N = w.shape[0]
+    _lib.check(lib.laya_op_gemm(PRECISIONS[prec][0], epi, ptr(x), ptr(w), M, N, K, ptr(out), ldo, ptr(residual), ldr,
+                                ptr(bias), heads, ptr(cos), ptr(sin), ptr(positions), splits, block_n, ptr(err),
+                                stream()))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+
+
+def rand16(shape, prec, rng, scale=1.0):
+    a = rng.normal(0, scale, shape).astype(np.float32)
+    t = torch.from_numpy(a).to(PRECISIONS[prec][1])
+    return t.cuda(), t.float().double().numpy()
+
+
+@pytest.mark.parametrize("prec", ["bf16", "f16"])
+@pytest.mark.parametrize("M,N,K,block_n", [(7, 64, 64, 0), (96, 768, 768, 0), (200, 2304, 768, 256),
+                                           (513, 768, 3072, 128), (1000, 256, 768, 64), (128, 512, 256, 0)])
+def test_gemm_store_matches_fp64(lib, prec, M, N, K, block_n):
+    rng = np.random.default_rng(M + N + K)
+    x, xd = rand16((M, K), prec, rng)
+    w, wd = rand16((N, K), prec, rng, 0.05)
+    bias = torch.from_numpy(rng.normal(0, 0.1, N).astype(np.float32)).cuda()
+    out = torch.full((M, N), float("nan"), dtype=PRECISIONS[prec][1], device="cuda")
+    gemm(lib, prec, 0, x, w, out, N, bias=bias, block_n=block_n)
+    expected = xd @ wd.T + bias.double().cpu().numpy()
+    got = out.double().cpu().numpy()
+    tol = ROUND[prec] * np.abs(expected) + 1e-4 * math.sqrt(K)
+    assert np.all(np.abs(got - expected) <= tol), float(np.max(np.abs(got - expected) - tol))
+
+
+@pytest.mark.parametrize("prec", ["bf16", "f16"])
+@pytest.mark.parametrize("epi", [1, 2])
+def test_gemm_relu_gelu_epilogues(lib, prec, epi):
+    rng = np.random.default_rng(3 + epi)
+    M, N, K = 150, 3072, 768
+    x, xd = rand16((M, K), prec, rng)
+    w, wd = rand16((N, K), prec, rng, 0.05)
+    bias = torch.from_numpy(rng.normal(0, 0.1, N).astype(np.float32)).cuda()
+    out = torch.empty((M, N), dtype=PRECISIONS[prec][1], device="cuda")
+    gemm(lib, prec, epi, x, w, out, N, bias=bias)
+    pre = xd @ wd.T + bias.double().cpu().numpy()
+    expected = np.maximum(pre, 0) if epi == 1 else 0.5 * pre * (1 + np.vectorize(math.erf)(pre / math.sqrt(2)))
+    got = out.double().cpu().numpy()
+    assert np.max(np.abs(got - expected) - ROUND[prec] * np.abs(expected)) < 3e-3
+
+
+@pytest.mark.parametrize("prec", ["bf16", "f16"])
+@pytest.mark.parametrize("M,F", [(96, 3072), (333, 512)])
+def test_gemm_geglu_epilogue(lib, prec, M, F):
+    rng = np.random.default_rng(M)
+    K = 768
+    x, xd = rand16((M, K), prec, rng)
+    w, wd = rand16((2 * F, K), prec, rng, 0.05)
+    host = w.cpu().view(torch.int16).numpy().astype(np.uint16)
+    inter = np.empty_like(host)
+    _lib.check(lib.laya_interleave_geglu(host.ctypes.data, inter.ctypes.data, F, K))
+    wi = torch.from_numpy(inter.view(np.int16)).view(PRECISIONS[prec][1]).cuda()
+    out = torch.empty((M, F), dtype=PRECISIONS[prec][1], device="cuda")
+    gemm(lib, prec, 3, x, wi, out, F)
+    h = xd @ wd.T
+    g, u = h[:, :F], h[:, F:]
+    expected = 0.5 * g * (1 + np.vectorize(math.erf)(g / math.sqrt(2))) * u
+    got = out.double().cpu().numpy()
+    assert np.max(np.abs(got - expected) - ROUND[prec] * np.abs(expected)) < 3e-3
+
+
+def rope_tables(theta, rows):
+    freq = 1 / (np.float32(theta) ** (np.arange(0, 64, 2, dtype=np.float32) / 64))
+    angle = np.arange(rows, dtype=np.float32)[:, None] * freq
+    return np.cos(angle).astype(np.float32), np.sin(angle).astype(np.float32)
+
+
+@pytest.mark.parametrize("prec", ["bf16", "f16"])
+@pytest.mark.parametrize("rope", [True, False])
+def test_gemm_qkv_rope_layout(lib, prec, rope):
+    """Encoder QKV (RoPE, no bias) and head in_proj (bias, no RoPE) epilogues; cf. tests/test_gpu.py:36-53."""
+    rng = np.random.default_rng(17)
+    heads, M, K = 2, 208, 128
+    N = 3 * heads * 64
+    x, xd = rand16((M, K), prec, rng)
+    w, wd = rand16((N, K), prec, rng, 0.1)
+    positions = np.concatenate([np.arange(112), np.arange(96)]).astype(np.int32)
+    cos, sin = rope_tables(10000, 128)
+    bias = None if rope else torch.from_numpy(rng.normal(0, 0.1, N).astype(np.float32)).cuda()
+    out = torch.full((3, heads, M, 64), float("nan"), dtype=PRECISIONS[prec][1], device="cuda")
+    gemm(lib, prec, 4, x, w, out, heads=heads,
+         cos=torch.from_numpy(cos).cuda() if rope else None, sin=torch.from_numpy(sin).cuda() if rope else None,
+         positions=torch.from_numpy(positions).cuda(), bias=bias)
+    h = xd @ wd.T
+    if bias is not None:
+        h = h + bias.double().cpu().numpy()
+    h = h.reshape(M, 3, heads, 64).transpose(1, 2, 0, 3).copy()
+    if rope:
+        c = np.concatenate([cos, cos], -1)[positions].astype(np.float64)
+        s = np.concatenate([sin, sin], -1)[positions].astype(np.float64)
+        for part in (0, 1):
+            o = h[part]
+            rot = np.concatenate([-o[..., 32:], o[..., :32]], -1)
+            h[part] = o * c + rot * s
+    got = out.double().cpu().numpy()
+    assert np.max(np.abs(got - h) - ROUND[prec] * np.abs(h)) < 2e-3
+
+
+@pytest.mark.parametrize("prec", ["bf16"])
+@pytest.mark.parametrize("splits", [1, 3])
+def test_gemm_residual_and_partials(lib, prec, splits):
+    rng = np.random.default_rng(5)
+    M, N, K = 300, 768, 3072
+    x, xd = rand16((M, K), prec, rng)
+    w, wd = rand16((N, K), prec, rng, 0.02)
+    base = rng.normal(0, 1, (M, N)).astype(np.float32)
+    bias = rng.normal(0, 0.1, N).astype(np.float32)
+    residual = torch.from_numpy(base.copy()).cuda()
+    gemm(lib, prec, 5, x, w, residual=residual, ldr=N, bias=torch.from_numpy(bias).cuda())
+    expected = base + xd @ wd.T + bias
+    assert np.max(np.abs(residual.cpu().numpy() - expected)) < 2e-4 * math.sqrt(K)
+    partial = torch.zeros((splits, M, N), dtype=torch.float32, device="cuda")
+    gemm(lib, prec, 6, x, w, residual=partial, ldr=N, splits=splits, block_n=64)
+    assert np.max(np.abs(partial.sum(0).double().cpu().numpy() - xd @ wd.T)) < 2e-4 * math.sqrt(K)
+
+
+def packed_case(lengths):
+    starts = np.cumsum([0] + [span(n) for n in lengths])[:-1].astype(np.int32)
+    M = span(sum(span(n) for n in lengths) + 16)  # include tokens past the last row
+    return starts, np.asarray(lengths, np.int32), M
+
+
+@pytest.mark.parametrize("prec,split_p", [("bf16", 0), ("bf16", 1), ("f16", 1)])
+@pytest.mark.parametrize("lengths,window", [([32], -1), ([7, 96], 64), ([128, 1], -1), ([250, 131], 64),
+                                            ([256, 219, 145], -1), ([500], 64), ([1024, 333], -1)])
+def test_packed_attention_matches_oracle(lib, prec, split_p, lengths, window):
+    """Cases and float64 oracle of tests/test_attention.py:12-56 (h=2, seeded by M)."""
+    h = 2
+    starts, lens, M = packed_case(lengths)
+    cap = (M + 48 * len(lengths) + 63) // 64 + 1
+    tiles = np.zeros((cap, 4), np.int32)
+    n_tiles = lib.laya_attention_tiles(starts.ctypes.data, lens.ctypes.data, len(lengths), M, tiles.ctypes.data, cap)
+    assert n_tiles > 0
+    x = np.random.default_rng(M).normal(0, 1, (M, 3, h, 64)).astype(np.float32)
+    xt = torch.from_numpy(x).to(PRECISIONS[prec][1])
+    xd = xt.double().numpy()
+    layout = xt.permute(1, 2, 0, 3).contiguous().cuda()          # [3][h][M][64]
+    out = torch.full((M, h * 64), float("nan"), dtype=PRECISIONS[prec][1], device="cuda")
+    dev = [torch.from_numpy(v).cuda() for v in (tiles, starts, lens)]
+    _lib.check(lib.laya_op_attention(PRECISIONS[prec][0], ptr(layout), ptr(out), ptr(dev[0]), cap, ptr(dev[1]),
+                                     ptr(dev[2]), M, h, window, split_p, stream()))
+    torch.cuda.synchronize()
+    got = out.double().cpu().numpy()
+    real = np.zeros(M, bool)
+    worst = 0.0
+    for start, n in zip(starts, lens):
+        real[start:start + n] = True
+        q, k, v = xd[start:start + n].transpose(1, 2, 0, 3)
+        s = q @ k.transpose(0, 2, 1) / 8
+        if window >= 0:
+            s[:, np.abs(np.arange(n)[:, None] - np.arange(n)) > window] = -np.inf
+        p = np.exp(s - s.max(-1, keepdims=True))
+        p /= p.sum(-1, keepdims=True)
+        expected = (p @ v).transpose(1, 0, 2).reshape(n, h * 64)
+        err = np.abs(got[start:start + n] - expected) - ROUND[prec] * np.abs(expected)
+        worst = max(worst, float(err.max()))
+    # 16-bit output rounding plus probability rounding (split_p keeps fp32-level probabilities).
+    limit = {("bf16", 0): 6e-3, ("bf16", 1): 1.5e-3, ("f16", 1): 6e-4}[(prec, split_p)]
+    assert worst < limit, worst
+    np.testing.assert_array_equal(got[~real], 0)
+
+
+@pytest.mark.parametrize("prec", ["bf16", "f16"])
+@pytest.mark.parametrize("width", [64, 768, 1024])
+def test_embed_norm(lib, prec, width):
+    rng = np.random.default_rng(width)
+    vocab, rows = 1000, 77
+    table = rng.normal(0, 0.5, (vocab, width)).astype(np.float32)
+    gamma = rng.normal(1, 0.1, width).astype(np.float32)
+    ids = rng.integers(0, vocab, rows).astype(np.int32)
+    residual = torch.empty((rows, width), dtype=torch.float32, device="cuda")
+    x = torch.empty((rows, width), dtype=PRECISIONS[prec][1], device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    t = [torch.from_numpy(v).cuda() for v in (ids, table, gamma)]
+    _lib.check(lib.laya_op_embed_norm(PRECISIONS[prec][0], ptr(t[0]), ptr(t[1]), ptr(t[2]), 1e-5, rows, width, vocab,
+                                      ptr(residual), ptr(x), ptr(err), stream()))
+    torch.cuda.synchronize()
+    e = table[ids].astype(np.float64)
+    expected = (e - e.mean(-1, keepdims=True)) / np.sqrt(e.var(-1, keepdims=True) + 1e-5) * gamma
+    np.testing.assert_allclose(residual.cpu().numpy(), expected, atol=2e-5, rtol=1e-5)
+    np.testing.assert_array_equal(x.cpu().float().numpy(), residual.to(PRECISIONS[prec][1]).cpu().float().numpy())
+    assert int(err.item()) == 0
+
+
+@pytest.mark.parametrize("prec", ["bf16", "f16"])
+@pytest.mark.parametrize("width", [64, 768, 1024])
+@pytest.mark.parametrize("splits,beta", [(0, False), (2, True)])
+def test_norm_residual_partials(lib, prec, width, splits, beta):
+    """cf. tests/test_gpu.py:68-103: residual accumulation then LayerNorm with/without beta."""
+    rng = np.random.default_rng(31)
+    rows = 3 * 8 + 5
+    source = rng.normal(2, .3, (rows, width)).astype(np.float32)
+    parts = rng.normal(0, .1, (max(splits, 1), rows, width)).astype(np.float32)
+    gamma = rng.normal(1, .1, width).astype(np.float32)
+    b = rng.normal(0, .1, width).astype(np.float32)
+    residual = torch.from_numpy(source.copy()).cuda()
+    x = torch.empty((rows, width), dtype=PRECISIONS[prec][1], device="cuda")
+    t = [torch.from_numpy(v).cuda() for v in (parts, gamma, b)]
+    _lib.check(lib.laya_op_norm(PRECISIONS[prec][0], ptr(residual), ptr(t[0]) if splits else None, splits, ptr(t[1]),
+                                ptr(t[2]) if beta else None, 1e-5, ptr(x), rows, width, stream()))
+    torch.cuda.synchronize()
+    added = source.astype(np.float64) + (parts[:splits].sum(0) if splits else 0)
+    np.testing.assert_allclose(residual.cpu().numpy(), added, atol=1e-6, rtol=1e-6)
+    expected = (added - added.mean(-1, keepdims=True)) / np.sqrt(added.var(-1, keepdims=True) + 1e-5) * gamma
+    if beta:
+        expected = expected + b
+    got = x.cpu().double().numpy()
+    assert np.max(np.abs(got - expected) - ROUND[prec] * np.abs(expected)) < 1e-4
