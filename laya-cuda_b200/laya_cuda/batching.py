@@ -148,7 +148,7 @@ class BatchEngine:
                                       "queue_ms": (executed - started) * 1000,
                                       "api_ms": (time.perf_counter() - started) * 1000,
                                       "tokens_per_question": [len(x[0]) for x in rows], "backend": "cuda",
-                                      "precision": getattr(engine.runtime, "precision", "bfloat16")}
+                                      "precision": getattr(engine.runtime, "precision", "float16")}
                     active.remove(request)
                     self._finish(request, result)
                 except Exception as error:

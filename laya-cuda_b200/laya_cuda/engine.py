@@ -20,7 +20,7 @@ def _device_index(device):
 
 class Engine:
     def __init__(self, model="laya", *, revision=None, device="cuda:0", backend="cuda", max_cached_shapes=16,
-                 registry=None, precision="bfloat16"):
+                 registry=None, precision="float16"):
         if backend not in ("cuda", "official"):
             raise ValueError("backend must be 'cuda' or 'official'")
         if type(max_cached_shapes) is not int or not 1 <= max_cached_shapes <= 64:

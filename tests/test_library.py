@@ -1,0 +1,153 @@
+"""The C ABI library on the host (no GPU needed): it loads, exports every symbol the header
+declares, and its host-side packing, shape classes and attention tile tables match a Python
+restatement of the reference's Slot.fill (laya_cuda/runtime.py:52-68) and classes (20-25)."""
+import ctypes as ct
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from laya_cuda import _lib
+from laya_cuda.runtime import classes, flatten, span
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return _lib.load()
+
+
+def test_library_exports_every_declared_symbol(lib):
+    header = (ROOT / "include/laya_b200.h").read_text()
+    declared = set(re.findall(r"^\s*(?:int|int64_t|void\*|const char\*)\s+(laya_\w+)\s*\(", header, re.M))
+    assert declared == set(_lib.EXPORTS)
+    for name in declared:
+        assert hasattr(lib, name), name
+
+
+def test_create_without_device_fails_cleanly(lib):
+    """No GPU here: laya_create must return an error status with a message, not crash."""
+    cfg = _lib.Config(vocab=100, width=64, heads=1, layers=1, intermediate=128, global_every=3, window=64,
+                      theta_global=160000., theta_local=10000., eps=1e-5, max_len=128, head_layers=1, n_act=2,
+                      precision=0)
+    handle = ct.c_void_p()
+    code = lib.laya_create(ct.byref(cfg), 0, 4, ct.byref(handle))
+    try:
+        import torch
+        has_gpu = torch.cuda.is_available()
+    except ImportError:
+        has_gpu = False
+    if has_gpu:
+        lib.laya_destroy(handle)
+        pytest.skip("a GPU is present")
+    assert code == _lib.ERR_NO_DEVICE and not handle.value
+    assert lib.laya_last_error(None)
+
+
+def fill_reference(items, pad, m, b, k):
+    """Python restatement of Slot.fill: ids/positions/rows/kinds per token, starts/lengths/
+    counts per question, (k+1) gather indices per question (CLS, then marker tokens)."""
+    ids = np.full(m, pad, np.int32)
+    positions = np.zeros(m, np.int32)
+    rows = np.full(m, -1, np.int32)
+    kinds = np.zeros(m, np.int32)
+    starts, lengths, counts = (np.zeros(b, np.int32) for _ in range(3))
+    indices = np.zeros(b * (k + 1), np.int32)
+    offset = 0
+    for r, (tok, markers, kind) in enumerate(items):
+        n = len(tok)
+        end = offset + span(n)
+        ids[offset:offset + n] = tok
+        positions[offset:end] = np.arange(end - offset)
+        rows[offset:end], kinds[offset:end] = r, kind
+        starts[r], lengths[r], counts[r] = offset, n, len(markers)
+        block = indices[r * (k + 1):(r + 1) * (k + 1)]
+        block[:] = offset
+        block[1:len(markers) + 1] += markers
+        offset = end
+    return ids, positions, rows, kinds, starts, lengths, counts, indices
+
+
+def pack(lib, items, pad=0):
+    m, b, k = classes(items)
+    tokens, lengths, markers, counts, kinds = flatten(items)
+    out = np.zeros(lib.laya_packed_ints(m, b, k), np.int32)
+    code = lib.laya_pack(tokens.ctypes.data, lengths.ctypes.data, markers.ctypes.data, counts.ctypes.data,
+                         kinds.ctypes.data, len(items), pad, m, b, k, out.ctypes.data)
+    return code, out, (m, b, k)
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_pack_matches_reference_fill(lib, seed):
+    rng = np.random.default_rng(seed)
+    items = []
+    for j in range(int(rng.integers(1, 9))):
+        n = int(rng.integers(1, 700))
+        markers = sorted(rng.choice(n, size=int(rng.integers(1, min(n, 40) + 1)), replace=False).tolist())
+        items.append((rng.integers(0, 1000, n).tolist(), markers, j % 3))
+    code, out, (m, b, k) = pack(lib, items, pad=7)
+    assert code == 0
+    want = fill_reference(items, 7, m, b, k)
+    o = 0
+    for field, size in zip(want, (m, m, m, m, b, b, b, b * (k + 1))):
+        np.testing.assert_array_equal(out[o:o + size], field)
+        o += size
+    # Attention tiles: every token of every row span is covered exactly once by a tile of its
+    # row; tokens past the last row by zero-fill tiles; no tile straddles rows.
+    o = (o + 3) // 4 * 4
+    tiles = out[o:].reshape(-1, 4)
+    cover = np.zeros(m, np.int32)
+    for t0, t1, row, _ in tiles:
+        if row == -2:
+            continue
+        assert 0 <= t0 < t1 <= m and t1 - t0 <= 64
+        cover[t0:t1] += 1
+        if row >= 0:
+            s, n = want[4][row], want[5][row]
+            assert s <= t0 and t1 <= s + span(n) and (t0 - s) % 64 == 0
+        else:
+            assert np.all(want[2][t0:t1] == -1)
+    np.testing.assert_array_equal(cover, 1)
+
+
+def test_shape_class_matches_reference(lib):
+    cases = [[([1] * 17, [1, 2], 0), ([1] * 250, [1] * 9, 1)], [([1] * 83, [1, 2, 3, 4], 0)],
+             [([1] * 600, [3], 0)] * 5, [([1] * 1, [0], 2)], [([1] * 300, list(range(77)), 0)] * 3]
+    for items in cases:
+        _, lengths, _, counts, _ = flatten(items)
+        got = [ct.c_int32() for _ in range(3)]
+        assert lib.laya_shape_class(lengths.ctypes.data, counts.ctypes.data, len(items), *map(ct.byref, got)) == 0
+        assert tuple(v.value for v in got) == classes(items)
+    assert classes(cases[0]) == (320, 2, 16) and classes(cases[1]) == (96, 1, 8)
+
+
+@pytest.mark.parametrize("bad", ["marker", "kind", "empty"])
+def test_pack_rejects_invalid_items(lib, bad):
+    items = [([5] * 20, [3, 9], 0)]
+    if bad == "marker":
+        items = [([5] * 20, [3, 20], 0)]
+    elif bad == "kind":
+        items = [([5] * 20, [3], 3)]
+    elif bad == "empty":
+        items = [([], [], 0)]
+    if bad == "empty":
+        lengths = np.zeros(1, np.int32)
+        counts = np.zeros(1, np.int32)
+        got = [ct.c_int32() for _ in range(3)]
+        assert lib.laya_shape_class(lengths.ctypes.data, counts.ctypes.data, 1, *map(ct.byref, got)) == _lib.ERR_INVALID
+        return
+    code, _, _ = pack(lib, items)
+    assert code == _lib.ERR_INVALID
+    assert lib.laya_last_error(None)
+
+
+def test_geglu_interleave(lib):
+    F, K = 128, 8
+    src = np.arange(2 * F * K, dtype=np.uint16).reshape(2 * F, K)
+    dst = np.zeros_like(src)
+    assert lib.laya_interleave_geglu(src.ctypes.data, dst.ctypes.data, F, K) == 0
+    for blk in range(F // 64):
+        np.testing.assert_array_equal(dst[blk * 128:blk * 128 + 64], src[blk * 64:blk * 64 + 64])
+        np.testing.assert_array_equal(dst[blk * 128 + 64:blk * 128 + 128], src[F + blk * 64:F + blk * 64 + 64])
