@@ -1,0 +1,368 @@
+"""Benchmark of the Laya forward pass on B200 (one JSON line on rank 0).
+
+Workload (one "step"): configuration 5 of the benchmark plan -- the `laya` encoder geometry
+(12 layers, d 768, 12 heads, F 3072, vocab 50368) with positions extended to 1024, 4096
+requests of uniform length in [256, 1024], 3 questions x 8 options each (12,288 packed
+sequences), run as micro-batches of 64 sequences.  Under torchrun every rank processes its own
+4096-request set (per-GPU work fixed: weak scaling) on its own weight replica; nothing is
+exchanged between ranks (the NCCL group only carries the timing barrier and the max-reduction).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--latency none|basic]
+
+metric: sequences/s over all ranks (device time, max over ranks).  Extra keys: batch-1 latency
+(configs 1/2: 83 and 512 tokens through Engine.predict), per-kernel-family device times, the
+roofline of the dominant kernel (FFN-up GEMM), the oracle on the host cores (cpu_baseline),
+and the end-to-end number through the public Runtime.predict with host buffers (e2e).
+"""
+import argparse
+import ctypes as ct
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "laya-cuda_b200"))
+
+REQUESTS = 4096
+QUESTIONS = 3
+OPTIONS = 8
+MICRO = 64
+LENGTHS = (256, 1024)
+FAMILIES = ["gemm_qkv_rope", "gemm_attn_out_residual", "gemm_ffn_up_geglu", "gemm_ffn_down_residual",
+            "gemm_head", "attention", "row_kernels", "head_tail"]
+CACHE = Path(os.environ.get("LAYA_BENCH_CACHE", Path(tempfile.gettempdir()) / "laya_b200_bench"))
+
+
+def peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.is_file():
+        data = json.loads(path.read_text())
+        return data["hbm_gbs"], data["bf16_tflops"], data["bf16_tflops_sustained"], "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def per_token_flops(arch):
+    """Encoder GEMM FLOPs per useful token: 2 * L * d * (3d + d + 2F + F)."""
+    d, f, layers = arch["width"], arch["intermediate"], arch["layers"]
+    return {"qkv": 2 * layers * d * 3 * d, "attn_out": 2 * layers * d * d, "ffn_up": 2 * layers * d * 2 * f,
+            "ffn_down": 2 * layers * f * d}
+
+
+def attention_flops(lengths, arch):
+    """4 * d * sum over queries of visible keys, per layer (global: all keys; local: |i-j|<=w)."""
+    d, w = arch["width"], arch["local_attention"] // 2
+    n_global = sum(1 for layer in range(arch["layers"]) if layer % arch["global_every"] == 0)
+    total = 0
+    for n in lengths:
+        q = np.arange(n)
+        local = int((np.minimum(n, q + w + 1) - np.maximum(0, q - w)).sum())
+        total += 4 * d * (n_global * n * n + (arch["layers"] - n_global) * local)
+    return total
+
+
+class Clocks:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    def __init__(self, index):
+        self.index, self.samples, self.proc = index, [], None
+
+    def __enter__(self):
+        query = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                 "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={query}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append([v.strip() for v in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self):
+        rows = [s for s in self.samples if len(s) >= 9 and s[1].isdigit()]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm = sorted(int(r[1]) for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": int(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+def build_micro_batches(items):
+    batches = [items[i:i + MICRO] for i in range(0, len(items), MICRO)]
+    return batches
+
+
+def oracle_rate(arch, weights, items, budget_s):
+    """Sequences/s of the FP32 oracle on the host cores over a bounded sample of the workload."""
+    sys.path.insert(0, str(ROOT))
+    from oracle.laya_oracle import Oracle
+    oracle = Oracle(weights, arch)
+    oracle.item(*items[0])  # warm caches
+    done, t0 = 0, time.perf_counter()
+    while done < len(items) and (time.perf_counter() - t0 < budget_s or done == 0):
+        oracle.item(*items[done])
+        done += 1
+    return done / (time.perf_counter() - t0), done
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the CPU implementation of this path (the oracle restatement; the
+    reference's own path needs CuPy and a GPU), timed on this host's cores."""
+    if rank != 0:
+        return
+    from laya_cuda import synthetic as S
+    arch = S.architecture("laya", max_len=1024)
+    weights = S.make_weights(arch, seed=0)
+    requests = S.throughput_requests(1000, 64, arch["vocab"], LENGTHS, QUESTIONS, OPTIONS)
+    items = [item for req in requests for item in req]
+    cores = os.cpu_count()
+    sys.path.insert(0, str(ROOT))
+    from oracle.laya_oracle import Oracle
+    oracle = Oracle(weights, arch)
+    t0 = time.perf_counter()
+    oracle.item(*items[0])
+    per_seq = time.perf_counter() - t0
+    per_step = max(1, min(len(items), int(2.0 / max(per_seq, 1e-3))))
+    cursor = 0
+
+    def step():
+        nonlocal cursor
+        for _ in range(per_step):
+            oracle.item(*items[cursor % len(items)])
+            cursor += 1
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    elapsed = time.perf_counter() - t0
+    value = args.steps * per_step / elapsed
+    sample = f"{per_step} sequences per step (lengths 256-1024, 8 options) of the config-5 workload"
+    line = {"impl": "reference", "metric": "sequences/s", "value": round(value, 3), "unit": "sequences/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(elapsed / args.steps * 1000, 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config5-throughput laya 12L d768 F3072 V50368 ctx1024, 3q x 8 options",
+                       "sample": sample},
+            "cpu_baseline": {"value": round(value, 3), "unit": "sequences/s", "cores": cores, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": "sequences/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "note": "reference GPU path requires CuPy (absent); CPU FP32 restatement of it timed with numpy BLAS"}
+    print(json.dumps(line), flush=True)
+
+
+def latency(engine, arch, rng, lengths, repeats=200, warmup=20):
+    from laya_cuda import synthetic as S
+    out = {}
+    for n in lengths:
+        state, questions, _ = S.request_texts(rng, n, 4, arch["vocab"])
+        for _ in range(warmup):
+            engine.predict(state, questions)
+        api, gpu = [], []
+        for _ in range(repeats):
+            engine.predict(state, questions)
+            api.append(engine.last_metrics["api_ms"])
+            gpu.append(engine.last_metrics["gpu_ms"])
+        out[f"{n}tok"] = {"api_p50_ms": round(float(np.percentile(api, 50)), 4),
+                          "api_p95_ms": round(float(np.percentile(api, 95)), 4),
+                          "gpu_p50_ms": round(float(np.percentile(gpu, 50)), 4),
+                          "gpu_p95_ms": round(float(np.percentile(gpu, 95)), 4),
+                          "repeats": repeats, "graph_replay": engine.last_metrics["graph_replay"]}
+    return out
+
+
+def run_engine(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    from laya_cuda import Engine
+    from laya_cuda import _lib
+    from laya_cuda import synthetic as S
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local_rank))
+    arch = S.architecture("laya", max_len=1024)
+    CACHE.mkdir(parents=True, exist_ok=True)
+    if rank == 0:
+        path = S.cached_checkpoint(CACHE, "laya", seed=0, max_len=1024)
+    if world > 1:
+        dist.barrier()
+    path = S.cached_checkpoint(CACHE, "laya", seed=0, max_len=1024)
+    engine = Engine(path, device=f"cuda:{local_rank}", max_cached_shapes=16)
+    rt, lib = engine.runtime, engine.runtime._lib
+    h = rt._handle
+
+    requests = S.throughput_requests(1000 + rank, args.requests, arch["vocab"], LENGTHS, QUESTIONS, OPTIONS)
+    items = [item for req in requests for item in req]
+    batches = build_micro_batches(items)
+    tokens = sum(len(i[0]) for i in items)
+    packed, shapes, maxes = [], [], [0, 0, 0]
+    from laya_cuda.runtime import classes, flatten
+    for batch in batches:
+        m, b, k = classes(batch)
+        toks, lens, marks, counts, kinds = flatten(batch)
+        buf = np.zeros(lib.laya_packed_ints(m, b, k), np.int32)
+        _lib.check(lib.laya_pack(toks.ctypes.data, lens.ctypes.data, marks.ctypes.data, counts.ctypes.data,
+                                 kinds.ctypes.data, len(batch), 0, m, b, k, buf.ctypes.data))
+        packed.append(torch.from_numpy(buf).cuda())
+        shapes.append((m, b, k))
+        maxes = [max(a, v) for a, v in zip(maxes, (m, b, k))]
+    _lib.check(lib.laya_reserve(h, *maxes), h)
+    out_logits = torch.empty((maxes[1] * (maxes[2] + 1),), dtype=torch.float32, device="cuda")
+    out_acts = torch.empty((maxes[1] * arch["n_act"],), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.ExternalStream(lib.laya_stream(h))
+
+    def step():
+        for buf, (m, b, k) in zip(packed, shapes):
+            _lib.check(lib.laya_forward_device(h, ct.c_void_p(buf.data_ptr()), m, b, k, 2,
+                                               ct.c_void_p(out_logits.data_ptr()), ct.c_void_p(out_acts.data_ptr())), h)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    # Timed region: inputs resident in HBM; the working set of a step (12,288 sequences, ~7.9M
+    # tokens, >40 GB of activations streamed) is far larger than L2, so no flush is needed.
+    _lib.check(lib.laya_set_profiling(h, 1), h)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with Clocks(local_rank) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    _lib.check(lib.laya_set_profiling(h, 0), h)
+    ms = start.elapsed_time(end)
+    fam = {}
+    launches = 0
+    for i, name in enumerate(FAMILIES):
+        t, n, fl = ct.c_double(), ct.c_int64(), ct.c_double()
+        _lib.check(lib.laya_profile_read(h, i, ct.byref(t), ct.byref(n), ct.byref(fl)), h)
+        fam[name] = {"ms": round(t.value, 3), "launches": n.value, "share": None}
+        launches += n.value
+    busy = sum(v["ms"] for v in fam.values())
+    for v in fam.values():
+        v["share"] = round(v["ms"] / busy, 4) if busy else None
+    t_max = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    ms_max = float(t_max.item())
+    seqs_all = len(items) * world
+    value = seqs_all / (ms_max / 1000) * args.steps
+
+    # Roofline of the dominant kernel: the FFN-up GEMM (+GeGLU epilogue), algorithmic FLOPs of
+    # useful tokens, per launch, over its event-timed average launch duration.
+    hbm, tf_burst, tf_sust, peak_kind = peaks()
+    ptf = per_token_flops(arch)
+    up = fam["gemm_ffn_up_geglu"]
+    up_launch_ms = up["ms"] / max(up["launches"], 1)
+    up_flops_per_launch = tokens * ptf["ffn_up"] / arch["layers"] / len(batches)
+    achieved = up_flops_per_launch / (up_launch_ms / 1000) / 1e12
+    enc_gemm_ms = sum(fam[k]["ms"] for k in FAMILIES[:4])
+    enc_achieved = tokens * sum(ptf.values()) * args.steps / (enc_gemm_ms / 1000) / 1e12
+    roofline = {"kernel": "gemm_ffn_up_geglu (tcgen05, M=128 N=256 tiles)", "bound": "tensor",
+                "achieved": round(achieved, 1), "peak": tf_sust, "unit": "TFLOP/s",
+                "frac": round(achieved / tf_sust, 4), "peak_kind": f"{peak_kind} bf16 dense sustained (f16 same rate)",
+                "traffic": TRAFFIC_FFN_UP_PER_LAUNCH_BYTES,
+                "all_encoder_gemms": {"achieved": round(enc_achieved, 1), "frac": round(enc_achieved / tf_sust, 4)}}
+
+    line = None
+    if rank == 0:
+        # End to end through the public Runtime.predict: host items -> pinned staging -> H2D ->
+        # forward -> D2H of logits/acts, every micro-batch (one step = the whole rank workload).
+        e2e_ms, h2d, d2h = None, 0, 0
+        e2e_steps = 1
+        for batch, (m, b, k) in zip(batches, shapes):
+            h2d += lib.laya_packed_ints(m, b, k) * 4
+            d2h += (b * (k + 1) + b * arch["n_act"] + 1) * 4
+        rt.predict(batches[0])
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            for batch in batches:
+                rt.predict(batch)
+        e2e_ms = (time.perf_counter() - t0) * 1000 / e2e_steps
+        e2e = {"value": round(len(items) / (e2e_ms / 1000), 2), "unit": "sequences/s", "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h), "api": "Runtime.predict(items) per 64-sequence micro-batch"}
+        lat = None
+        if world == 1 and args.latency != "none":
+            lat = latency(engine, arch, np.random.default_rng(0), (83, 512))
+        cpu = None
+        if world == 1 and args.cpu_budget > 0:
+            weights = S.make_weights(arch, seed=0)
+            rate, n = oracle_rate(arch, weights, items, args.cpu_budget)
+            cpu = {"value": round(rate, 3), "unit": "sequences/s", "cores": os.cpu_count(), "kind": "port",
+                   "sample": f"first {n} sequences of the rank-0 workload, FP32 numpy oracle, all host threads"}
+        line = {"metric": "sequences/s", "value": round(value, 2), "unit": "sequences/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+                "data": "synthetic (seeded random-init weights, uniform token ids)",
+                "config": {"workload": "config5-throughput: laya 12L d768 h12 F3072 V50368, positions 1024; "
+                                       f"{args.requests} requests x 3 questions x 8 options, lengths U[256,1024], "
+                                       "64-sequence micro-batches, per rank",
+                           "sequences_per_rank": len(items), "tokens_per_rank": tokens, "micro_batches": len(batches),
+                           "parallelism": f"replicas{world}", "l2": "inputs larger than L2 (no flush)"},
+                "gpu_launches": launches, "kernels": fam, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "clocks": clocks.summary(), "latency_batch1": lat,
+                "attention_flops_per_step": attention_flops([len(i[0]) for i in items], arch)}
+    engine.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+# dram__bytes_read.sum + dram__bytes_write.sum of one FFN-up GEMM launch (ncu capture summarised
+# in profiles/gemm_ffn_up_geglu_config5.md); None until a capture exists.
+TRAFFIC_FFN_UP_PER_LAUNCH_BYTES = None
+
+
+def main():
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=3)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=["laya_b200", "reference"], default="laya_b200")
+    parser.add_argument("--latency", choices=["none", "basic"], default="basic")
+    parser.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of oracle time for cpu_baseline")
+    parser.add_argument("--requests", type=int, default=REQUESTS,
+                        help="requests per rank (4096 = configuration 5; smaller only for profiler captures)")
+    args = parser.parse_args()
+    if args.warmup < 3:
+        parser.error("--warmup must be at least 3")
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", args.gpus if "RANK" in os.environ else 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+    else:
+        run_engine(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

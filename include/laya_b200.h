@@ -92,7 +92,8 @@ int laya_finalize(laya_engine* e);
  * uploads them, runs the class's CUDA graph (capturing it on first use) or the eager pass,
  * and writes logits_out[i * options + j] (option logits, fp32, options = the class's option
  * count reported in metrics->options; the caller sizes the buffer with laya_shape_class) and
- * acts_out[i * n_act + a]. */
+ * acts_out[i * n_act + a].  capture: 0 eager pass, 1 CUDA graph of the class (captured on first
+ * use, kept in the LRU), 2 auto: graph for classes of at most 8192 packed rows, eager above. */
 int laya_predict(laya_engine* e, const int32_t* tokens, const int32_t* lengths, const int32_t* markers,
                  const int32_t* marker_counts, const int32_t* kinds, int n_items, int capture,
                  float* logits_out, float* acts_out, laya_metrics* metrics);
@@ -113,12 +114,18 @@ int64_t laya_packed_ints(int rows, int batch, int options);
 int laya_pack(const int32_t* tokens, const int32_t* lengths, const int32_t* markers, const int32_t* marker_counts,
               const int32_t* kinds, int n_items, int pad_id, int rows, int batch, int options, int32_t* packed);
 
+/* Grows the shared activation workspace to fit a class up front (throughput callers), so no
+ * forward pass has to synchronise to grow it. */
+int laya_reserve(laya_engine* e, int rows, int batch, int options);
+
 /* The engine's CUDA stream (cudaStream_t), for callers that time laya_forward_device. */
 void* laya_stream(laya_engine* e);
 
 /* Per-kernel-family device time accumulated over forward passes run with profiling on
- * (CUDA events on the engine stream around each launch of the family).  family: 0 GEMM,
- * 1 attention, 2 row kernels (embedding, norms, gather), 3 head tail.  Eager passes only. */
+ * (CUDA events on the engine stream around each launch of the family; eager passes only).
+ * family: 0 QKV GEMM (+RoPE), 1 attention-out GEMM (+residual), 2 FFN-up GEMM (+GeGLU),
+ * 3 FFN-down GEMM (+residual), 4 decision-head GEMMs, 5 attention, 6 row kernels (embedding,
+ * norms, gather), 7 head tail.  flops counts 2*M*N*K over the launched (padded) rows. */
 int laya_set_profiling(laya_engine* e, int enabled);
 int laya_profile_read(laya_engine* e, int family, double* total_ms, int64_t* launches, double* flops);
 

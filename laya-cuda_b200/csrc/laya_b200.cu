@@ -331,6 +331,16 @@ struct Slot {
   int launches = 0;
 };
 
+// Kernel families for laya_profile_read.
+enum Family : int {
+  FAM_GEMM_QKV = 0, FAM_GEMM_ATTN_OUT = 1, FAM_GEMM_FFN_UP = 2, FAM_GEMM_FFN_DOWN = 3, FAM_GEMM_HEAD = 4,
+  FAM_ATTENTION = 5, FAM_ROWS = 6, FAM_HEAD_TAIL = 7, kFamilies = 8
+};
+// Classes with more packed rows than this run eagerly under capture mode "auto": their kernels
+// are long enough that launch overhead is negligible, and a graph per distinct large class
+// would cost a capture per batch.
+constexpr int kAutoGraphRows = 8192;
+
 struct ProfEvent {
   int family;
   cudaEvent_t a, b;
@@ -364,9 +374,9 @@ struct Engine {
   bool profiling = false;
   std::vector<ProfEvent> prof_pending;
   std::vector<cudaEvent_t> prof_pool;
-  double prof_ms[4] = {0, 0, 0, 0};
-  double prof_flops[4] = {0, 0, 0, 0};
-  int64_t prof_launches[4] = {0, 0, 0, 0};
+  double prof_ms[kFamilies] = {};
+  double prof_flops[kFamilies] = {};
+  int64_t prof_launches[kFamilies] = {};
   int launches = 0;
 
   bool bf16() const { return cfg.precision == LAYA_PRECISION_BF16; }
@@ -633,8 +643,8 @@ void prof_resolve(Engine& e) {
 }
 
 template <typename T>
-void gemm(Engine& e, bool prof, int epi, const CUtensorMap& ta, const std::string& wname, int M, void* out, int ldo,
-          float* residual, int ldr, const float* bias, int* err, int rope = -1, const int* positions = nullptr) {
+void gemm(Engine& e, bool prof, int family, int epi, const CUtensorMap& ta, const std::string& wname, int M, void* out,
+          int ldo, float* residual, int ldr, const float* bias, int* err, int rope = -1, const int* positions = nullptr) {
   const Tensor& w = W(e, wname);
   const int N = (int)w.shape[0], K = (int)w.shape[1];
   const int bn = pick_bn(M, N, epi, e.sms);
@@ -646,7 +656,7 @@ void gemm(Engine& e, bool prof, int epi, const CUtensorMap& ta, const std::strin
   a.positions = positions;
   a.err = err;
   const CUtensorMap& tb = weight_map(e, wname, bn);
-  launch(e, prof, 0, 2.0 * M * N * K, [&] { launch_gemm<T>(epi, bn, ta, tb, a, e.sms, e.stream); });
+  launch(e, prof, family, 2.0 * M * N * K, [&] { launch_gemm<T>(epi, bn, ta, tb, a, e.sms, e.stream); });
 }
 
 // The whole forward pass of one shape class (runtime.py:90-113 + laya.py:214-245), enqueued
@@ -682,7 +692,7 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
 
   CK(cudaMemsetAsync(err, 0, sizeof(int), e.stream));
   const double rowbytes = (double)m * d;
-  launch(e, prof, 2, 0, [&] {
+  launch(e, prof, FAM_ROWS, 0, [&] {
     launch_embed<T>(ids, Wf(e, "encoder.embeddings.tok_embeddings.weight"), Wf(e, "encoder.embeddings.norm.weight"),
                     c.eps, m, d, c.vocab, residual, x, err, e.stream);
   });
@@ -692,25 +702,25 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
     AttnArgs a{};
     a.qkv = qkv; a.out = attn; a.tiles = tiles; a.starts = starts; a.lengths = lengths;
     a.M = m; a.heads = c.heads; a.window = window;
-    launch(e, prof, 1, 0, [&] { launch_attention<T>(a, L.tiles_cap, false, e.stream); });
+    launch(e, prof, FAM_ATTENTION, 0, [&] { launch_attention<T>(a, L.tiles_cap, false, e.stream); });
   };
   auto norm = [&](float* res, int rows, const float* g, const float* b, float eps, T* out) {
     NormArgs a{};
     a.residual = res; a.partials = nullptr; a.splits = 0;
     a.gamma1 = g; a.beta1 = b; a.eps1 = eps; a.fused_final = 0;
     a.x = out; a.rows = rows; a.d = d;
-    launch(e, prof, 2, 0, [&] { launch_norm<T>(a, e.stream); });
+    launch(e, prof, FAM_ROWS, 0, [&] { launch_norm<T>(a, e.stream); });
   };
 
   for (int i = 0; i < c.layers; ++i) {
     const std::string p = "encoder.layers." + std::to_string(i) + ".";
     const bool local = i % c.global_every != 0;
-    gemm<T>(e, prof, EPI_QKV, s.map_x, p + "attn.Wqkv.weight", m, qkv, 0, nullptr, 0, nullptr, err, local ? 1 : 0, positions);
+    gemm<T>(e, prof, FAM_GEMM_QKV, EPI_QKV, s.map_x, p + "attn.Wqkv.weight", m, qkv, 0, nullptr, 0, nullptr, err, local ? 1 : 0, positions);
     attention(local ? c.window : -1);
-    gemm<T>(e, prof, EPI_RESIDUAL, s.map_attn, p + "attn.Wo.weight", m, nullptr, 0, residual, d, nullptr, err);
+    gemm<T>(e, prof, FAM_GEMM_ATTN_OUT, EPI_RESIDUAL, s.map_attn, p + "attn.Wo.weight", m, nullptr, 0, residual, d, nullptr, err);
     norm(residual, m, Wf(e, p + "mlp_norm.weight"), nullptr, c.eps, x);
-    gemm<T>(e, prof, EPI_GEGLU, s.map_x, p + "mlp.Wi.weight", m, ff, e.F(), nullptr, 0, nullptr, err);
-    gemm<T>(e, prof, EPI_RESIDUAL, s.map_ff, p + "mlp.Wo.weight", m, nullptr, 0, residual, d, nullptr, err);
+    gemm<T>(e, prof, FAM_GEMM_FFN_UP, EPI_GEGLU, s.map_x, p + "mlp.Wi.weight", m, ff, e.F(), nullptr, 0, nullptr, err);
+    gemm<T>(e, prof, FAM_GEMM_FFN_DOWN, EPI_RESIDUAL, s.map_ff, p + "mlp.Wo.weight", m, nullptr, 0, residual, d, nullptr, err);
     if (i + 1 < c.layers) {
       norm(residual, m, Wf(e, "encoder.layers." + std::to_string(i + 1) + ".attn_norm.weight"), nullptr, c.eps, x);
     } else {
@@ -721,40 +731,40 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
       a.fused_final = 1; a.type_emb = Wf(e, "type_emb.weight"); a.kinds = kinds;
       a.gamma2 = Wf(e, "head.layers.0.norm1.weight"); a.beta2 = Wf(e, "head.layers.0.norm1.bias"); a.eps2 = 1e-5f;
       a.x = x; a.rows = m; a.d = d;
-      launch(e, prof, 2, 0, [&] { launch_norm<T>(a, e.stream); });
+      launch(e, prof, FAM_ROWS, 0, [&] { launch_norm<T>(a, e.stream); });
     }
   }
 
   for (int i = 0; i < c.head_layers; ++i) {
     const std::string p = "head.layers." + std::to_string(i) + ".";
     if (i > 0) norm(residual, m, Wf(e, p + "norm1.weight"), Wf(e, p + "norm1.bias"), 1e-5f, x);
-    gemm<T>(e, prof, EPI_QKV, s.map_x, p + "self_attn.in_proj_weight", m, qkv, 0, nullptr, 0,
+    gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_QKV, s.map_x, p + "self_attn.in_proj_weight", m, qkv, 0, nullptr, 0,
             Wf(e, p + "self_attn.in_proj_bias"), err);
     attention(-1);
     if (i + 1 == c.head_layers) {
-      launch(e, prof, 2, 0, [&] {
+      launch(e, prof, FAM_ROWS, 0, [&] {
         gather_rows_kernel<T><<<count, 256, 0, e.stream>>>(residual, attn, indices, count, d, m, sel, scored, err);
         CK(cudaGetLastError());
       });
-      gemm<T>(e, prof, EPI_RESIDUAL, s.map_scored, p + "self_attn.out_proj.weight", count, nullptr, 0, sel, d,
+      gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_RESIDUAL, s.map_scored, p + "self_attn.out_proj.weight", count, nullptr, 0, sel, d,
               Wf(e, p + "self_attn.out_proj.bias"), err);
       norm(sel, count, Wf(e, p + "norm2.weight"), Wf(e, p + "norm2.bias"), 1e-5f, selx);
-      gemm<T>(e, prof, EPI_RELU, s.map_selx, p + "linear1.weight", count, ffsel, 4 * d, nullptr, 0,
+      gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_RELU, s.map_selx, p + "linear1.weight", count, ffsel, 4 * d, nullptr, 0,
               Wf(e, p + "linear1.bias"), err);
-      gemm<T>(e, prof, EPI_RESIDUAL, s.map_ffsel, p + "linear2.weight", count, nullptr, 0, sel, d,
+      gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_RESIDUAL, s.map_ffsel, p + "linear2.weight", count, nullptr, 0, sel, d,
               Wf(e, p + "linear2.bias"), err);
     } else {
-      gemm<T>(e, prof, EPI_RESIDUAL, s.map_attn, p + "self_attn.out_proj.weight", m, nullptr, 0, residual, d,
+      gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_RESIDUAL, s.map_attn, p + "self_attn.out_proj.weight", m, nullptr, 0, residual, d,
               Wf(e, p + "self_attn.out_proj.bias"), err);
       norm(residual, m, Wf(e, p + "norm2.weight"), Wf(e, p + "norm2.bias"), 1e-5f, x);
-      gemm<T>(e, prof, EPI_RELU, s.map_x, p + "linear1.weight", m, ff, 4 * d, nullptr, 0, Wf(e, p + "linear1.bias"), err);
+      gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_RELU, s.map_x, p + "linear1.weight", m, ff, 4 * d, nullptr, 0, Wf(e, p + "linear1.bias"), err);
       const CUtensorMap ffmap = make_map(ff, m, 4 * d, kBM, e.bf16());
-      gemm<T>(e, prof, EPI_RESIDUAL, ffmap, p + "linear2.weight", m, nullptr, 0, residual, d,
+      gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_RESIDUAL, ffmap, p + "linear2.weight", m, nullptr, 0, residual, d,
               Wf(e, p + "linear2.bias"), err);
     }
   }
   norm(sel, count, Wf(e, "scorer.0.weight"), Wf(e, "scorer.0.bias"), 1e-5f, selx);
-  gemm<T>(e, prof, EPI_GELU, s.map_selx, "scorer.1.weight", count, scored, d, nullptr, 0, Wf(e, "scorer.1.bias"), err);
+  gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_GELU, s.map_selx, "scorer.1.weight", count, scored, d, nullptr, 0, Wf(e, "scorer.1.bias"), err);
   TailArgs t{};
   t.selected = sel; t.scored = scored; t.counts = counts;
   t.w3 = Wf(e, "scorer.3.weight"); t.b3 = Wf(e, "scorer.3.bias");
@@ -762,7 +772,7 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
   t.wa2 = Wf(e, "act_head.2.weight"); t.ba2 = Wf(e, "act_head.2.bias");
   t.logits = logits; t.acts = acts; t.k = L.k; t.d = d; t.n_act = c.n_act;
   const size_t tail_smem = ((size_t)(L.k + 1) + d + 4 + kActHidden) * sizeof(float);
-  launch(e, prof, 3, 0, [&] {
+  launch(e, prof, FAM_HEAD_TAIL, 0, [&] {
     head_tail_kernel<T><<<L.b, kTailThreads, tail_smem, e.stream>>>(t);
     CK(cudaGetLastError());
   });
@@ -773,10 +783,19 @@ void forward(Engine& e, Slot& s, bool prof) {
   else enqueue_forward<__half>(e, s, prof);
 }
 
-Slot& get_slot(Engine& e, int m, int b, int k, bool& miss) {
+// The slot of a class.  Graph runs use the LRU (inserting, and evicting the least recently
+// used class when full); eager runs use a cached slot when there is one and otherwise a
+// transient slot that is not cached, so large one-off classes never evict graphs.
+Slot& get_slot(Engine& e, int m, int b, int k, bool cache, bool& miss, std::unique_ptr<Slot>& transient) {
   auto key = std::make_tuple(m, b, k);
   auto it = e.slots.find(key);
   miss = it == e.slots.end();
+  if (miss && !cache) {
+    transient = std::make_unique<Slot>();
+    transient->m = m; transient->b = b; transient->k = k;
+    transient->L = make_layout(e, m, b, k);
+    return *transient;
+  }
   if (miss) {
     if ((int)e.slots.size() >= e.limit) {
       CK(cudaStreamSynchronize(e.stream));
@@ -796,6 +815,9 @@ Slot& get_slot(Engine& e, int m, int b, int k, bool& miss) {
   e.lru.push_back(key);
   return *it->second;
 }
+
+// Capture modes of laya_predict / laya_forward_device: 0 eager, 1 graph, 2 auto.
+bool wants_graph(int capture, int rows) { return capture == 1 || (capture == 2 && rows <= kAutoGraphRows); }
 
 // Runs one pass of slot `s` whose inputs are already in the workspace.  Returns the launch count.
 int run_slot(Engine& e, Slot& s, bool capture, bool& captured) {
@@ -1008,8 +1030,10 @@ int laya_predict(laya_engine* h, const int32_t* tokens, const int32_t* lengths, 
   CK(cudaSetDevice(e.device));
   int m, b, k;
   shape_class(lengths, marker_counts, n_items, m, b, k);
+  const bool graph = wants_graph(capture, m);
   bool miss = false;
-  Slot& s = get_slot(e, m, b, k, miss);
+  std::unique_ptr<Slot> transient;
+  Slot& s = get_slot(e, m, b, k, graph, miss, transient);
   ensure_workspace(e, s.L.total);
   ensure_host(e, (size_t)s.L.pack.total, s.L.n_out_floats);
   // The pad id is the tokenizer's [PAD]; padded positions are never attended by real tokens.
@@ -1017,7 +1041,7 @@ int laya_predict(laya_engine* h, const int32_t* tokens, const int32_t* lengths, 
   CK(cudaMemcpyAsync(e.ws + s.L.packed, e.h_packed, (size_t)s.L.pack.total * 4, cudaMemcpyHostToDevice, e.stream));
   bool captured = false;
   CK(cudaEventRecord(e.ev_start, e.stream));
-  const int launches = run_slot(e, s, capture != 0, captured);
+  const int launches = run_slot(e, s, graph, captured);
   CK(cudaEventRecord(e.ev_end, e.stream));
   CK(cudaMemcpyAsync(e.h_out, e.ws + s.L.out, s.L.n_out_floats * 4, cudaMemcpyDeviceToHost, e.stream));
   CK(cudaStreamSynchronize(e.stream));
@@ -1037,7 +1061,7 @@ int laya_predict(laya_engine* h, const int32_t* tokens, const int32_t* lengths, 
     metrics->rows = m; metrics->batch = b; metrics->options = k;
     metrics->cache_miss = miss;
     metrics->graph_capture = captured;
-    metrics->graph_replay = capture && s.graph != nullptr;
+    metrics->graph_replay = graph && s.graph != nullptr;
     metrics->kernel_launches = launches;
     metrics->owned_gpu_bytes = e.owned();
   }
@@ -1051,18 +1075,29 @@ int laya_forward_device(laya_engine* h, const int32_t* packed, int rows, int bat
   Engine& e = h->impl;
   if (!e.finalized) fail(LAYA_ERR_STATE, "engine not finalised");
   CK(cudaSetDevice(e.device));
+  const bool graph = wants_graph(capture, rows);
   bool miss = false;
-  Slot& s = get_slot(e, rows, batch, options, miss);
+  std::unique_ptr<Slot> transient;
+  Slot& s = get_slot(e, rows, batch, options, graph, miss, transient);
   ensure_workspace(e, s.L.total);
   CK(cudaMemcpyAsync(e.ws + s.L.packed, packed, (size_t)s.L.pack.total * 4, cudaMemcpyDeviceToDevice, e.stream));
   bool captured = false;
-  run_slot(e, s, capture != 0, captured);
+  run_slot(e, s, graph, captured);
   const float* outf = reinterpret_cast<const float*>(e.ws + s.L.out);
   if (logits_dev)
     CK(cudaMemcpyAsync(logits_dev, outf, (size_t)batch * (options + 1) * 4, cudaMemcpyDeviceToDevice, e.stream));
   if (acts_dev)
     CK(cudaMemcpyAsync(acts_dev, outf + (size_t)batch * (options + 1), (size_t)batch * e.cfg.n_act * 4,
                        cudaMemcpyDeviceToDevice, e.stream));
+  API_END(h)
+}
+
+int laya_reserve(laya_engine* h, int rows, int batch, int options) {
+  API_BEGIN
+  if (!h || rows <= 0 || batch <= 0 || options <= 0) fail(LAYA_ERR_INVALID, "bad reservation");
+  Engine& e = h->impl;
+  CK(cudaSetDevice(e.device));
+  ensure_workspace(e, make_layout(e, rows, batch, options).total);
   API_END(h)
 }
 
@@ -1077,7 +1112,7 @@ int laya_set_profiling(laya_engine* h, int enabled) {
 
 int laya_profile_read(laya_engine* h, int family, double* total_ms, int64_t* launches, double* flops) {
   API_BEGIN
-  if (!h || family < 0 || family > 3) fail(LAYA_ERR_INVALID, "bad profile family");
+  if (!h || family < 0 || family >= kFamilies) fail(LAYA_ERR_INVALID, "bad profile family");
   Engine& e = h->impl;
   CK(cudaSetDevice(e.device));
   prof_resolve(e);

@@ -16,7 +16,7 @@ PRECISION_BF16, PRECISION_F16 = 0, 1
 # Every symbol declared in include/laya_b200.h.
 EXPORTS = (
     "laya_create", "laya_load_tensor", "laya_finalize", "laya_predict", "laya_shape_class",
-    "laya_forward_device", "laya_packed_ints", "laya_pack", "laya_stream", "laya_set_profiling",
+    "laya_forward_device", "laya_packed_ints", "laya_pack", "laya_reserve", "laya_stream", "laya_set_profiling",
     "laya_profile_read", "laya_read_tensor", "laya_cached_shapes", "laya_pool_bytes", "laya_destroy",
     "laya_last_error", "laya_op_gemm", "laya_interleave_geglu", "laya_op_attention",
     "laya_attention_tiles", "laya_op_embed_norm", "laya_op_norm",
@@ -59,6 +59,7 @@ def load():
         "laya_forward_device": (i, [p, p, i, i, i, i, p, p]),
         "laya_packed_ints": (ct.c_int64, [i, i, i]),
         "laya_pack": (i, [p, p, p, p, p, i, i, i, i, i, p]),
+        "laya_reserve": (i, [p, i, i, i]),
         "laya_stream": (p, [p]),
         "laya_set_profiling": (i, [p, i]),
         "laya_profile_read": (i, [p, i, ct.POINTER(ct.c_double), i64p, ct.POINTER(ct.c_double)]),

@@ -162,6 +162,8 @@ class Runtime:
                    self._handle)
 
     def predict(self, items, capture=True):
+        """capture=True runs the class's CUDA graph (captured on first use) for classes of up
+        to 8192 packed rows and an eager pass above that; capture=False always runs eagerly."""
         from . import _lib
         if self._handle is None:
             raise RuntimeError("Runtime is closed")
@@ -171,7 +173,7 @@ class Runtime:
         acts = np.empty((len(items), self.adapter.n_act), np.float32)
         m = _lib.Metrics()
         _lib.check(self._lib.laya_predict(self._handle, _ptr(tokens), _ptr(lengths), _ptr(markers), _ptr(counts),
-                                          _ptr(kinds), len(items), int(bool(capture)), _ptr(logits), _ptr(acts),
+                                          _ptr(kinds), len(items), 2 if capture else 0, _ptr(logits), _ptr(acts),
                                           ct.byref(m)), self._handle)
         metrics = {"gpu_ms": m.gpu_ms, "shape": (rows, batch, options), "cache_miss": bool(m.cache_miss),
                    "graph_capture": bool(m.graph_capture), "graph_replay": bool(m.graph_replay),
