@@ -180,6 +180,27 @@ int laya_op_embed_norm(int precision, const int32_t* ids, const float* table, co
 int laya_op_norm(int precision, float* residual, const float* partials, int splits, const float* gamma,
                  const float* beta, float eps, void* x, int rows, int width, void* stream);
 
+/* ------------------------------------------------------------------------------------------
+ * Allocation-free split-K residual GEMM.  No counterpart in the reference: an addition for
+ * callers that cannot allocate device memory on this path, for example a serving host whose
+ * own allocator owns every byte of the GPU, or a latency-critical loop where cudaMalloc /
+ * cudaFree would implicitly synchronise the device and stall other streams.
+ *
+ *   residual[M][N] += x[M][K] @ w[N][K]^T (+ bias[N])      (same result as laya_op_gemm epi 5)
+ *
+ * The caller passes inputs and outputs only.  The split-K partial sums live in a static device
+ * array inside the library of LAYA_STATIC_SCRATCH_FLOATS floats (16 MiB), held by every GPU that
+ * loads the library until the process exits; M*N*splits must not exceed it (LAYA_ERR_INVALID
+ * otherwise).  The first call on a device looks the array's device address up, so make that
+ * first call before any stream capture.  All calls share the array: calls whose executions
+ * overlap on the GPU (different streams, or different host threads on one device) race.  The
+ * array keeps the last call's contents; every partial a call reads is written by the same call
+ * first, so nothing needs clearing.  No cudaMalloc, cudaFree or allocating library routine is
+ * called.  Enqueued on `stream` like the other kernel-level entry points. */
+#define LAYA_STATIC_SCRATCH_FLOATS (4 * 1024 * 1024)
+int laya_op_gemm_residual_static(int precision, const void* x, const void* w, int M, int N, int K, int splits,
+                                 float* residual, const float* bias, int* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

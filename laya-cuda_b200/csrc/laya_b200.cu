@@ -20,6 +20,7 @@
 #include <list>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <tuple>
 #include <unordered_map>
@@ -1272,3 +1273,90 @@ int laya_op_norm(int precision, float* residual, const float* partials, int spli
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------------
+// Split-K residual GEMM without allocation (laya_op_gemm_residual_static).
+//
+// Its split-K partial sums live in this file-scope device array rather than in memory the
+// caller or the library allocates.  Every GPU that loads the library holds the array until the
+// process exits.  In host code the symbol is only a host-side stand-in: kernels receive the
+// device address obtained with cudaGetSymbolAddress, looked up once per device below.
+// ---------------------------------------------------------------------------------------------
+static __device__ __align__(256) float g_static_partials[LAYA_STATIC_SCRATCH_FLOATS];
+
+namespace {
+
+std::mutex g_static_mutex;
+float* g_static_ptr[64] = {};
+
+// Device address of g_static_partials on the current device; the first call on a device looks
+// it up (with that device current) and caches it.
+float* static_partials_address() {
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) fail(LAYA_ERR_INVALID, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  if (!g_static_ptr[dev]) {
+    void* ptr = nullptr;
+    CK(cudaGetSymbolAddress(&ptr, g_static_partials));
+    if (!ptr) fail(LAYA_ERR_CUDA, "cudaGetSymbolAddress returned no address");
+    g_static_ptr[dev] = static_cast<float*>(ptr);
+  }
+  return g_static_ptr[dev];
+}
+
+// residual[r][c] += bias[c] + sum_s partials[s][r][c], summed in split order.
+__global__ void __launch_bounds__(256) add_partials_kernel(float* residual, const float* partials, int splits,
+                                                           int rows, int cols, const float* bias) {
+  const int64_t n4 = (int64_t)rows * cols / 4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < splits; ++sp) {
+      const float4 p = reinterpret_cast<const float4*>(partials)[(int64_t)sp * n4 + i];
+      acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+    }
+    if (bias) {
+      const int c = (int)((i * 4) % cols);
+      acc.x += bias[c]; acc.y += bias[c + 1]; acc.z += bias[c + 2]; acc.w += bias[c + 3];
+    }
+    float4 r = reinterpret_cast<float4*>(residual)[i];
+    r.x += acc.x; r.y += acc.y; r.z += acc.z; r.w += acc.w;
+    reinterpret_cast<float4*>(residual)[i] = r;
+  }
+}
+
+}  // namespace
+
+extern "C" int laya_op_gemm_residual_static(int precision, const void* x, const void* w, int M, int N, int K,
+                                            int splits, float* residual, const float* bias, int* err, void* stream) {
+  API_BEGIN
+  if (!x || !w || !residual) fail(LAYA_ERR_INVALID, "null argument");
+  if (M <= 0 || N <= 0 || K <= 0 || splits < 1) fail(LAYA_ERR_INVALID, "bad GEMM shape %dx%dx%d split %d", M, N, K, splits);
+  if (N % 64 || K % kBK) fail(LAYA_ERR_INVALID, "N must be a multiple of 64 and K of %d", kBK);
+  if ((K / kBK) % splits) fail(LAYA_ERR_INVALID, "split-K %d does not divide %d k-blocks", splits, K / kBK);
+  const int64_t need = (int64_t)M * N * splits;
+  if (need > LAYA_STATIC_SCRATCH_FLOATS)
+    fail(LAYA_ERR_INVALID, "M*N*splits = %lld partial sums exceed the static scratch of %d floats", (long long)need,
+         LAYA_STATIC_SCRATCH_FLOATS);
+  float* partials = static_partials_address();
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  const int sms = sm_count(dev);
+  const bool bf = precision == LAYA_PRECISION_BF16;
+  const int bn = pick_bn(M, N, EPI_PARTIAL, sms);
+  GemmArgs a{};
+  a.M = M; a.N = N; a.K = K; a.splits = splits;
+  a.residual = partials; a.ldr = N; a.err = err;
+  const CUtensorMap ta = make_map(x, M, K, kBM, bf);
+  const CUtensorMap tb = make_map(w, N, K, bn, bf);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Every partial element read below is written by this GEMM first, so the array needs no
+  // clearing between calls.
+  if (bf) launch_gemm<__nv_bfloat16>(EPI_PARTIAL, bn, ta, tb, a, sms, st);
+  else launch_gemm<__half>(EPI_PARTIAL, bn, ta, tb, a, sms, st);
+  const int64_t n4 = (int64_t)M * N / 4;
+  const int grid = (int)std::min<int64_t>((n4 + 255) / 256, 4LL * sms);
+  add_partials_kernel<<<grid, 256, 0, st>>>(residual, partials, splits, M, N, bias);
+  CK(cudaGetLastError());
+  API_END(nullptr)
+}

@@ -19,8 +19,9 @@ EXPORTS = (
     "laya_forward_device", "laya_packed_ints", "laya_pack", "laya_reserve", "laya_stream", "laya_set_profiling",
     "laya_profile_read", "laya_read_tensor", "laya_cached_shapes", "laya_pool_bytes", "laya_destroy",
     "laya_last_error", "laya_op_gemm", "laya_interleave_geglu", "laya_op_attention",
-    "laya_attention_tiles", "laya_op_embed_norm", "laya_op_norm",
+    "laya_attention_tiles", "laya_op_embed_norm", "laya_op_norm", "laya_op_gemm_residual_static",
 )
+STATIC_SCRATCH_FLOATS = 4 * 1024 * 1024
 
 
 class Config(ct.Structure):
@@ -74,6 +75,7 @@ def load():
         "laya_attention_tiles": (i, [p, p, i, i, p, i]),
         "laya_op_embed_norm": (i, [i, p, p, p, ct.c_float, i, i, i, p, p, p, p]),
         "laya_op_norm": (i, [i, p, p, i, p, p, ct.c_float, p, i, i, p]),
+        "laya_op_gemm_residual_static": (i, [i, p, p, i, i, i, i, p, p, p, p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
