@@ -151,12 +151,13 @@ const char* laya_last_error(laya_engine* e);
  * ------------------------------------------------------------------------------------------ */
 
 /* out/residual = epilogue(x[M][K] @ w[N][K]^T).  epi: 0 store, 1 relu, 2 gelu, 3 geglu (w rows
- * pre-interleaved by laya_interleave_geglu; out is [M][N/2]), 4 qkv (RoPE when cos/sin given;
- * out is [3][heads][M][64]), 5 residual += (fp32), 6 split-K partials.  bias: fp32 [N] or NULL.
- * Replaces cublasGemmEx + bias/activate/layout (ops.py:58-66; kernels.cu:50-82). */
+ * pre-interleaved by laya_interleave_geglu; out is [M][N/2]), 4 qkv (RoPE when cos/sin given,
+ * tables transposed [32][rope_rows] indexed by positions[row]; out is [3][heads][M][64]),
+ * 5 residual += (fp32), 6 split-K partials ([splits][M][N] fp32 in `residual`).  bias: fp32 [N]
+ * or NULL.  Replaces cublasGemmEx + bias/activate/layout (ops.py:58-66; kernels.cu:50-82). */
 int laya_op_gemm(int precision, int epi, const void* x, const void* w, int M, int N, int K, void* out, int ldo,
                  float* residual, int ldr, const float* bias, int heads, const float* cos_tab, const float* sin_tab,
-                 const int32_t* positions, int splits, int block_n, int* err, void* stream);
+                 int rope_rows, const int32_t* positions, int splits, int block_n, int* err, void* stream);
 
 /* Reorders Wi [2F][K] (gate rows then up rows) into 64-row blocks [gate_i, up_i] (host memory). */
 int laya_interleave_geglu(const uint16_t* src, uint16_t* dst, int F, int K);

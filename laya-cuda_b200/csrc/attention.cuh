@@ -80,6 +80,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
   __shared__ __align__(128) uint8_t sK[2][kAttnKB * 128];
   __shared__ __align__(128) uint8_t sV[2][kAttnKB * 128];
 
+  pdl_trigger();
+  pdl_wait();
   const int4 tile = a.tiles[blockIdx.x];
   const int head = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;

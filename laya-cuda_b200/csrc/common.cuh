@@ -184,6 +184,15 @@ __host__ __device__ constexpr uint32_t mma_idesc(int M, int N) {
 }
 
 // ---------------------------------------------------------------------------------------------
+// Programmatic dependent launch.  Every kernel of the forward pass is launched with programmatic
+// stream serialisation: it may start while its predecessor drains, runs its prologue, and waits
+// in pdl_wait() for the predecessor's completion (and memory flush) before touching anything the
+// predecessor wrote.  Without the launch attribute both are no-ops.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------------------------
 // Element conversions
 // ---------------------------------------------------------------------------------------------
 template <typename T> __device__ __forceinline__ T from_f32(float x);

@@ -43,8 +43,9 @@ struct GemmArgs {
   const float* bias;      // fp32 [N] (GeGLU: unused) or nullptr
   // EPI_QKV
   int heads;
-  const float* cos_tab;   // [positions][32] or nullptr (no rotary embedding)
+  const float* cos_tab;   // [32][rope_rows] (transposed, so a warp's rows read contiguously) or nullptr
   const float* sin_tab;
+  int rope_rows;
   const int* positions;   // [M]
   int* err;               // device error word
 };
@@ -154,6 +155,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // The prologue above touches no predecessor output.
+  pdl_trigger();
 
   // Tile order: split outermost, then row block, then column block, so CTAs running together
   // share an A row block (it stays in L2 while all its column blocks are computed).
@@ -169,14 +172,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0; uint32_t phase = 0;
       uint32_t issued = 0, last_par = 0;
       bool ok = true;
+      // Weights do not depend on the previous kernel: the first tile's weight stages are loaded
+      // before waiting for it, so their HBM latency overlaps the predecessor's tail.
+      int pre = 0;
+      if ((int)blockIdx.x < tiles) {
+        int split, mb, nb; decode(blockIdx.x, split, mb, nb);
+        pre = k_blocks < S ? k_blocks : S;
+        for (int kb = 0; kb < pre; ++kb) {
+          mbar_arrive_expect_tx(&full[kb], Cfg::kStageBytes);
+          tma_load_2d(sB + kb * Cfg::kStageB, &tmB, &full[kb], (split * k_blocks + kb) * kBK, nb * BN);
+        }
+      }
+      pdl_wait();
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         int split, mb, nb; decode(t, split, mb, nb);
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrGemmProducerWait, abort_flag)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
           const int kx = (split * k_blocks + kb) * kBK;
-          tma_load_2d(sA + stage * Cfg::kStageA, &tmA, &full[stage], kx, mb * kBM);
-          tma_load_2d(sB + stage * Cfg::kStageB, &tmB, &full[stage], kx, nb * BN);
+          if (t == (int)blockIdx.x && kb < pre) {
+            // Stage `kb` already expects this k-block's bytes and holds its weights.
+            tma_load_2d(sA + stage * Cfg::kStageA, &tmA, &full[stage], kx, mb * kBM);
+          } else {
+            if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrGemmProducerWait, abort_flag)) { ok = false; break; }
+            mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+            tma_load_2d(sA + stage * Cfg::kStageA, &tmA, &full[stage], kx, mb * kBM);
+            tma_load_2d(sB + stage * Cfg::kStageB, &tmB, &full[stage], kx, nb * BN);
+          }
           issued |= 1u << stage;
           last_par = (last_par & ~(1u << stage)) | (phase << stage);
           if (++stage == S) { stage = 0; phase ^= 1; }
@@ -187,8 +207,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         for (int s = 0; s < S; ++s)
           if (issued & (1u << s)) mbar_wait(&full[s], (last_par >> s) & 1, nullptr, 0, abort_flag);
       }
+    } else {
+      pdl_wait();
     }
   } else if (warp == 1) {
+    pdl_wait();
     if (lane == 0) {
       const uint32_t idesc = mma_idesc<std::is_same<T, __nv_bfloat16>::value>(kBM, BN);
       int stage = 0; uint32_t phase = 0;
@@ -220,6 +243,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_wait(drain, 0, nullptr, 0, abort_flag);
     }
   } else {
+    pdl_wait();
     // Epilogue warps 2..5 -> TMEM lane quarter (warp % 4).
     const int quarter = warp & 3;
     int acc = 0; uint32_t acc_phase = 0;
@@ -277,12 +301,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (part < 2 && args.cos_tab) {
               // Rotate-half RoPE: out[d] = x[d] cos - x[d+32] sin (d < 32),
               //                   out[d] = x[d] cos + x[d-32] sin (d >= 32).
+              // Tables are [32][rope_rows]: the 32 lanes (consecutive rows, mostly consecutive
+              // positions) read one contiguous run per frequency.
               const int pos = args.positions[row];
-              const float* cs = args.cos_tab + (size_t)pos * 32;
-              const float* sn = args.sin_tab + (size_t)pos * 32;
+              const float* cs = args.cos_tab + pos;
+              const float* sn = args.sin_tab + pos;
 #pragma unroll
               for (int i = 0; i < 32; ++i) {
-                const float c0 = cs[i], s0 = sn[i];
+                const float c0 = __ldg(cs + (size_t)i * args.rope_rows), s0 = __ldg(sn + (size_t)i * args.rope_rows);
                 const float a = x[i], b = x[i + 32];
                 x[i] = a * c0 - b * s0;
                 x[i + 32] = b * c0 + a * s0;

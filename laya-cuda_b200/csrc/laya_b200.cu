@@ -60,6 +60,11 @@ struct Failure {
     if (e_ != cudaSuccess) fail(LAYA_ERR_CUDA, "%s failed: %s", #call, cudaGetErrorString(e_));     \
   } while (0)
 
+// Residual GEMMs of classes up to this many rows may split K across CTAs (their partial sums are
+// added, in split order, by the LayerNorm that follows), so small batches fill the SMs.
+constexpr int kSplitRowsMax = 2048;
+constexpr int kMaxSplits = 8;
+
 // ---------------------------------------------------------------------------------------------
 // Driver entry point for tensor-map encoding (no link-time dependency on libcuda).
 // ---------------------------------------------------------------------------------------------
@@ -106,6 +111,30 @@ int sm_count(int device) {
   return n;
 }
 
+// Programmatic dependent launch on every kernel (LAYA_PDL=0 in the environment turns it off).
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("LAYA_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  CK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
+}
+
 // ---------------------------------------------------------------------------------------------
 // Kernel dispatch
 // ---------------------------------------------------------------------------------------------
@@ -119,8 +148,7 @@ void launch_gemm_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
     CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmCfg<BN>::kSmemBytes));
     configured |= 1ull << dev;
   }
-  kern<<<grid, kGemmThreads, GemmCfg<BN>::kSmemBytes, st>>>(ta, tb, a);
-  CK(cudaGetLastError());
+  launch_k(kern, dim3(grid), dim3(kGemmThreads), GemmCfg<BN>::kSmemBytes, st, ta, tb, a);
 }
 
 template <typename T, int BN>
@@ -174,29 +202,59 @@ int pick_bn(int M, int N, int epi, int sms) {
   return best;
 }
 
+// Split-K factor for a GEMM whose output tiles leave most SMs idle: the largest divisor of the
+// k-block count that keeps at least 3 k-blocks per split and the tile count within one wave.
+int pick_splits(int M, int N, int K, int bn, int sms) {
+  const int tiles = ((M + kBM - 1) / kBM) * (N / bn);
+  const int kb = K / kBK;
+  if (2 * tiles >= sms) return 1;
+  int best = 1;
+  for (int s = 2; s <= kMaxSplits; ++s)
+    if (kb % s == 0 && kb / s >= 3 && tiles * s <= sms) best = s;
+  return best;
+}
+
 template <typename T>
 void launch_attention(const AttnArgs& a, int n_tiles, bool split_p, cudaStream_t st) {
   dim3 grid(n_tiles, a.heads);
-  if (split_p) attention_kernel<T, true><<<grid, kAttnThreads, 0, st>>>(a);
-  else attention_kernel<T, false><<<grid, kAttnThreads, 0, st>>>(a);
-  CK(cudaGetLastError());
+  if (split_p) launch_k(attention_kernel<T, true>, grid, dim3(kAttnThreads), 0, st, a);
+  else launch_k(attention_kernel<T, false>, grid, dim3(kAttnThreads), 0, st, a);
 }
+
+// Row kernels are instantiated per width (d = 32 * NPL, d a multiple of 64 up to 1024).
+#define LAYA_FOR_EACH_WIDTH(X) X(2) X(4) X(6) X(8) X(10) X(12) X(14) X(16) X(18) X(20) X(22) X(24) X(26) X(28) X(30) X(32)
 
 template <typename T>
 void launch_embed(const int* ids, const float* table, const float* gamma, float eps, int rows, int d, int vocab,
                   float* residual, T* x, int* err, cudaStream_t st) {
   const int grid = (rows + kRowWarps - 1) / kRowWarps;
-  if (d % 128 == 0) embed_norm_kernel<4, T><<<grid, kRowWarps * 32, 0, st>>>(ids, table, gamma, eps, rows, d, vocab, residual, x, err);
-  else embed_norm_kernel<2, T><<<grid, kRowWarps * 32, 0, st>>>(ids, table, gamma, eps, rows, d, vocab, residual, x, err);
-  CK(cudaGetLastError());
+  switch (d / 32) {
+#define LAYA_EMBED_CASE(N)                                                                                  \
+  case N:                                                                                                   \
+    launch_k(embed_norm_kernel<N, T>, dim3(grid), dim3(kRowWarps * 32), 0, st, ids, table, gamma, eps, rows, d, \
+             vocab, residual, x, err);                                                                      \
+    break;
+    LAYA_FOR_EACH_WIDTH(LAYA_EMBED_CASE)
+#undef LAYA_EMBED_CASE
+    default: fail(LAYA_ERR_INVALID, "unsupported width %d", d);
+  }
 }
 
 template <typename T>
 void launch_norm(const NormArgs& a, cudaStream_t st) {
+  if (a.d % 64 || a.d > 1024) fail(LAYA_ERR_INVALID, "unsupported width %d", a.d);
   const int grid = (a.rows + kRowWarps - 1) / kRowWarps;
-  if (a.d % 128 == 0) norm_kernel<4, T><<<grid, kRowWarps * 32, 0, st>>>(a);
-  else norm_kernel<2, T><<<grid, kRowWarps * 32, 0, st>>>(a);
-  CK(cudaGetLastError());
+  const bool partials = a.splits > 0;
+  switch (a.d / 32) {
+#define LAYA_NORM_CASE(N)                                                                   \
+  case N:                                                                                   \
+    if (partials) launch_k(norm_kernel<N, T, true>, dim3(grid), dim3(kRowWarps * 32), 0, st, a); \
+    else launch_k(norm_kernel<N, T, false>, dim3(grid), dim3(kRowWarps * 32), 0, st, a);         \
+    break;
+    LAYA_FOR_EACH_WIDTH(LAYA_NORM_CASE)
+#undef LAYA_NORM_CASE
+    default: fail(LAYA_ERR_INVALID, "unsupported width %d", a.d);
+  }
 }
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -318,7 +376,8 @@ struct Tensor {
 struct ClassLayout {
   int m = 0, b = 0, k = 0, count = 0, tiles_cap = 0;
   PackLayout pack{};
-  size_t packed, residual, x, qkv, attn, ff, sel, selx, scored, ffsel, out, total;
+  size_t packed, residual, x, qkv, attn, ff, sel, selx, scored, ffsel, partials, hidden, out, total;
+  bool has_partials = false;
   size_t n_out_floats;  // logits b*(k+1) + acts b*n_act + 1 error word
 };
 
@@ -532,8 +591,13 @@ ClassLayout make_layout(const Engine& e, int m, int b, int k) {
   L.selx = take((size_t)L.count * d * es);
   L.scored = take((size_t)L.count * d * es);
   L.ffsel = take((size_t)L.count * 4 * d * es);
+  L.has_partials = m <= kSplitRowsMax;
+  L.partials = take(L.has_partials ? (size_t)kMaxSplits * std::max(m, L.count) * d * 4 : 0);
+  L.hidden = take((size_t)b * kActHidden * 4);
+  // logits [b][k+1], acts [b][n_act], the error word, then the head tail's per-question
+  // arrival counters (zeroed with the error word at the start of every pass).
   L.n_out_floats = (size_t)b * (k + 1) + (size_t)b * e.cfg.n_act + 1;
-  L.out = take(L.n_out_floats * 4);
+  L.out = take((L.n_out_floats + b) * 4);
   L.total = o;
   return L;
 }
@@ -653,11 +717,24 @@ void gemm(Engine& e, bool prof, int family, int epi, const CUtensorMap& ta, cons
   a.M = M; a.N = N; a.K = K; a.splits = 1;
   a.out = out; a.ldo = ldo; a.residual = residual; a.ldr = ldr; a.bias = bias;
   a.heads = e.cfg.heads;
-  if (rope >= 0) { a.cos_tab = e.rope_cos[rope]; a.sin_tab = e.rope_sin[rope]; }
+  if (rope >= 0) { a.cos_tab = e.rope_cos[rope]; a.sin_tab = e.rope_sin[rope]; a.rope_rows = e.rope_rows; }
   a.positions = positions;
   a.err = err;
   const CUtensorMap& tb = weight_map(e, wname, bn);
   launch(e, prof, family, 2.0 * M * N * K, [&] { launch_gemm<T>(epi, bn, ta, tb, a, e.sms, e.stream); });
+}
+
+template <typename T>
+void gemm_partial(Engine& e, bool prof, int family, const CUtensorMap& ta, const std::string& wname, int M, int splits,
+                  float* partials, int* err) {
+  const Tensor& w = W(e, wname);
+  const int N = (int)w.shape[0], K = (int)w.shape[1];
+  const int bn = pick_bn(M, N, EPI_PARTIAL, e.sms);
+  GemmArgs a{};
+  a.M = M; a.N = N; a.K = K; a.splits = splits;
+  a.residual = partials; a.ldr = N; a.err = err;
+  const CUtensorMap& tb = weight_map(e, wname, bn);
+  launch(e, prof, family, 2.0 * M * N * K, [&] { launch_gemm<T>(EPI_PARTIAL, bn, ta, tb, a, e.sms, e.stream); });
 }
 
 // The whole forward pass of one shape class (runtime.py:90-113 + laya.py:214-245), enqueued
@@ -686,12 +763,14 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
   T* selx = reinterpret_cast<T*>(ws + L.selx);
   T* scored = reinterpret_cast<T*>(ws + L.scored);
   T* ffsel = reinterpret_cast<T*>(ws + L.ffsel);
+  float* partials = L.has_partials ? reinterpret_cast<float*>(ws + L.partials) : nullptr;
   float* outf = reinterpret_cast<float*>(ws + L.out);
   float* logits = outf;
   float* acts = outf + (size_t)L.b * (L.k + 1);
   int* err = reinterpret_cast<int*>(acts + (size_t)L.b * c.n_act);
 
-  CK(cudaMemsetAsync(err, 0, sizeof(int), e.stream));
+  int* arrivals = err + 1;
+  CK(cudaMemsetAsync(err, 0, sizeof(int) * (1 + (size_t)L.b), e.stream));
   const double rowbytes = (double)m * d;
   launch(e, prof, FAM_ROWS, 0, [&] {
     launch_embed<T>(ids, Wf(e, "encoder.embeddings.tok_embeddings.weight"), Wf(e, "encoder.embeddings.norm.weight"),
@@ -705,12 +784,31 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
     a.M = m; a.heads = c.heads; a.window = window;
     launch(e, prof, FAM_ATTENTION, 0, [&] { launch_attention<T>(a, L.tiles_cap, false, e.stream); });
   };
-  auto norm = [&](float* res, int rows, const float* g, const float* b, float eps, T* out) {
+  // A residual GEMM whose sum the next norm must still add: split count and the GEMM bias.
+  struct Pending { int splits = 0; const float* bias = nullptr; };
+  auto norm = [&](float* res, int rows, const float* g, const float* b, float eps, T* out, Pending pend) {
     NormArgs a{};
-    a.residual = res; a.partials = nullptr; a.splits = 0;
+    a.residual = res; a.partials = pend.splits ? partials : nullptr; a.splits = pend.splits;
+    a.partial_bias = pend.bias;
     a.gamma1 = g; a.beta1 = b; a.eps1 = eps; a.fused_final = 0;
     a.x = out; a.rows = rows; a.d = d;
     launch(e, prof, FAM_ROWS, 0, [&] { launch_norm<T>(a, e.stream); });
+  };
+  // residual += A W^T + bias: the fused residual epilogue, or, for small classes, split-K
+  // partials that the following norm adds.
+  auto residual_gemm = [&](int family, const CUtensorMap& ta, const std::string& wname, int rows, float* res,
+                           const float* bias) -> Pending {
+    const Tensor& w = W(e, wname);
+    const int N = (int)w.shape[0], K = (int)w.shape[1];
+    int splits = 1;
+    if (partials && rows <= kSplitRowsMax && N == d)
+      splits = pick_splits(rows, N, K, pick_bn(rows, N, EPI_PARTIAL, e.sms), e.sms);
+    if (splits > 1) {
+      gemm_partial<T>(e, prof, family, ta, wname, rows, splits, partials, err);
+      return Pending{splits, bias};
+    }
+    gemm<T>(e, prof, family, EPI_RESIDUAL, ta, wname, rows, nullptr, 0, res, d, bias, err);
+    return Pending{};
   };
 
   for (int i = 0; i < c.layers; ++i) {
@@ -718,16 +816,17 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
     const bool local = i % c.global_every != 0;
     gemm<T>(e, prof, FAM_GEMM_QKV, EPI_QKV, s.map_x, p + "attn.Wqkv.weight", m, qkv, 0, nullptr, 0, nullptr, err, local ? 1 : 0, positions);
     attention(local ? c.window : -1);
-    gemm<T>(e, prof, FAM_GEMM_ATTN_OUT, EPI_RESIDUAL, s.map_attn, p + "attn.Wo.weight", m, nullptr, 0, residual, d, nullptr, err);
-    norm(residual, m, Wf(e, p + "mlp_norm.weight"), nullptr, c.eps, x);
+    Pending pend = residual_gemm(FAM_GEMM_ATTN_OUT, s.map_attn, p + "attn.Wo.weight", m, residual, nullptr);
+    norm(residual, m, Wf(e, p + "mlp_norm.weight"), nullptr, c.eps, x, pend);
     gemm<T>(e, prof, FAM_GEMM_FFN_UP, EPI_GEGLU, s.map_x, p + "mlp.Wi.weight", m, ff, e.F(), nullptr, 0, nullptr, err);
-    gemm<T>(e, prof, FAM_GEMM_FFN_DOWN, EPI_RESIDUAL, s.map_ff, p + "mlp.Wo.weight", m, nullptr, 0, residual, d, nullptr, err);
+    pend = residual_gemm(FAM_GEMM_FFN_DOWN, s.map_ff, p + "mlp.Wo.weight", m, residual, nullptr);
     if (i + 1 < c.layers) {
-      norm(residual, m, Wf(e, "encoder.layers." + std::to_string(i + 1) + ".attn_norm.weight"), nullptr, c.eps, x);
+      norm(residual, m, Wf(e, "encoder.layers." + std::to_string(i + 1) + ".attn_norm.weight"), nullptr, c.eps, x, pend);
     } else {
       // encoder.final_norm -> residual; residual += type_emb[kind]; x = head.layers.0.norm1(residual)
       NormArgs a{};
-      a.residual = residual; a.splits = 0;
+      a.residual = residual;
+      a.partials = pend.splits ? partials : nullptr; a.splits = pend.splits; a.partial_bias = pend.bias;
       a.gamma1 = Wf(e, "encoder.final_norm.weight"); a.beta1 = nullptr; a.eps1 = c.eps;
       a.fused_final = 1; a.type_emb = Wf(e, "type_emb.weight"); a.kinds = kinds;
       a.gamma2 = Wf(e, "head.layers.0.norm1.weight"); a.beta2 = Wf(e, "head.layers.0.norm1.bias"); a.eps2 = 1e-5f;
@@ -736,35 +835,36 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
     }
   }
 
+  Pending head_pend;
   for (int i = 0; i < c.head_layers; ++i) {
     const std::string p = "head.layers." + std::to_string(i) + ".";
-    if (i > 0) norm(residual, m, Wf(e, p + "norm1.weight"), Wf(e, p + "norm1.bias"), 1e-5f, x);
+    if (i > 0) norm(residual, m, Wf(e, p + "norm1.weight"), Wf(e, p + "norm1.bias"), 1e-5f, x, Pending{});
     gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_QKV, s.map_x, p + "self_attn.in_proj_weight", m, qkv, 0, nullptr, 0,
             Wf(e, p + "self_attn.in_proj_bias"), err);
     attention(-1);
     if (i + 1 == c.head_layers) {
       launch(e, prof, FAM_ROWS, 0, [&] {
-        gather_rows_kernel<T><<<count, 256, 0, e.stream>>>(residual, attn, indices, count, d, m, sel, scored, err);
-        CK(cudaGetLastError());
+        launch_k(gather_rows_kernel<T>, dim3(count), dim3(256), 0, e.stream, (const float*)residual, (const T*)attn,
+                 indices, count, d, m, sel, scored, err);
       });
-      gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_RESIDUAL, s.map_scored, p + "self_attn.out_proj.weight", count, nullptr, 0, sel, d,
-              Wf(e, p + "self_attn.out_proj.bias"), err);
-      norm(sel, count, Wf(e, p + "norm2.weight"), Wf(e, p + "norm2.bias"), 1e-5f, selx);
+      Pending pend = residual_gemm(FAM_GEMM_HEAD, s.map_scored, p + "self_attn.out_proj.weight", count, sel,
+                                   Wf(e, p + "self_attn.out_proj.bias"));
+      norm(sel, count, Wf(e, p + "norm2.weight"), Wf(e, p + "norm2.bias"), 1e-5f, selx, pend);
       gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_RELU, s.map_selx, p + "linear1.weight", count, ffsel, 4 * d, nullptr, 0,
               Wf(e, p + "linear1.bias"), err);
-      gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_RESIDUAL, s.map_ffsel, p + "linear2.weight", count, nullptr, 0, sel, d,
-              Wf(e, p + "linear2.bias"), err);
+      head_pend = residual_gemm(FAM_GEMM_HEAD, s.map_ffsel, p + "linear2.weight", count, sel, Wf(e, p + "linear2.bias"));
     } else {
-      gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_RESIDUAL, s.map_attn, p + "self_attn.out_proj.weight", m, nullptr, 0, residual, d,
-              Wf(e, p + "self_attn.out_proj.bias"), err);
-      norm(residual, m, Wf(e, p + "norm2.weight"), Wf(e, p + "norm2.bias"), 1e-5f, x);
+      Pending pend = residual_gemm(FAM_GEMM_HEAD, s.map_attn, p + "self_attn.out_proj.weight", m, residual,
+                                   Wf(e, p + "self_attn.out_proj.bias"));
+      norm(residual, m, Wf(e, p + "norm2.weight"), Wf(e, p + "norm2.bias"), 1e-5f, x, pend);
       gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_RELU, s.map_x, p + "linear1.weight", m, ff, 4 * d, nullptr, 0, Wf(e, p + "linear1.bias"), err);
       const CUtensorMap ffmap = make_map(ff, m, 4 * d, kBM, e.bf16());
+      // The next head layer's norm1 reads the residual directly, so this GEMM never splits.
       gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_RESIDUAL, ffmap, p + "linear2.weight", m, nullptr, 0, residual, d,
               Wf(e, p + "linear2.bias"), err);
     }
   }
-  norm(sel, count, Wf(e, "scorer.0.weight"), Wf(e, "scorer.0.bias"), 1e-5f, selx);
+  norm(sel, count, Wf(e, "scorer.0.weight"), Wf(e, "scorer.0.bias"), 1e-5f, selx, head_pend);
   gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_GELU, s.map_selx, "scorer.1.weight", count, scored, d, nullptr, 0, Wf(e, "scorer.1.bias"), err);
   TailArgs t{};
   t.selected = sel; t.scored = scored; t.counts = counts;
@@ -772,10 +872,10 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
   t.wa0 = Wf(e, "act_head.0.weight"); t.ba0 = Wf(e, "act_head.0.bias");
   t.wa2 = Wf(e, "act_head.2.weight"); t.ba2 = Wf(e, "act_head.2.bias");
   t.logits = logits; t.acts = acts; t.k = L.k; t.d = d; t.n_act = c.n_act;
+  t.hidden = reinterpret_cast<float*>(ws + L.hidden); t.arrivals = arrivals;
   const size_t tail_smem = ((size_t)(L.k + 1) + d + 4 + kActHidden) * sizeof(float);
   launch(e, prof, FAM_HEAD_TAIL, 0, [&] {
-    head_tail_kernel<T><<<L.b, kTailThreads, tail_smem, e.stream>>>(t);
-    CK(cudaGetLastError());
+    launch_k(head_tail_kernel<T>, dim3(L.b, kTailParts), dim3(kTailThreads), tail_smem, e.stream, t);
   });
 }
 
@@ -980,14 +1080,15 @@ int laya_finalize(laya_engine* h) {
   e.rope_rows = span16(e.cfg.max_len);
   const float thetas[2] = {e.cfg.theta_global, e.cfg.theta_local};
   for (int t = 0; t < 2; ++t) {
+    // Stored transposed, [32][rope_rows], so the QKV epilogue's lanes read contiguously.
     std::vector<float> cs((size_t)e.rope_rows * 32), sn((size_t)e.rope_rows * 32);
     for (int j = 0; j < 32; ++j) {
       const float expo = (float)(2 * j) / 64.0f;
       const float freq = 1.0f / powf(thetas[t], expo);
       for (int pos = 0; pos < e.rope_rows; ++pos) {
         const float angle = (float)pos * freq;
-        cs[(size_t)pos * 32 + j] = (float)cos((double)angle);
-        sn[(size_t)pos * 32 + j] = (float)sin((double)angle);
+        cs[(size_t)j * e.rope_rows + pos] = (float)cos((double)angle);
+        sn[(size_t)j * e.rope_rows + pos] = (float)sin((double)angle);
       }
     }
     if (e.rope_cos[t]) { cudaFree(e.rope_cos[t]); cudaFree(e.rope_sin[t]); }
@@ -1204,7 +1305,7 @@ const char* laya_last_error(laya_engine* h) { return h ? h->impl.error.c_str() :
 // ---------------------------------------------------------------------------------------------
 int laya_op_gemm(int precision, int epi, const void* x, const void* w, int M, int N, int K, void* out, int ldo,
                  float* residual, int ldr, const float* bias, int heads, const float* cos_tab, const float* sin_tab,
-                 const int32_t* positions, int splits, int block_n, int* err, void* stream) {
+                 int rope_rows, const int32_t* positions, int splits, int block_n, int* err, void* stream) {
   API_BEGIN
   int dev = 0;
   CK(cudaGetDevice(&dev));
@@ -1215,7 +1316,8 @@ int laya_op_gemm(int precision, int epi, const void* x, const void* w, int M, in
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K; a.splits = splits;
   a.out = out; a.ldo = ldo; a.residual = residual; a.ldr = ldr; a.bias = bias;
-  a.heads = heads; a.cos_tab = cos_tab; a.sin_tab = sin_tab; a.positions = positions; a.err = err;
+  a.heads = heads; a.cos_tab = cos_tab; a.sin_tab = sin_tab; a.rope_rows = rope_rows; a.positions = positions;
+  a.err = err;
   const CUtensorMap ta = make_map(x, M, K, kBM, bf);
   const CUtensorMap tb = make_map(w, N, K, bn, bf);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -1308,6 +1410,9 @@ float* static_partials_address() {
 // residual[r][c] += bias[c] + sum_s partials[s][r][c], summed in split order.
 __global__ void __launch_bounds__(256) add_partials_kernel(float* residual, const float* partials, int splits,
                                                            int rows, int cols, const float* bias) {
+  // Launched with programmatic serialisation like every kernel here: wait for the split-K GEMM.
+  pdl_trigger();
+  pdl_wait();
   const int64_t n4 = (int64_t)rows * cols / 4;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1356,7 +1461,6 @@ extern "C" int laya_op_gemm_residual_static(int precision, const void* x, const 
   else launch_gemm<__half>(EPI_PARTIAL, bn, ta, tb, a, sms, st);
   const int64_t n4 = (int64_t)M * N / 4;
   const int grid = (int)std::min<int64_t>((n4 + 255) / 256, 4LL * sms);
-  add_partials_kernel<<<grid, 256, 0, st>>>(residual, partials, splits, M, N, bias);
-  CK(cudaGetLastError());
+  launch_k(add_partials_kernel, dim3(grid), dim3(256), 0, st, residual, (const float*)partials, splits, M, N, bias);
   API_END(nullptr)
 }

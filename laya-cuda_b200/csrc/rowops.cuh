@@ -11,51 +11,52 @@
 namespace laya {
 
 constexpr int kRowWarps = 8;           // rows per 256-thread block
-constexpr int kMaxPerLane = 32;        // supports widths up to 1024
 
-// Loads row `src` (fp32, width d) into v[0 .. d/32): element i of the lane lives at column
-// lane*CH + (i/CH)*32*CH + i%CH (vectors of CH consecutive floats).
-template <int CH>
-__device__ __forceinline__ void row_load(const float* src, int d, int lane, float (&v)[kMaxPerLane]) {
+// A warp holds one row of width d = 32 * NPL (NPL even, 2..32: widths 64..1024): lane `lane`
+// keeps NPL floats, in vectors of CH consecutive columns at col = j*32*CH + lane*CH.
+template <int NPL>
+struct RowVec {
+  static constexpr int CH = (NPL % 4 == 0) ? 4 : 2;
+};
+
+template <int NPL>
+__device__ __forceinline__ void row_load(const float* src, int lane, float (&v)[NPL]) {
+  constexpr int CH = RowVec<NPL>::CH;
 #pragma unroll
-  for (int j = 0; j < kMaxPerLane / CH; ++j) {
+  for (int j = 0; j < NPL / CH; ++j) {
     const int col = j * 32 * CH + lane * CH;
-    if (col < d) {
-      if (CH == 4) {
-        float4 t = *reinterpret_cast<const float4*>(src + col);
-        v[j * 4] = t.x; v[j * 4 + 1] = t.y; v[j * 4 + 2] = t.z; v[j * 4 + 3] = t.w;
-      } else {
-        float2 t = *reinterpret_cast<const float2*>(src + col);
-        v[j * 2] = t.x; v[j * 2 + 1] = t.y;
-      }
+    if (CH == 4) {
+      const float4 t = *reinterpret_cast<const float4*>(src + col);
+      v[j * 4] = t.x; v[j * 4 + 1] = t.y; v[j * 4 + 2] = t.z; v[j * 4 + 3] = t.w;
+    } else {
+      const float2 t = *reinterpret_cast<const float2*>(src + col);
+      v[j * 2] = t.x; v[j * 2 + 1] = t.y;
     }
   }
 }
 
-template <int CH>
-__device__ __forceinline__ void row_store(float* dst, int d, int lane, const float (&v)[kMaxPerLane]) {
+template <int NPL>
+__device__ __forceinline__ void row_store(float* dst, int lane, const float (&v)[NPL]) {
+  constexpr int CH = RowVec<NPL>::CH;
 #pragma unroll
-  for (int j = 0; j < kMaxPerLane / CH; ++j) {
+  for (int j = 0; j < NPL / CH; ++j) {
     const int col = j * 32 * CH + lane * CH;
-    if (col < d) {
-      if (CH == 4) *reinterpret_cast<float4*>(dst + col) = make_float4(v[j * 4], v[j * 4 + 1], v[j * 4 + 2], v[j * 4 + 3]);
-      else *reinterpret_cast<float2*>(dst + col) = make_float2(v[j * 2], v[j * 2 + 1]);
-    }
+    if (CH == 4) *reinterpret_cast<float4*>(dst + col) = make_float4(v[j * 4], v[j * 4 + 1], v[j * 4 + 2], v[j * 4 + 3]);
+    else *reinterpret_cast<float2*>(dst + col) = make_float2(v[j * 2], v[j * 2 + 1]);
   }
 }
 
-template <int CH, typename T>
-__device__ __forceinline__ void row_store_t(T* dst, int d, int lane, const float (&v)[kMaxPerLane]) {
+template <int NPL, typename T>
+__device__ __forceinline__ void row_store_t(T* dst, int lane, const float (&v)[NPL]) {
+  constexpr int CH = RowVec<NPL>::CH;
 #pragma unroll
-  for (int j = 0; j < kMaxPerLane / CH; ++j) {
+  for (int j = 0; j < NPL / CH; ++j) {
     const int col = j * 32 * CH + lane * CH;
-    if (col < d) {
-      if (CH == 4) {
-        uint2 w; w.x = pack2<T>(v[j * 4], v[j * 4 + 1]); w.y = pack2<T>(v[j * 4 + 2], v[j * 4 + 3]);
-        *reinterpret_cast<uint2*>(dst + col) = w;
-      } else {
-        *reinterpret_cast<uint32_t*>(dst + col) = pack2<T>(v[j * 2], v[j * 2 + 1]);
-      }
+    if (CH == 4) {
+      uint2 w; w.x = pack2<T>(v[j * 4], v[j * 4 + 1]); w.y = pack2<T>(v[j * 4 + 2], v[j * 4 + 3]);
+      *reinterpret_cast<uint2*>(dst + col) = w;
+    } else {
+      *reinterpret_cast<uint32_t*>(dst + col) = pack2<T>(v[j * 2], v[j * 2 + 1]);
     }
   }
 }
@@ -67,32 +68,34 @@ __device__ __forceinline__ float warp_sum(float x) {
 }
 
 // In-place LayerNorm of the lane's slice: v = (v - mean) * rsqrt(var + eps) * gamma (+ beta).
-template <int CH>
-__device__ __forceinline__ void row_layernorm(float (&v)[kMaxPerLane], int d, int lane, const float* gamma,
-                                              const float* beta, float eps) {
+template <int NPL>
+__device__ __forceinline__ void row_layernorm(float (&v)[NPL], int lane, const float* gamma, const float* beta,
+                                              float eps) {
+  constexpr int CH = RowVec<NPL>::CH;
+  constexpr float inv_d = 1.0f / (32 * NPL);
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
-    if ((i / CH) * 32 * CH + lane * CH < d) s += v[i];
-  const float mean = warp_sum(s) / d;
+  for (int i = 0; i < NPL; ++i) s += v[i];
+  const float mean = warp_sum(s) * inv_d;
   float q = 0.f;
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i)
-    if ((i / CH) * 32 * CH + lane * CH < d) { const float t = v[i] - mean; q += t * t; }
-  const float inv = rsqrtf(warp_sum(q) / d + eps);
+  for (int i = 0; i < NPL; ++i) { const float t = v[i] - mean; q += t * t; }
+  const float inv = rsqrtf(warp_sum(q) * inv_d + eps);
 #pragma unroll
-  for (int i = 0; i < kMaxPerLane; ++i) {
+  for (int i = 0; i < NPL; ++i) {
     const int col = (i / CH) * 32 * CH + lane * CH + i % CH;
-    if (col < d) v[i] = (v[i] - mean) * inv * gamma[col] + (beta ? beta[col] : 0.f);
+    v[i] = (v[i] - mean) * inv * gamma[col] + (beta ? beta[col] : 0.f);
   }
 }
 
 // residual[t] = LN_gamma(E[ids[t]]) (fp32); x[t] = residual[t] rounded to T.
 // Replaces kernels.cu:16-19 + the embeddings.norm and copy passes of runtime.py:93-95.
-template <int CH, typename T>
+template <int NPL, typename T>
 __global__ void __launch_bounds__(kRowWarps * 32) embed_norm_kernel(const int* ids, const float* table,
                                                                     const float* gamma, float eps, int rows, int d,
                                                                     int vocab, float* residual, T* x, int* err) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   int id = ids[row];
@@ -100,17 +103,18 @@ __global__ void __launch_bounds__(kRowWarps * 32) embed_norm_kernel(const int* i
     if (lane == 0) atomicCAS(err, 0, kErrBadIndex);
     id = 0;
   }
-  float v[kMaxPerLane];
-  row_load<CH>(table + (size_t)id * d, d, lane, v);
-  row_layernorm<CH>(v, d, lane, gamma, nullptr, eps);
-  row_store<CH>(residual + (size_t)row * d, d, lane, v);
-  row_store_t<CH>(x + (size_t)row * d, d, lane, v);
+  float v[NPL];
+  row_load<NPL>(table + (size_t)id * d, lane, v);
+  row_layernorm<NPL>(v, lane, gamma, nullptr, eps);
+  row_store<NPL>(residual + (size_t)row * d, lane, v);
+  row_store_t<NPL, T>(x + (size_t)row * d, lane, v);
 }
 
 struct NormArgs {
   float* residual;          // [rows][d] fp32, updated in place
   const float* partials;    // split-K partial sums [splits][rows][d] to add first, or nullptr
   int splits;
+  const float* partial_bias;  // bias [d] of the split GEMM, added with the partials (or nullptr)
   const float* gamma1; const float* beta1; float eps1;
   // Final-norm fusion (encoder.final_norm -> + type_emb[kind] -> head norm1):
   int fused_final;
@@ -120,35 +124,64 @@ struct NormArgs {
   int rows, d;
 };
 
-// Normal:  residual += sum(partials); x = LN1(residual).
-// Fused:   residual = LN1(residual + sum(partials)) + type_emb[kind]; x = LN2(residual).
-// Replaces kernels.cu:20-49 and kernels.cu:155-158 (type_add).
-template <int CH, typename T>
+// Normal:  residual += sum(partials) + bias; x = LN1(residual).
+// Fused:   residual = LN1(residual + sum(partials) + bias) + type_emb[kind]; x = LN2(residual).
+// PARTIALS selects the split-K variant (only used for small classes), keeping the common
+// variant's register footprint small.  Replaces kernels.cu:20-49 and kernels.cu:155-158.
+template <int NPL, typename T, bool PARTIALS>
 __global__ void __launch_bounds__(kRowWarps * 32) norm_kernel(const NormArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= a.rows) return;
-  float* r = a.residual + (size_t)row * a.d;
-  float v[kMaxPerLane];
-  row_load<CH>(r, a.d, lane, v);
-  for (int s = 0; s < a.splits; ++s) {
-    float p[kMaxPerLane];
-    row_load<CH>(a.partials + ((size_t)s * a.rows + row) * a.d, a.d, lane, p);
+  const int d = 32 * NPL;
+  float* r = a.residual + (size_t)row * d;
+  float v[NPL];
+  row_load<NPL>(r, lane, v);
+  if (PARTIALS) {
+    // Partial sums in split order, then the GEMM bias, then the residual: a fixed order, so the
+    // result does not depend on the batch or on scheduling.  Three partial rows in flight per
+    // step: the reduction is latency-bound at the small batches that use it.
+    float acc[NPL];
+    row_load<NPL>(a.partials + (size_t)row * d, lane, acc);
+    for (int s = 1; s < a.splits; s += 3) {
+      float p0[NPL], p1[NPL], p2[NPL];
+      row_load<NPL>(a.partials + ((size_t)s * a.rows + row) * d, lane, p0);
+      if (s + 1 < a.splits) row_load<NPL>(a.partials + ((size_t)(s + 1) * a.rows + row) * d, lane, p1);
+      if (s + 2 < a.splits) row_load<NPL>(a.partials + ((size_t)(s + 2) * a.rows + row) * d, lane, p2);
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) v[i] += p[i];
+      for (int i = 0; i < NPL; ++i) acc[i] += p0[i];
+      if (s + 1 < a.splits) {
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) acc[i] += p1[i];
+      }
+      if (s + 2 < a.splits) {
+#pragma unroll
+        for (int i = 0; i < NPL; ++i) acc[i] += p2[i];
+      }
+    }
+    if (a.partial_bias) {
+      float b[NPL];
+      row_load<NPL>(a.partial_bias, lane, b);
+#pragma unroll
+      for (int i = 0; i < NPL; ++i) acc[i] += b[i];
+    }
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) v[i] += acc[i];
   }
   if (a.fused_final) {
-    row_layernorm<CH>(v, a.d, lane, a.gamma1, a.beta1, a.eps1);
-    float t[kMaxPerLane];
-    row_load<CH>(a.type_emb + (size_t)a.kinds[row] * a.d, a.d, lane, t);
+    row_layernorm<NPL>(v, lane, a.gamma1, a.beta1, a.eps1);
+    float t[NPL];
+    row_load<NPL>(a.type_emb + (size_t)a.kinds[row] * d, lane, t);
 #pragma unroll
-    for (int i = 0; i < kMaxPerLane; ++i) v[i] += t[i];
-    row_store<CH>(r, a.d, lane, v);
-    row_layernorm<CH>(v, a.d, lane, a.gamma2, a.beta2, a.eps2);
+    for (int i = 0; i < NPL; ++i) v[i] += t[i];
+    row_store<NPL>(r, lane, v);
+    row_layernorm<NPL>(v, lane, a.gamma2, a.beta2, a.eps2);
   } else {
-    if (a.splits > 0) row_store<CH>(r, a.d, lane, v);
-    row_layernorm<CH>(v, a.d, lane, a.gamma1, a.beta1, a.eps1);
+    if (PARTIALS) row_store<NPL>(r, lane, v);
+    row_layernorm<NPL>(v, lane, a.gamma1, a.beta1, a.eps1);
   }
-  if (a.x) row_store_t<CH>(reinterpret_cast<T*>(a.x) + (size_t)row * a.d, a.d, lane, v);
+  if (a.x) row_store_t<NPL, T>(reinterpret_cast<T*>(a.x) + (size_t)row * d, lane, v);
 }
 
 // selected[i] = residual[indices[i]] (fp32); scored[i] = attention[indices[i]] (T).
@@ -157,6 +190,8 @@ template <typename T>
 __global__ void __launch_bounds__(256) gather_rows_kernel(const float* residual, const T* attention,
                                                           const int* indices, int count, int d, int rows,
                                                           float* selected, T* scored, int* err) {
+  pdl_trigger();
+  pdl_wait();
   const int i = blockIdx.x;
   if (i >= count) return;
   int src = indices[i];
@@ -179,66 +214,126 @@ struct TailArgs {
   const float* wa2; const float* ba2;    // act_head.2: [n_act][256], [n_act]
   float* logits;           // [b][k+1]
   float* acts;             // [b][n_act]
+  float* hidden;           // [b][256] scratch: act_head.0 outputs
+  int* arrivals;           // [b] zero at launch: CTAs of the question that finished their part
   int k, d, n_act;
 };
 
 constexpr int kTailThreads = 256;
+constexpr int kTailWarps = kTailThreads / 32;
+constexpr int kTailParts = 8;            // CTAs per question, each owning 256/8 hidden units
 constexpr int kActHidden = 256;
 
-// One CTA per question.  Restates laya.py:241-245 and kernels.cu:167-183 (features) in fp32:
-// logits = scored . w3 + b3; features = [CLS row, p1, p1 - p2, H / log(max(c,2)), max(c,2)/255]
-// over the option logits; acts = act_head.2(gelu(act_head.0(features))).
+__device__ __forceinline__ float warp_max(float x) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+  return x;
+}
+
+// Decision-head tail, kTailParts CTAs per question (blockIdx.x = question, blockIdx.y = part).
+// Restates laya.py:241-245 and kernels.cu:167-183 (features) in fp32:
+//   logits   = scored . w3 + b3                       (every part; part 0 stores them)
+//   features = [CLS row, p1, p1 - p2, H / log(max(c,2)), max(c,2)/255] over the option logits
+//   hidden   = gelu(act_head.0(features))             (each part its 32 units, to global scratch)
+//   acts     = act_head.2(hidden)                     (the part that finishes last)
+// Dynamic shared memory: features [d+4], hidden [256], logits [k+1].
 template <typename T>
 __global__ void __launch_bounds__(kTailThreads) head_tail_kernel(const TailArgs a) {
+  pdl_trigger();
+  pdl_wait();
   extern __shared__ float sh[];
-  const int q = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ int s_last;
+  const int q = blockIdx.x, part = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k1 = a.k + 1, d = a.d;
-  float* logit = sh;                 // [k1]
-  float* feat = sh + k1;             // [d + 4]
-  float* hidden = feat + d + 4;      // [256]
+  float* feat = sh;                    // [d + 4]
+  float* hidden = sh + d + 4;          // [256]
+  float* logit = hidden + kActHidden;  // [k1]
   const T* scored = reinterpret_cast<const T*>(a.scored);
-  for (int j = warp; j < k1; j += kTailThreads / 32) {
+  // scorer.3: one warp per gathered row, 8 elements per lane step.
+  for (int j = warp; j < k1; j += kTailWarps) {
     const T* x = scored + ((size_t)q * k1 + j) * d;
     float s = 0.f;
-    for (int c = lane; c < d; c += 32) s += to_f32(x[c]) * a.w3[c];
+    for (int c = lane * 8; c < d; c += 256) {
+      const uint4 v = *reinterpret_cast<const uint4*>(x + c);
+      const float4 w0 = *reinterpret_cast<const float4*>(a.w3 + c);
+      const float4 w1 = *reinterpret_cast<const float4*>(a.w3 + c + 4);
+      const float2 p0 = unpack2_f32(v.x, (T*)nullptr), p1 = unpack2_f32(v.y, (T*)nullptr);
+      const float2 p2 = unpack2_f32(v.z, (T*)nullptr), p3 = unpack2_f32(v.w, (T*)nullptr);
+      s += p0.x * w0.x + p0.y * w0.y + p1.x * w0.z + p1.y * w0.w + p2.x * w1.x + p2.y * w1.y + p3.x * w1.z + p3.y * w1.w;
+    }
     s = warp_sum(s);
-    if (lane == 0) { logit[j] = s + a.b3[0]; a.logits[(size_t)q * k1 + j] = s + a.b3[0]; }
+    if (lane == 0) {
+      logit[j] = s + a.b3[0];
+      if (part == 0) a.logits[(size_t)q * k1 + j] = s + a.b3[0];
+    }
   }
   const float* cls = a.selected + (size_t)q * k1 * d;
   for (int c = threadIdx.x; c < d; c += kTailThreads) feat[c] = cls[c];
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (warp == 0) {
+    // Softmax over the question's options, its entropy and top-2 probabilities, warp-parallel.
     const int count = a.counts[q];
-    float top = -INFINITY, total = 0.f, p1 = 0.f, p2 = 0.f, entropy = 0.f;
-    for (int j = 0; j < count; ++j) top = fmaxf(top, logit[j + 1]);
-    for (int j = 0; j < count; ++j) total += expf(logit[j + 1] - top);
-    for (int j = 0; j < count; ++j) {
+    float top = -INFINITY;
+    for (int j = lane; j < count; j += 32) top = fmaxf(top, logit[j + 1]);
+    top = warp_max(top);
+    float total = 0.f;
+    for (int j = lane; j < count; j += 32) total += expf(logit[j + 1] - top);
+    total = warp_sum(total);
+    float entropy = 0.f, p1 = 0.f, p2 = 0.f;
+    for (int j = lane; j < count; j += 32) {
       const float p = expf(logit[j + 1] - top) / total;
       entropy -= p * logf(fmaxf(p, 1e-9f));
       if (p > p1) { p2 = p1; p1 = p; } else p2 = fmaxf(p2, p);
     }
-    const int c2 = count > 2 ? count : 2;
-    feat[d] = p1;
-    feat[d + 1] = p1 - p2;
-    feat[d + 2] = entropy / logf((float)c2);
-    feat[d + 3] = (float)c2 / 255.f;
+    entropy = warp_sum(entropy);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float o1 = __shfl_xor_sync(0xffffffffu, p1, o), o2 = __shfl_xor_sync(0xffffffffu, p2, o);
+      const float n2 = fmaxf(fminf(p1, o1), fmaxf(p2, o2));
+      p1 = fmaxf(p1, o1);
+      p2 = n2;
+    }
+    if (lane == 0) {
+      const int c2 = count > 2 ? count : 2;
+      feat[d] = p1;
+      feat[d + 1] = p1 - p2;
+      feat[d + 2] = entropy / logf((float)c2);
+      feat[d + 3] = (float)c2 / 255.f;
+    }
   }
   __syncthreads();
-  for (int o = warp; o < kActHidden; o += kTailThreads / 32) {
-    const float* w = a.wa0 + (size_t)o * (d + 4);
+  // act_head.0 + GELU for this part's hidden units: one warp per unit, float4 over d+4.
+  constexpr int kUnits = kActHidden / kTailParts;
+  const int n4 = (d + 4) / 4;
+  const float4* f4 = reinterpret_cast<const float4*>(feat);
+  for (int u = warp; u < kUnits; u += kTailWarps) {
+    const int o = part * kUnits + u;
+    const float4* w = reinterpret_cast<const float4*>(a.wa0 + (size_t)o * (d + 4));
     float s = 0.f;
-    for (int c = lane; c < d + 4; c += 32) s += w[c] * feat[c];
+    for (int c = lane; c < n4; c += 32) {
+      const float4 x = f4[c], y = __ldg(w + c);
+      s += x.x * y.x + x.y * y.y + x.z * y.z + x.w * y.w;
+    }
     s = warp_sum(s);
-    if (lane == 0) hidden[o] = gelu_erf(s + a.ba0[o]);
+    if (lane == 0) a.hidden[(size_t)q * kActHidden + o] = gelu_erf(s + a.ba0[o]);
   }
+  // The part that finishes last computes the action logits from all 256 hidden units.
+  __threadfence();
   __syncthreads();
-  for (int o = warp; o < a.n_act; o += kTailThreads / 32) {
+  if (threadIdx.x == 0) s_last = atomicAdd(&a.arrivals[q], 1) == kTailParts - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  for (int c = threadIdx.x; c < kActHidden; c += kTailThreads) hidden[c] = __ldcg(a.hidden + (size_t)q * kActHidden + c);
+  __syncthreads();
+  for (int o = warp; o < a.n_act; o += kTailWarps) {
     const float* w = a.wa2 + (size_t)o * kActHidden;
     float s = 0.f;
     for (int c = lane; c < kActHidden; c += 32) s += w[c] * hidden[c];
     s = warp_sum(s);
     if (lane == 0) a.acts[(size_t)q * a.n_act + o] = s + a.ba2[o];
   }
+  if (threadIdx.x == 0) a.arrivals[q] = 0;
 }
 
 }  // namespace laya

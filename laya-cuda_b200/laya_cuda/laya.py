@@ -147,11 +147,12 @@ class Laya:
 
     def _encode_all(self, texts):
         texts = [v.replace(self.mask_text, " ") for v in texts]
-        # Batch encoding pays a thread-pool dispatch, which wins from about a dozen texts on;
-        # each text is encoded independently either way, so the ids are identical.
-        if len(texts) >= 12:
-            return [e.ids for e in self.tokenizer.encode_batch(texts, add_special_tokens=False)]
-        return [self.tokenizer.encode(v, add_special_tokens=False).ids for v in texts]
+        # Each text is encoded independently, so one batch call gives the same ids as per-text
+        # calls; the "fast" batch path skips offset tracking, which the contract never reads.
+        fast = getattr(self.tokenizer, "encode_batch_fast", None)
+        if fast is not None:
+            return [e.ids for e in fast(texts, add_special_tokens=False)]
+        return [e.ids for e in self.tokenizer.encode_batch(texts, add_special_tokens=False)]
 
     def prepare(self, state, questions):
         """One (ids, markers, kind) item per question (laya.py:104-135):

@@ -247,3 +247,32 @@ def test_batch_engine_matches_engine(laya_ckpt):
         assert futures[-1].result()["answers"]["same"]["probabilities"] == {"only": 1.0}
     assert max(diffs) <= 2e-3
 
+
+
+def test_programmatic_launch_does_not_change_results(laya_ckpt, tmp_path):
+    """Every kernel waits for its predecessor before reading its outputs, so results with
+    programmatic dependent launch equal those of plain stream order bit for bit."""
+    import subprocess
+    import sys
+    from pathlib import Path
+    path, arch, _ = laya_ckpt
+    root = Path(__file__).resolve().parents[1]
+    script = tmp_path / "run.py"
+    script.write_text(f"""
+import sys, numpy as np
+sys.path.insert(0, {str(root / 'laya-cuda_b200')!r})
+from laya_cuda import Engine, synthetic as S
+rng = np.random.default_rng(8)
+items = [S.build_item(rng, n, k, {arch['vocab']}, kind=j % 3) for j, (n, k) in enumerate([(83, 4), (512, 8), (300, 5)])]
+with Engine({str(path)!r}) as e:
+    outs = [e.runtime.predict(items, capture=c) for c in (True, False)] + [e.runtime.predict(items[:1])]
+np.savez(sys.argv[1], *[a for o in outs for a in o[:2]])
+""")
+    results = []
+    for pdl in ("1", "0"):
+        out = tmp_path / f"pdl{pdl}.npz"
+        env = dict(__import__("os").environ, LAYA_PDL=pdl)
+        subprocess.run([sys.executable, str(script), str(out)], check=True, env=env)
+        results.append(np.load(out))
+    for key in results[0].files:
+        np.testing.assert_array_equal(results[0][key], results[1][key])

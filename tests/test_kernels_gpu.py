@@ -39,12 +39,14 @@ def stream():
 
 def gemm(lib, prec, epi, x, w, out=None, ldo=0, residual=None, ldr=0, bias=None, heads=0, cos=None, sin=None,
          positions=None, splits=1, block_n=0):
+    """cos/sin: transposed RoPE tables [32][rope_rows] (or None)."""
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     M, K = x.shape
     N = w.shape[0]
+    rope_rows = cos.shape[1] if cos is not None else 0
     _lib.check(lib.laya_op_gemm(PRECISIONS[prec][0], epi, ptr(x), ptr(w), M, N, K, ptr(out), ldo, ptr(residual), ldr,
-                                ptr(bias), heads, ptr(cos), ptr(sin), ptr(positions), splits, block_n, ptr(err),
-                                stream()))
+                                ptr(bias), heads, ptr(cos), ptr(sin), rope_rows, ptr(positions), splits, block_n,
+                                ptr(err), stream()))
     torch.cuda.synchronize()
     assert int(err.item()) == 0
 
@@ -127,7 +129,8 @@ def test_gemm_qkv_rope_layout(lib, prec, rope):
     bias = None if rope else torch.from_numpy(rng.normal(0, 0.1, N).astype(np.float32)).cuda()
     out = torch.full((3, heads, M, 64), float("nan"), dtype=PRECISIONS[prec][1], device="cuda")
     gemm(lib, prec, 4, x, w, out, heads=heads,
-         cos=torch.from_numpy(cos).cuda() if rope else None, sin=torch.from_numpy(sin).cuda() if rope else None,
+         cos=torch.from_numpy(cos.T.copy()).cuda() if rope else None,
+         sin=torch.from_numpy(sin.T.copy()).cuda() if rope else None,
          positions=torch.from_numpy(positions).cuda(), bias=bias)
     h = xd @ wd.T
     if bias is not None:
