@@ -106,6 +106,27 @@ class Clocks:
                 "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
 
 
+def rank_workload(rank, requests, vocab):
+    """This rank's sequences: its own seeded request set (weak scaling: per-rank work is fixed)."""
+    from laya_cuda import synthetic as S
+    reqs = S.throughput_requests(1000 + rank, requests, vocab, LENGTHS, QUESTIONS, OPTIONS)
+    return [item for req in reqs for item in req]
+
+
+def job_rate(local_ms, local_sequences, steps, world, device):
+    """Whole-job sequences/s: all ranks' sequences over the slowest rank's device time.
+    Returns (sequences_per_second, max_ms, total_sequences_per_step)."""
+    import torch
+    t = torch.tensor([local_ms], dtype=torch.float64, device=device)
+    n = torch.tensor([local_sequences], dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(n, op=dist.ReduceOp.SUM)
+    ms_max, total = float(t.item()), float(n.item())
+    return total * steps / (ms_max / 1000), ms_max, total
+
+
 def build_micro_batches(items):
     batches = [items[i:i + MICRO] for i in range(0, len(items), MICRO)]
     return batches
@@ -170,11 +191,17 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def latency(engine, arch, rng, lengths, repeats=200, warmup=20):
+def percentiles(values):
+    return {"p50_ms": round(float(np.percentile(values, 50)), 4), "p95_ms": round(float(np.percentile(values, 95)), 4)}
+
+
+def latency(engine, arch, rng, lengths, repeats=200, warmup=20, zipf=None, tag=""):
+    """Batch-1 latency of Engine.predict(text) at the given sequence lengths (one question with
+    4 options): p50/p95 of the API time and of the device time."""
     from laya_cuda import synthetic as S
     out = {}
     for n in lengths:
-        state, questions, _ = S.request_texts(rng, n, 4, arch["vocab"])
+        state, questions, _ = S.request_texts(rng, n, 4, arch["vocab"], zipf=zipf)
         for _ in range(warmup):
             engine.predict(state, questions)
         api, gpu = [], []
@@ -182,12 +209,33 @@ def latency(engine, arch, rng, lengths, repeats=200, warmup=20):
             engine.predict(state, questions)
             api.append(engine.last_metrics["api_ms"])
             gpu.append(engine.last_metrics["gpu_ms"])
-        out[f"{n}tok"] = {"api_p50_ms": round(float(np.percentile(api, 50)), 4),
+        out[f"{tag}{n}tok"] = {"api_p50_ms": round(float(np.percentile(api, 50)), 4),
                           "api_p95_ms": round(float(np.percentile(api, 95)), 4),
                           "gpu_p50_ms": round(float(np.percentile(gpu, 50)), 4),
                           "gpu_p95_ms": round(float(np.percentile(gpu, 95)), 4),
                           "repeats": repeats, "graph_replay": engine.last_metrics["graph_replay"]}
     return out
+
+
+def stream_latency(path, arch, count=200, seed=2):
+    """Configuration 4: a mixed-shape request stream through BatchEngine, one request at a time
+    (per-request API latency, cold shape classes included)."""
+    from laya_cuda import BatchEngine
+    from laya_cuda import synthetic as S
+    rng = np.random.default_rng(seed)
+    requests = [S.stream_request_texts(rng, arch["vocab"]) for _ in range(count)]
+    api, gpu, cold, tokens = [], [], 0, []
+    with BatchEngine(path, max_batch_size=8, max_batch_tokens=8192, max_wait_ms=0) as engine:
+        for state, questions in requests:
+            future = engine.submit(state, questions)
+            future.result(120)
+            m = future.metrics
+            api.append(m["api_ms"])
+            gpu.append(m["gpu_ms"])
+            cold += bool(m.get("graph_capture"))
+            tokens.append(sum(m["tokens_per_question"]))
+    return {"requests": count, "api": percentiles(api), "gpu": percentiles(gpu), "cold_captures": cold,
+            "tokens_per_request_mean": round(float(np.mean(tokens)), 1)}
 
 
 def run_engine(args, rank, world, local_rank):
@@ -212,8 +260,7 @@ def run_engine(args, rank, world, local_rank):
     rt, lib = engine.runtime, engine.runtime._lib
     h = rt._handle
 
-    requests = S.throughput_requests(1000 + rank, args.requests, arch["vocab"], LENGTHS, QUESTIONS, OPTIONS)
-    items = [item for req in requests for item in req]
+    items = rank_workload(rank, args.requests, arch["vocab"])
     batches = build_micro_batches(items)
     tokens = sum(len(i[0]) for i in items)
     packed, shapes, maxes = [], [], [0, 0, 0]
@@ -267,12 +314,7 @@ def run_engine(args, rank, world, local_rank):
     busy = sum(v["ms"] for v in fam.values())
     for v in fam.values():
         v["share"] = round(v["ms"] / busy, 4) if busy else None
-    t_max = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
-    ms_max = float(t_max.item())
-    seqs_all = len(items) * world
-    value = seqs_all / (ms_max / 1000) * args.steps
+    value, ms_max, _ = job_rate(ms, len(items), args.steps, world, "cuda")
 
     # Roofline of the dominant kernel: the FFN-up GEMM (+GeGLU epilogue), algorithmic FLOPs of
     # useful tokens, per launch, over its event-timed average launch duration.
@@ -287,7 +329,7 @@ def run_engine(args, rank, world, local_rank):
     roofline = {"kernel": "gemm_ffn_up_geglu (tcgen05, M=128 N=256 tiles)", "bound": "tensor",
                 "achieved": round(achieved, 1), "peak": tf_sust, "unit": "TFLOP/s",
                 "frac": round(achieved / tf_sust, 4), "peak_kind": f"{peak_kind} bf16 dense sustained (f16 same rate)",
-                "traffic": TRAFFIC_FFN_UP_PER_LAUNCH_BYTES,
+                "traffic": round(TRAFFIC_FFN_UP_BYTES_PER_TOKEN * tokens / len(batches)),
                 "all_encoder_gemms": {"achieved": round(enc_achieved, 1), "frac": round(enc_achieved / tf_sust, 4)}}
 
     line = None
@@ -308,9 +350,21 @@ def run_engine(args, rank, world, local_rank):
         e2e_ms = (time.perf_counter() - t0) * 1000 / e2e_steps
         e2e = {"value": round(len(items) / (e2e_ms / 1000), 2), "unit": "sequences/s", "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(d2h), "api": "Runtime.predict(items) per 64-sequence micro-batch"}
-        lat = None
+        lat, stream = None, None
         if world == 1 and args.latency != "none":
-            lat = latency(engine, arch, np.random.default_rng(0), (83, 512))
+            # Configurations 1/2 (83 and 512 tokens) and 1024 tokens on the `laya` geometry.
+            lat = latency(engine, arch, np.random.default_rng(0), (83, 512, 1024), tag="laya_")
+            if args.latency == "full":
+                # Configuration 3: the multilingual geometry (250k vocabulary), Zipf(1.1) ids.
+                from laya_cuda import Engine as _Engine
+                ml = S.architecture("laya-multilingual")
+                ml_path = S.cached_checkpoint(CACHE, "laya-multilingual", seed=0)
+                with _Engine(ml_path, device=f"cuda:{local_rank}") as ml_engine:
+                    lat.update(latency(ml_engine, ml, np.random.default_rng(3), (81, 1024), zipf=1.1,
+                                       tag="multilingual_zipf_"))
+                # Configuration 4: the typed-decisions geometry (1024 context) through BatchEngine.
+                typed = S.architecture("laya-typed-decisions")
+                stream = stream_latency(S.cached_checkpoint(CACHE, "laya-typed-decisions", seed=0), typed)
         cpu = None
         if world == 1 and args.cpu_budget > 0:
             weights = S.make_weights(arch, seed=0)
@@ -327,7 +381,7 @@ def run_engine(args, rank, world, local_rank):
                            "sequences_per_rank": len(items), "tokens_per_rank": tokens, "micro_batches": len(batches),
                            "parallelism": f"replicas{world}", "l2": "inputs larger than L2 (no flush)"},
                 "gpu_launches": launches, "kernels": fam, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-                "clocks": clocks.summary(), "latency_batch1": lat,
+                "clocks": clocks.summary(), "latency_batch1": lat, "stream_config4": stream,
                 "attention_flops_per_step": attention_flops([len(i[0]) for i in items], arch)}
     engine.close()
     if world > 1:
@@ -337,9 +391,10 @@ def run_engine(args, rank, world, local_rank):
         print(json.dumps(line), flush=True)
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one FFN-up GEMM launch (ncu capture summarised
-# in profiles/gemm_ffn_up_geglu_config5.md); None until a capture exists.
-TRAFFIC_FFN_UP_PER_LAUNCH_BYTES = None
+# dram__bytes_read.sum + dram__bytes_write.sum of one FFN-up GEMM launch per token (ncu capture
+# of a 28,617-token launch, summarised in profiles/gemm_ffn_up_geglu_config5.md: 179.8 MB);
+# traffic grows in proportion to the rows, so a full launch is this times its tokens.
+TRAFFIC_FFN_UP_BYTES_PER_TOKEN = 179.8e6 / 28617
 
 
 def main():
@@ -348,7 +403,8 @@ def main():
     parser.add_argument("--steps", type=int, default=3)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["laya_b200", "reference"], default="laya_b200")
-    parser.add_argument("--latency", choices=["none", "basic"], default="basic")
+    parser.add_argument("--latency", choices=["none", "basic", "full"], default="full",
+                        help="basic: configurations 1/2 (+1024 tokens); full: also 3 (multilingual) and 4 (stream)")
     parser.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of oracle time for cpu_baseline")
     parser.add_argument("--requests", type=int, default=REQUESTS,
                         help="requests per rank (4096 = configuration 5; smaller only for profiler captures)")

@@ -162,16 +162,19 @@ int laya_op_gemm(int precision, int epi, const void* x, const void* w, int M, in
 /* Reorders Wi [2F][K] (gate rows then up rows) into 64-row blocks [gate_i, up_i] (host memory). */
 int laya_interleave_geglu(const uint16_t* src, uint16_t* dst, int F, int K);
 
-/* Packed attention (kernels.cu:90-154).  qkv [3][heads][M][64], out [M][heads*64], tiles from
- * laya_attention_tiles. */
-int laya_op_attention(int precision, const void* qkv, void* out, const int32_t* tiles, int n_tiles,
+/* Packed attention (kernels.cu:90-154).  qkv: q, k [heads][M][64] each, then v transposed
+ * [heads][64][M] (the layout the QKV GEMM epilogue writes); out [M][heads*64].  impl 0: mma.sync
+ * kernel over 64-query tiles (split_p: probabilities as high + low 16-bit parts); impl 1: the
+ * tcgen05/TMEM kernel the forward pass uses, over 128-query tiles.  Tiles from
+ * laya_attention_tiles with the matching tile size; err: device error word (impl 1). */
+int laya_op_attention(int precision, int impl, const void* qkv, void* out, const int32_t* tiles, int n_tiles,
                       const int32_t* starts, const int32_t* lengths, int M, int heads, int window, int split_p,
-                      void* stream);
+                      int* err, void* stream);
 
-/* Builds the attention tile table for rows packed at `starts` with `lengths` into M tokens.
- * Returns the number of tiles written (<= capacity) or -1. */
-int laya_attention_tiles(const int32_t* starts, const int32_t* lengths, int n_rows, int M, int32_t* tiles,
-                         int capacity);
+/* Builds the attention tile table (tile_q = 64 or 128) for rows packed at `starts` with
+ * `lengths` into M tokens.  Returns the number of tiles written (<= capacity) or -1. */
+int laya_attention_tiles(const int32_t* starts, const int32_t* lengths, int n_rows, int M, int tile_q,
+                         int32_t* tiles, int capacity);
 
 /* residual = LN(E[ids]); x = residual (16-bit).  (kernels.cu:16-19 + runtime.py:93-95) */
 int laya_op_embed_norm(int precision, const int32_t* ids, const float* table, const float* gamma, float eps, int rows,

@@ -7,12 +7,16 @@
 //   * scores are scaled by 1/8 (64-wide heads), softmax in fp32;
 //   * padding queries (and every token past the last row) produce exact zeros.
 //
+// This file holds the mma.sync variant (kernel-level tests; 64-query tiles).  The forward pass
+// uses the tcgen05 variant in tc_attention.cuh.
+//
 // Work unit: one CTA per (64-query tile of one row, head).  The host builds the tile table
 // while packing the inputs, so a tile never straddles two rows and a CTA stages one K/V block
-// per step that all four of its warps share.  Q/K/V come from the QKV GEMM epilogue in
-// head-major layout [3][heads][M][64]; the output is token-major [M][heads*64] (the next GEMM's
-// A operand).  Tensor-core math is mma.sync m16n8k16 with fp32 accumulation; K/V blocks are
-// double-buffered in XOR-swizzled shared memory with cp.async, fragments via ldmatrix.
+// per step that all four of its warps share.  Q and K come from the QKV GEMM epilogue in
+// head-major layout [heads][M][64], V transposed [heads][64][M]; the output is token-major
+// [M][heads*64] (the next GEMM's A operand).  Tensor-core math is mma.sync m16n8k16 with fp32
+// accumulation; K/V blocks are double-buffered in XOR-swizzled shared memory with cp.async,
+// fragments via ldmatrix.
 #pragma once
 #include "common.cuh"
 
@@ -23,7 +27,7 @@ constexpr int kAttnKB = 64;       // keys per block
 constexpr int kAttnThreads = 128;
 
 struct AttnArgs {
-  const void* qkv;      // [3][heads][M][64]
+  const void* qkv;      // q, k: [heads][M][64] each; then v transposed: [heads][64][M]
   void* out;            // [M][heads*64]
   const int4* tiles;    // (t0, t1, row, 0); row -1: zero-fill [t0,t1); row -2: unused slot
   const int* starts;
@@ -43,11 +47,6 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(addr));
 }
@@ -103,7 +102,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
   const size_t plane = (size_t)a.heads * a.M * 64;
   const T* Q = reinterpret_cast<const T*>(a.qkv) + ((size_t)head * a.M + first) * 64;
   const T* K = Q + plane;
-  const T* V = Q + 2 * plane;
+  const T* Vt = reinterpret_cast<const T*>(a.qkv) + 2 * plane + (size_t)head * 64 * a.M + first;
 
   int k_lo = 0, k_hi = valid;
   if (a.window >= 0) {
@@ -128,7 +127,9 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
       const bool ok = kb + r < valid;
       const size_t off = (size_t)(ok ? kb + r : 0) * 64 + c * 8;
       cp_async16(kbase + swz(r, c), K + off, ok);
-      cp_async16(vbase + swz(r, c), V + off, ok);
+      // V^T tile: row r = dimension, chunk c = keys kb+8c .. kb+8c+7.
+      const bool vok = kb + 8 * c < valid;
+      cp_async16(vbase + swz(r, c), Vt + (size_t)r * a.M + (vok ? kb + 8 * c : 0), vok);
     }
   };
   if (n_blocks > 0) load_kv(0, 0);
@@ -235,10 +236,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
         if (kSplitP) { pb[0] = pl[0]; pb[1] = pl[1]; pb[2] = pl[2]; pb[3] = pl[3]; }
 #pragma unroll
         for (int np = 0; np < 4; ++np) {
-          const int key = j * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
-          const int ch = np * 2 + (lane >> 4);
+          const int dim = np * 16 + (lane & 7) + ((lane >> 4) << 3);
+          const int kch = j * 2 + ((lane >> 3) & 1);
           uint32_t b0, b1, b2, b3;
-          ldsm_x4_t(vbase + swz(key, ch), b0, b1, b2, b3);
+          ldsm_x4(vbase + swz(dim, kch), b0, b1, b2, b3);
           mma16816<T>(o[2 * np], pa, b0, b1);
           mma16816<T>(o[2 * np + 1], pa, b2, b3);
           if (kSplitP) {

@@ -21,6 +21,7 @@ enum DeviceError : int {
   kErrGemmMmaWait = 2,
   kErrGemmEpilogueWait = 3,
   kErrBadIndex = 4,
+  kErrAttnWait = 5,
 };
 
 __device__ __forceinline__ unsigned long long global_ns() {
@@ -136,6 +137,12 @@ __device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uin
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// Makes this thread's generic-proxy shared-memory writes visible to the async proxy (tcgen05.mma
+// operands written with st.shared).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 // Arrives on `bar` once all previously issued tcgen05.mma of this thread have completed.

@@ -28,7 +28,7 @@ enum EpiKind : int {
   EPI_RELU = 1,     // out = relu(acc + bias)
   EPI_GELU = 2,     // out = gelu(acc + bias)
   EPI_GEGLU = 3,    // W rows interleaved in 64-row blocks [gate_i, up_i]: out = gelu(gate) * up
-  EPI_QKV = 4,      // (+bias) RoPE on q/k, scatter into [3][heads][M][64]
+  EPI_QKV = 4,      // (+bias) RoPE on q/k; q, k -> [heads][M][64], v -> transposed [heads][64][M]
   EPI_RESIDUAL = 5, // residual(fp32) += acc + bias
   EPI_PARTIAL = 6,  // partial[split](fp32) = acc          (split-K)
 };
@@ -314,13 +314,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 x[i + 32] = b * c0 + a * s0;
               }
             }
-            T* out = reinterpret_cast<T*>(args.out) + (((size_t)part * args.heads + head) * args.M + row) * 64;
+            if (part < 2) {
+              T* out = reinterpret_cast<T*>(args.out) + (((size_t)part * args.heads + head) * args.M + row) * 64;
 #pragma unroll
-            for (int i = 0; i < 64; i += 8) {
-              uint4 w;
-              w.x = pack2<T>(x[i + 0], x[i + 1]); w.y = pack2<T>(x[i + 2], x[i + 3]);
-              w.z = pack2<T>(x[i + 4], x[i + 5]); w.w = pack2<T>(x[i + 6], x[i + 7]);
-              *reinterpret_cast<uint4*>(out + i) = w;
+              for (int i = 0; i < 64; i += 8) {
+                uint4 w;
+                w.x = pack2<T>(x[i + 0], x[i + 1]); w.y = pack2<T>(x[i + 2], x[i + 3]);
+                w.z = pack2<T>(x[i + 4], x[i + 5]); w.w = pack2<T>(x[i + 6], x[i + 7]);
+                *reinterpret_cast<uint4*>(out + i) = w;
+              }
+            } else {
+              // V transposed, [heads][64][M]: the attention's P.V product reads it K-major
+              // (keys contiguous).  The warp's lanes are consecutive rows, so each dimension's
+              // 32 stores fill one contiguous 64-byte run.
+              T* vt = reinterpret_cast<T*>(args.out) + ((size_t)2 * args.heads + head) * args.M * 64 + row;
+#pragma unroll
+              for (int i = 0; i < 64; ++i) vt[(size_t)i * args.M] = from_f32<T>(x[i]);
             }
           }
         }

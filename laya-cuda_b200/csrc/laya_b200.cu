@@ -30,6 +30,7 @@
 #include "attention.cuh"
 #include "gemm.cuh"
 #include "rowops.cuh"
+#include "tc_attention.cuh"
 
 using namespace laya;
 
@@ -215,6 +216,19 @@ int pick_splits(int M, int N, int K, int bn, int sms) {
 }
 
 template <typename T>
+void launch_tc_attention(const CUtensorMap& qk, const CUtensorMap& vt, const TcAttnArgs& a, int n_tiles,
+                         cudaStream_t st) {
+  static uint64_t configured = 0;  // one bit per device
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  if (!(configured & (1ull << dev))) {
+    CK(cudaFuncSetAttribute(tc_attention_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcAttnSmem::kBytes));
+    configured |= 1ull << dev;
+  }
+  launch_k(tc_attention_kernel<T>, dim3(n_tiles, a.heads), dim3(kTcThreads), TcAttnSmem::kBytes, st, qk, vt, a);
+}
+
+template <typename T>
 void launch_attention(const AttnArgs& a, int n_tiles, bool split_p, cudaStream_t st) {
   dim3 grid(n_tiles, a.heads);
   if (split_p) launch_k(attention_kernel<T, true>, grid, dim3(kAttnThreads), 0, st, a);
@@ -280,10 +294,12 @@ void shape_class(const int32_t* lengths, const int32_t* marker_counts, int n, in
   options = pow2(std::max(kmax, 1), 8);
 }
 
-int tiles_capacity(int rows, int batch) { return (rows + 48 * batch + 63) / 64 + 1; }
+// Attention tiles of `tile_q` queries: a row of span S gives ceil(S / tile_q) tiles, the tokens
+// past the last row ceil(rest / tile_q) zero-fill tiles.
+int tiles_capacity(int rows, int batch, int tile_q) { return (rows + (tile_q - 16) * batch + tile_q - 1) / tile_q + 1; }
 
 struct PackLayout {
-  int64_t ids, positions, rows_, kinds, starts, lengths, counts, indices, tiles, total;
+  int64_t ids, positions, rows_, kinds, starts, lengths, counts, indices, tiles64, tiles128, total;
 };
 PackLayout pack_layout(int m, int b, int k) {
   PackLayout p;
@@ -296,13 +312,15 @@ PackLayout pack_layout(int m, int b, int k) {
   p.lengths = o; o += b;
   p.counts = o; o += b;
   p.indices = o; o += (int64_t)b * (k + 1);
-  o = (o + 3) / 4 * 4;  // int4 alignment of the tile table
-  p.tiles = o; o += 4LL * tiles_capacity(m, b);
+  o = (o + 3) / 4 * 4;  // int4 alignment of the tile tables
+  p.tiles64 = o; o += 4LL * tiles_capacity(m, b, kAttnQ);    // mma.sync attention
+  p.tiles128 = o; o += 4LL * tiles_capacity(m, b, kTcQ);     // tcgen05 attention
   p.total = o;
   return p;
 }
 
-int build_tiles(const int32_t* starts, const int32_t* lengths, int n_rows, int M, int32_t* tiles, int capacity) {
+int build_tiles(const int32_t* starts, const int32_t* lengths, int n_rows, int M, int tile_q, int32_t* tiles,
+                int capacity) {
   int t = 0, end = 0;
   auto put = [&](int a, int b, int r) {
     if (t >= capacity) return false;
@@ -312,12 +330,12 @@ int build_tiles(const int32_t* starts, const int32_t* lengths, int n_rows, int M
   };
   for (int r = 0; r < n_rows; ++r) {
     const int s = starts[r], sp = span16(lengths[r]);
-    for (int q = 0; q < sp; q += kAttnQ)
-      if (!put(s + q, std::min(s + q + kAttnQ, s + sp), r)) return -1;
+    for (int q = 0; q < sp; q += tile_q)
+      if (!put(s + q, std::min(s + q + tile_q, s + sp), r)) return -1;
     end = std::max(end, s + sp);
   }
-  for (int q = end; q < M; q += kAttnQ)
-    if (!put(q, std::min(q + kAttnQ, M), -1)) return -1;
+  for (int q = end; q < M; q += tile_q)
+    if (!put(q, std::min(q + tile_q, M), -1)) return -1;
   const int used = t;
   while (t < capacity) put(0, 0, -2);
   return used;
@@ -359,7 +377,8 @@ void pack(const int32_t* tokens, const int32_t* lengths, const int32_t* markers,
     mk += cnt;
     offset = end;
   }
-  if (build_tiles(out + L.starts, out + L.lengths, n, m, out + L.tiles, tiles_capacity(m, b)) < 0)
+  if (build_tiles(out + L.starts, out + L.lengths, n, m, kAttnQ, out + L.tiles64, tiles_capacity(m, b, kAttnQ)) < 0 ||
+      build_tiles(out + L.starts, out + L.lengths, n, m, kTcQ, out + L.tiles128, tiles_capacity(m, b, kTcQ)) < 0)
     fail(LAYA_ERR_INVALID, "attention tile table overflow");
 }
 
@@ -374,7 +393,7 @@ struct Tensor {
 };
 
 struct ClassLayout {
-  int m = 0, b = 0, k = 0, count = 0, tiles_cap = 0;
+  int m = 0, b = 0, k = 0, count = 0, tiles64 = 0, tiles128 = 0;
   PackLayout pack{};
   size_t packed, residual, x, qkv, attn, ff, sel, selx, scored, ffsel, partials, hidden, out, total;
   bool has_partials = false;
@@ -387,7 +406,7 @@ struct Slot {
   cudaGraphExec_t graph = nullptr;
   bool maps_ready = false;
   size_t maps_ws = 0;  // workspace generation the maps point into
-  CUtensorMap map_x, map_attn, map_ff, map_selx, map_scored, map_ffsel;
+  CUtensorMap map_x, map_attn, map_ff, map_selx, map_scored, map_ffsel, map_qk, map_vt;
   int launches = 0;
 };
 
@@ -432,6 +451,9 @@ struct Engine {
   std::map<std::tuple<const void*, int>, CUtensorMap> wmaps;
   std::string error;
   bool profiling = false;
+  // Attention kernel of the forward pass: mma.sync (default) or the tcgen05/TMEM kernel
+  // (LAYA_ATTENTION=tcgen05 in the environment at engine creation).
+  bool tc_attention = false;
   std::vector<ProfEvent> prof_pending;
   std::vector<cudaEvent_t> prof_pool;
   double prof_ms[kFamilies] = {};
@@ -576,7 +598,8 @@ ClassLayout make_layout(const Engine& e, int m, int b, int k) {
   ClassLayout L;
   L.m = m; L.b = b; L.k = k;
   L.count = b * (k + 1);
-  L.tiles_cap = tiles_capacity(m, b);
+  L.tiles64 = tiles_capacity(m, b, kAttnQ);
+  L.tiles128 = tiles_capacity(m, b, kTcQ);
   L.pack = pack_layout(m, b, k);
   const size_t d = e.d(), es = 2, A = 256;
   size_t o = 0;
@@ -660,6 +683,11 @@ void prepare_maps(Engine& e, Slot& s) {
   s.map_selx = make_map(e.ws + L.selx, L.count, d, kBM, bf);
   s.map_scored = make_map(e.ws + L.scored, L.count, d, kBM, bf);
   s.map_ffsel = make_map(e.ws + L.ffsel, L.count, 4 * d, kBM, bf);
+  // Attention: Q/K rows of the qkv buffer ([3*heads*m][64], 128-row boxes) and V^T
+  // ([heads*64][m], 64x64 boxes), both 128-byte swizzled.
+  const int64_t hm = (int64_t)e.cfg.heads * L.m;
+  s.map_qk = make_map(e.ws + L.qkv, 3 * hm, 64, kTcQ, bf);
+  s.map_vt = make_map(e.ws + L.qkv + (size_t)2 * hm * 64 * 2, (int64_t)e.cfg.heads * 64, L.m, 64, bf);
   s.maps_ready = true;
   s.maps_ws = e.ws_generation;
 }
@@ -753,7 +781,8 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
   const int* lengths = in + L.pack.lengths;
   const int* counts = in + L.pack.counts;
   const int* indices = in + L.pack.indices;
-  const int4* tiles = reinterpret_cast<const int4*>(in + L.pack.tiles);
+  const int4* tiles64 = reinterpret_cast<const int4*>(in + L.pack.tiles64);
+  const int4* tiles128 = reinterpret_cast<const int4*>(in + L.pack.tiles128);
   float* residual = reinterpret_cast<float*>(ws + L.residual);
   T* x = reinterpret_cast<T*>(ws + L.x);
   T* qkv = reinterpret_cast<T*>(ws + L.qkv);
@@ -779,10 +808,17 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
   (void)rowbytes;
 
   auto attention = [&](int window) {
-    AttnArgs a{};
-    a.qkv = qkv; a.out = attn; a.tiles = tiles; a.starts = starts; a.lengths = lengths;
-    a.M = m; a.heads = c.heads; a.window = window;
-    launch(e, prof, FAM_ATTENTION, 0, [&] { launch_attention<T>(a, L.tiles_cap, false, e.stream); });
+    if (e.tc_attention) {
+      TcAttnArgs a{};
+      a.out = attn; a.tiles = tiles128; a.starts = starts; a.lengths = lengths;
+      a.M = m; a.heads = c.heads; a.window = window; a.err = err;
+      launch(e, prof, FAM_ATTENTION, 0, [&] { launch_tc_attention<T>(s.map_qk, s.map_vt, a, L.tiles128, e.stream); });
+    } else {
+      AttnArgs a{};
+      a.qkv = qkv; a.out = attn; a.tiles = tiles64; a.starts = starts; a.lengths = lengths;
+      a.M = m; a.heads = c.heads; a.window = window;
+      launch(e, prof, FAM_ATTENTION, 0, [&] { launch_attention<T>(a, L.tiles64, false, e.stream); });
+    }
   };
   // A residual GEMM whose sum the next norm must still add: split count and the GEMM bias.
   struct Pending { int splits = 0; const float* bias = nullptr; };
@@ -1001,6 +1037,10 @@ int laya_create(const laya_config* cfg, int device, int max_cached_shapes, laya_
   e.device = device;
   e.limit = max_cached_shapes;
   e.sms = sm_count(device);
+  {
+    const char* v = getenv("LAYA_ATTENTION");
+    e.tc_attention = v && std::string(v) == "tcgen05";
+  }
   build_expected(e);
   CK(cudaStreamCreateWithFlags(&e.stream, cudaStreamNonBlocking));
   CK(cudaEventCreate(&e.ev_start));
@@ -1336,13 +1376,29 @@ int laya_interleave_geglu(const uint16_t* src, uint16_t* dst, int F, int K) {
   API_END(nullptr)
 }
 
-int laya_attention_tiles(const int32_t* starts, const int32_t* lengths, int n_rows, int M, int32_t* tiles, int capacity) {
-  return build_tiles(starts, lengths, n_rows, M, tiles, capacity);
+int laya_attention_tiles(const int32_t* starts, const int32_t* lengths, int n_rows, int M, int tile_q, int32_t* tiles,
+                         int capacity) {
+  if (tile_q != kAttnQ && tile_q != kTcQ) return -1;
+  return build_tiles(starts, lengths, n_rows, M, tile_q, tiles, capacity);
 }
 
-int laya_op_attention(int precision, const void* qkv, void* out, const int32_t* tiles, int n_tiles, const int32_t* starts,
-                      const int32_t* lengths, int M, int heads, int window, int split_p, void* stream) {
+int laya_op_attention(int precision, int impl, const void* qkv, void* out, const int32_t* tiles, int n_tiles,
+                      const int32_t* starts, const int32_t* lengths, int M, int heads, int window, int split_p, int* err,
+                      void* stream) {
   API_BEGIN
+  if (impl == 1) {
+    const bool bf = precision == LAYA_PRECISION_BF16;
+    const int64_t hm = (int64_t)heads * M;
+    const CUtensorMap qk = make_map(qkv, 3 * hm, 64, kTcQ, bf);
+    const CUtensorMap vt = make_map(static_cast<const uint8_t*>(qkv) + (size_t)2 * hm * 64 * 2, (int64_t)heads * 64, M, 64, bf);
+    TcAttnArgs t{};
+    t.out = out; t.tiles = reinterpret_cast<const int4*>(tiles); t.starts = starts; t.lengths = lengths;
+    t.M = M; t.heads = heads; t.window = window; t.err = err;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (bf) launch_tc_attention<__nv_bfloat16>(qk, vt, t, n_tiles, st);
+    else launch_tc_attention<__half>(qk, vt, t, n_tiles, st);
+    return LAYA_OK;
+  }
   AttnArgs a{};
   a.qkv = qkv; a.out = out; a.tiles = reinterpret_cast<const int4*>(tiles); a.starts = starts; a.lengths = lengths;
   a.M = M; a.heads = heads; a.window = window;

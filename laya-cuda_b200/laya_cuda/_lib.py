@@ -71,8 +71,8 @@ def load():
         "laya_last_error": (ct.c_char_p, [p]),
         "laya_op_gemm": (i, [i, i, p, p, i, i, i, p, i, p, i, p, i, p, p, i, p, i, i, p, p]),
         "laya_interleave_geglu": (i, [p, p, i, i]),
-        "laya_op_attention": (i, [i, p, p, p, i, p, p, i, i, i, i, p]),
-        "laya_attention_tiles": (i, [p, p, i, i, p, i]),
+        "laya_op_attention": (i, [i, i, p, p, p, i, p, p, i, i, i, i, p, p]),
+        "laya_attention_tiles": (i, [p, p, i, i, i, p, i]),
         "laya_op_embed_norm": (i, [i, p, p, p, ct.c_float, i, i, i, p, p, p, p]),
         "laya_op_norm": (i, [i, p, p, i, p, p, ct.c_float, p, i, i, p]),
         "laya_op_gemm_residual_static": (i, [i, p, p, i, i, i, i, p, p, p, p]),

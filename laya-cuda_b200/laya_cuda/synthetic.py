@@ -203,3 +203,22 @@ def throughput_requests(seed, count, vocab, lengths=(256, 1024), questions=3, op
         length = int(rng.integers(lengths[0], lengths[1] + 1))
         out.append([build_item(rng, length, options, vocab, kind=q % 3) for q in range(questions)])
     return out
+
+
+def stream_request_texts(rng, vocab, lengths=(40, 900), questions=(1, 5), options=(4, 77)):
+    """One request of the mixed-shape stream as texts for Engine/BatchEngine: a state of
+    U[lengths] words and U[questions] choice questions with U[options] labels of 1-3 words.
+    The adapter's budgets and max_len truncation apply exactly as for real text."""
+    state = " ".join(word(int(t)) for t in rng.integers(FIRST_WORD, vocab, int(rng.integers(lengths[0], lengths[1] + 1))))
+    qs = {}
+    for q in range(int(rng.integers(questions[0], questions[1] + 1))):
+        k = int(rng.integers(options[0], options[1] + 1))
+        labels = []
+        while len(labels) < k:
+            label = " ".join(word(int(t)) for t in rng.integers(FIRST_WORD, vocab, int(rng.integers(1, 4))))
+            if label not in labels:
+                labels.append(label)
+        instruction = " ".join(word(int(t)) for t in rng.integers(FIRST_WORD, vocab, 6))
+        qs[f"q{q}"] = {"type": "choice", "instructions": instruction, "criteria": labels}
+    return state, qs
+

@@ -135,7 +135,7 @@ def test_gemm_qkv_rope_layout(lib, prec, rope):
     h = xd @ wd.T
     if bias is not None:
         h = h + bias.double().cpu().numpy()
-    h = h.reshape(M, 3, heads, 64).transpose(1, 2, 0, 3).copy()
+    h = h.reshape(M, 3, heads, 64).transpose(1, 2, 0, 3).copy()       # [3][heads][M][64]
     if rope:
         c = np.concatenate([cos, cos], -1)[positions].astype(np.float64)
         s = np.concatenate([sin, sin], -1)[positions].astype(np.float64)
@@ -144,6 +144,8 @@ def test_gemm_qkv_rope_layout(lib, prec, rope):
             rot = np.concatenate([-o[..., 32:], o[..., :32]], -1)
             h[part] = o * c + rot * s
     got = out.double().cpu().numpy()
+    # v is stored transposed: the buffer's third plane is [heads][64][M].
+    got[2] = got[2].reshape(heads, 64, M).transpose(0, 2, 1)
     assert np.max(np.abs(got - h) - ROUND[prec] * np.abs(h)) < 2e-3
 
 
@@ -171,26 +173,34 @@ def packed_case(lengths):
     return starts, np.asarray(lengths, np.int32), M
 
 
-@pytest.mark.parametrize("prec,split_p", [("bf16", 0), ("bf16", 1), ("f16", 1)])
+@pytest.mark.parametrize("prec,impl,split_p", [("bf16", 0, 0), ("bf16", 0, 1), ("f16", 0, 1), ("f16", 1, 0),
+                                               ("bf16", 1, 0)])
 @pytest.mark.parametrize("lengths,window", [([32], -1), ([7, 96], 64), ([128, 1], -1), ([250, 131], 64),
                                             ([256, 219, 145], -1), ([500], 64), ([1024, 333], -1)])
-def test_packed_attention_matches_oracle(lib, prec, split_p, lengths, window):
-    """Cases and float64 oracle of tests/test_attention.py:12-56 (h=2, seeded by M)."""
+def test_packed_attention_matches_oracle(lib, prec, impl, split_p, lengths, window):
+    """Cases and float64 oracle of tests/test_attention.py:12-56 (h=2, seeded by M), for the
+    mma.sync kernel (impl 0, 64-query tiles) and the tcgen05 kernel (impl 1, 128-query tiles)."""
     h = 2
+    tile_q = 64 if impl == 0 else 128
     starts, lens, M = packed_case(lengths)
-    cap = (M + 48 * len(lengths) + 63) // 64 + 1
+    cap = (M + (tile_q - 16) * len(lengths) + tile_q - 1) // tile_q + 1
     tiles = np.zeros((cap, 4), np.int32)
-    n_tiles = lib.laya_attention_tiles(starts.ctypes.data, lens.ctypes.data, len(lengths), M, tiles.ctypes.data, cap)
+    n_tiles = lib.laya_attention_tiles(starts.ctypes.data, lens.ctypes.data, len(lengths), M, tile_q,
+                                       tiles.ctypes.data, cap)
     assert n_tiles > 0
     x = np.random.default_rng(M).normal(0, 1, (M, 3, h, 64)).astype(np.float32)
     xt = torch.from_numpy(x).to(PRECISIONS[prec][1])
     xd = xt.double().numpy()
-    layout = xt.permute(1, 2, 0, 3).contiguous().cuda()          # [3][h][M][64]
+    layout = xt.permute(1, 2, 0, 3).contiguous()                  # [3][h][M][64]
+    layout[2] = layout[2].transpose(1, 2).reshape(h, M, 64)       # v stored transposed: [h][64][M]
+    layout = layout.cuda()
     out = torch.full((M, h * 64), float("nan"), dtype=PRECISIONS[prec][1], device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
     dev = [torch.from_numpy(v).cuda() for v in (tiles, starts, lens)]
-    _lib.check(lib.laya_op_attention(PRECISIONS[prec][0], ptr(layout), ptr(out), ptr(dev[0]), cap, ptr(dev[1]),
-                                     ptr(dev[2]), M, h, window, split_p, stream()))
+    _lib.check(lib.laya_op_attention(PRECISIONS[prec][0], impl, ptr(layout), ptr(out), ptr(dev[0]), cap, ptr(dev[1]),
+                                     ptr(dev[2]), M, h, window, split_p, ptr(err), stream()))
     torch.cuda.synchronize()
+    assert int(err.item()) == 0
     got = out.double().cpu().numpy()
     real = np.zeros(M, bool)
     worst = 0.0
@@ -203,10 +213,10 @@ def test_packed_attention_matches_oracle(lib, prec, split_p, lengths, window):
         p = np.exp(s - s.max(-1, keepdims=True))
         p /= p.sum(-1, keepdims=True)
         expected = (p @ v).transpose(1, 0, 2).reshape(n, h * 64)
-        err = np.abs(got[start:start + n] - expected) - ROUND[prec] * np.abs(expected)
-        worst = max(worst, float(err.max()))
+        err_ = np.abs(got[start:start + n] - expected) - ROUND[prec] * np.abs(expected)
+        worst = max(worst, float(err_.max()))
     # 16-bit output rounding plus probability rounding (split_p keeps fp32-level probabilities).
-    limit = {("bf16", 0): 6e-3, ("bf16", 1): 1.5e-3, ("f16", 1): 6e-4}[(prec, split_p)]
+    limit = {("bf16", 0): 6e-3, ("bf16", 1): 1.5e-3, ("f16", 1): 6e-4, ("f16", 0): 1.5e-3}[(prec, split_p)]
     assert worst < limit, worst
     np.testing.assert_array_equal(got[~real], 0)
 

@@ -94,22 +94,27 @@ def test_pack_matches_reference_fill(lib, seed):
     for field, size in zip(want, (m, m, m, m, b, b, b, b * (k + 1))):
         np.testing.assert_array_equal(out[o:o + size], field)
         o += size
-    # Attention tiles: every token of every row span is covered exactly once by a tile of its
-    # row; tokens past the last row by zero-fill tiles; no tile straddles rows.
+    # Attention tile tables (64 then 128 queries): every token of every row span is covered
+    # exactly once by a tile of its row; tokens past the last row by zero-fill tiles; no tile
+    # straddles rows.
     o = (o + 3) // 4 * 4
-    tiles = out[o:].reshape(-1, 4)
-    cover = np.zeros(m, np.int32)
-    for t0, t1, row, _ in tiles:
-        if row == -2:
-            continue
-        assert 0 <= t0 < t1 <= m and t1 - t0 <= 64
-        cover[t0:t1] += 1
-        if row >= 0:
-            s, n = want[4][row], want[5][row]
-            assert s <= t0 and t1 <= s + span(n) and (t0 - s) % 64 == 0
-        else:
-            assert np.all(want[2][t0:t1] == -1)
-    np.testing.assert_array_equal(cover, 1)
+    for tile_q in (64, 128):
+        cap = (m + (tile_q - 16) * b + tile_q - 1) // tile_q + 1
+        tiles = out[o:o + 4 * cap].reshape(-1, 4)
+        o += 4 * cap
+        cover = np.zeros(m, np.int32)
+        for t0, t1, row, _ in tiles:
+            if row == -2:
+                continue
+            assert 0 <= t0 < t1 <= m and t1 - t0 <= tile_q
+            cover[t0:t1] += 1
+            if row >= 0:
+                s, n = want[4][row], want[5][row]
+                assert s <= t0 and t1 <= s + span(n) and (t0 - s) % tile_q == 0
+            else:
+                assert np.all(want[2][t0:t1] == -1)
+        np.testing.assert_array_equal(cover, 1)
+    assert o == len(out)
 
 
 def test_shape_class_matches_reference(lib):
