@@ -166,13 +166,26 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
     if (a.window >= 0) need = need && (kb <= wq + 15 + a.window) && (kb + kAttnKB - 1 >= wq - a.window);
     if (need) {
       const uint32_t kbase = smem_u32(sK[buf]), vbase = smem_u32(sV[buf]);
+      // 16-key groups [g_lo, g_hi] of this block that any of the warp's 16 queries can see;
+      // the others are skipped in both products.  A block with every key visible to every
+      // query of the warp ("interior") needs no per-element mask.
+      int g_lo = 0, hi_key = valid - 1 - kb;
+      if (a.window >= 0) {
+        const int lo_key = wq - a.window - kb;
+        hi_key = min(hi_key, wq + 15 + a.window - kb);
+        g_lo = lo_key <= 0 ? 0 : lo_key >> 4;
+      }
+      const int g_hi = min(3, hi_key >> 4);
+      const bool interior =
+          kb + kAttnKB - 1 < valid && (a.window < 0 || (kb >= wq + 15 - a.window && kb + kAttnKB - 1 <= wq + a.window));
       float s[8][4];
 #pragma unroll
       for (int n = 0; n < 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int np = 0; np < 4; ++np) {
+        if (np < g_lo || np > g_hi) continue;
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
+        for (int c = 0; c < 4; ++c) {
           const int key = np * 16 + (lane & 7) + ((lane >> 4) << 3);
           const int ch = c * 2 + ((lane >> 3) & 1);
           uint32_t b0, b1, b2, b3;
@@ -183,18 +196,28 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
       }
       // Mask and scale.
       float nm0 = m0, nm1 = m1;
+      if (interior) {
 #pragma unroll
-      for (int n = 0; n < 8; ++n) {
+        for (int n = 0; n < 8; ++n) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int key = kb + n * 8 + (lane & 3) * 2 + (e & 1);
-          const int q = e < 2 ? r0 : r1;
-          bool keep = key < valid;
-          if (a.window >= 0) keep = keep && abs(key - q) <= a.window;
-          s[n][e] = keep ? s[n][e] * kScaleLog2 : -INFINITY;
+          for (int e = 0; e < 4; ++e) s[n][e] *= kScaleLog2;
+          nm0 = fmaxf(nm0, fmaxf(s[n][0], s[n][1]));
+          nm1 = fmaxf(nm1, fmaxf(s[n][2], s[n][3]));
         }
-        nm0 = fmaxf(nm0, fmaxf(s[n][0], s[n][1]));
-        nm1 = fmaxf(nm1, fmaxf(s[n][2], s[n][3]));
+      } else {
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = kb + n * 8 + (lane & 3) * 2 + (e & 1);
+            const int q = e < 2 ? r0 : r1;
+            bool keep = key < valid;
+            if (a.window >= 0) keep = keep && abs(key - q) <= a.window;
+            s[n][e] = keep ? s[n][e] * kScaleLog2 : -INFINITY;
+          }
+          nm0 = fmaxf(nm0, fmaxf(s[n][0], s[n][1]));
+          nm1 = fmaxf(nm1, fmaxf(s[n][2], s[n][3]));
+        }
       }
 #pragma unroll
       for (int d = 1; d < 4; d <<= 1) {
@@ -210,6 +233,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
       const float sub0 = m0 == -INFINITY ? 0.f : m0, sub1 = m1 == -INFINITY ? 0.f : m1;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {  // 16-key chunk j = S n-tiles 2j, 2j+1
+        if (j < g_lo || j > g_hi) continue;  // every probability of the group is 0
         uint32_t ph[4], pl[4];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {

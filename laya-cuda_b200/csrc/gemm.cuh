@@ -6,13 +6,15 @@
 // the FFN up-projection, residual accumulation for the attention-out and FFN down projections,
 // bias + ReLU / GELU for the decision head, split-K partials for small row counts).
 //
-// One CTA per SM, 6 warps:
+// One CTA per SM, 10 warps:
 //   warp 0      TMA producer: A/W tiles (BK = 64 16-bit elements, 128-byte swizzle) into a
 //               ring of shared-memory stages (no multicast).
 //   warp 1      TMEM allocator + MMA issuer: one elected thread issues tcgen05.mma
 //               (M = 128, N = BN, K = 16) into one of two TMEM accumulators.
-//   warps 2..5  epilogue: tcgen05.ld of the finished accumulator (warp w reads TMEM lanes
-//               32*(w%4) .. +31, i.e. tile rows), fused transform, global stores.
+//   warps 2..9  epilogue: tcgen05.ld of the finished accumulator (warp w reads TMEM lanes
+//               32*(w%4) .. +31, i.e. tile rows; warps 2-5 and 6-9 split the tile's column
+//               chunks), fused transform, global stores.  Two warps per lane quarter keep the
+//               epilogue (exact-erf GELU, RoPE) shorter than the next tile's MMAs.
 // The two accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
 //
 // Replaces the reference's cuBLAS GemmEx calls (laya_cuda/ops.py:58-66 called from
@@ -52,7 +54,8 @@ struct GemmArgs {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;
+constexpr int kEpiWarps = 8;
 
 template <int BN>
 struct GemmCfg {
@@ -144,7 +147,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 4); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], kEpiWarps); }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -244,8 +247,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     pdl_wait();
-    // Epilogue warps 2..5 -> TMEM lane quarter (warp % 4).
+    // Epilogue warps 2..9 -> TMEM lane quarter (warp % 4); `half` picks every other chunk.
     const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
     int acc = 0; uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
       int split, mb, nb; decode(t, split, mb, nb);
@@ -258,7 +262,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (EPI == EPI_GEGLU) {
         // Tile columns: [gate 64 | up 64] x (BN / 128); output column = n0/2 + 64*c + j.
 #pragma unroll 1
-        for (int c = 0; c < BN / 128; ++c) {
+        for (int c = half; c < BN / 128; c += 2) {
 #pragma unroll 1
           for (int h = 0; h < 2; ++h) {
             float g[32], u[32];
@@ -281,7 +285,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       } else if (EPI == EPI_QKV) {
         const int width = args.heads * 64;
 #pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
+        for (int c = half; c < BN / 64; c += 2) {
           float x[64];
           {
             float lo[32], hi[32];
@@ -335,7 +339,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half; c < BN / 32; c += 2) {
           float v[32];
           tmem_ld32(tbase + c * 32, v);
           if (live) {
