@@ -248,6 +248,8 @@ def run_engine(args, rank, world, local_rank):
     torch.cuda.set_device(local_rank)
     if world > 1:
         from datetime import timedelta
+        # rank 0's stdout carries exactly one JSON line: keep NCCL's version banner off it.
+        os.environ["NCCL_DEBUG"] = "WARN"
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local_rank))
     arch = S.architecture("laya", max_len=1024)
     CACHE.mkdir(parents=True, exist_ok=True)
@@ -332,24 +334,26 @@ def run_engine(args, rank, world, local_rank):
                 "traffic": round(TRAFFIC_FFN_UP_BYTES_PER_TOKEN * tokens / len(batches)),
                 "all_encoder_gemms": {"achieved": round(enc_achieved, 1), "frac": round(enc_achieved / tf_sust, 4)}}
 
+    # End to end through the public Runtime.predict on every rank: host items -> pinned
+    # staging -> H2D -> forward -> D2H of logits/acts, every micro-batch (one step = the rank's
+    # whole workload); whole-job rate = all ranks' sequences over the slowest rank's time.
+    h2d, d2h = 0, 0
+    for batch, (m, b, k) in zip(batches, shapes):
+        h2d += lib.laya_packed_ints(m, b, k) * 4
+        d2h += (b * (k + 1) + b * arch["n_act"] + 1) * 4
+    rt.predict(batches[0])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for batch in batches:
+        rt.predict(batch)
+    e2e_rate, _, _ = job_rate((time.perf_counter() - t0) * 1000, len(items), 1, world, "cuda")
+    e2e = {"value": round(e2e_rate, 2), "unit": "sequences/s", "h2d_bytes_per_step": int(h2d) * world,
+           "d2h_bytes_per_step": int(d2h) * world, "api": "Runtime.predict(items) per 64-sequence micro-batch"}
+
     line = None
     if rank == 0:
-        # End to end through the public Runtime.predict: host items -> pinned staging -> H2D ->
-        # forward -> D2H of logits/acts, every micro-batch (one step = the whole rank workload).
-        e2e_ms, h2d, d2h = None, 0, 0
-        e2e_steps = 1
-        for batch, (m, b, k) in zip(batches, shapes):
-            h2d += lib.laya_packed_ints(m, b, k) * 4
-            d2h += (b * (k + 1) + b * arch["n_act"] + 1) * 4
-        rt.predict(batches[0])
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        for _ in range(e2e_steps):
-            for batch in batches:
-                rt.predict(batch)
-        e2e_ms = (time.perf_counter() - t0) * 1000 / e2e_steps
-        e2e = {"value": round(len(items) / (e2e_ms / 1000), 2), "unit": "sequences/s", "h2d_bytes_per_step": int(h2d),
-               "d2h_bytes_per_step": int(d2h), "api": "Runtime.predict(items) per 64-sequence micro-batch"}
         lat, stream = None, None
         if world == 1 and args.latency != "none":
             # Configurations 1/2 (83 and 512 tokens) and 1024 tokens on the `laya` geometry.

@@ -154,7 +154,9 @@ const char* laya_last_error(laya_engine* e);
  * pre-interleaved by laya_interleave_geglu; out is [M][N/2]), 4 qkv (RoPE when cos/sin given,
  * tables transposed [32][rope_rows] indexed by positions[row]; out is [3][heads][M][64]),
  * 5 residual += (fp32), 6 split-K partials ([splits][M][N] fp32 in `residual`).  bias: fp32 [N]
- * or NULL.  Replaces cublasGemmEx + bias/activate/layout (ops.py:58-66; kernels.cu:50-82). */
+ * or NULL.  block_n: column tile (64, 128, 256), 0 to choose, or -128 / -256 for the CTA-pair
+ * (cta_group::2, 256-row tile) kernel.  Replaces cublasGemmEx + bias/activate/layout
+ * (ops.py:58-66; kernels.cu:50-82). */
 int laya_op_gemm(int precision, int epi, const void* x, const void* w, int M, int N, int K, void* out, int ldo,
                  float* residual, int ldr, const float* bias, int heads, const float* cos_tab, const float* sin_tab,
                  int rope_rows, const int32_t* positions, int splits, int block_n, int* err, void* stream);

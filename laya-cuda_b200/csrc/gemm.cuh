@@ -116,6 +116,106 @@ __device__ __forceinline__ void epi_partial_chunk(const GemmArgs& a, int split, 
   for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(r + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
 }
 
+// Epilogue of one accumulator tile for one thread: TMEM lane `row` of the tile (columns from
+// `tbase`), output column base n0; `half` selects every other column chunk (two warps share a
+// TMEM lane quarter).
+template <int BN, int EPI, typename T>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tbase, int row, int n0, int split,
+                                              int half) {
+  const bool live = row < args.M;
+  if (EPI == EPI_GEGLU) {
+    // Tile columns: [gate 64 | up 64] x (BN / 128); output column = n0/2 + 64*c + j.
+#pragma unroll 1
+    for (int c = half; c < BN / 128; c += 2) {
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        float g[32], u[32];
+        tmem_ld32(tbase + c * 128 + h * 32, g);
+        tmem_ld32(tbase + c * 128 + 64 + h * 32, u);
+        if (live) {
+          T* out = reinterpret_cast<T*>(args.out) + (size_t)row * args.ldo + n0 / 2 + c * 64 + h * 32;
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 w;
+            w.x = pack2<T>(gelu_erf(g[i + 0]) * u[i + 0], gelu_erf(g[i + 1]) * u[i + 1]);
+            w.y = pack2<T>(gelu_erf(g[i + 2]) * u[i + 2], gelu_erf(g[i + 3]) * u[i + 3]);
+            w.z = pack2<T>(gelu_erf(g[i + 4]) * u[i + 4], gelu_erf(g[i + 5]) * u[i + 5]);
+            w.w = pack2<T>(gelu_erf(g[i + 6]) * u[i + 6], gelu_erf(g[i + 7]) * u[i + 7]);
+            *reinterpret_cast<uint4*>(out + i) = w;
+          }
+        }
+      }
+    }
+  } else if (EPI == EPI_QKV) {
+    const int width = args.heads * 64;
+#pragma unroll 1
+    for (int c = half; c < BN / 64; c += 2) {
+      float x[64];
+      {
+        float lo[32], hi[32];
+        tmem_ld32(tbase + c * 64, lo);
+        tmem_ld32(tbase + c * 64 + 32, hi);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) { x[i] = lo[i]; x[32 + i] = hi[i]; }
+      }
+      if (live) {
+        const int n = n0 + c * 64;
+        const int part = n / width;
+        const int head = (n - part * width) >> 6;
+        if (args.bias) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i) x[i] += args.bias[n + i];
+        }
+        if (part < 2 && args.cos_tab) {
+          // Rotate-half RoPE: out[d] = x[d] cos - x[d+32] sin (d < 32),
+          //                   out[d] = x[d] cos + x[d-32] sin (d >= 32).
+          // Tables are [32][rope_rows]: the 32 lanes (consecutive rows, mostly consecutive
+          // positions) read one contiguous run per frequency.
+          const int pos = args.positions[row];
+          const float* cs = args.cos_tab + pos;
+          const float* sn = args.sin_tab + pos;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float c0 = __ldg(cs + (size_t)i * args.rope_rows), s0 = __ldg(sn + (size_t)i * args.rope_rows);
+            const float a = x[i], b = x[i + 32];
+            x[i] = a * c0 - b * s0;
+            x[i + 32] = b * c0 + a * s0;
+          }
+        }
+        if (part < 2) {
+          T* out = reinterpret_cast<T*>(args.out) + (((size_t)part * args.heads + head) * args.M + row) * 64;
+#pragma unroll
+          for (int i = 0; i < 64; i += 8) {
+            uint4 w;
+            w.x = pack2<T>(x[i + 0], x[i + 1]); w.y = pack2<T>(x[i + 2], x[i + 3]);
+            w.z = pack2<T>(x[i + 4], x[i + 5]); w.w = pack2<T>(x[i + 6], x[i + 7]);
+            *reinterpret_cast<uint4*>(out + i) = w;
+          }
+        } else {
+          // V transposed, [heads][64][M]: the attention's P.V product reads it K-major
+          // (keys contiguous).  The warp's lanes are consecutive rows, so each dimension's
+          // 32 stores fill one contiguous 64-byte run.
+          T* vt = reinterpret_cast<T*>(args.out) + ((size_t)2 * args.heads + head) * args.M * 64 + row;
+#pragma unroll
+          for (int i = 0; i < 64; ++i) vt[(size_t)i * args.M] = from_f32<T>(x[i]);
+        }
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = half; c < BN / 32; c += 2) {
+      float v[32];
+      tmem_ld32(tbase + c * 32, v);
+      if (live) {
+        const int col = n0 + c * 32;
+        if (EPI == EPI_RESIDUAL) epi_residual_chunk(args, row, col, v);
+        else if (EPI == EPI_PARTIAL) epi_partial_chunk(args, split, row, col, v);
+        else epi_store_chunk<T, EPI>(args, row, col, v);
+      }
+    }
+  }
+}
+
 template <int BN, int EPI, typename T>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -256,100 +356,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag)) break;
       tc_fence_after();
       const int row = mb * kBM + quarter * 32 + lane;
-      const bool live = row < args.M;
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      const int n0 = nb * BN;
-      if (EPI == EPI_GEGLU) {
-        // Tile columns: [gate 64 | up 64] x (BN / 128); output column = n0/2 + 64*c + j.
-#pragma unroll 1
-        for (int c = half; c < BN / 128; c += 2) {
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
-            float g[32], u[32];
-            tmem_ld32(tbase + c * 128 + h * 32, g);
-            tmem_ld32(tbase + c * 128 + 64 + h * 32, u);
-            if (live) {
-              T* out = reinterpret_cast<T*>(args.out) + (size_t)row * args.ldo + n0 / 2 + c * 64 + h * 32;
-#pragma unroll
-              for (int i = 0; i < 32; i += 8) {
-                uint4 w;
-                w.x = pack2<T>(gelu_erf(g[i + 0]) * u[i + 0], gelu_erf(g[i + 1]) * u[i + 1]);
-                w.y = pack2<T>(gelu_erf(g[i + 2]) * u[i + 2], gelu_erf(g[i + 3]) * u[i + 3]);
-                w.z = pack2<T>(gelu_erf(g[i + 4]) * u[i + 4], gelu_erf(g[i + 5]) * u[i + 5]);
-                w.w = pack2<T>(gelu_erf(g[i + 6]) * u[i + 6], gelu_erf(g[i + 7]) * u[i + 7]);
-                *reinterpret_cast<uint4*>(out + i) = w;
-              }
-            }
-          }
-        }
-      } else if (EPI == EPI_QKV) {
-        const int width = args.heads * 64;
-#pragma unroll 1
-        for (int c = half; c < BN / 64; c += 2) {
-          float x[64];
-          {
-            float lo[32], hi[32];
-            tmem_ld32(tbase + c * 64, lo);
-            tmem_ld32(tbase + c * 64 + 32, hi);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) { x[i] = lo[i]; x[32 + i] = hi[i]; }
-          }
-          if (live) {
-            const int n = n0 + c * 64;
-            const int part = n / width;
-            const int head = (n - part * width) >> 6;
-            if (args.bias) {
-#pragma unroll
-              for (int i = 0; i < 64; ++i) x[i] += args.bias[n + i];
-            }
-            if (part < 2 && args.cos_tab) {
-              // Rotate-half RoPE: out[d] = x[d] cos - x[d+32] sin (d < 32),
-              //                   out[d] = x[d] cos + x[d-32] sin (d >= 32).
-              // Tables are [32][rope_rows]: the 32 lanes (consecutive rows, mostly consecutive
-              // positions) read one contiguous run per frequency.
-              const int pos = args.positions[row];
-              const float* cs = args.cos_tab + pos;
-              const float* sn = args.sin_tab + pos;
-#pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const float c0 = __ldg(cs + (size_t)i * args.rope_rows), s0 = __ldg(sn + (size_t)i * args.rope_rows);
-                const float a = x[i], b = x[i + 32];
-                x[i] = a * c0 - b * s0;
-                x[i + 32] = b * c0 + a * s0;
-              }
-            }
-            if (part < 2) {
-              T* out = reinterpret_cast<T*>(args.out) + (((size_t)part * args.heads + head) * args.M + row) * 64;
-#pragma unroll
-              for (int i = 0; i < 64; i += 8) {
-                uint4 w;
-                w.x = pack2<T>(x[i + 0], x[i + 1]); w.y = pack2<T>(x[i + 2], x[i + 3]);
-                w.z = pack2<T>(x[i + 4], x[i + 5]); w.w = pack2<T>(x[i + 6], x[i + 7]);
-                *reinterpret_cast<uint4*>(out + i) = w;
-              }
-            } else {
-              // V transposed, [heads][64][M]: the attention's P.V product reads it K-major
-              // (keys contiguous).  The warp's lanes are consecutive rows, so each dimension's
-              // 32 stores fill one contiguous 64-byte run.
-              T* vt = reinterpret_cast<T*>(args.out) + ((size_t)2 * args.heads + head) * args.M * 64 + row;
-#pragma unroll
-              for (int i = 0; i < 64; ++i) vt[(size_t)i * args.M] = from_f32<T>(x[i]);
-            }
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = half; c < BN / 32; c += 2) {
-          float v[32];
-          tmem_ld32(tbase + c * 32, v);
-          if (live) {
-            const int col = n0 + c * 32;
-            if (EPI == EPI_RESIDUAL) epi_residual_chunk(args, row, col, v);
-            else if (EPI == EPI_PARTIAL) epi_partial_chunk(args, split, row, col, v);
-            else epi_store_chunk<T, EPI>(args, row, col, v);
-          }
-        }
-      }
+      epilogue_tile<BN, EPI, T>(args, tbase, row, nb * BN, split, half);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -361,6 +369,161 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+}
+
+
+// ---------------------------------------------------------------------------------------------
+// CTA-pair variant (cluster of 2, tcgen05 cta_group::2): 256 x BN output tiles.  Each CTA loads
+// its 128 rows of A and BN/2 rows of W per k-block and holds its 128 accumulator rows in its own
+// TMEM; the pair leader (rank 0) issues the M=256 MMAs that read both CTAs' shared memory.  Per
+// CTA this moves (128 + BN/2) x 64 operand elements per k-block for a 128 x BN share of the
+// output instead of (128 + BN) x 64: a third less L2 -> shared traffic than the 1-CTA kernel.
+// Used for large row counts; small classes use the 1-CTA kernel (split-K included).
+//
+// Barriers: full[s] lives in the leader (both CTAs' TMA loads complete on it; the leader
+// expects both CTAs' bytes); empty[s] and tfull[a] live in both CTAs (the leader's MMA thread
+// commits to its own and, through the peer's cluster address, to the peer's); tempty[a] lives in
+// the leader (all 16 epilogue warps of the pair arrive, the peer's remotely).
+// ---------------------------------------------------------------------------------------------
+template <int BN>
+struct GemmPairCfg {
+  static constexpr int kStageA = kBM * kBK * 2;           // this CTA's 128 rows of A
+  static constexpr int kStageB = (BN / 2) * kBK * 2;      // this CTA's BN/2 rows of W
+  static constexpr int kStageBytes = kStageA + kStageB;
+  static constexpr int kStages = (192 * 1024) / kStageBytes;
+  static constexpr int kTmemCols = 2 * BN;
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+};
+
+template <int BN, int EPI, typename T>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmArgs args) {
+  using Cfg = GemmPairCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * Cfg::kStageA;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tfull = bars + 2 * S;
+  uint64_t* tempty = bars + 2 * S + 2;
+  uint64_t* drain = bars + 2 * S + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+
+  const int m_blocks = (args.M + 2 * kBM - 1) / (2 * kBM);
+  const int n_blocks = args.N / BN;
+  const int k_blocks = args.K / kBK;
+  const int tiles = m_blocks * n_blocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], 2 * kEpiWarps); }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) { tma_prefetch_desc(&tmA); tma_prefetch_desc(&tmB); }
+  if (warp == 1) { tmem_alloc_pair(tmem_slot, Cfg::kTmemCols); tmem_relinquish_pair(); }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised before any cross-CTA arrival
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();
+  pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0; uint32_t phase = 0;
+      uint32_t issued = 0, last_par = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += pairs) {
+        const int mb = t / n_blocks, nb = t - mb * n_blocks;
+        const int arow = mb * 2 * kBM + (int)rank * kBM;
+        const int brow = nb * BN + (int)rank * (BN / 2);
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrGemmProducerWait, abort_flag)) { ok = false; break; }
+          const uint32_t leader_full = cluster_addr(smem_u32(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
+          tma_load_2d_pair(sA + stage * Cfg::kStageA, &tmA, leader_full, kb * kBK, arow);
+          tma_load_2d_pair(sB + stage * Cfg::kStageB, &tmB, leader_full, kb * kBK, brow);
+          issued |= 1u << stage;
+          last_par = (last_par & ~(1u << stage)) | (phase << stage);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok && leader) {
+        for (int s = 0; s < S; ++s)
+          if (issued & (1u << s)) mbar_wait(&full[s], (last_par >> s) & 1, nullptr, 0, abort_flag);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      const uint32_t idesc = mma_idesc<std::is_same<T, __nv_bfloat16>::value>(2 * kBM, BN);
+      int stage = 0; uint32_t phase = 0;
+      int acc = 0; uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int t = pair; t < tiles && ok; t += pairs) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, args.err, kErrGemmMmaWait, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, args.err, kErrGemmMmaWait, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * Cfg::kStageA);
+          const uint32_t b0 = smem_u32(sB + stage * Cfg::kStageB);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            tc_mma_f16_pair(d_tmem, smem_desc_sw128(a0 + k * 32), smem_desc_sw128(b0 + k * 32), idesc,
+                            (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          const uint32_t e = smem_u32(&empty[stage]);
+          tc_commit_pair(cluster_addr(e, 0));
+          tc_commit_pair(cluster_addr(e, 1));
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        const uint32_t f = smem_u32(&tfull[acc]);
+        tc_commit_pair(cluster_addr(f, 0));
+        tc_commit_pair(cluster_addr(f, 1));
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+      tc_commit_pair(cluster_addr(smem_u32(drain), 0));
+      mbar_wait(drain, 0, nullptr, 0, abort_flag);
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t leader_tempty0 = cluster_addr(smem_u32(&tempty[0]), 0);
+    const uint32_t leader_tempty1 = cluster_addr(smem_u32(&tempty[1]), 0);
+    int acc = 0; uint32_t acc_phase = 0;
+    for (int t = pair; t < tiles; t += pairs) {
+      const int mb = t / n_blocks, nb = t - mb * n_blocks;
+      if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag)) break;
+      tc_fence_after();
+      const int row = mb * 2 * kBM + (int)rank * kBM + quarter * 32 + lane;
+      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      epilogue_tile<BN, EPI, T>(args, tbase, row, nb * BN, 0, half);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc == 0 ? leader_tempty0 : leader_tempty1);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // both CTAs done with TMEM and with the peer's barriers
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
 }
 
 }  // namespace laya

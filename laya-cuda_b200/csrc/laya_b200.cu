@@ -152,6 +152,59 @@ void launch_gemm_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
   launch_k(kern, dim3(grid), dim3(kGemmThreads), GemmCfg<BN>::kSmemBytes, st, ta, tb, a);
 }
 
+// CTA-pair GEMM: clusters of 2 (cta_group::2), plus programmatic serialisation.
+template <typename T, int BN, int EPI>
+void launch_gemm_pair_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t st) {
+  static uint64_t configured = 0;  // one bit per device
+  auto kern = gemm_pair_kernel<BN, EPI, T>;
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  if (!(configured & (1ull << dev))) {
+    CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmPairCfg<BN>::kSmemBytes));
+    configured |= 1ull << dev;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = GemmPairCfg<BN>::kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  CK(cudaLaunchKernelEx(&cfg, kern, ta, tb, a));
+}
+
+template <typename T, int BN>
+void launch_gemm_pair_bn(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid,
+                         cudaStream_t st) {
+  switch (epi) {
+    case EPI_STORE: launch_gemm_pair_inst<T, BN, EPI_STORE>(ta, tb, a, grid, st); break;
+    case EPI_RELU: launch_gemm_pair_inst<T, BN, EPI_RELU>(ta, tb, a, grid, st); break;
+    case EPI_GELU: launch_gemm_pair_inst<T, BN, EPI_GELU>(ta, tb, a, grid, st); break;
+    case EPI_GEGLU: launch_gemm_pair_inst<T, BN, EPI_GEGLU>(ta, tb, a, grid, st); break;
+    case EPI_QKV: launch_gemm_pair_inst<T, BN, EPI_QKV>(ta, tb, a, grid, st); break;
+    case EPI_RESIDUAL: launch_gemm_pair_inst<T, BN, EPI_RESIDUAL>(ta, tb, a, grid, st); break;
+    default: fail(LAYA_ERR_INVALID, "epilogue %d has no CTA-pair variant", epi);
+  }
+}
+
+// Rows from which GEMMs run as CTA pairs (256-row tiles); below, 1-CTA tiles (and split-K) fill
+// the SMs better.  LAYA_GEMM_PAIR=0 in the environment turns pairs off.
+constexpr int kPairMinRows = 2048;
+bool pair_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("LAYA_GEMM_PAIR");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 template <typename T, int BN>
 void launch_gemm_bn(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t st) {
   switch (epi) {
@@ -169,11 +222,20 @@ void launch_gemm_bn(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const
   }
 }
 
+// tb: W tensor map with BN-row boxes (1-CTA kernel) or BN/2-row boxes (pair kernel).
 template <typename T>
 void launch_gemm(int epi, int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int sms,
-                 cudaStream_t st) {
+                 cudaStream_t st, bool pair = false) {
   if (a.K % kBK != 0 || a.N % bn != 0 || a.M <= 0) fail(LAYA_ERR_INVALID, "GEMM shape %dx%dx%d not tileable", a.M, a.N, a.K);
   if ((a.K / kBK) % a.splits != 0) fail(LAYA_ERR_INVALID, "split-K %d does not divide %d k-blocks", a.splits, a.K / kBK);
+  if (pair) {
+    if (a.splits != 1 || (bn != 128 && bn != 256)) fail(LAYA_ERR_INVALID, "no CTA-pair variant for this GEMM");
+    const int tiles = ((a.M + 2 * kBM - 1) / (2 * kBM)) * (a.N / bn);
+    const int grid = 2 * std::min(tiles, sms / 2);
+    if (bn == 256) launch_gemm_pair_bn<T, 256>(epi, ta, tb, a, grid, st);
+    else launch_gemm_pair_bn<T, 128>(epi, ta, tb, a, grid, st);
+    return;
+  }
   const int tiles = ((a.M + kBM - 1) / kBM) * (a.N / bn) * a.splits;
   const int grid = std::min(tiles, sms);
   switch (bn) {
@@ -740,7 +802,9 @@ void gemm(Engine& e, bool prof, int family, int epi, const CUtensorMap& ta, cons
           int ldo, float* residual, int ldr, const float* bias, int* err, int rope = -1, const int* positions = nullptr) {
   const Tensor& w = W(e, wname);
   const int N = (int)w.shape[0], K = (int)w.shape[1];
-  const int bn = pick_bn(M, N, epi, e.sms);
+  int bn = pick_bn(M, N, epi, e.sms);
+  const bool pair = M >= kPairMinRows && pair_enabled() && N % 256 == 0;
+  if (pair) bn = 256;
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K; a.splits = 1;
   a.out = out; a.ldo = ldo; a.residual = residual; a.ldr = ldr; a.bias = bias;
@@ -748,8 +812,8 @@ void gemm(Engine& e, bool prof, int family, int epi, const CUtensorMap& ta, cons
   if (rope >= 0) { a.cos_tab = e.rope_cos[rope]; a.sin_tab = e.rope_sin[rope]; a.rope_rows = e.rope_rows; }
   a.positions = positions;
   a.err = err;
-  const CUtensorMap& tb = weight_map(e, wname, bn);
-  launch(e, prof, family, 2.0 * M * N * K, [&] { launch_gemm<T>(epi, bn, ta, tb, a, e.sms, e.stream); });
+  const CUtensorMap& tb = weight_map(e, wname, pair ? bn / 2 : bn);
+  launch(e, prof, family, 2.0 * M * N * K, [&] { launch_gemm<T>(epi, bn, ta, tb, a, e.sms, e.stream, pair); });
 }
 
 template <typename T>
@@ -1352,17 +1416,19 @@ int laya_op_gemm(int precision, int epi, const void* x, const void* w, int M, in
   const int sms = sm_count(dev);
   const bool bf = precision == LAYA_PRECISION_BF16;
   if (splits < 1) splits = 1;
-  const int bn = block_n ? block_n : pick_bn(M, N, epi, sms);
+  // block_n < 0 selects the CTA-pair kernel with |block_n| columns per tile.
+  const bool pair = block_n < 0;
+  const int bn = block_n > 0 ? block_n : block_n < 0 ? -block_n : pick_bn(M, N, epi, sms);
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K; a.splits = splits;
   a.out = out; a.ldo = ldo; a.residual = residual; a.ldr = ldr; a.bias = bias;
   a.heads = heads; a.cos_tab = cos_tab; a.sin_tab = sin_tab; a.rope_rows = rope_rows; a.positions = positions;
   a.err = err;
   const CUtensorMap ta = make_map(x, M, K, kBM, bf);
-  const CUtensorMap tb = make_map(w, N, K, bn, bf);
+  const CUtensorMap tb = make_map(w, N, K, pair ? bn / 2 : bn, bf);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (bf) launch_gemm<__nv_bfloat16>(epi, bn, ta, tb, a, sms, st);
-  else launch_gemm<__half>(epi, bn, ta, tb, a, sms, st);
+  if (bf) launch_gemm<__nv_bfloat16>(epi, bn, ta, tb, a, sms, st, pair);
+  else launch_gemm<__half>(epi, bn, ta, tb, a, sms, st, pair);
   API_END(nullptr)
 }
 

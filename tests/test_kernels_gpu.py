@@ -116,22 +116,23 @@ def rope_tables(theta, rows):
 
 
 @pytest.mark.parametrize("prec", ["bf16", "f16"])
-@pytest.mark.parametrize("rope", [True, False])
-def test_gemm_qkv_rope_layout(lib, prec, rope):
-    """Encoder QKV (RoPE, no bias) and head in_proj (bias, no RoPE) epilogues; cf. tests/test_gpu.py:36-53."""
+@pytest.mark.parametrize("rope,M,block_n", [(True, 208, 0), (False, 208, 0), (True, 2320, -256), (False, 2320, -128)])
+def test_gemm_qkv_rope_layout(lib, prec, rope, M, block_n):
+    """Encoder QKV (RoPE, no bias) and head in_proj (bias, no RoPE) epilogues, 1-CTA and CTA-pair
+    kernels; cf. tests/test_gpu.py:36-53."""
     rng = np.random.default_rng(17)
-    heads, M, K = 2, 208, 128
+    heads, K = 4, 128
     N = 3 * heads * 64
     x, xd = rand16((M, K), prec, rng)
     w, wd = rand16((N, K), prec, rng, 0.1)
-    positions = np.concatenate([np.arange(112), np.arange(96)]).astype(np.int32)
+    positions = (np.arange(M) % 112).astype(np.int32)
     cos, sin = rope_tables(10000, 128)
     bias = None if rope else torch.from_numpy(rng.normal(0, 0.1, N).astype(np.float32)).cuda()
     out = torch.full((3, heads, M, 64), float("nan"), dtype=PRECISIONS[prec][1], device="cuda")
     gemm(lib, prec, 4, x, w, out, heads=heads,
          cos=torch.from_numpy(cos.T.copy()).cuda() if rope else None,
          sin=torch.from_numpy(sin.T.copy()).cuda() if rope else None,
-         positions=torch.from_numpy(positions).cuda(), bias=bias)
+         positions=torch.from_numpy(positions).cuda(), bias=bias, block_n=block_n)
     h = xd @ wd.T
     if bias is not None:
         h = h + bias.double().cpu().numpy()
@@ -147,6 +148,42 @@ def test_gemm_qkv_rope_layout(lib, prec, rope):
     # v is stored transposed: the buffer's third plane is [heads][64][M].
     got[2] = got[2].reshape(heads, 64, M).transpose(0, 2, 1)
     assert np.max(np.abs(got - h) - ROUND[prec] * np.abs(h)) < 2e-3
+
+
+@pytest.mark.parametrize("prec", ["f16", "bf16"])
+@pytest.mark.parametrize("epi,bn", [(0, -256), (0, -128), (2, -256), (3, -256), (3, -128), (5, -256), (5, -128)])
+def test_gemm_cta_pair_kernel(lib, prec, epi, bn):
+    """The cta_group::2 kernel (256-row tiles over a CTA pair), with a row count that leaves the
+    second CTA of the last pair partly and wholly out of range."""
+    rng = np.random.default_rng(abs(bn) + epi)
+    M, K = 2500, 768
+    N = 2048 if epi == 3 else 768
+    x, xd = rand16((M, K), prec, rng)
+    w, wd = rand16((N, K), prec, rng, 0.05)
+    bias = torch.from_numpy(rng.normal(0, 0.1, N).astype(np.float32)).cuda() if epi in (0, 2, 5) else None
+    h = xd @ wd.T + (bias.double().cpu().numpy() if bias is not None else 0)
+    if epi == 3:
+        host = w.cpu().view(torch.int16).numpy().astype(np.uint16)
+        inter = np.empty_like(host)
+        _lib.check(lib.laya_interleave_geglu(host.ctypes.data, inter.ctypes.data, N // 2, K))
+        w = torch.from_numpy(inter.view(np.int16)).view(PRECISIONS[prec][1]).cuda()
+        out = torch.empty((M, N // 2), dtype=PRECISIONS[prec][1], device="cuda")
+        gemm(lib, prec, 3, x, w, out, N // 2, block_n=bn)
+        g, u = h[:, :N // 2], h[:, N // 2:]
+        expected = 0.5 * g * (1 + np.vectorize(math.erf)(g / math.sqrt(2))) * u
+    elif epi == 5:
+        base = rng.normal(0, 1, (M, N)).astype(np.float32)
+        out = torch.from_numpy(base.copy()).cuda()
+        gemm(lib, prec, 5, x, w, residual=out, ldr=N, bias=bias, block_n=bn)
+        expected = base + h
+        assert np.max(np.abs(out.cpu().double().numpy() - expected)) < 2e-4 * math.sqrt(K)
+        return
+    else:
+        out = torch.full((M, N), float("nan"), dtype=PRECISIONS[prec][1], device="cuda")
+        gemm(lib, prec, epi, x, w, out, N, bias=bias, block_n=bn)
+        expected = h if epi == 0 else 0.5 * h * (1 + np.vectorize(math.erf)(h / math.sqrt(2)))
+    got = out.double().cpu().numpy()
+    assert np.max(np.abs(got - expected) - ROUND[prec] * np.abs(expected)) < 3e-3
 
 
 @pytest.mark.parametrize("prec", ["bf16"])
