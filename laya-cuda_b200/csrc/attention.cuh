@@ -7,8 +7,8 @@
 //   * scores are scaled by 1/8 (64-wide heads), softmax in fp32;
 //   * padding queries (and every token past the last row) produce exact zeros.
 //
-// This file holds the mma.sync variant (kernel-level tests; 64-query tiles).  The forward pass
-// uses the tcgen05 variant in tc_attention.cuh.
+// This file holds the mma.sync variant (64-query tiles): kernel-level tests and the forward pass
+// under LAYA_ATTENTION=mma_sync.  The forward pass uses the tcgen05 variant in tc_attention.cuh.
 //
 // Work unit: one CTA per (64-query tile of one row, head).  The host builds the tile table
 // while packing the inputs, so a tile never straddles two rows and a CTA stages one K/V block

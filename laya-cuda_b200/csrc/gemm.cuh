@@ -97,17 +97,53 @@ __device__ __forceinline__ void epi_store_chunk(const GemmArgs& a, int row, int 
   }
 }
 
-__device__ __forceinline__ void epi_residual_chunk(const GemmArgs& a, int row, int col, const float (&v)[32]) {
-  float* r = a.residual + (size_t)row * a.ldr + col;
+// Residual epilogue (residual[row, n0 + ...] += accumulator + bias), software-pipelined: a
+// thread's residual chunks (every other 32-column chunk of its row) are loaded two ahead, the
+// first two before the accumulator is waited on, so the fp32 read latency overlaps the tile's
+// MMAs and the previous chunk's adds instead of following each TMEM load.
+template <int BN>
+struct ResidualPipe {
+  static constexpr int kChunks = BN / 64;
+  float4 buf[2][8];
+
+  __device__ __forceinline__ void load(const GemmArgs& a, int row, int n0, int half, int i) {
+    const float* r = a.residual + (size_t)row * a.ldr + n0 + (half + 2 * i) * 32;
 #pragma unroll
-  for (int i = 0; i < 32; i += 4) {
-    float4 t = *reinterpret_cast<float4*>(r + i);
-    float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (a.bias) bb = *reinterpret_cast<const float4*>(a.bias + col + i);
-    t.x += v[i] + bb.x; t.y += v[i + 1] + bb.y; t.z += v[i + 2] + bb.z; t.w += v[i + 3] + bb.w;
-    *reinterpret_cast<float4*>(r + i) = t;
+    for (int k = 0; k < 8; ++k) buf[i & 1][k] = *reinterpret_cast<const float4*>(r + 4 * k);
   }
-}
+
+  __device__ __forceinline__ void start(const GemmArgs& a, int row, int n0, int half) {
+    if (row >= a.M) return;
+    load(a, row, n0, half, 0);
+    if (kChunks > 1) load(a, row, n0, half, 1);
+  }
+
+  __device__ __forceinline__ void finish(const GemmArgs& a, uint32_t tbase, int row, int n0, int half) {
+    const bool live = row < a.M;
+#pragma unroll
+    for (int i = 0; i < kChunks; ++i) {
+      const int c = half + 2 * i;
+      uint32_t v[32];
+      tmem_ld32_async(tbase + c * 32, v);
+      tmem_wait_ld(v);
+      if (!live) continue;
+      const int col = n0 + c * 32;
+      float* r = a.residual + (size_t)row * a.ldr + col;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        float4 t = buf[i & 1][k];
+        float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (a.bias) bb = *reinterpret_cast<const float4*>(a.bias + col + 4 * k);
+        t.x += __uint_as_float(v[4 * k]) + bb.x;
+        t.y += __uint_as_float(v[4 * k + 1]) + bb.y;
+        t.z += __uint_as_float(v[4 * k + 2]) + bb.z;
+        t.w += __uint_as_float(v[4 * k + 3]) + bb.w;
+        *reinterpret_cast<float4*>(r + 4 * k) = t;
+      }
+      if (i + 2 < kChunks) load(a, row, n0, half, i + 2);
+    }
+  }
+};
 
 __device__ __forceinline__ void epi_partial_chunk(const GemmArgs& a, int split, int row, int col,
                                                   const float (&v)[32]) {
@@ -202,14 +238,14 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tba
       }
     }
   } else {
+    // EPI_RESIDUAL is handled by ResidualPipe.
 #pragma unroll 1
     for (int c = half; c < BN / 32; c += 2) {
       float v[32];
       tmem_ld32(tbase + c * 32, v);
       if (live) {
         const int col = n0 + c * 32;
-        if (EPI == EPI_RESIDUAL) epi_residual_chunk(args, row, col, v);
-        else if (EPI == EPI_PARTIAL) epi_partial_chunk(args, split, row, col, v);
+        if (EPI == EPI_PARTIAL) epi_partial_chunk(args, split, row, col, v);
         else epi_store_chunk<T, EPI>(args, row, col, v);
       }
     }
@@ -353,11 +389,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int acc = 0; uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
       int split, mb, nb; decode(t, split, mb, nb);
+      const int row = mb * kBM + quarter * 32 + lane;
+      ResidualPipe<BN> rp;
+      if (EPI == EPI_RESIDUAL) rp.start(args, row, nb * BN, half);
       if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag)) break;
       tc_fence_after();
-      const int row = mb * kBM + quarter * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      epilogue_tile<BN, EPI, T>(args, tbase, row, nb * BN, split, half);
+      if (EPI == EPI_RESIDUAL) rp.finish(args, tbase, row, nb * BN, half);
+      else epilogue_tile<BN, EPI, T>(args, tbase, row, nb * BN, split, half);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -508,11 +547,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int acc = 0; uint32_t acc_phase = 0;
     for (int t = pair; t < tiles; t += pairs) {
       const int mb = t / n_blocks, nb = t - mb * n_blocks;
+      const int row = mb * 2 * kBM + (int)rank * kBM + quarter * 32 + lane;
+      ResidualPipe<BN> rp;
+      if (EPI == EPI_RESIDUAL) rp.start(args, row, nb * BN, half);
       if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag)) break;
       tc_fence_after();
-      const int row = mb * 2 * kBM + (int)rank * kBM + quarter * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      epilogue_tile<BN, EPI, T>(args, tbase, row, nb * BN, 0, half);
+      if (EPI == EPI_RESIDUAL) rp.finish(args, tbase, row, nb * BN, half);
+      else epilogue_tile<BN, EPI, T>(args, tbase, row, nb * BN, 0, half);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc == 0 ? leader_tempty0 : leader_tempty1);

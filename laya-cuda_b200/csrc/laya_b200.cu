@@ -513,9 +513,9 @@ struct Engine {
   std::map<std::tuple<const void*, int>, CUtensorMap> wmaps;
   std::string error;
   bool profiling = false;
-  // Attention kernel of the forward pass: mma.sync (default) or the tcgen05/TMEM kernel
-  // (LAYA_ATTENTION=tcgen05 in the environment at engine creation).
-  bool tc_attention = false;
+  // Attention kernel of the forward pass: the tcgen05/TMEM kernel (default) or the mma.sync
+  // kernel (LAYA_ATTENTION=mma_sync in the environment at engine creation).
+  bool tc_attention = true;
   std::vector<ProfEvent> prof_pending;
   std::vector<cudaEvent_t> prof_pool;
   double prof_ms[kFamilies] = {};
@@ -1103,7 +1103,7 @@ int laya_create(const laya_config* cfg, int device, int max_cached_shapes, laya_
   e.sms = sm_count(device);
   {
     const char* v = getenv("LAYA_ATTENTION");
-    e.tc_attention = v && std::string(v) == "tcgen05";
+    e.tc_attention = !(v && std::string(v) == "mma_sync");
   }
   build_expected(e);
   CK(cudaStreamCreateWithFlags(&e.stream, cudaStreamNonBlocking));

@@ -5,26 +5,37 @@
 // fp32 softmax, padding queries and tokens past the last row produce zeros.
 //
 // Work unit: one CTA per (128-query tile of one row, head); the host's tile table never lets a
-// tile straddle rows.  6 warps:
-//   warp 0     TMA: the Q tile once, then per 128-key block the K tile and the V^T tile
-//              (128-byte swizzle, no multicast).
-//   warp 1     TMEM allocation + MMA issue (one thread): S = Q K^T (M=128, N=128, K=64) into
-//              TMEM columns [0,128); O_blk = P V (M=128, N=64, K=128) into columns [128,192).
-//   warps 2-5  softmax, one thread per query row: reads its S row from TMEM, online max and
-//              sum in fp32, writes P (16-bit, swizzled K-major) to shared memory for the P V
-//              product, and accumulates O in registers: o = o * exp2(m_old - m_new) + O_blk.
+// tile straddle rows.  Two CTAs share an SM (82 KB shared memory and 256 TMEM columns each).
+// 6 warps:
+//   warp 0     TMA: the Q tile once, then per 128-key block the K tile and the V^T tile into
+//              double-buffered stages (128-byte swizzle, no multicast).
+//   warp 1     TMEM allocation + MMA issue (one thread):
+//                S_j = Q K_j^T        (M=128, N=128, K=64)   TMEM columns [0,128), fp32
+//                O  += P_j V_j        (M=128, N=64,  K=128)  A = P from TMEM, O in [192,256)
+//              S_{j+1} is issued as soon as the softmax has read S_j, so the tensor core works on
+//              the next block while the softmax computes this one.
+//   warps 2-5  softmax, one thread per query row (its TMEM lane): loads its row of S_j with all
+//              loads in flight before one wait, masks only the 32-key chunks that straddle a
+//              boundary and skips chunks no query of the warp can see, keeps the running
+//              maximum m and sum l in fp32, and writes P = 2^(s*log2e/8 - m) as 16-bit pairs
+//              into TMEM columns [128,192) for the P V product.  O stays in TMEM: it is rescaled
+//              (read, scaled, written back) only when the row maximum grows by more than 2^8, so
+//              P is at most 256 and the final O / l is unchanged.
+// Key blocks start at the window's first key (rounded down to 16 tokens), not at a multiple of
+// 128, so a 128-query tile of a window-64 layer reads two blocks.
 // Inputs (from the QKV GEMM epilogue): Q, K [heads][M][64] (K-major rows of 128 bytes) and V
-// transposed [heads][64][M], so every MMA operand is K-major, as in gemm.cuh.  Every wait is
-// bounded and reports through the error word.
+// transposed [heads][64][M], so every shared-memory operand is K-major, as in gemm.cuh.  Every
+// wait is bounded and reports through the error word.
 #pragma once
 #include "common.cuh"
 
 namespace laya {
 
-constexpr int kTcQ = 128;          // queries per CTA
-constexpr int kTcKB = 128;         // keys per block
+constexpr int kTcQ = 128;              // queries per CTA
+constexpr int kTcKB = 128;             // keys per block
 constexpr int kTcThreads = 192;
-constexpr int kTcTmemCols = 256;   // S: [0,128), O: [128,192)
+constexpr int kTcTmemCols = 256;       // S: [0,128), P: [128,192), O: [192,256)
+constexpr float kTcRescaleLog2 = 8.f;  // O is rescaled when the row maximum grows by more than 2^8
 
 struct TcAttnArgs {
   void* out;            // [M][heads*64]
@@ -39,46 +50,131 @@ struct TcAttnArgs {
 
 struct TcAttnSmem {
   static constexpr int kQ = kTcQ * 128;            // 16 KB: [128 queries][64 dims]
-  static constexpr int kK = kTcKB * 128;           // 16 KB: [128 keys][64 dims]
-  static constexpr int kV = 2 * 64 * 128;          // 16 KB: two [64 dims][64 keys] tiles
-  static constexpr int kP = 2 * kTcQ * 128;        // 32 KB: two [128 queries][64 keys] tiles
-  static constexpr int kOffQ = 0, kOffK = kQ, kOffV = kQ + kK, kOffP = kQ + kK + kV;
-  static constexpr int kOffBar = kOffP + kP;
+  static constexpr int kK = kTcKB * 128;           // 16 KB per stage: [128 keys][64 dims]
+  static constexpr int kV = 2 * 64 * 128;          // 16 KB per stage: two [64 dims][64 keys] tiles
+  static constexpr int kStages = 2;
+  static constexpr int kOffQ = 0, kOffK = kQ, kOffV = kQ + kStages * kK;
+  static constexpr int kOffBar = kOffV + kStages * kV;
   static constexpr int kBytes = kOffBar + 256 + 1024;  // barriers + alignment slack
 };
+
+// Softmax helpers for one thread's row of a 128-key block held in registers as four 32-key
+// chunks (raw fp32 scores).  `vis` bit c: chunk c is loaded (some query of the warp sees one of
+// its keys); `full` bit c: every query of the warp sees every key of chunk c (no mask).  Both
+// are warp-uniform; kAll = every chunk visible and full (the common case of global layers),
+// which compiles without a branch.
+//
+// Masks the scores this thread's query may not see to -inf and returns the block maximum.
+// Key ck + i is visible iff (unsigned)(ck + i - lo_key) <= span_keys.
+template <bool kAll>
+__device__ __forceinline__ float tc_block_max(uint32_t (&sx)[4][32], uint32_t vis, uint32_t full, int kb, int lo_key,
+                                              uint32_t span_keys) {
+  float mx[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    if (!kAll && !((vis >> c) & 1)) continue;
+    if (!kAll && !((full >> c) & 1)) {
+      const int d = kb + 32 * c - lo_key;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if ((uint32_t)(d + i) > span_keys) sx[c][i] = __float_as_uint(-INFINITY);
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sx[c][i]));
+  }
+#pragma unroll
+  for (int w = 4; w >= 1; w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
+  return mx[0];
+}
+
+// P = 2^(s * scale - sub) for the loaded chunks (zeros for the others), stored as 16-bit pairs
+// into TMEM columns p_tmem + 16c; returns the row sum of the fp32 probabilities.
+template <bool kAll, typename T>
+__device__ __forceinline__ float tc_block_probs(const uint32_t (&sx)[4][32], uint32_t vis, float scale, float sub,
+                                                uint32_t p_tmem) {
+  float sm[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t pk[16];
+    if (kAll || ((vis >> c) & 1)) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 2) {
+        const float p0 = ex2_approx(fmaf(__uint_as_float(sx[c][i]), scale, -sub));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(sx[c][i + 1]), scale, -sub));
+        sm[(i >> 1) & 3] += p0 + p1;
+        pk[i >> 1] = pack2<T>(p0, p1);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) pk[i] = 0u;
+    }
+    tmem_st16(p_tmem + 16 * c, pk);
+  }
+  return (sm[0] + sm[1]) + (sm[2] + sm[3]);
+}
 
 template <typename T>
 __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __grid_constant__ CUtensorMap tmQK,
                                                                     const __grid_constant__ CUtensorMap tmVt,
                                                                     const TcAttnArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // The tile table, starts and lengths are written by the host before the forward pass, so they
+  // are read before waiting on the previous kernel.
+  const int4 tile = a.tiles[blockIdx.x];
+  const int t0 = tile.x, t1 = tile.y, row = tile.z;
+  if (row == -2) return;
+  const int head = blockIdx.y;
+  const int width = a.heads * 64;
+  T* out = reinterpret_cast<T*>(a.out);
+  if (row < 0) {
+    // Tokens past the last row: zeros (8 x 16 bytes per token and head).
+    pdl_trigger();
+    pdl_wait();
+    for (int i = threadIdx.x; i < (t1 - t0) * 8; i += kTcThreads) {
+      const int t = t0 + (i >> 3);
+      *reinterpret_cast<uint4*>(out + (size_t)t * width + head * 64 + (i & 7) * 8) = make_uint4(0, 0, 0, 0);
+    }
+    return;
+  }
+  const int first = a.starts[row];
+  const int valid = a.lengths[row];
+  const int q0 = t0 - first;  // row-relative index of the tile's first query
+  int k_lo = 0, k_hi = valid;
+  if (a.window >= 0) {
+    k_lo = max(0, q0 - a.window) & ~15;  // 16-token aligned: the V^T copy's inner coordinate
+    k_hi = min(valid, q0 + kTcQ + a.window);
+  }
+  const int n_blocks = k_hi > k_lo ? (k_hi - k_lo + kTcKB - 1) / kTcKB : 0;
+
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + TcAttnSmem::kOffQ;
   uint8_t* sK = smem + TcAttnSmem::kOffK;
   uint8_t* sV = smem + TcAttnSmem::kOffV;
-  uint8_t* sP = smem + TcAttnSmem::kOffP;
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + TcAttnSmem::kOffBar);
   uint64_t* q_full = bar + 0;
-  uint64_t* k_full = bar + 1;
-  uint64_t* k_empty = bar + 2;
-  uint64_t* v_full = bar + 3;
-  uint64_t* v_empty = bar + 4;
-  uint64_t* s_full = bar + 5;
-  uint64_t* s_free = bar + 6;
-  uint64_t* p_full = bar + 7;
-  uint64_t* o_full = bar + 8;
-  uint64_t* drain = bar + 9;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 10);
+  uint64_t* k_full = bar + 1;   // [2]
+  uint64_t* k_empty = bar + 3;  // [2]
+  uint64_t* v_full = bar + 5;   // [2]
+  uint64_t* v_empty = bar + 7;  // [2]
+  uint64_t* s_full = bar + 9;
+  uint64_t* s_free = bar + 10;
+  uint64_t* p_full = bar + 11;
+  uint64_t* o_full = bar + 12;
+  uint64_t* drain = bar + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int head = blockIdx.y;
-  const int width = a.heads * 64;
-
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1); mbar_init(k_full, 1); mbar_init(k_empty, 1); mbar_init(v_full, 1);
-    mbar_init(v_empty, 1); mbar_init(s_full, 1); mbar_init(s_free, 4); mbar_init(p_full, 4);
-    mbar_init(o_full, 1); mbar_init(drain, 1);
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(k_full + s, 1); mbar_init(k_empty + s, 1); mbar_init(v_full + s, 1); mbar_init(v_empty + s, 1);
+    }
+    mbar_init(s_full, 1); mbar_init(s_free, 4); mbar_init(p_full, 4); mbar_init(o_full, 1); mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -91,54 +187,32 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
   pdl_trigger();
   pdl_wait();
 
-  const int4 tile = a.tiles[blockIdx.x];
-  const int t0 = tile.x, t1 = tile.y, row = tile.z;
-  T* out = reinterpret_cast<T*>(a.out);
-  int first = 0, valid = 0, q0 = 0, k_lo = 0, n_blocks = 0;
-  if (row >= 0) {
-    first = a.starts[row];
-    valid = a.lengths[row];
-    q0 = t0 - first;
-    int k_hi = valid;
-    if (a.window >= 0) {
-      k_lo = max(0, q0 - a.window);
-      k_hi = min(valid, q0 + kTcQ + a.window);
-    }
-    k_lo = (k_lo / kTcKB) * kTcKB;
-    n_blocks = k_hi > k_lo ? (k_hi - k_lo + kTcKB - 1) / kTcKB : 0;
-  }
-
-  if (row < 0 || n_blocks == 0) {
-    // Unused slot, or tokens past the last row: zeros (8 x 16 bytes per token and head).
-    if (row == -1) {
-      for (int i = threadIdx.x; i < (t1 - t0) * 8; i += kTcThreads) {
-        const int t = t0 + (i >> 3);
-        *reinterpret_cast<uint4*>(out + (size_t)t * width + head * 64 + (i & 7) * 8) = make_uint4(0, 0, 0, 0);
-      }
-    }
-  } else if (warp == 0) {
+  if (warp == 0) {
     if (lane == 0) {
       const int plane_rows = a.heads * a.M;
-      bool ok = true;
-      uint32_t k_inflight = 0, v_inflight = 0;  // 1 while a load has been issued but not consumed
+      int k_issued = 0, v_issued = 0;
       mbar_arrive_expect_tx(q_full, TcAttnSmem::kQ);
       tma_load_2d(sQ, &tmQK, q_full, 0, head * a.M + t0);
-      for (int j = 0; j < n_blocks && ok; ++j) {
+      for (int j = 0; j < n_blocks; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
         const int key0 = first + k_lo + j * kTcKB;  // absolute token of the block's first key
-        if (!mbar_wait(k_empty, (j & 1) ^ 1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
-        mbar_arrive_expect_tx(k_full, TcAttnSmem::kK);
-        tma_load_2d(sK, &tmQK, k_full, 0, plane_rows + head * a.M + key0);
-        k_inflight = 1;
-        if (!mbar_wait(v_empty, (j & 1) ^ 1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
-        mbar_arrive_expect_tx(v_full, TcAttnSmem::kV);
-        tma_load_2d(sV, &tmVt, v_full, key0, head * 64);
-        tma_load_2d(sV + 64 * 128, &tmVt, v_full, key0 + 64, head * 64);
-        v_inflight = 1;
+        if (!mbar_wait(k_empty + st, ph ^ 1, a.err, kErrAttnWait, abort_flag)) break;
+        mbar_arrive_expect_tx(k_full + st, TcAttnSmem::kK);
+        tma_load_2d(sK + st * TcAttnSmem::kK, &tmQK, k_full + st, 0, plane_rows + head * a.M + key0);
+        k_issued = j + 1;
+        if (!mbar_wait(v_empty + st, ph ^ 1, a.err, kErrAttnWait, abort_flag)) break;
+        mbar_arrive_expect_tx(v_full + st, TcAttnSmem::kV);
+        uint8_t* v = sV + st * TcAttnSmem::kV;
+        tma_load_2d(v, &tmVt, v_full + st, key0, head * 64);
+        tma_load_2d(v + 64 * 128, &tmVt, v_full + st, key0 + 64, head * 64);
+        v_issued = j + 1;
       }
-      if (!ok) {
-        // Let copies already in flight land before the CTA exits.
-        mbar_wait(q_full, 0, nullptr, 0, abort_flag);
-        (void)k_inflight; (void)v_inflight;
+      if (*abort_flag) {
+        // Let the copies already issued land before the CTA exits.
+        mbar_drain(q_full, 0);
+        for (int j = max(0, k_issued - 2); j < k_issued; ++j) mbar_drain(k_full + (j & 1), (j >> 1) & 1);
+        for (int j = max(0, v_issued - 2); j < v_issued; ++j) mbar_drain(v_full + (j & 1), (j >> 1) & 1);
       }
     }
   } else if (warp == 1) {
@@ -146,128 +220,154 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
       constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
       const uint32_t idesc_s = mma_idesc<bf>(kTcQ, kTcKB);
       const uint32_t idesc_o = mma_idesc<bf>(kTcQ, 64);
-      const uint32_t s_tmem = tmem_base, o_tmem = tmem_base + kTcKB;
-      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV), p_addr = smem_u32(sP);
+      const uint32_t s_tmem = tmem_base, p_tmem = tmem_base + 128, o_tmem = tmem_base + 192;
+      const uint32_t q_addr = smem_u32(sQ);
+      // O += P_i V_i once the softmax has written P_i and V_i has landed.
+      auto issue_pv = [&](int i) -> bool {
+        if (!mbar_wait(p_full, i & 1, a.err, kErrAttnWait, abort_flag)) return false;
+        if (!mbar_wait(v_full + (i & 1), (i >> 1) & 1, a.err, kErrAttnWait, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sV + (i & 1) * TcAttnSmem::kV);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          tc_mma_f16_ts(o_tmem, p_tmem + 8 * k, smem_desc_sw128(v_addr + (k >> 2) * 64 * 128 + (k & 3) * 32),
+                        idesc_o, (i | k) != 0);
+        tc_commit(o_full);
+        tc_commit(v_empty + (i & 1));
+        return true;
+      };
       bool ok = mbar_wait(q_full, 0, a.err, kErrAttnWait, abort_flag);
       for (int j = 0; j < n_blocks && ok; ++j) {
+        const int st = j & 1;
         // S_j = Q K_j^T once K_j has landed and the softmax has read S_{j-1}.
-        if (!mbar_wait(k_full, j & 1, a.err, kErrAttnWait, abort_flag)) break;
-        if (!mbar_wait(s_free, (j & 1) ^ 1, a.err, kErrAttnWait, abort_flag)) break;
+        if (!mbar_wait(k_full + st, (j >> 1) & 1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
+        if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
         tc_fence_after();
+        const uint32_t k_addr = smem_u32(sK + st * TcAttnSmem::kK);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           tc_mma_f16(s_tmem, smem_desc_sw128(q_addr + k * 32), smem_desc_sw128(k_addr + k * 32), idesc_s, k > 0);
         tc_commit(s_full);
-        tc_commit(k_empty);
-        // O_j = P_j V_j once the softmax has written P_j and V_j has landed.
-        if (!mbar_wait(p_full, j & 1, a.err, kErrAttnWait, abort_flag)) break;
-        if (!mbar_wait(v_full, j & 1, a.err, kErrAttnWait, abort_flag)) break;
-        tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            tc_mma_f16(o_tmem, smem_desc_sw128(p_addr + c * kTcQ * 128 + k * 32),
-                       smem_desc_sw128(v_addr + c * 64 * 128 + k * 32), idesc_o, (c | k) != 0);
-        tc_commit(o_full);
-        tc_commit(v_empty);
+        tc_commit(k_empty + st);
+        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
       }
+      if (ok && n_blocks > 0) issue_pv(n_blocks - 1);
+      // Every MMA issued by this thread completes before the TMEM is released.
       tc_commit(drain);
-      mbar_wait(drain, 0, nullptr, 0, abort_flag);
+      mbar_drain(drain, 0);
     }
   } else {
     // Softmax warps: thread <-> query row r (TMEM lane r).
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
-    const int q = q0 + r;                                 // row-relative query index
+    const int q = q0 + r;                  // row-relative query index of this thread
+    const int qa = q0 + quarter * 32;      // the warp's first query
     const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    const uint32_t s_tmem = tmem_base + lane_addr, o_tmem = tmem_base + lane_addr + kTcKB;
+    const uint32_t s_tmem = tmem_base + lane_addr, p_tmem = s_tmem + 128, o_tmem = s_tmem + 192;
     constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;
-    float m = -INFINITY, l = 0.f;
-    float acc[64];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) acc[i] = 0.f;
-    uint8_t* p_row0 = sP + r * 128;                       // P tile 0 (keys 0-63), row r
-    uint8_t* p_row1 = sP + kTcQ * 128 + r * 128;          // P tile 1 (keys 64-127), row r
+    // Keys this query may see: row-relative [lo_key, lo_key + span_keys]; an empty range (a
+    // padding query of a windowed layer) sees nothing.
+    int lo_key = a.window >= 0 ? q - a.window : 0;
+    const int hi_key = a.window >= 0 ? min(valid - 1, q + a.window) : valid - 1;
+    uint32_t span_keys = (uint32_t)(hi_key - lo_key);
+    if (hi_key < lo_key) { lo_key = 1 << 30; span_keys = 0; }
+    const bool warp_live = qa < valid;
+    float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_blocks && ok; ++j) {
+    for (int j = 0; j < n_blocks; ++j) {
       const int kb = k_lo + j * kTcKB;
-      if (!mbar_wait(s_full, j & 1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
+      ok = mbar_wait(s_full, j & 1, a.err, kErrAttnWait, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      // Pass 1: the row maximum over this block's visible keys.
-      float bm = -INFINITY;
-#pragma unroll 1
+      // Chunk c holds keys [kb + 32c, kb + 32c + 32).  vis bit c: some query of the warp sees a
+      // key of the chunk; full bit c: every query of the warp sees every key.  Warp-uniform.
+      uint32_t vis = 0, full = 0;
+#pragma unroll
       for (int c = 0; c < 4; ++c) {
-        float x[32];
-        tmem_ld32(s_tmem + c * 32, x);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int key = kb + c * 32 + i;
-          bool keep = key < valid;
-          if (a.window >= 0) keep = keep && abs(key - q) <= a.window;
-          if (keep) bm = fmaxf(bm, x[i] * kScaleLog2);
-        }
+        const int ck = kb + 32 * c;
+        if (warp_live && ck < valid && (a.window < 0 || (ck + 31 >= qa - a.window && ck <= qa + 31 + a.window)))
+          vis |= 1u << c;
+        if (ck + 31 < valid && (a.window < 0 || (ck >= qa + 31 - a.window && ck + 31 <= qa + a.window)))
+          full |= 1u << c;
       }
-      const float m_new = fmaxf(m, bm);
-      const float alpha = m_new == -INFINITY ? 1.f : exp2f(m - m_new);
-      const float sub = m_new == -INFINITY ? 0.f : m_new;
-      // Pass 2: probabilities, their sum, and P (16-bit, 128-byte swizzled rows) in smem.
-      float sum = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        float x[32];
-        tmem_ld32(s_tmem + c * 32, x);
-        uint32_t pk[16];
+      full &= vis;
+      uint32_t sx[4][32];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float p2[2];
+      for (int c = 0; c < 4; ++c)
+        if ((vis >> c) & 1) tmem_ld32_async(s_tmem + 32 * c, sx[c]);
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int key = kb + c * 32 + i + e;
-            bool keep = key < valid;
-            if (a.window >= 0) keep = keep && abs(key - q) <= a.window;
-            p2[e] = keep ? exp2f(x[i + e] * kScaleLog2 - sub) : 0.f;
-            sum += p2[e];
-          }
-          pk[i / 2] = pack2<T>(p2[0], p2[1]);
-        }
-        uint8_t* prow = (c < 2) ? p_row0 : p_row1;
-#pragma unroll
-        for (int piece = 0; piece < 4; ++piece) {
-          const int logical = (c & 1) * 4 + piece;      // 16-byte piece within the 128-byte row
-          const int phys = logical ^ (r & 7);
-          *reinterpret_cast<uint4*>(prow + phys * 16) =
-              make_uint4(pk[piece * 4], pk[piece * 4 + 1], pk[piece * 4 + 2], pk[piece * 4 + 3]);
-        }
-      }
+      for (int c = 0; c < 4; ++c)
+        if ((vis >> c) & 1) tmem_wait_ld(sx[c]);
       tc_fence_before();
-      fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) { mbar_arrive(s_free); mbar_arrive(p_full); }
-      l = l * alpha + sum;
-      m = m_new;
-      if (!mbar_wait(o_full, j & 1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        float o[32];
-        tmem_ld32(o_tmem + h * 32, o);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) acc[h * 32 + i] = acc[h * 32 + i] * alpha + o[i];
+      if (lane == 0) mbar_arrive(s_free);
+      const bool all = full == 0xFu;
+      const float bmax = all ? tc_block_max<true>(sx, vis, full, kb, lo_key, span_keys)
+                             : tc_block_max<false>(sx, vis, full, kb, lo_key, span_keys);
+      const float m_new = bmax * kScaleLog2;
+      float alpha = 1.f;
+      bool o_dirty = false;
+      if (m_new > m_used + kTcRescaleLog2) {  // false while every visible key is masked
+        if (m_used != -INFINITY) { alpha = ex2_approx(m_used - m_new); o_dirty = true; }
+        m_used = m_new;
       }
+      const float sub = m_used == -INFINITY ? 0.f : m_used;
+      // P_j overwrites P_{j-1}: wait for the previous P V product.
+      if (j > 0) {
+        ok = mbar_wait(o_full, (j - 1) & 1, a.err, kErrAttnWait, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        tc_fence_after();
+      }
+      const float sum = all ? tc_block_probs<true, T>(sx, vis, kScaleLog2, sub, p_tmem)
+                            : tc_block_probs<false, T>(sx, vis, kScaleLog2, sub, p_tmem);
+      l = l * alpha + sum;
+      // Rows whose maximum grew by more than 2^8 rescale O before P_j V_j accumulates into it.
+      if (__any_sync(0xffffffffu, o_dirty)) {
+#pragma unroll 1
+        for (int h = 0; h < 2; ++h) {
+          uint32_t o[32];
+          tmem_ld32_async(o_tmem + 32 * h, o);
+          tmem_wait_ld(o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(o_tmem + 32 * h, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
     }
     // Normalise and store this row (zeros for padding queries); rows past the tile belong to
     // other tiles and are not written.
-    const int token = t0 + r;
-    if (token < t1) {
-      const float inv = (ok && q < valid && l > 0.f) ? 1.f / l : 0.f;
-      T* dst = out + (size_t)token * width + head * 64;
+    if (ok && n_blocks > 0) {
+      ok = mbar_wait(o_full, (n_blocks - 1) & 1, a.err, kErrAttnWait, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok) {
+      const int token = t0 + r;
+      uint32_t o[2][32];
+      tc_fence_after();
+      tmem_ld32_async(o_tmem, o[0]);
+      tmem_ld32_async(o_tmem + 32, o[1]);
+      tmem_wait_ld(o[0]);
+      tmem_wait_ld(o[1]);
+      if (token < t1) {
+        const bool live = n_blocks > 0 && q < valid && l > 0.f;
+        const float inv = live ? 1.f / l : 0.f;
+        T* dst = out + (size_t)token * width + head * 64;
 #pragma unroll
-      for (int i = 0; i < 64; i += 8) {
-        uint4 w;
-        w.x = pack2<T>(acc[i] * inv, acc[i + 1] * inv); w.y = pack2<T>(acc[i + 2] * inv, acc[i + 3] * inv);
-        w.z = pack2<T>(acc[i + 4] * inv, acc[i + 5] * inv); w.w = pack2<T>(acc[i + 6] * inv, acc[i + 7] * inv);
-        *reinterpret_cast<uint4*>(dst + i) = w;
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] = live ? __uint_as_float(o[h][i + e]) * inv : 0.f;
+            uint4 w;
+            w.x = pack2<T>(v[0], v[1]); w.y = pack2<T>(v[2], v[3]);
+            w.z = pack2<T>(v[4], v[5]); w.w = pack2<T>(v[6], v[7]);
+            *reinterpret_cast<uint4*>(dst + h * 32 + i) = w;
+          }
       }
     }
   }

@@ -77,6 +77,22 @@ def test_laya_geometry_matches_fp32_oracle(laya_ckpt, precision):
     assert max(r["logit"] for r in rows) <= (0.02 if precision == "bfloat16" else 0.005)
 
 
+def test_mma_sync_attention_forward_matches_fp32_oracle(laya_ckpt, monkeypatch):
+    """The forward pass with the mma.sync attention kernel (LAYA_ATTENTION=mma_sync) instead of
+    the default tcgen05 kernel meets the same parity bar."""
+    path, arch, weights = laya_ckpt
+    oracle = Oracle(weights, arch)
+    rng = np.random.default_rng(2)
+    items = [S.build_item(rng, n, k, arch["vocab"], kind=j % 3) for j, (n, k) in
+             enumerate([(83, 4), (512, 8), (300, 5), (129, 2)])]
+    monkeypatch.setenv("LAYA_ATTENTION", "mma_sync")
+    with Engine(path) as engine:
+        rows = compare(engine, oracle, items)
+    assert max(r["prob"] for r in rows) <= 2e-3
+    assert max(r["act"] for r in rows) <= 2e-3
+    assert max(r["logit"] for r in rows) <= 0.005
+
+
 @pytest.mark.parametrize("precision", ["bfloat16", "float16"])
 def test_decisive_checkpoint_argmax_and_probabilities(peaky_ckpt, precision):
     path, arch, weights = peaky_ckpt

@@ -213,10 +213,29 @@ def packed_case(lengths):
 @pytest.mark.parametrize("prec,impl,split_p", [("bf16", 0, 0), ("bf16", 0, 1), ("f16", 0, 1), ("f16", 1, 0),
                                                ("bf16", 1, 0)])
 @pytest.mark.parametrize("lengths,window", [([32], -1), ([7, 96], 64), ([128, 1], -1), ([250, 131], 64),
-                                            ([256, 219, 145], -1), ([500], 64), ([1024, 333], -1)])
+                                            ([256, 219, 145], -1), ([500], 64), ([1024, 333], -1), ([300, 77], 40)])
 def test_packed_attention_matches_oracle(lib, prec, impl, split_p, lengths, window):
     """Cases and float64 oracle of tests/test_attention.py:12-56 (h=2, seeded by M), for the
     mma.sync kernel (impl 0, 64-query tiles) and the tcgen05 kernel (impl 1, 128-query tiles)."""
+    check_packed_attention(lib, prec, impl, split_p, lengths, window, ramp=False)
+
+
+@pytest.mark.parametrize("prec,impl", [("f16", 0), ("f16", 1), ("bf16", 1)])
+@pytest.mark.parametrize("lengths,window", [([1024, 333], -1), ([700], 64), ([513, 200], -1)])
+def test_packed_attention_growing_scores(lib, prec, impl, lengths, window):
+    """Scores that grow along the row (keys scaled up with position), so the running maximum
+    rises by far more than 2^8 between key blocks: exercises the rescaling of O."""
+    check_packed_attention(lib, prec, impl, 0, lengths, window, ramp=True)
+
+
+# Worst |error| - 16-bit output rounding, by (precision, split_p): probability rounding (split_p
+# keeps fp32-level probabilities).  Scores that grow along the row concentrate the softmax on a
+# few keys, so one rounded bf16 probability weighs more.
+ATTN_LIMIT = {("bf16", 0): 6e-3, ("bf16", 1): 1.5e-3, ("f16", 1): 6e-4, ("f16", 0): 1.5e-3}
+ATTN_LIMIT_RAMP = {("bf16", 0): 1e-2, ("f16", 0): 1.5e-3}
+
+
+def check_packed_attention(lib, prec, impl, split_p, lengths, window, ramp):
     h = 2
     tile_q = 64 if impl == 0 else 128
     starts, lens, M = packed_case(lengths)
@@ -226,6 +245,10 @@ def test_packed_attention_matches_oracle(lib, prec, impl, split_p, lengths, wind
                                        tiles.ctypes.data, cap)
     assert n_tiles > 0
     x = np.random.default_rng(M).normal(0, 1, (M, 3, h, 64)).astype(np.float32)
+    if ramp:
+        for start, n in zip(starts, lengths):
+            x[start:start + n, 0] *= 2.0
+            x[start:start + n, 1] *= (1.0 + np.arange(n, dtype=np.float32) / 64.0)[:, None, None]
     xt = torch.from_numpy(x).to(PRECISIONS[prec][1])
     xd = xt.double().numpy()
     layout = xt.permute(1, 2, 0, 3).contiguous()                  # [3][h][M][64]
@@ -252,8 +275,7 @@ def test_packed_attention_matches_oracle(lib, prec, impl, split_p, lengths, wind
         expected = (p @ v).transpose(1, 0, 2).reshape(n, h * 64)
         err_ = np.abs(got[start:start + n] - expected) - ROUND[prec] * np.abs(expected)
         worst = max(worst, float(err_.max()))
-    # 16-bit output rounding plus probability rounding (split_p keeps fp32-level probabilities).
-    limit = {("bf16", 0): 6e-3, ("bf16", 1): 1.5e-3, ("f16", 1): 6e-4, ("f16", 0): 1.5e-3}[(prec, split_p)]
+    limit = (ATTN_LIMIT_RAMP if ramp else ATTN_LIMIT)[(prec, split_p)]
     assert worst < limit, worst
     np.testing.assert_array_equal(got[~real], 0)
 
