@@ -173,8 +173,18 @@ int laya_op_attention(int precision, int impl, const void* qkv, void* out, const
                       const int32_t* starts, const int32_t* lengths, int M, int heads, int window, int split_p,
                       int* err, void* stream);
 
+/* Global attention for gathered queries only (the decision head's last layer,
+ * laya.py:214-245 followed by the gather of kernels.cu:159-166): row r attends from the tokens
+ * q_index[r*q_per_row .. +q_per_row) (token indices into the packed rows, duplicates allowed)
+ * to every key of the row; only those rows of `out` are written.  Rows with length 0 are
+ * skipped.  Layouts as laya_op_attention; tcgen05 kernel. */
+int laya_op_attention_gathered(int precision, const void* qkv, void* out, const int32_t* q_index, int q_per_row,
+                               const int32_t* starts, const int32_t* lengths, int n_rows, int M, int heads, int* err,
+                               void* stream);
+
 /* Builds the attention tile table (tile_q = 64 or 128) for rows packed at `starts` with
- * `lengths` into M tokens.  Returns the number of tiles written (<= capacity) or -1. */
+ * `lengths` into M tokens, rows longest first, then zero-fill tiles for tokens past the last
+ * row, then unused slots.  Returns the number of tiles written (<= capacity) or -1. */
 int laya_attention_tiles(const int32_t* starts, const int32_t* lengths, int n_rows, int M, int tile_q,
                          int32_t* tiles, int capacity);
 

@@ -81,8 +81,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
 
   pdl_trigger();
   pdl_wait();
-  const int4 tile = a.tiles[blockIdx.x];
-  const int head = blockIdx.y;
+  const int4 tile = a.tiles[blockIdx.y];  // grid: (heads, tiles), all heads of a tile together
+  const int head = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = tile.x, t1 = tile.y, row = tile.z;
   const int width = a.heads * 64;

@@ -287,12 +287,14 @@ void launch_tc_attention(const CUtensorMap& qk, const CUtensorMap& vt, const TcA
     CK(cudaFuncSetAttribute(tc_attention_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcAttnSmem::kBytes));
     configured |= 1ull << dev;
   }
-  launch_k(tc_attention_kernel<T>, dim3(n_tiles, a.heads), dim3(kTcThreads), TcAttnSmem::kBytes, st, qk, vt, a);
+  if (n_tiles > 65535) fail(LAYA_ERR_INVALID, "%d attention tiles exceed the grid limit", n_tiles);
+  launch_k(tc_attention_kernel<T>, dim3(a.heads, n_tiles), dim3(kTcThreads), TcAttnSmem::kBytes, st, qk, vt, a);
 }
 
 template <typename T>
 void launch_attention(const AttnArgs& a, int n_tiles, bool split_p, cudaStream_t st) {
-  dim3 grid(n_tiles, a.heads);
+  if (n_tiles > 65535) fail(LAYA_ERR_INVALID, "%d attention tiles exceed the grid limit", n_tiles);
+  dim3 grid(a.heads, n_tiles);
   if (split_p) launch_k(attention_kernel<T, true>, grid, dim3(kAttnThreads), 0, st, a);
   else launch_k(attention_kernel<T, false>, grid, dim3(kAttnThreads), 0, st, a);
 }
@@ -390,7 +392,13 @@ int build_tiles(const int32_t* starts, const int32_t* lengths, int n_rows, int M
     ++t;
     return true;
   };
-  for (int r = 0; r < n_rows; ++r) {
+  // Rows longest first: the attention grid runs tiles in table order (all heads of a tile
+  // together), so the longest global-attention tiles start first and the short ones fill the
+  // last wave.
+  std::vector<int> order(n_rows);
+  for (int r = 0; r < n_rows; ++r) order[r] = r;
+  std::stable_sort(order.begin(), order.end(), [&](int x, int y) { return lengths[x] > lengths[y]; });
+  for (int r : order) {
     const int s = starts[r], sp = span16(lengths[r]);
     for (int q = 0; q < sp; q += tile_q)
       if (!put(s + q, std::min(s + q + tile_q, s + sp), r)) return -1;
@@ -871,12 +879,19 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
   });
   (void)rowbytes;
 
-  auto attention = [&](int window) {
+  // gathered: only the rows gather_rows_kernel reads (each question's CLS and marker tokens)
+  // attend; the other rows of `attn` are left as they are (global attention only).
+  auto attention = [&](int window, bool gathered) {
     if (e.tc_attention) {
       TcAttnArgs a{};
-      a.out = attn; a.tiles = tiles128; a.starts = starts; a.lengths = lengths;
+      a.qk = qkv; a.out = attn; a.tiles = tiles128; a.starts = starts; a.lengths = lengths;
       a.M = m; a.heads = c.heads; a.window = window; a.err = err;
-      launch(e, prof, FAM_ATTENTION, 0, [&] { launch_tc_attention<T>(s.map_qk, s.map_vt, a, L.tiles128, e.stream); });
+      int n_tiles = L.tiles128;
+      if (gathered) {
+        a.q_index = indices; a.q_per_row = L.k + 1; a.q_tiles = (L.k + 1 + kTcQ - 1) / kTcQ;
+        n_tiles = L.b * a.q_tiles;
+      }
+      launch(e, prof, FAM_ATTENTION, 0, [&] { launch_tc_attention<T>(s.map_qk, s.map_vt, a, n_tiles, e.stream); });
     } else {
       AttnArgs a{};
       a.qkv = qkv; a.out = attn; a.tiles = tiles64; a.starts = starts; a.lengths = lengths;
@@ -915,7 +930,7 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
     const std::string p = "encoder.layers." + std::to_string(i) + ".";
     const bool local = i % c.global_every != 0;
     gemm<T>(e, prof, FAM_GEMM_QKV, EPI_QKV, s.map_x, p + "attn.Wqkv.weight", m, qkv, 0, nullptr, 0, nullptr, err, local ? 1 : 0, positions);
-    attention(local ? c.window : -1);
+    attention(local ? c.window : -1, false);
     Pending pend = residual_gemm(FAM_GEMM_ATTN_OUT, s.map_attn, p + "attn.Wo.weight", m, residual, nullptr);
     norm(residual, m, Wf(e, p + "mlp_norm.weight"), nullptr, c.eps, x, pend);
     gemm<T>(e, prof, FAM_GEMM_FFN_UP, EPI_GEGLU, s.map_x, p + "mlp.Wi.weight", m, ff, e.F(), nullptr, 0, nullptr, err);
@@ -941,7 +956,8 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
     if (i > 0) norm(residual, m, Wf(e, p + "norm1.weight"), Wf(e, p + "norm1.bias"), 1e-5f, x, Pending{});
     gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_QKV, s.map_x, p + "self_attn.in_proj_weight", m, qkv, 0, nullptr, 0,
             Wf(e, p + "self_attn.in_proj_bias"), err);
-    attention(-1);
+    // The last head layer only needs the attention rows that are gathered next.
+    attention(-1, i + 1 == c.head_layers);
     if (i + 1 == c.head_layers) {
       launch(e, prof, FAM_ROWS, 0, [&] {
         launch_k(gather_rows_kernel<T>, dim3(count), dim3(256), 0, e.stream, (const float*)residual, (const T*)attn,
@@ -1458,7 +1474,7 @@ int laya_op_attention(int precision, int impl, const void* qkv, void* out, const
     const CUtensorMap qk = make_map(qkv, 3 * hm, 64, kTcQ, bf);
     const CUtensorMap vt = make_map(static_cast<const uint8_t*>(qkv) + (size_t)2 * hm * 64 * 2, (int64_t)heads * 64, M, 64, bf);
     TcAttnArgs t{};
-    t.out = out; t.tiles = reinterpret_cast<const int4*>(tiles); t.starts = starts; t.lengths = lengths;
+    t.qk = qkv; t.out = out; t.tiles = reinterpret_cast<const int4*>(tiles); t.starts = starts; t.lengths = lengths;
     t.M = M; t.heads = heads; t.window = window; t.err = err;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (bf) launch_tc_attention<__nv_bfloat16>(qk, vt, t, n_tiles, st);
@@ -1471,6 +1487,25 @@ int laya_op_attention(int precision, int impl, const void* qkv, void* out, const
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (precision == LAYA_PRECISION_BF16) launch_attention<__nv_bfloat16>(a, n_tiles, split_p != 0, st);
   else launch_attention<__half>(a, n_tiles, split_p != 0, st);
+  API_END(nullptr)
+}
+
+int laya_op_attention_gathered(int precision, const void* qkv, void* out, const int32_t* q_index, int q_per_row,
+                               const int32_t* starts, const int32_t* lengths, int n_rows, int M, int heads, int* err,
+                               void* stream) {
+  API_BEGIN
+  if (q_per_row <= 0 || n_rows <= 0) fail(LAYA_ERR_INVALID, "gathered attention needs rows and queries");
+  const bool bf = precision == LAYA_PRECISION_BF16;
+  const int64_t hm = (int64_t)heads * M;
+  const CUtensorMap qk = make_map(qkv, 3 * hm, 64, kTcQ, bf);
+  const CUtensorMap vt = make_map(static_cast<const uint8_t*>(qkv) + (size_t)2 * hm * 64 * 2, (int64_t)heads * 64, M, 64, bf);
+  TcAttnArgs t{};
+  t.qk = qkv; t.out = out; t.starts = starts; t.lengths = lengths;
+  t.M = M; t.heads = heads; t.window = -1; t.err = err;
+  t.q_index = q_index; t.q_per_row = q_per_row; t.q_tiles = (q_per_row + kTcQ - 1) / kTcQ;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (bf) launch_tc_attention<__nv_bfloat16>(qk, vt, t, n_rows * t.q_tiles, st);
+  else launch_tc_attention<__half>(qk, vt, t, n_rows * t.q_tiles, st);
   API_END(nullptr)
 }
 

@@ -38,6 +38,7 @@ constexpr int kTcTmemCols = 256;       // S: [0,128), P: [128,192), O: [192,256)
 constexpr float kTcRescaleLog2 = 8.f;  // O is rescaled when the row maximum grows by more than 2^8
 
 struct TcAttnArgs {
+  const void* qk;       // q, k: [heads][M][64] each (read directly only for gathered queries)
   void* out;            // [M][heads*64]
   const int4* tiles;    // (t0, t1, row, 0): 128-query tiles; row -1: zero-fill; row -2: unused
   const int* starts;
@@ -46,6 +47,12 @@ struct TcAttnArgs {
   int heads;
   int window;           // -1: global
   int* err;
+  // Gathered queries (global attention only): when q_index is set, tile y of the grid is part
+  // y % q_tiles of row y / q_tiles, whose queries are the tokens q_index[row * q_per_row + i]
+  // (the decision head's CLS and marker rows); `tiles` is unused and rows of length 0 are skipped.
+  const int* q_index;
+  int q_per_row;
+  int q_tiles;
 };
 
 struct TcAttnSmem {
@@ -124,10 +131,22 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // The tile table, starts and lengths are written by the host before the forward pass, so they
   // are read before waiting on the previous kernel.
-  const int4 tile = a.tiles[blockIdx.x];
-  const int t0 = tile.x, t1 = tile.y, row = tile.z;
-  if (row == -2) return;
-  const int head = blockIdx.y;
+  const bool gathered = a.q_index != nullptr;
+  int t0, t1, row, nq = kTcQ;  // nq: queries of a gathered tile
+  const int* qidx = nullptr;
+  if (gathered) {
+    row = blockIdx.y / a.q_tiles;
+    const int part = blockIdx.y - row * a.q_tiles;
+    nq = min(kTcQ, a.q_per_row - part * kTcQ);
+    qidx = a.q_index + (size_t)row * a.q_per_row + part * kTcQ;
+    t0 = t1 = 0;
+    if (a.lengths[row] == 0) return;  // unused row of the shape class
+  } else {
+    const int4 tile = a.tiles[blockIdx.y];  // grid: (heads, tiles), all heads of a tile together
+    t0 = tile.x; t1 = tile.y; row = tile.z;
+    if (row == -2) return;
+  }
+  const int head = blockIdx.x;
   const int width = a.heads * 64;
   T* out = reinterpret_cast<T*>(a.out);
   if (row < 0) {
@@ -142,7 +161,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
   }
   const int first = a.starts[row];
   const int valid = a.lengths[row];
-  const int q0 = t0 - first;  // row-relative index of the tile's first query
+  const int q0 = gathered ? 0 : t0 - first;  // row-relative index of the tile's first query
   int k_lo = 0, k_hi = valid;
   if (a.window >= 0) {
     k_lo = max(0, q0 - a.window) & ~15;  // 16-token aligned: the V^T copy's inner coordinate
@@ -170,7 +189,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
+    mbar_init(q_full, gathered ? 4 : 1);  // gathered: the four softmax warps write Q
     for (int s = 0; s < 2; ++s) {
       mbar_init(k_full + s, 1); mbar_init(k_empty + s, 1); mbar_init(v_full + s, 1); mbar_init(v_empty + s, 1);
     }
@@ -191,8 +210,10 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
     if (lane == 0) {
       const int plane_rows = a.heads * a.M;
       int k_issued = 0, v_issued = 0;
-      mbar_arrive_expect_tx(q_full, TcAttnSmem::kQ);
-      tma_load_2d(sQ, &tmQK, q_full, 0, head * a.M + t0);
+      if (!gathered) {
+        mbar_arrive_expect_tx(q_full, TcAttnSmem::kQ);
+        tma_load_2d(sQ, &tmQK, q_full, 0, head * a.M + t0);
+      }
       for (int j = 0; j < n_blocks; ++j) {
         const int st = j & 1;
         const uint32_t ph = (j >> 1) & 1;
@@ -210,7 +231,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
       }
       if (*abort_flag) {
         // Let the copies already issued land before the CTA exits.
-        mbar_drain(q_full, 0);
+        if (!gathered) mbar_drain(q_full, 0);
         for (int j = max(0, k_issued - 2); j < k_issued; ++j) mbar_drain(k_full + (j & 1), (j >> 1) & 1);
         for (int j = max(0, v_issued - 2); j < v_issued; ++j) mbar_drain(v_full + (j & 1), (j >> 1) & 1);
       }
@@ -271,7 +292,20 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
     const int hi_key = a.window >= 0 ? min(valid - 1, q + a.window) : valid - 1;
     uint32_t span_keys = (uint32_t)(hi_key - lo_key);
     if (hi_key < lo_key) { lo_key = 1 << 30; span_keys = 0; }
-    const bool warp_live = qa < valid;
+    const bool warp_live = gathered ? quarter * 32 < nq : qa < valid;
+    if (gathered) {
+      // Q row r <- token qidx[r] (zeros past nq), written in the 128-byte swizzled K-major layout
+      // the TMA would produce, then handed to the async proxy.
+      const T* qsrc = reinterpret_cast<const T*>(a.qk) + ((size_t)head * a.M + (r < nq ? qidx[r] : 0)) * 64;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint4 v = r < nq ? *reinterpret_cast<const uint4*>(qsrc + c * 8) : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(sQ + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_full);
+    }
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_blocks; ++j) {
@@ -345,15 +379,15 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
       ok = __all_sync(0xffffffffu, ok);
     }
     if (ok) {
-      const int token = t0 + r;
+      const int token = gathered ? (r < nq ? qidx[r] : -1) : t0 + r;
       uint32_t o[2][32];
       tc_fence_after();
       tmem_ld32_async(o_tmem, o[0]);
       tmem_ld32_async(o_tmem + 32, o[1]);
       tmem_wait_ld(o[0]);
       tmem_wait_ld(o[1]);
-      if (token < t1) {
-        const bool live = n_blocks > 0 && q < valid && l > 0.f;
+      if (gathered ? token >= 0 : token < t1) {
+        const bool live = n_blocks > 0 && (gathered || q < valid) && l > 0.f;
         const float inv = live ? 1.f / l : 0.f;
         T* dst = out + (size_t)token * width + head * 64;
 #pragma unroll

@@ -18,7 +18,7 @@ EXPORTS = (
     "laya_create", "laya_load_tensor", "laya_finalize", "laya_predict", "laya_shape_class",
     "laya_forward_device", "laya_packed_ints", "laya_pack", "laya_reserve", "laya_stream", "laya_set_profiling",
     "laya_profile_read", "laya_read_tensor", "laya_cached_shapes", "laya_pool_bytes", "laya_destroy",
-    "laya_last_error", "laya_op_gemm", "laya_interleave_geglu", "laya_op_attention",
+    "laya_last_error", "laya_op_gemm", "laya_interleave_geglu", "laya_op_attention", "laya_op_attention_gathered",
     "laya_attention_tiles", "laya_op_embed_norm", "laya_op_norm", "laya_op_gemm_residual_static",
 )
 STATIC_SCRATCH_FLOATS = 4 * 1024 * 1024
@@ -72,6 +72,7 @@ def load():
         "laya_op_gemm": (i, [i, i, p, p, i, i, i, p, i, p, i, p, i, p, p, i, p, i, i, p, p]),
         "laya_interleave_geglu": (i, [p, p, i, i]),
         "laya_op_attention": (i, [i, i, p, p, p, i, p, p, i, i, i, i, p, p]),
+        "laya_op_attention_gathered": (i, [i, p, p, p, i, p, p, i, i, i, p, p]),
         "laya_attention_tiles": (i, [p, p, i, i, i, p, i]),
         "laya_op_embed_norm": (i, [i, p, p, p, ct.c_float, i, i, i, p, p, p, p]),
         "laya_op_norm": (i, [i, p, p, i, p, p, ct.c_float, p, i, i, p]),

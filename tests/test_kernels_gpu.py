@@ -326,3 +326,53 @@ def test_norm_residual_partials(lib, prec, width, splits, beta):
         expected = expected + b
     got = x.cpu().double().numpy()
     assert np.max(np.abs(got - expected) - ROUND[prec] * np.abs(expected)) < 1e-4
+
+
+@pytest.mark.parametrize("prec", ["f16", "bf16"])
+@pytest.mark.parametrize("lengths,q_per_row", [([300, 77, 1024], 9), ([129], 1), ([700, 40], 130)])
+def test_gathered_query_attention_matches_oracle(lib, prec, lengths, q_per_row):
+    """Global attention from gathered query rows only (CLS + markers of the decision head, with
+    duplicate indices as packing pads them): those rows match the float64 oracle, every other
+    row of the output is left untouched, and an unused (length-0) row is skipped."""
+    h = 2
+    starts, lens, M = packed_case(lengths)
+    starts = np.append(starts, 0).astype(np.int32)
+    lens = np.append(lens, 0).astype(np.int32)                       # unused row of the class
+    rng = np.random.default_rng(M + q_per_row)
+    index = np.zeros((len(lens), q_per_row), np.int32)
+    for r, (s0, n) in enumerate(zip(starts, lens)):
+        if n:
+            picks = rng.integers(0, n, q_per_row)
+            picks[0] = 0
+            picks[-1] = 0 if q_per_row > 1 else picks[-1]             # duplicate of the CLS row
+            index[r] = s0 + picks
+    x = rng.normal(0, 1, (M, 3, h, 64)).astype(np.float32)
+    xt = torch.from_numpy(x).to(PRECISIONS[prec][1])
+    xd = xt.double().numpy()
+    layout = xt.permute(1, 2, 0, 3).contiguous()
+    layout[2] = layout[2].transpose(1, 2).reshape(h, M, 64)
+    layout = layout.cuda()
+    out = torch.full((M, h * 64), 7.0, dtype=PRECISIONS[prec][1], device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    dev = [torch.from_numpy(np.ascontiguousarray(v)).cuda() for v in (index, starts, lens)]
+    _lib.check(lib.laya_op_attention_gathered(PRECISIONS[prec][0], ptr(layout), ptr(out), ptr(dev[0]), q_per_row,
+                                              ptr(dev[1]), ptr(dev[2]), len(lens), M, h, ptr(err), stream()))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    got = out.double().cpu().numpy()
+    written = np.zeros(M, bool)
+    worst = 0.0
+    for r, (s0, n) in enumerate(zip(starts, lens)):
+        if not n:
+            continue
+        q, k, v = xd[s0:s0 + n].transpose(1, 2, 0, 3)
+        s = q @ k.transpose(0, 2, 1) / 8
+        p = np.exp(s - s.max(-1, keepdims=True))
+        p /= p.sum(-1, keepdims=True)
+        expected = (p @ v).transpose(1, 0, 2).reshape(n, h * 64)
+        for t in index[r]:
+            written[t] = True
+            e = expected[t - s0]
+            worst = max(worst, float(np.max(np.abs(got[t] - e) - ROUND[prec] * np.abs(e))))
+    assert worst < ATTN_LIMIT[(prec, 0)], worst
+    np.testing.assert_array_equal(got[~written], 7.0)

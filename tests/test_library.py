@@ -103,6 +103,11 @@ def test_pack_matches_reference_fill(lib, seed):
         tiles = out[o:o + 4 * cap].reshape(-1, 4)
         o += 4 * cap
         cover = np.zeros(m, np.int32)
+        # Order: row tiles with rows longest first, then zero-fill tiles, then unused slots.
+        kinds = [0 if row >= 0 else 1 if row == -1 else 2 for row in tiles[:, 2]]
+        assert kinds == sorted(kinds)
+        row_lengths = [want[5][row] for row in tiles[:, 2] if row >= 0]
+        assert row_lengths == sorted(row_lengths, reverse=True)
         for t0, t1, row, _ in tiles:
             if row == -2:
                 continue
