@@ -57,6 +57,13 @@ constexpr int kBK = 64;
 constexpr int kGemmThreads = 320;
 constexpr int kEpiWarps = 8;
 
+// Per epilogue warp: a [32 rows][128 B] staging block in shared memory.  The warp's lanes own
+// one tile row each (the TMEM lane layout); global memory is accessed through the block in the
+// transposed mapping (lane -> row 4k + lane/8, 16-byte piece lane%8 for k = 0..7), so every
+// warp-wide global access covers four whole 128-byte lines instead of 32 partial ones.
+constexpr int kEpiStageBytes = 32 * 128;
+constexpr int kEpiSmemBytes = kEpiWarps * kEpiStageBytes;
+
 template <int BN>
 struct GemmCfg {
   static constexpr int kStageA = kBM * kBK * 2;
@@ -64,123 +71,128 @@ struct GemmCfg {
   static constexpr int kStageBytes = kStageA + kStageB;
   static constexpr int kStages = (192 * 1024) / kStageBytes;
   static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kOffEpi = kStages * kStageBytes;
+  static constexpr int kSmemBytes = kOffEpi + kEpiSmemBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
-template <typename T, int EPI>
-__device__ __forceinline__ void epi_store_chunk(const GemmArgs& a, int row, int col, const float (&v)[32]) {
-  T* out = reinterpret_cast<T*>(a.out) + (size_t)row * a.ldo + col;
-  float b[32];
+// Byte offset of 16-byte piece j of row r in a staging block (pieces XOR-swizzled by row, so both
+// the row-per-lane writes and the transposed reads are free of bank conflicts).
+__device__ __forceinline__ uint32_t stage_off(int r, int j) { return (uint32_t)(r * 128 + ((j ^ (r & 7)) << 4)); }
+
+// Lane `lane` writes its row (8 pieces) into the block; the previous contents must be consumed.
+__device__ __forceinline__ void stage_put(uint8_t* buf, int lane, const uint4 (&p)[8]) {
+  __syncwarp();
 #pragma unroll
-  for (int i = 0; i < 32; ++i) b[i] = 0.f;
-  if (a.bias) {
+  for (int j = 0; j < 8; ++j) *reinterpret_cast<uint4*>(buf + stage_off(lane, j)) = p[j];
+  __syncwarp();
+}
+
+// Piece (row 4k + lane/8, lane%8) of the block.
+__device__ __forceinline__ uint4 stage_get(const uint8_t* buf, int k, int lane) {
+  return *reinterpret_cast<const uint4*>(buf + stage_off(4 * k + (lane >> 3), lane & 7));
+}
+
+__device__ __forceinline__ uint4 u4(float a, float b, float c, float d) {
+  return make_uint4(__float_as_uint(a), __float_as_uint(b), __float_as_uint(c), __float_as_uint(d));
+}
+__device__ __forceinline__ float4 f4(uint4 v) {
+  return make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w));
+}
+
+// Writes a staged block of 16-bit rows (64 elements each) to dst_row(r) for tile rows r < rows.
+template <typename RowPtr>
+__device__ __forceinline__ void stage_store16(const uint8_t* buf, int lane, int rows, RowPtr dst_row) {
 #pragma unroll
-    for (int i = 0; i < 32; i += 4) {
-      float4 t = *reinterpret_cast<const float4*>(a.bias + col + i);
-      b[i] = t.x; b[i + 1] = t.y; b[i + 2] = t.z; b[i + 3] = t.w;
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < 32; i += 8) {
-    float x[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float t = v[i + j] + b[i + j];
-      if (EPI == EPI_RELU) t = fmaxf(t, 0.f);
-      if (EPI == EPI_GELU) t = gelu_erf(t);
-      x[j] = t;
-    }
-    uint4 w;
-    w.x = pack2<T>(x[0], x[1]); w.y = pack2<T>(x[2], x[3]);
-    w.z = pack2<T>(x[4], x[5]); w.w = pack2<T>(x[6], x[7]);
-    *reinterpret_cast<uint4*>(out + i) = w;
+  for (int k = 0; k < 8; ++k) {
+    const int r = 4 * k + (lane >> 3);
+    if (r < rows) *reinterpret_cast<uint4*>(dst_row(r) + (lane & 7) * 8) = stage_get(buf, k, lane);
   }
 }
 
-// Residual epilogue (residual[row, n0 + ...] += accumulator + bias), software-pipelined: a
-// thread's residual chunks (every other 32-column chunk of its row) are loaded two ahead, the
-// first two before the accumulator is waited on, so the fp32 read latency overlaps the tile's
-// MMAs and the previous chunk's adds instead of following each TMEM load.
+// Residual epilogue (residual[row, n0 + ...] += accumulator + bias), software-pipelined: a warp's
+// residual chunks (32 rows x 32 columns, every other chunk of the tile) are loaded two ahead in
+// the coalesced mapping, the first two before the accumulator is waited on, so the fp32 read
+// latency overlaps the tile's MMAs and the previous chunk's work.
 template <int BN>
 struct ResidualPipe {
   static constexpr int kChunks = BN / 64;
   float4 buf[2][8];
 
-  __device__ __forceinline__ void load(const GemmArgs& a, int row, int n0, int half, int i) {
-    const float* r = a.residual + (size_t)row * a.ldr + n0 + (half + 2 * i) * 32;
+  __device__ __forceinline__ void load(const GemmArgs& a, int row0, int n0, int half, int lane, int i) {
+    const float* base = a.residual + n0 + (half + 2 * i) * 32 + (lane & 7) * 4;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) buf[i & 1][k] = *reinterpret_cast<const float4*>(r + 4 * k);
+    for (int k = 0; k < 8; ++k) {
+      const int r = row0 + 4 * k + (lane >> 3);
+      buf[i & 1][k] = r < a.M ? *reinterpret_cast<const float4*>(base + (size_t)r * a.ldr) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
   }
 
-  __device__ __forceinline__ void start(const GemmArgs& a, int row, int n0, int half) {
-    if (row >= a.M) return;
-    load(a, row, n0, half, 0);
-    if (kChunks > 1) load(a, row, n0, half, 1);
+  __device__ __forceinline__ void start(const GemmArgs& a, int row0, int n0, int half, int lane) {
+    load(a, row0, n0, half, lane, 0);
+    if (kChunks > 1) load(a, row0, n0, half, lane, 1);
   }
 
-  __device__ __forceinline__ void finish(const GemmArgs& a, uint32_t tbase, int row, int n0, int half) {
-    const bool live = row < a.M;
+  __device__ __forceinline__ void finish(const GemmArgs& a, uint32_t tbase, int row0, int n0, int half, int lane,
+                                         uint8_t* stage) {
 #pragma unroll
     for (int i = 0; i < kChunks; ++i) {
       const int c = half + 2 * i;
+      const int col = n0 + c * 32;
       uint32_t v[32];
       tmem_ld32_async(tbase + c * 32, v);
       tmem_wait_ld(v);
-      if (!live) continue;
-      const int col = n0 + c * 32;
-      float* r = a.residual + (size_t)row * a.ldr + col;
+      uint4 p[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (a.bias) bb = *reinterpret_cast<const float4*>(a.bias + col + 4 * j);
+        p[j] = u4(__uint_as_float(v[4 * j]) + bb.x, __uint_as_float(v[4 * j + 1]) + bb.y,
+                  __uint_as_float(v[4 * j + 2]) + bb.z, __uint_as_float(v[4 * j + 3]) + bb.w);
+      }
+      stage_put(stage, lane, p);
+      float* base = a.residual + col + (lane & 7) * 4;
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
+        const int r = row0 + 4 * k + (lane >> 3);
+        const float4 add = f4(stage_get(stage, k, lane));
         float4 t = buf[i & 1][k];
-        float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (a.bias) bb = *reinterpret_cast<const float4*>(a.bias + col + 4 * k);
-        t.x += __uint_as_float(v[4 * k]) + bb.x;
-        t.y += __uint_as_float(v[4 * k + 1]) + bb.y;
-        t.z += __uint_as_float(v[4 * k + 2]) + bb.z;
-        t.w += __uint_as_float(v[4 * k + 3]) + bb.w;
-        *reinterpret_cast<float4*>(r + 4 * k) = t;
+        t.x += add.x; t.y += add.y; t.z += add.z; t.w += add.w;
+        if (r < a.M) *reinterpret_cast<float4*>(base + (size_t)r * a.ldr) = t;
       }
-      if (i + 2 < kChunks) load(a, row, n0, half, i + 2);
+      if (i + 2 < kChunks) load(a, row0, n0, half, lane, i + 2);
     }
   }
 };
 
-__device__ __forceinline__ void epi_partial_chunk(const GemmArgs& a, int split, int row, int col,
-                                                  const float (&v)[32]) {
-  float* r = a.residual + ((size_t)split * a.M + row) * a.ldr + col;
-#pragma unroll
-  for (int i = 0; i < 32; i += 4) *reinterpret_cast<float4*>(r + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-}
-
-// Epilogue of one accumulator tile for one thread: TMEM lane `row` of the tile (columns from
-// `tbase`), output column base n0; `half` selects every other column chunk (two warps share a
-// TMEM lane quarter).
+// Epilogue of one accumulator tile for one warp: TMEM lanes row0 .. row0+31 of the tile (this
+// lane: row0 + lane), columns from `tbase`, output column base n0; `half` selects every other
+// column chunk (two warps share a TMEM lane quarter).  EPI_RESIDUAL is handled by ResidualPipe.
 template <int BN, int EPI, typename T>
-__device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tbase, int row, int n0, int split,
-                                              int half) {
-  const bool live = row < args.M;
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tbase, int row0, int n0, int split,
+                                              int half, int lane, uint8_t* stage) {
+  const int row = row0 + lane;
+  const int rows = min(32, args.M - row0);  // live rows of this warp's block
   if (EPI == EPI_GEGLU) {
-    // Tile columns: [gate 64 | up 64] x (BN / 128); output column = n0/2 + 64*c + j.
+    // Tile columns: [gate 64 | up 64] x (BN / 128); output columns n0/2 + 64c + [0, 64).
 #pragma unroll 1
     for (int c = half; c < BN / 128; c += 2) {
-#pragma unroll 1
+      uint4 p[8];
+#pragma unroll
       for (int h = 0; h < 2; ++h) {
         float g[32], u[32];
         tmem_ld32(tbase + c * 128 + h * 32, g);
         tmem_ld32(tbase + c * 128 + 64 + h * 32, u);
-        if (live) {
-          T* out = reinterpret_cast<T*>(args.out) + (size_t)row * args.ldo + n0 / 2 + c * 64 + h * 32;
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 w;
-            w.x = pack2<T>(gelu_erf(g[i + 0]) * u[i + 0], gelu_erf(g[i + 1]) * u[i + 1]);
-            w.y = pack2<T>(gelu_erf(g[i + 2]) * u[i + 2], gelu_erf(g[i + 3]) * u[i + 3]);
-            w.z = pack2<T>(gelu_erf(g[i + 4]) * u[i + 4], gelu_erf(g[i + 5]) * u[i + 5]);
-            w.w = pack2<T>(gelu_erf(g[i + 6]) * u[i + 6], gelu_erf(g[i + 7]) * u[i + 7]);
-            *reinterpret_cast<uint4*>(out + i) = w;
-          }
+        for (int i = 0; i < 32; i += 8) {
+          p[h * 4 + i / 8] = make_uint4(pack2<T>(gelu_erf(g[i + 0]) * u[i + 0], gelu_erf(g[i + 1]) * u[i + 1]),
+                                        pack2<T>(gelu_erf(g[i + 2]) * u[i + 2], gelu_erf(g[i + 3]) * u[i + 3]),
+                                        pack2<T>(gelu_erf(g[i + 4]) * u[i + 4], gelu_erf(g[i + 5]) * u[i + 5]),
+                                        pack2<T>(gelu_erf(g[i + 6]) * u[i + 6], gelu_erf(g[i + 7]) * u[i + 7]));
         }
       }
+      stage_put(stage, lane, p);
+      T* out = reinterpret_cast<T*>(args.out) + n0 / 2 + c * 64;
+      stage_store16(stage, lane, rows, [&](int r) { return out + (size_t)(row0 + r) * args.ldo; });
     }
   } else if (EPI == EPI_QKV) {
     const int width = args.heads * 64;
@@ -194,60 +206,94 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tba
 #pragma unroll
         for (int i = 0; i < 32; ++i) { x[i] = lo[i]; x[32 + i] = hi[i]; }
       }
-      if (live) {
-        const int n = n0 + c * 64;
-        const int part = n / width;
-        const int head = (n - part * width) >> 6;
-        if (args.bias) {
+      const bool live = row < args.M;
+      const int n = n0 + c * 64;
+      const int part = n / width;
+      const int head = (n - part * width) >> 6;
+      if (args.bias) {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) x[i] += args.bias[n + i];
+        for (int i = 0; i < 64; ++i) x[i] += args.bias[n + i];
+      }
+      if (part < 2 && args.cos_tab && live) {
+        // Rotate-half RoPE: out[d] = x[d] cos - x[d+32] sin (d < 32),
+        //                   out[d] = x[d] cos + x[d-32] sin (d >= 32).
+        // Tables are [32][rope_rows]: the 32 lanes (consecutive rows, mostly consecutive
+        // positions) read one contiguous run per frequency.
+        const int pos = args.positions[row];
+        const float* cs = args.cos_tab + pos;
+        const float* sn = args.sin_tab + pos;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float c0 = __ldg(cs + (size_t)i * args.rope_rows), s0 = __ldg(sn + (size_t)i * args.rope_rows);
+          const float a = x[i], b = x[i + 32];
+          x[i] = a * c0 - b * s0;
+          x[i + 32] = b * c0 + a * s0;
         }
-        if (part < 2 && args.cos_tab) {
-          // Rotate-half RoPE: out[d] = x[d] cos - x[d+32] sin (d < 32),
-          //                   out[d] = x[d] cos + x[d-32] sin (d >= 32).
-          // Tables are [32][rope_rows]: the 32 lanes (consecutive rows, mostly consecutive
-          // positions) read one contiguous run per frequency.
-          const int pos = args.positions[row];
-          const float* cs = args.cos_tab + pos;
-          const float* sn = args.sin_tab + pos;
+      }
+      if (part < 2) {
+        // q, k -> [part][heads][M][64]: the warp's 32 rows are one contiguous 4 KB block.
+        uint4 p[8];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float c0 = __ldg(cs + (size_t)i * args.rope_rows), s0 = __ldg(sn + (size_t)i * args.rope_rows);
-            const float a = x[i], b = x[i + 32];
-            x[i] = a * c0 - b * s0;
-            x[i + 32] = b * c0 + a * s0;
-          }
-        }
-        if (part < 2) {
-          T* out = reinterpret_cast<T*>(args.out) + (((size_t)part * args.heads + head) * args.M + row) * 64;
+        for (int i = 0; i < 64; i += 8)
+          p[i / 8] = make_uint4(pack2<T>(x[i + 0], x[i + 1]), pack2<T>(x[i + 2], x[i + 3]),
+                                pack2<T>(x[i + 4], x[i + 5]), pack2<T>(x[i + 6], x[i + 7]));
+        stage_put(stage, lane, p);
+        T* out = reinterpret_cast<T*>(args.out) + ((size_t)part * args.heads + head) * args.M * 64;
+        stage_store16(stage, lane, rows, [&](int r) { return out + (size_t)(row0 + r) * 64; });
+      } else if (live) {
+        // V transposed, [heads][64][M]: the attention's P.V product reads it K-major
+        // (keys contiguous).  The warp's lanes are consecutive rows, so each dimension's
+        // 32 stores fill one contiguous 64-byte run.
+        T* vt = reinterpret_cast<T*>(args.out) + ((size_t)2 * args.heads + head) * args.M * 64 + row;
 #pragma unroll
-          for (int i = 0; i < 64; i += 8) {
-            uint4 w;
-            w.x = pack2<T>(x[i + 0], x[i + 1]); w.y = pack2<T>(x[i + 2], x[i + 3]);
-            w.z = pack2<T>(x[i + 4], x[i + 5]); w.w = pack2<T>(x[i + 6], x[i + 7]);
-            *reinterpret_cast<uint4*>(out + i) = w;
-          }
-        } else {
-          // V transposed, [heads][64][M]: the attention's P.V product reads it K-major
-          // (keys contiguous).  The warp's lanes are consecutive rows, so each dimension's
-          // 32 stores fill one contiguous 64-byte run.
-          T* vt = reinterpret_cast<T*>(args.out) + ((size_t)2 * args.heads + head) * args.M * 64 + row;
+        for (int i = 0; i < 64; ++i) vt[(size_t)i * args.M] = from_f32<T>(x[i]);
+      }
+    }
+  } else if (EPI == EPI_PARTIAL) {
+    // partial[split][row][col] = acc (fp32), 32 columns (128 B per row) per chunk.
+#pragma unroll 1
+    for (int c = half; c < BN / 32; c += 2) {
+      uint32_t v[32];
+      tmem_ld32_async(tbase + c * 32, v);
+      tmem_wait_ld(v);
+      uint4 p[8];
 #pragma unroll
-          for (int i = 0; i < 64; ++i) vt[(size_t)i * args.M] = from_f32<T>(x[i]);
-        }
+      for (int j = 0; j < 8; ++j) p[j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      stage_put(stage, lane, p);
+      float* base = args.residual + ((size_t)split * args.M) * args.ldr + n0 + c * 32 + (lane & 7) * 4;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int r = 4 * k + (lane >> 3);
+        if (r < rows) *reinterpret_cast<uint4*>(base + (size_t)(row0 + r) * args.ldr) = stage_get(stage, k, lane);
       }
     }
   } else {
-    // EPI_RESIDUAL is handled by ResidualPipe.
+    // EPI_STORE / EPI_RELU / EPI_GELU: out = act(acc + bias), 64 columns per chunk.
 #pragma unroll 1
-    for (int c = half; c < BN / 32; c += 2) {
-      float v[32];
-      tmem_ld32(tbase + c * 32, v);
-      if (live) {
-        const int col = n0 + c * 32;
-        if (EPI == EPI_PARTIAL) epi_partial_chunk(args, split, row, col, v);
-        else epi_store_chunk<T, EPI>(args, row, col, v);
+    for (int c = half; c < BN / 64; c += 2) {
+      const int col = n0 + c * 64;
+      uint4 p[8];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float v[32];
+        tmem_ld32(tbase + c * 64 + h * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          float x[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float t = v[i + j] + (args.bias ? args.bias[col + h * 32 + i + j] : 0.f);
+            if (EPI == EPI_RELU) t = fmaxf(t, 0.f);
+            if (EPI == EPI_GELU) t = gelu_erf(t);
+            x[j] = t;
+          }
+          p[h * 4 + i / 8] = make_uint4(pack2<T>(x[0], x[1]), pack2<T>(x[2], x[3]), pack2<T>(x[4], x[5]),
+                                        pack2<T>(x[6], x[7]));
+        }
       }
+      stage_put(stage, lane, p);
+      T* out = reinterpret_cast<T*>(args.out) + col;
+      stage_store16(stage, lane, rows, [&](int r) { return out + (size_t)(row0 + r) * args.ldo; });
     }
   }
 }
@@ -262,7 +308,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + S * Cfg::kStageA;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffEpi + kEpiSmemBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* tfull = bars + 2 * S;
@@ -386,17 +432,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // Epilogue warps 2..9 -> TMEM lane quarter (warp % 4); `half` picks every other chunk.
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
+    uint8_t* stage = smem + Cfg::kOffEpi + (warp - 2) * kEpiStageBytes;
     int acc = 0; uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
       int split, mb, nb; decode(t, split, mb, nb);
-      const int row = mb * kBM + quarter * 32 + lane;
+      const int row0 = mb * kBM + quarter * 32;
       ResidualPipe<BN> rp;
-      if (EPI == EPI_RESIDUAL) rp.start(args, row, nb * BN, half);
+      if (EPI == EPI_RESIDUAL) rp.start(args, row0, nb * BN, half, lane);
       if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      if (EPI == EPI_RESIDUAL) rp.finish(args, tbase, row, nb * BN, half);
-      else epilogue_tile<BN, EPI, T>(args, tbase, row, nb * BN, split, half);
+      if (EPI == EPI_RESIDUAL) rp.finish(args, tbase, row0, nb * BN, half, lane, stage);
+      else epilogue_tile<BN, EPI, T>(args, tbase, row0, nb * BN, split, half, lane, stage);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
@@ -431,7 +478,8 @@ struct GemmPairCfg {
   static constexpr int kStageBytes = kStageA + kStageB;
   static constexpr int kStages = (192 * 1024) / kStageBytes;
   static constexpr int kTmemCols = 2 * BN;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+  static constexpr int kOffEpi = kStages * kStageBytes;
+  static constexpr int kSmemBytes = kOffEpi + kEpiSmemBytes + 1024 + 256;
 };
 
 template <int BN, int EPI, typename T>
@@ -444,7 +492,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + S * Cfg::kStageA;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffEpi + kEpiSmemBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* tfull = bars + 2 * S;
@@ -542,19 +590,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
+    uint8_t* stage = smem + Cfg::kOffEpi + (warp - 2) * kEpiStageBytes;
     const uint32_t leader_tempty0 = cluster_addr(smem_u32(&tempty[0]), 0);
     const uint32_t leader_tempty1 = cluster_addr(smem_u32(&tempty[1]), 0);
     int acc = 0; uint32_t acc_phase = 0;
     for (int t = pair; t < tiles; t += pairs) {
       const int mb = t / n_blocks, nb = t - mb * n_blocks;
-      const int row = mb * 2 * kBM + (int)rank * kBM + quarter * 32 + lane;
+      const int row0 = mb * 2 * kBM + (int)rank * kBM + quarter * 32;
       ResidualPipe<BN> rp;
-      if (EPI == EPI_RESIDUAL) rp.start(args, row, nb * BN, half);
+      if (EPI == EPI_RESIDUAL) rp.start(args, row0, nb * BN, half, lane);
       if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
-      if (EPI == EPI_RESIDUAL) rp.finish(args, tbase, row, nb * BN, half);
-      else epilogue_tile<BN, EPI, T>(args, tbase, row, nb * BN, 0, half);
+      if (EPI == EPI_RESIDUAL) rp.finish(args, tbase, row0, nb * BN, half, lane, stage);
+      else epilogue_tile<BN, EPI, T>(args, tbase, row0, nb * BN, 0, half, lane, stage);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(acc == 0 ? leader_tempty0 : leader_tempty1);
