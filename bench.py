@@ -12,7 +12,7 @@ exchanged between ranks (the NCCL group only carries the timing barrier and the 
 metric: sequences/s over all ranks (device time, max over ranks).  Extra keys: batch-1 latency
 (configs 1/2: 83 and 512 tokens through Engine.predict), per-kernel-family device times, the
 roofline of the dominant kernel (FFN-up GEMM), the oracle on the host cores (cpu_baseline),
-and the end-to-end number through the public Runtime.predict with host buffers (e2e).
+and the end-to-end number through the public Runtime.predict_many with host buffers (e2e).
 """
 import argparse
 import ctypes as ct
@@ -334,23 +334,22 @@ def run_engine(args, rank, world, local_rank):
                 "traffic": round(TRAFFIC_FFN_UP_BYTES_PER_TOKEN * tokens / len(batches)),
                 "all_encoder_gemms": {"achieved": round(enc_achieved, 1), "frac": round(enc_achieved / tf_sust, 4)}}
 
-    # End to end through the public Runtime.predict on every rank: host items -> pinned
+    # End to end through the public Runtime.predict_many on every rank: host items -> pinned
     # staging -> H2D -> forward -> D2H of logits/acts, every micro-batch (one step = the rank's
     # whole workload); whole-job rate = all ranks' sequences over the slowest rank's time.
     h2d, d2h = 0, 0
     for batch, (m, b, k) in zip(batches, shapes):
         h2d += lib.laya_packed_ints(m, b, k) * 4
         d2h += (b * (k + 1) + b * arch["n_act"] + 1) * 4
-    rt.predict(batches[0])
+    rt.predict_many(batches[:4])
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
-    for batch in batches:
-        rt.predict(batch)
+    rt.predict_many(batches)
     e2e_rate, _, _ = job_rate((time.perf_counter() - t0) * 1000, len(items), 1, world, "cuda")
     e2e = {"value": round(e2e_rate, 2), "unit": "sequences/s", "h2d_bytes_per_step": int(h2d) * world,
-           "d2h_bytes_per_step": int(d2h) * world, "api": "Runtime.predict(items) per 64-sequence micro-batch"}
+           "d2h_bytes_per_step": int(d2h) * world, "api": "Runtime.predict_many(64-sequence micro-batches), two in flight"}
 
     line = None
     if rank == 0:

@@ -98,6 +98,17 @@ int laya_predict(laya_engine* e, const int32_t* tokens, const int32_t* lengths, 
                  const int32_t* marker_counts, const int32_t* kinds, int n_items, int capture,
                  float* logits_out, float* acts_out, laya_metrics* metrics);
 
+/* laya_predict in two halves, so a host can pack and launch the next batch while the previous
+ * one runs (no counterpart in the reference, whose Runtime.predict is synchronous).
+ * laya_submit packs and uploads the items and enqueues the forward pass and the read-back on the
+ * engine stream; it returns at once with a ticket.  At most two passes may be in flight
+ * (LAYA_ERR_STATE otherwise).  laya_collect waits for the ticket's pass and writes its outputs
+ * exactly as laya_predict does; tickets may be collected in any order.  The item arrays are
+ * consumed by laya_submit. */
+int laya_submit(laya_engine* e, const int32_t* tokens, const int32_t* lengths, const int32_t* markers,
+                const int32_t* marker_counts, const int32_t* kinds, int n_items, int capture, int64_t* ticket);
+int laya_collect(laya_engine* e, int64_t ticket, float* logits_out, float* acts_out, laya_metrics* metrics);
+
 /* Shape class of a request (runtime.py:20-25): packed rows, batch and option counts. */
 int laya_shape_class(const int32_t* lengths, const int32_t* marker_counts, int n_items, int32_t* rows,
                      int32_t* batch, int32_t* options);

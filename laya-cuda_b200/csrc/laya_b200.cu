@@ -277,9 +277,21 @@ int pick_splits(int M, int N, int K, int bn, int sms) {
   return best;
 }
 
+// Tensor maps of the tcgen05 attention over a qkv buffer of M tokens: 128-row tiles of the q/k
+// planes, and 64 dims x 64 keys tiles of V^T.
+struct AttnMaps {
+  CUtensorMap qk, vt;
+};
+AttnMaps attn_maps(const void* qkv, int M, int heads, bool bf) {
+  const int64_t hm = (int64_t)heads * M;
+  AttnMaps m;
+  m.qk = make_map(qkv, 3 * hm, 64, kTcQ, bf);
+  m.vt = make_map(static_cast<const uint8_t*>(qkv) + (size_t)2 * hm * 64 * 2, (int64_t)heads * 64, M, 64, bf);
+  return m;
+}
+
 template <typename T>
-void launch_tc_attention(const CUtensorMap& qk, const CUtensorMap& vt, const TcAttnArgs& a, int n_tiles,
-                         cudaStream_t st) {
+void launch_tc_attention(const AttnMaps& maps, const TcAttnArgs& a, int n_tiles, cudaStream_t st) {
   static uint64_t configured = 0;  // one bit per device
   int dev = 0;
   CK(cudaGetDevice(&dev));
@@ -288,7 +300,7 @@ void launch_tc_attention(const CUtensorMap& qk, const CUtensorMap& vt, const TcA
     configured |= 1ull << dev;
   }
   if (n_tiles > 65535) fail(LAYA_ERR_INVALID, "%d attention tiles exceed the grid limit", n_tiles);
-  launch_k(tc_attention_kernel<T>, dim3(a.heads, n_tiles), dim3(kTcThreads), TcAttnSmem::kBytes, st, qk, vt, a);
+  launch_k(tc_attention_kernel<T>, dim3(a.heads, n_tiles), dim3(kTcThreads), TcAttnSmem::kBytes, st, maps.qk, maps.vt, a);
 }
 
 template <typename T>
@@ -476,7 +488,8 @@ struct Slot {
   cudaGraphExec_t graph = nullptr;
   bool maps_ready = false;
   size_t maps_ws = 0;  // workspace generation the maps point into
-  CUtensorMap map_x, map_attn, map_ff, map_selx, map_scored, map_ffsel, map_qk, map_vt;
+  CUtensorMap map_x, map_attn, map_ff, map_selx, map_scored, map_ffsel;
+  AttnMaps attn_maps;
   int launches = 0;
 };
 
@@ -496,6 +509,23 @@ struct ProfEvent {
   double flops;
 };
 
+// One forward pass submitted by laya_submit and not yet collected: its pinned staging buffers,
+// events and result metadata.  Two exist, so the host can pack and launch a pass while the
+// previous one runs.
+struct Inflight {
+  bool busy = false;
+  int64_t ticket = 0;
+  int n_items = 0, m = 0, b = 0, k = 0;
+  int32_t* h_packed = nullptr;
+  size_t h_packed_cap = 0;
+  float* h_out = nullptr;
+  size_t h_out_cap = 0;
+  size_t n_out_floats = 0;
+  cudaEvent_t ev_start = nullptr, ev_end = nullptr, done = nullptr;
+  bool miss = false, captured = false, replay = false;
+  int launches = 0;
+};
+
 struct Engine {
   laya_config cfg{};
   int device = 0;
@@ -503,7 +533,6 @@ struct Engine {
   int sms = 148;
   bool finalized = false;
   cudaStream_t stream = nullptr;
-  cudaEvent_t ev_start = nullptr, ev_end = nullptr;
   std::unordered_map<std::string, Tensor> weights;
   std::map<std::string, std::vector<int64_t>> expected;
   float* rope_cos[2] = {nullptr, nullptr};
@@ -512,10 +541,8 @@ struct Engine {
   uint8_t* ws = nullptr;
   size_t ws_bytes = 0;
   size_t ws_generation = 0;
-  int32_t* h_packed = nullptr;
-  size_t h_packed_cap = 0;
-  float* h_out = nullptr;
-  size_t h_out_cap = 0;
+  Inflight inflight[2];
+  int64_t next_ticket = 1;
   std::list<std::tuple<int, int, int>> lru;  // front = least recently used
   std::map<std::tuple<int, int, int>, std::unique_ptr<Slot>> slots;
   std::map<std::tuple<const void*, int>, CUtensorMap> wmaps;
@@ -708,18 +735,28 @@ void ensure_workspace(Engine& e, size_t bytes) {
   ++e.ws_generation;
 }
 
-void ensure_host(Engine& e, size_t ints, size_t floats) {
-  if (ints > e.h_packed_cap) {
-    if (e.h_packed) CK(cudaFreeHost(e.h_packed));
-    e.h_packed = nullptr;
-    CK(cudaHostAlloc(reinterpret_cast<void**>(&e.h_packed), ints * 4, cudaHostAllocDefault));
-    e.h_packed_cap = ints;
+// Pinned staging of a free in-flight record (none of its copies is pending).  Capacities grow to
+// powers of two: pinning and unpinning are slow and cudaFreeHost synchronises the device, so a
+// stream of slightly growing classes must not reallocate every time.
+size_t pow2_at_least(size_t n) {
+  size_t c = 4096;
+  while (c < n) c <<= 1;
+  return c;
+}
+void ensure_host(Inflight& r, size_t ints, size_t floats) {
+  ints = pow2_at_least(ints);
+  floats = pow2_at_least(floats);
+  if (ints > r.h_packed_cap) {
+    if (r.h_packed) CK(cudaFreeHost(r.h_packed));
+    r.h_packed = nullptr;
+    CK(cudaHostAlloc(reinterpret_cast<void**>(&r.h_packed), ints * 4, cudaHostAllocDefault));
+    r.h_packed_cap = ints;
   }
-  if (floats > e.h_out_cap) {
-    if (e.h_out) CK(cudaFreeHost(e.h_out));
-    e.h_out = nullptr;
-    CK(cudaHostAlloc(reinterpret_cast<void**>(&e.h_out), floats * 4, cudaHostAllocDefault));
-    e.h_out_cap = floats;
+  if (floats > r.h_out_cap) {
+    if (r.h_out) CK(cudaFreeHost(r.h_out));
+    r.h_out = nullptr;
+    CK(cudaHostAlloc(reinterpret_cast<void**>(&r.h_out), floats * 4, cudaHostAllocDefault));
+    r.h_out_cap = floats;
   }
 }
 
@@ -755,9 +792,7 @@ void prepare_maps(Engine& e, Slot& s) {
   s.map_ffsel = make_map(e.ws + L.ffsel, L.count, 4 * d, kBM, bf);
   // Attention: Q/K rows of the qkv buffer ([3*heads*m][64], 128-row boxes) and V^T
   // ([heads*64][m], 64x64 boxes), both 128-byte swizzled.
-  const int64_t hm = (int64_t)e.cfg.heads * L.m;
-  s.map_qk = make_map(e.ws + L.qkv, 3 * hm, 64, kTcQ, bf);
-  s.map_vt = make_map(e.ws + L.qkv + (size_t)2 * hm * 64 * 2, (int64_t)e.cfg.heads * 64, L.m, 64, bf);
+  s.attn_maps = attn_maps(e.ws + L.qkv, L.m, e.cfg.heads, bf);
   s.maps_ready = true;
   s.maps_ws = e.ws_generation;
 }
@@ -811,7 +846,9 @@ void gemm(Engine& e, bool prof, int family, int epi, const CUtensorMap& ta, cons
   const Tensor& w = W(e, wname);
   const int N = (int)w.shape[0], K = (int)w.shape[1];
   int bn = pick_bn(M, N, epi, e.sms);
-  const bool pair = M >= kPairMinRows && pair_enabled() && N % 256 == 0;
+  // The CTA pair wins for the 16-bit output epilogues; the fp32 residual read-modify-write is as
+  // fast or faster on the 1-CTA kernel (measured at 41k rows).
+  const bool pair = M >= kPairMinRows && pair_enabled() && N % 256 == 0 && epi != EPI_RESIDUAL;
   if (pair) bn = 256;
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K; a.splits = 1;
@@ -891,7 +928,7 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
         a.q_index = indices; a.q_per_row = L.k + 1; a.q_tiles = (L.k + 1 + kTcQ - 1) / kTcQ;
         n_tiles = L.b * a.q_tiles;
       }
-      launch(e, prof, FAM_ATTENTION, 0, [&] { launch_tc_attention<T>(s.map_qk, s.map_vt, a, n_tiles, e.stream); });
+      launch(e, prof, FAM_ATTENTION, 0, [&] { launch_tc_attention<T>(s.attn_maps, a, n_tiles, e.stream); });
     } else {
       AttnArgs a{};
       a.qkv = qkv; a.out = attn; a.tiles = tiles64; a.starts = starts; a.lengths = lengths;
@@ -1123,8 +1160,7 @@ int laya_create(const laya_config* cfg, int device, int max_cached_shapes, laya_
   }
   build_expected(e);
   CK(cudaStreamCreateWithFlags(&e.stream, cudaStreamNonBlocking));
-  CK(cudaEventCreate(&e.ev_start));
-  CK(cudaEventCreate(&e.ev_end));
+
   *out = h.release();
   API_END(nullptr)
 }
@@ -1241,52 +1277,108 @@ int laya_pack(const int32_t* tokens, const int32_t* lengths, const int32_t* mark
   API_END(nullptr)
 }
 
-int laya_predict(laya_engine* h, const int32_t* tokens, const int32_t* lengths, const int32_t* markers,
-                 const int32_t* marker_counts, const int32_t* kinds, int n_items, int capture, float* logits_out,
-                 float* acts_out, laya_metrics* metrics) {
-  API_BEGIN
-  if (!h) fail(LAYA_ERR_INVALID, "null engine");
-  Engine& e = h->impl;
+namespace {
+// Packs the items into a free in-flight record, enqueues H2D, the forward pass and D2H on the
+// engine stream, and returns the record's ticket.  Nothing here waits for the GPU except a
+// workspace growth or a graph eviction (both synchronise the stream first).
+int64_t submit(Engine& e, const int32_t* tokens, const int32_t* lengths, const int32_t* markers,
+               const int32_t* marker_counts, const int32_t* kinds, int n_items, int capture) {
   if (!e.finalized) fail(LAYA_ERR_STATE, "engine not finalised");
-  if (!tokens || !lengths || !marker_counts || !kinds || !logits_out || !acts_out) fail(LAYA_ERR_INVALID, "null argument");
+  if (!tokens || !lengths || !marker_counts || !kinds) fail(LAYA_ERR_INVALID, "null argument");
+  Inflight* r = !e.inflight[0].busy ? &e.inflight[0] : !e.inflight[1].busy ? &e.inflight[1] : nullptr;
+  if (!r) fail(LAYA_ERR_STATE, "two passes are in flight: collect one first");
   CK(cudaSetDevice(e.device));
   int m, b, k;
   shape_class(lengths, marker_counts, n_items, m, b, k);
   const bool graph = wants_graph(capture, m);
   bool miss = false;
-  std::unique_ptr<Slot> transient;
+  std::unique_ptr<Slot> transient;  // launches copy everything they need; safe to drop after enqueue
   Slot& s = get_slot(e, m, b, k, graph, miss, transient);
   ensure_workspace(e, s.L.total);
-  ensure_host(e, (size_t)s.L.pack.total, s.L.n_out_floats);
+  ensure_host(*r, (size_t)s.L.pack.total, s.L.n_out_floats);
+  if (!r->done) {
+    CK(cudaEventCreate(&r->ev_start));
+    CK(cudaEventCreate(&r->ev_end));
+    CK(cudaEventCreateWithFlags(&r->done, cudaEventDisableTiming));
+  }
   // The pad id is the tokenizer's [PAD]; padded positions are never attended by real tokens.
-  pack(tokens, lengths, markers, marker_counts, kinds, n_items, 0, m, b, k, e.cfg.max_len, e.h_packed);
-  CK(cudaMemcpyAsync(e.ws + s.L.packed, e.h_packed, (size_t)s.L.pack.total * 4, cudaMemcpyHostToDevice, e.stream));
+  pack(tokens, lengths, markers, marker_counts, kinds, n_items, 0, m, b, k, e.cfg.max_len, r->h_packed);
+  CK(cudaMemcpyAsync(e.ws + s.L.packed, r->h_packed, (size_t)s.L.pack.total * 4, cudaMemcpyHostToDevice, e.stream));
   bool captured = false;
-  CK(cudaEventRecord(e.ev_start, e.stream));
-  const int launches = run_slot(e, s, graph, captured);
-  CK(cudaEventRecord(e.ev_end, e.stream));
-  CK(cudaMemcpyAsync(e.h_out, e.ws + s.L.out, s.L.n_out_floats * 4, cudaMemcpyDeviceToHost, e.stream));
-  CK(cudaStreamSynchronize(e.stream));
+  CK(cudaEventRecord(r->ev_start, e.stream));
+  r->launches = run_slot(e, s, graph, captured);
+  CK(cudaEventRecord(r->ev_end, e.stream));
+  CK(cudaMemcpyAsync(r->h_out, e.ws + s.L.out, s.L.n_out_floats * 4, cudaMemcpyDeviceToHost, e.stream));
+  CK(cudaEventRecord(r->done, e.stream));
+  r->busy = true;
+  r->ticket = e.next_ticket++;
+  r->n_items = n_items; r->m = m; r->b = b; r->k = k;
+  r->n_out_floats = s.L.n_out_floats;
+  r->miss = miss; r->captured = captured; r->replay = graph && s.graph != nullptr;
+  return r->ticket;
+}
+
+// Waits for the pass of `ticket` and copies its outputs: logits [n_items][k] (options of the
+// class; the CLS slot is dropped) and acts [n_items][n_act].
+void collect(Engine& e, int64_t ticket, float* logits_out, float* acts_out, laya_metrics* metrics) {
+  Inflight* r = nullptr;
+  for (auto& x : e.inflight)
+    if (x.busy && x.ticket == ticket) r = &x;
+  if (!r) fail(LAYA_ERR_INVALID, "no pass in flight with ticket %lld", (long long)ticket);
+  CK(cudaSetDevice(e.device));
+  const cudaError_t sync = cudaEventSynchronize(r->done);
+  r->busy = false;
+  if (sync != cudaSuccess) fail(LAYA_ERR_CUDA, "forward pass: %s", cudaGetErrorString(sync));
   prof_resolve(e);
-  const float* outf = e.h_out;
+  const int b = r->b, k = r->k;
+  const float* outf = r->h_out;
   const int errword = *reinterpret_cast<const int*>(outf + (size_t)b * (k + 1) + (size_t)b * e.cfg.n_act);
   if (errword) fail(LAYA_ERR_DEVICE, "device error %d during the forward pass", errword);
-  for (int i = 0; i < n_items; ++i) {
-    memcpy(logits_out + (size_t)i * k, outf + (size_t)i * (k + 1) + 1, (size_t)k * 4);
-    memcpy(acts_out + (size_t)i * e.cfg.n_act, outf + (size_t)b * (k + 1) + (size_t)i * e.cfg.n_act,
-           (size_t)e.cfg.n_act * 4);
+  if (logits_out && acts_out) {
+    for (int i = 0; i < r->n_items; ++i) {
+      memcpy(logits_out + (size_t)i * k, outf + (size_t)i * (k + 1) + 1, (size_t)k * 4);
+      memcpy(acts_out + (size_t)i * e.cfg.n_act, outf + (size_t)b * (k + 1) + (size_t)i * e.cfg.n_act,
+             (size_t)e.cfg.n_act * 4);
+    }
   }
   if (metrics) {
     float ms = 0;
-    CK(cudaEventElapsedTime(&ms, e.ev_start, e.ev_end));
+    CK(cudaEventElapsedTime(&ms, r->ev_start, r->ev_end));
     metrics->gpu_ms = ms;
-    metrics->rows = m; metrics->batch = b; metrics->options = k;
-    metrics->cache_miss = miss;
-    metrics->graph_capture = captured;
-    metrics->graph_replay = graph && s.graph != nullptr;
-    metrics->kernel_launches = launches;
+    metrics->rows = r->m; metrics->batch = b; metrics->options = k;
+    metrics->cache_miss = r->miss;
+    metrics->graph_capture = r->captured;
+    metrics->graph_replay = r->replay;
+    metrics->kernel_launches = r->launches;
     metrics->owned_gpu_bytes = e.owned();
   }
+}
+}  // namespace
+
+int laya_predict(laya_engine* h, const int32_t* tokens, const int32_t* lengths, const int32_t* markers,
+                 const int32_t* marker_counts, const int32_t* kinds, int n_items, int capture, float* logits_out,
+                 float* acts_out, laya_metrics* metrics) {
+  API_BEGIN
+  if (!h) fail(LAYA_ERR_INVALID, "null engine");
+  if (!logits_out || !acts_out) fail(LAYA_ERR_INVALID, "null argument");
+  Engine& e = h->impl;
+  const int64_t ticket = submit(e, tokens, lengths, markers, marker_counts, kinds, n_items, capture);
+  collect(e, ticket, logits_out, acts_out, metrics);
+  API_END(h)
+}
+
+int laya_submit(laya_engine* h, const int32_t* tokens, const int32_t* lengths, const int32_t* markers,
+                const int32_t* marker_counts, const int32_t* kinds, int n_items, int capture, int64_t* ticket) {
+  API_BEGIN
+  if (!h || !ticket) fail(LAYA_ERR_INVALID, "null argument");
+  *ticket = submit(h->impl, tokens, lengths, markers, marker_counts, kinds, n_items, capture);
+  API_END(h)
+}
+
+int laya_collect(laya_engine* h, int64_t ticket, float* logits_out, float* acts_out, laya_metrics* metrics) {
+  API_BEGIN
+  if (!h || !logits_out || !acts_out) fail(LAYA_ERR_INVALID, "null argument");
+  collect(h->impl, ticket, logits_out, acts_out, metrics);
   API_END(h)
 }
 
@@ -1407,12 +1499,16 @@ int laya_destroy(laya_engine* h) {
     if (e.rope_sin[i]) cudaFree(e.rope_sin[i]);
   }
   if (e.ws) cudaFree(e.ws);
-  if (e.h_packed) cudaFreeHost(e.h_packed);
-  if (e.h_out) cudaFreeHost(e.h_out);
+  for (auto& r : e.inflight) {
+    if (r.h_packed) cudaFreeHost(r.h_packed);
+    if (r.h_out) cudaFreeHost(r.h_out);
+    if (r.ev_start) cudaEventDestroy(r.ev_start);
+    if (r.ev_end) cudaEventDestroy(r.ev_end);
+    if (r.done) cudaEventDestroy(r.done);
+  }
   for (auto& p : e.prof_pending) { cudaEventDestroy(p.a); cudaEventDestroy(p.b); }
   for (auto ev : e.prof_pool) cudaEventDestroy(ev);
-  if (e.ev_start) cudaEventDestroy(e.ev_start);
-  if (e.ev_end) cudaEventDestroy(e.ev_end);
+
   if (e.stream) cudaStreamDestroy(e.stream);
   delete h;
   return rc;
@@ -1470,15 +1566,13 @@ int laya_op_attention(int precision, int impl, const void* qkv, void* out, const
   API_BEGIN
   if (impl == 1) {
     const bool bf = precision == LAYA_PRECISION_BF16;
-    const int64_t hm = (int64_t)heads * M;
-    const CUtensorMap qk = make_map(qkv, 3 * hm, 64, kTcQ, bf);
-    const CUtensorMap vt = make_map(static_cast<const uint8_t*>(qkv) + (size_t)2 * hm * 64 * 2, (int64_t)heads * 64, M, 64, bf);
+    const AttnMaps maps = attn_maps(qkv, M, heads, bf);
     TcAttnArgs t{};
     t.qk = qkv; t.out = out; t.tiles = reinterpret_cast<const int4*>(tiles); t.starts = starts; t.lengths = lengths;
     t.M = M; t.heads = heads; t.window = window; t.err = err;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (bf) launch_tc_attention<__nv_bfloat16>(qk, vt, t, n_tiles, st);
-    else launch_tc_attention<__half>(qk, vt, t, n_tiles, st);
+    if (bf) launch_tc_attention<__nv_bfloat16>(maps, t, n_tiles, st);
+    else launch_tc_attention<__half>(maps, t, n_tiles, st);
     return LAYA_OK;
   }
   AttnArgs a{};
@@ -1496,16 +1590,14 @@ int laya_op_attention_gathered(int precision, const void* qkv, void* out, const 
   API_BEGIN
   if (q_per_row <= 0 || n_rows <= 0) fail(LAYA_ERR_INVALID, "gathered attention needs rows and queries");
   const bool bf = precision == LAYA_PRECISION_BF16;
-  const int64_t hm = (int64_t)heads * M;
-  const CUtensorMap qk = make_map(qkv, 3 * hm, 64, kTcQ, bf);
-  const CUtensorMap vt = make_map(static_cast<const uint8_t*>(qkv) + (size_t)2 * hm * 64 * 2, (int64_t)heads * 64, M, 64, bf);
+  const AttnMaps maps = attn_maps(qkv, M, heads, bf);
   TcAttnArgs t{};
   t.qk = qkv; t.out = out; t.starts = starts; t.lengths = lengths;
   t.M = M; t.heads = heads; t.window = -1; t.err = err;
   t.q_index = q_index; t.q_per_row = q_per_row; t.q_tiles = (q_per_row + kTcQ - 1) / kTcQ;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (bf) launch_tc_attention<__nv_bfloat16>(qk, vt, t, n_rows * t.q_tiles, st);
-  else launch_tc_attention<__half>(qk, vt, t, n_rows * t.q_tiles, st);
+  if (bf) launch_tc_attention<__nv_bfloat16>(maps, t, n_rows * t.q_tiles, st);
+  else launch_tc_attention<__half>(maps, t, n_rows * t.q_tiles, st);
   API_END(nullptr)
 }
 

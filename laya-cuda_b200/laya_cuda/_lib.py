@@ -15,7 +15,8 @@ PRECISION_BF16, PRECISION_F16 = 0, 1
 
 # Every symbol declared in include/laya_b200.h.
 EXPORTS = (
-    "laya_create", "laya_load_tensor", "laya_finalize", "laya_predict", "laya_shape_class",
+    "laya_create", "laya_load_tensor", "laya_finalize", "laya_predict", "laya_submit", "laya_collect",
+    "laya_shape_class",
     "laya_forward_device", "laya_packed_ints", "laya_pack", "laya_reserve", "laya_stream", "laya_set_profiling",
     "laya_profile_read", "laya_read_tensor", "laya_cached_shapes", "laya_pool_bytes", "laya_destroy",
     "laya_last_error", "laya_op_gemm", "laya_interleave_geglu", "laya_op_attention", "laya_op_attention_gathered",
@@ -56,6 +57,8 @@ def load():
         "laya_load_tensor": (i, [p, ct.c_char_p, i, i64p, i, p]),
         "laya_finalize": (i, [p]),
         "laya_predict": (i, [p, p, p, p, p, p, i, i, p, p, ct.POINTER(Metrics)]),
+        "laya_submit": (i, [p, p, p, p, p, p, i, i, i64p]),
+        "laya_collect": (i, [p, ct.c_int64, p, p, ct.POINTER(Metrics)]),
         "laya_shape_class": (i, [p, p, i, i32p, i32p, i32p]),
         "laya_forward_device": (i, [p, p, i, i, i, i, p, p]),
         "laya_packed_ints": (ct.c_int64, [i, i, i]),

@@ -128,6 +128,7 @@ class Runtime:
         self.adapter, self.device, self.limit, self.precision = adapter, device, max_cached_shapes, precision
         self._lib = _lib.load()
         self._handle = None
+        self._pending = {}  # ticket -> (items, options, shape class) of submitted batches
         self.pool, self.slots = _Pool(self), _Slots(self)
         handle = ct.c_void_p()
         cfg = config_of(adapter, precision)
@@ -179,6 +180,44 @@ class Runtime:
                    "graph_capture": bool(m.graph_capture), "graph_replay": bool(m.graph_replay),
                    "owned_gpu_bytes": m.owned_gpu_bytes, "kernel_launches": m.kernel_launches}
         return logits, acts, metrics
+
+    def submit(self, items, capture=True):
+        """Packs and launches one batch without waiting for it (at most two in flight); returns a
+        ticket for collect().  The pair lets a caller prepare batch i+1 while batch i runs."""
+        from . import _lib
+        if self._handle is None:
+            raise RuntimeError("Runtime is closed")
+        rows, batch, options = classes(items)
+        tokens, lengths, markers, counts, kinds = flatten(items)
+        ticket = ct.c_int64()
+        _lib.check(self._lib.laya_submit(self._handle, _ptr(tokens), _ptr(lengths), _ptr(markers), _ptr(counts),
+                                         _ptr(kinds), len(items), 2 if capture else 0, ct.byref(ticket)), self._handle)
+        self._pending[ticket.value] = (len(items), options, (rows, batch, options))
+        return ticket.value
+
+    def collect(self, ticket):
+        """(logits, acts, metrics) of a submitted batch, as predict() returns them."""
+        from . import _lib
+        n, options, shape = self._pending.pop(ticket)
+        logits = np.empty((n, options), np.float32)
+        acts = np.empty((n, self.adapter.n_act), np.float32)
+        m = _lib.Metrics()
+        _lib.check(self._lib.laya_collect(self._handle, ticket, _ptr(logits), _ptr(acts), ct.byref(m)), self._handle)
+        metrics = {"gpu_ms": m.gpu_ms, "shape": shape, "cache_miss": bool(m.cache_miss),
+                   "graph_capture": bool(m.graph_capture), "graph_replay": bool(m.graph_replay),
+                   "owned_gpu_bytes": m.owned_gpu_bytes, "kernel_launches": m.kernel_launches}
+        return logits, acts, metrics
+
+    def predict_many(self, batches, capture=True):
+        """predict() over a sequence of batches with two in flight: each batch is packed and
+        launched while the previous one runs.  Returns the results in order."""
+        results, pending = [], []
+        for items in batches:
+            if len(pending) == 2:
+                results.append(self.collect(pending.pop(0)))
+            pending.append(self.submit(items, capture))
+        results.extend(self.collect(t) for t in pending)
+        return results
 
     def close(self):
         if self._handle is not None:

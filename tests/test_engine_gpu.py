@@ -292,3 +292,27 @@ np.savez(sys.argv[1], *[a for o in outs for a in o[:2]])
         results.append(np.load(out))
     for key in results[0].files:
         np.testing.assert_array_equal(results[0][key], results[1][key])
+
+
+def test_submit_collect_pipeline_matches_predict(laya_ckpt):
+    """Runtime.submit/collect (two passes in flight, pinned staging per pass) returns exactly
+    what predict returns for the same batches, in any collection order; a third submit while two
+    are in flight is refused."""
+    path, arch, _ = laya_ckpt
+    rng = np.random.default_rng(11)
+    batches = [[S.build_item(rng, n, k, arch["vocab"], kind=j % 3) for j, (n, k) in enumerate(shape)]
+               for shape in ([(83, 4)], [(512, 8), (300, 5)], [(129, 2)] * 3, [(500, 4)], [(64, 1), (480, 6)])]
+    with Engine(path) as engine:
+        rt = engine.runtime
+        expected = [rt.predict(b) for b in batches]
+        got = rt.predict_many(batches)
+        for (l0, a0, _), (l1, a1, _) in zip(expected, got):
+            np.testing.assert_array_equal(l0, l1)
+            np.testing.assert_array_equal(a0, a1)
+        t0, t1 = rt.submit(batches[0]), rt.submit(batches[1])
+        with pytest.raises(RuntimeError, match="in flight"):
+            rt.submit(batches[2])
+        l1, a1, _ = rt.collect(t1)
+        l0, a0, _ = rt.collect(t0)
+        np.testing.assert_array_equal(l0, expected[0][0])
+        np.testing.assert_array_equal(l1, expected[1][0])
