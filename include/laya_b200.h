@@ -172,6 +172,15 @@ int laya_op_gemm(int precision, int epi, const void* x, const void* w, int M, in
                  float* residual, int ldr, const float* bias, int heads, const float* cos_tab, const float* sin_tab,
                  int rope_rows, const int32_t* positions, int splits, int block_n, int* err, void* stream);
 
+/* Residual GEMM with the following LayerNorm fused (runtime.py:96-108: linear, add, layer_norm
+ * of kernels.cu:20-49): residual[M][N] (fp32, row stride ldr) += x W^T + bias, then
+ * out[M][N] (16-bit, row stride ldo) = LN(residual) * gamma (+ beta), population variance of the
+ * centred row, eps inside the square root.  N must be 256, 512, 768 or 1024 (N/256 CTAs form a
+ * cluster that owns each 128-row block); K a multiple of 64.  bias and beta may be null. */
+int laya_op_gemm_ln(int precision, const void* x, const void* w, int M, int N, int K, float* residual, int ldr,
+                    const float* bias, const float* gamma, const float* beta, float eps, void* out, int ldo, int* err,
+                    void* stream);
+
 /* Reorders Wi [2F][K] (gate rows then up rows) into 64-row blocks [gate_i, up_i] (host memory). */
 int laya_interleave_geglu(const uint16_t* src, uint16_t* dst, int F, int K);
 

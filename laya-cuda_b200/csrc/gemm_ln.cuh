@@ -1,0 +1,364 @@
+// Residual GEMM with the following LayerNorm fused into its epilogue:
+//
+//   residual[M, N] += A[M, K] * W[N, K]^T + bias;   x = LN(residual) * gamma (+ beta)
+//
+// for the encoder's attention-out -> mlp_norm and FFN-down -> next attn_norm pairs
+// (reference: runtime.py:96-108 calling linear, add and layer_norm, kernels.cu:20-49), so the
+// updated residual never makes a second trip through HBM for its normalisation.
+//
+// A LayerNorm needs whole rows, and a row of N = C x 256 fp32 accumulators does not fit one
+// SM's TMEM next to a second accumulator buffer, so C CTAs form a cluster that owns a 128-row
+// block: CTA `rank` computes columns [256 rank, 256 rank + 256) of it.  The row statistics are
+// combined through distributed shared memory: every epilogue warp writes its partial row sums
+// into every CTA of the cluster and arrives on that CTA's exchange mbarrier (release at cluster
+// scope; the waiter acquires at cluster scope).  Two rounds: the sum (mean), then the centred
+// sum of squares (variance), as the reference's two-pass LayerNorm.
+//
+// Per CTA the roles are those of gemm_kernel (warp 0 TMA, warp 1 TMEM + MMA, warps 2-9
+// epilogue; two 256-column TMEM accumulators so tile i's epilogue overlaps tile i+1's MMAs).
+// The epilogue keeps the updated residual in the accumulator's TMEM columns between its three
+// passes: (A) v = acc + bias + residual, written to HBM and back to TMEM, row sums; (B) centred
+// squares; (C) x = (v - mean) * rstd * gamma (+ beta), rounded once.  Global traffic goes
+// through the per-warp swizzled staging block of gemm.cuh, so it covers whole 128-byte lines.
+// Clusters walk the row blocks in lock step (same order in every CTA of a cluster).
+#pragma once
+#include "gemm.cuh"
+
+namespace laya {
+
+struct GemmLnArgs {
+  int M, N, K;              // N = C * 256
+  float* residual;          // [M][ldr] fp32, updated in place
+  int ldr;
+  const float* bias;        // [N] or nullptr
+  const float* gamma;       // [N]
+  const float* beta;        // [N] or nullptr
+  float eps;
+  void* x;                  // [M][ldx] T: the normalised rows
+  int ldx;
+  int* err;
+};
+
+constexpr int kLnBN = 256;
+
+template <int C>
+struct GemmLnCfg {
+  static constexpr int kStageA = kBM * kBK * 2;
+  static constexpr int kStageB = kLnBN * kBK * 2;
+  static constexpr int kStageBytes = kStageA + kStageB;
+  static constexpr int kStages = 3;
+  static constexpr int kOffEpi = kStages * kStageBytes;
+  // Exchange: [2 parity][2 round][2C partials][128 rows] fp32.
+  static constexpr int kOffX = kOffEpi + kEpiSmemBytes;
+  static constexpr int kXBytes = 2 * 2 * 2 * C * kBM * 4;
+  static constexpr int kOffBar = kOffX + kXBytes;
+  static constexpr int kSmemBytes = kOffBar + 256 + 1024;
+};
+
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// mbar_wait with cluster-scope acquire (the arrivals come from the cluster's other CTAs).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err, int code,
+                                                  volatile int* abort) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const unsigned long long start = global_ns();
+  for (uint32_t spin = 1;; ++spin) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((spin & 63) == 0) {
+      if (*abort) return false;
+      if (global_ns() - start > kWaitTimeoutNs) {
+        *abort = 1;
+        if (err) atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
+// Staging-block accessors for the coalesced <-> row-per-lane transposes (see gemm.cuh).
+__device__ __forceinline__ void stage_put_co(uint8_t* buf, int k, int lane, uint4 v) {
+  *reinterpret_cast<uint4*>(buf + stage_off(4 * k + (lane >> 3), lane & 7)) = v;
+}
+__device__ __forceinline__ uint4 stage_get_row(const uint8_t* buf, int lane, int j) {
+  return *reinterpret_cast<const uint4*>(buf + stage_off(lane, j));
+}
+
+template <int C, typename T>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_ln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmLnArgs args) {
+  using Cfg = GemmLnCfg<C>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + S * Cfg::kStageA;
+  float* xbuf = reinterpret_cast<float*>(smem + Cfg::kOffX);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + S;
+  uint64_t* tfull = bars + 2 * S;
+  uint64_t* tempty = bars + 2 * S + 2;
+  uint64_t* xbar = bars + 2 * S + 4;   // [2 parity][2 round]
+  uint64_t* drain = bars + 2 * S + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 9);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int rank = (int)cluster_rank();
+  const int cid = blockIdx.x / C, n_clusters = gridDim.x / C;
+  const int m_blocks = (args.M + kBM - 1) / kBM;
+  const int k_blocks = args.K / kBK;
+  const int nb = rank;  // this CTA's 256-column block
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], kEpiWarps); }
+    for (int i = 0; i < 4; ++i) mbar_init(&xbar[i], kEpiWarps * C);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) { tma_prefetch_desc(&tmA); tma_prefetch_desc(&tmB); }
+  if (warp == 1) { tmem_alloc(tmem_slot, 2 * kLnBN); tmem_relinquish(); }
+  tc_fence_before();
+  cluster_sync();  // every CTA's exchange barriers exist before the first remote arrival
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0; uint32_t phase = 0;
+      uint32_t issued = 0, last_par = 0;
+      bool ok = true;
+      // This CTA's weight slice does not depend on the previous kernel: the first tile's weight
+      // stages are loaded before waiting for it.
+      int pre = 0;
+      if (cid < m_blocks) {
+        pre = k_blocks < S ? k_blocks : S;
+        for (int kb = 0; kb < pre; ++kb) {
+          mbar_arrive_expect_tx(&full[kb], Cfg::kStageBytes);
+          tma_load_2d(sB + kb * Cfg::kStageB, &tmB, &full[kb], kb * kBK, nb * kLnBN);
+        }
+      }
+      pdl_wait();
+      for (int mb = cid; mb < m_blocks && ok; mb += n_clusters) {
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (mb == cid && kb < pre) {
+            tma_load_2d(sA + stage * Cfg::kStageA, &tmA, &full[stage], kb * kBK, mb * kBM);
+          } else {
+            if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrGemmProducerWait, abort_flag)) { ok = false; break; }
+            mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
+            tma_load_2d(sA + stage * Cfg::kStageA, &tmA, &full[stage], kb * kBK, mb * kBM);
+            tma_load_2d(sB + stage * Cfg::kStageB, &tmB, &full[stage], kb * kBK, nb * kLnBN);
+          }
+          issued |= 1u << stage;
+          last_par = (last_par & ~(1u << stage)) | (phase << stage);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+      }
+      if (!ok) {
+        for (int s = 0; s < S; ++s)
+          if (issued & (1u << s)) mbar_drain(&full[s], (last_par >> s) & 1);
+      }
+    } else {
+      pdl_wait();
+    }
+  } else if (warp == 1) {
+    pdl_wait();
+    if (lane == 0) {
+      const uint32_t idesc = mma_idesc<std::is_same<T, __nv_bfloat16>::value>(kBM, kLnBN);
+      int stage = 0; uint32_t phase = 0;
+      int acc = 0; uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int mb = cid; mb < m_blocks && ok; mb += n_clusters) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, args.err, kErrGemmMmaWait, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kLnBN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, args.err, kErrGemmMmaWait, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * Cfg::kStageA);
+          const uint32_t b0 = smem_u32(sB + stage * Cfg::kStageB);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            tc_mma_f16(d_tmem, smem_desc_sw128(a0 + k * 32), smem_desc_sw128(b0 + k * 32), idesc,
+                       (kb > 0 || k > 0) ? 1u : 0u);
+          tc_commit(&empty[stage]);
+          if (++stage == S) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(&tfull[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+      tc_commit(drain);
+      mbar_drain(drain, 0);
+    }
+  } else {
+    pdl_wait();
+    // Epilogue warp: TMEM lane quarter q (tile rows 32q..32q+31, one per lane) and column half h
+    // (this CTA's columns [128h, 128h + 128), four 32-column chunks).
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    uint8_t* stage = smem + Cfg::kOffEpi + (warp - 2) * kEpiStageBytes;
+    const int col0 = nb * kLnBN + half * 128;         // first global column of this warp
+    const float inv_n = 1.f / (float)args.N;
+    T* xout = reinterpret_cast<T*>(args.x);
+    // Exchange: publish this thread's partial (its row, this warp's 128 columns) into every CTA
+    // of the cluster, then wait for all C * 8 warps and return the row total.
+    auto exchange = [&](int par, int round, int lt, float partial, bool& fine) -> float {
+      const int slot = ((par * 2 + round) * 2 * C + rank * 2 + half) * kBM + quarter * 32 + lane;
+      const uint32_t local = smem_u32(xbuf + slot);
+      const uint32_t bar_local = smem_u32(&xbar[par * 2 + round]);
+#pragma unroll
+      for (int c = 0; c < C; ++c) st_cluster_f32(cluster_addr(local, c), partial);
+      __syncwarp();
+      if (lane == 0) {
+#pragma unroll
+        for (int c = 0; c < C; ++c) mbar_arrive_cluster(cluster_addr(bar_local, c));
+      }
+      fine = mbar_wait_cluster(&xbar[par * 2 + round], (lt >> 1) & 1, args.err, kErrGemmEpilogueWait, abort_flag);
+      float total = 0.f;
+      const float* row = xbuf + ((par * 2 + round) * 2 * C) * kBM + quarter * 32 + lane;
+#pragma unroll
+      for (int i = 0; i < 2 * C; ++i) total += row[i * kBM];
+      return total;
+    };
+    int acc = 0; uint32_t acc_phase = 0;
+    int lt = 0;  // local tile count
+    for (int mb = cid; mb < m_blocks; mb += n_clusters, ++lt) {
+      const int row0 = mb * kBM + quarter * 32;
+      const int rows = min(32, args.M - row0);  // may be <= 0: the warp still takes part in the exchanges
+      const int par = lt & 1;
+      // Residual chunks, coalesced (lane -> row 4k + lane/8, columns 4(lane%8)..+3), loaded two
+      // ahead; the first two before the accumulator is waited on.
+      float4 res[2][8];
+      auto load_res = [&](int j) {
+        const float* base = args.residual + col0 + 32 * j + (lane & 7) * 4;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int r = 4 * k + (lane >> 3);
+          res[j & 1][k] = r < rows ? *reinterpret_cast<const float4*>(base + (size_t)(row0 + r) * args.ldr)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      };
+      load_res(0);
+      load_res(1);
+      if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * kLnBN + half * 128;
+      // Pass A: v = acc + bias + residual -> HBM (residual) and TMEM (in place); row sums.
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t v[32];
+        tmem_ld32_async(tbase + 32 * j, v);
+        tmem_wait_ld(v);
+        uint4 p[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (args.bias) b = *reinterpret_cast<const float4*>(args.bias + col0 + 32 * j + 4 * q);
+          p[q] = u4(__uint_as_float(v[4 * q]) + b.x, __uint_as_float(v[4 * q + 1]) + b.y,
+                    __uint_as_float(v[4 * q + 2]) + b.z, __uint_as_float(v[4 * q + 3]) + b.w);
+        }
+        stage_put(stage, lane, p);  // row layout in
+        float* rbase = args.residual + col0 + 32 * j + (lane & 7) * 4;
+        // Each staged piece is read and rewritten by the same lane, so the update is in place.
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int r = 4 * k + (lane >> 3);
+          const float4 a = f4(stage_get(stage, k, lane));
+          const float4 t = res[j & 1][k];
+          const float4 nv = make_float4(t.x + a.x, t.y + a.y, t.z + a.z, t.w + a.w);
+          if (r < rows) *reinterpret_cast<float4*>(rbase + (size_t)(row0 + r) * args.ldr) = nv;
+          stage_put_co(stage, k, lane, make_uint4(__float_as_uint(nv.x), __float_as_uint(nv.y), __float_as_uint(nv.z),
+                                                  __float_as_uint(nv.w)));
+        }
+        if (j + 2 < 4) load_res(j + 2);
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint4 w = stage_get_row(stage, lane, q);
+          v[4 * q] = w.x; v[4 * q + 1] = w.y; v[4 * q + 2] = w.z; v[4 * q + 3] = w.w;
+          sum += (__uint_as_float(w.x) + __uint_as_float(w.y)) + (__uint_as_float(w.z) + __uint_as_float(w.w));
+        }
+        tmem_st32(tbase + 32 * j, v);
+      }
+      tmem_wait_st();
+      bool fine;
+      const float mean = exchange(par, 0, lt, sum, fine) * inv_n;
+      if (!__all_sync(0xffffffffu, fine)) break;
+      // Pass B: centred squares.
+      float sq = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t v[32];
+        tmem_ld32_async(tbase + 32 * j, v);
+        tmem_wait_ld(v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float d = __uint_as_float(v[i]) - mean;
+          sq = fmaf(d, d, sq);
+        }
+      }
+      const float var = exchange(par, 1, lt, sq, fine) * inv_n;
+      if (!__all_sync(0xffffffffu, fine)) break;
+      const float rstd = rsqrtf(var + args.eps);
+      // Pass C: x = (v - mean) * rstd * gamma (+ beta), 64 columns (128 bytes of T) per block.
+#pragma unroll
+      for (int pj = 0; pj < 2; ++pj) {
+        uint4 p[8];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int j = 2 * pj + h;
+          uint32_t v[32];
+          tmem_ld32_async(tbase + 32 * j, v);
+          tmem_wait_ld(v);
+          const int c0 = col0 + 32 * j;
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            float y[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              y[e] = (__uint_as_float(v[i + e]) - mean) * rstd * args.gamma[c0 + i + e];
+              if (args.beta) y[e] += args.beta[c0 + i + e];
+            }
+            p[h * 4 + i / 8] = make_uint4(pack2<T>(y[0], y[1]), pack2<T>(y[2], y[3]), pack2<T>(y[4], y[5]),
+                                          pack2<T>(y[6], y[7]));
+          }
+        }
+        stage_put(stage, lane, p);
+        T* xo = xout + col0 + 64 * pj;
+        stage_store16(stage, lane, rows, [&](int r) { return xo + (size_t)(row0 + r) * args.ldx; });
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while a peer may still write its exchange buffer
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, 2 * kLnBN);
+}
+
+}  // namespace laya

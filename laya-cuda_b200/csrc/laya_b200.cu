@@ -31,6 +31,7 @@
 #include "gemm.cuh"
 #include "rowops.cuh"
 #include "tc_attention.cuh"
+#include "gemm_ln.cuh"
 
 using namespace laya;
 
@@ -192,6 +193,66 @@ void launch_gemm_pair_bn(int epi, const CUtensorMap& ta, const CUtensorMap& tb, 
     case EPI_RESIDUAL: launch_gemm_pair_inst<T, BN, EPI_RESIDUAL>(ta, tb, a, grid, st); break;
     default: fail(LAYA_ERR_INVALID, "epilogue %d has no CTA-pair variant", epi);
   }
+}
+
+// Residual GEMM + LayerNorm: clusters of C = N/256 CTAs own 128-row blocks (persistent, as many
+// clusters as can be resident at once, at most one per row block).
+template <int C, typename T>
+void launch_gemm_ln_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmLnArgs& a, cudaStream_t st) {
+  static uint64_t configured = 0;  // one bit per device
+  static int max_clusters[64] = {};
+  auto kern = gemm_ln_kernel<C, T>;
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = GemmLnCfg<C>::kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = C;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  if (!(configured & (1ull << dev))) {
+    CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmLnCfg<C>::kSmemBytes));
+    int sms = 0;
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    cfg.gridDim = dim3(C * (sms / C));
+    cfg.numAttrs = 1;
+    int n = 0;
+    CK(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    max_clusters[dev & 63] = n > 0 ? n : 1;
+    configured |= 1ull << dev;
+  }
+  const int m_blocks = (a.M + kBM - 1) / kBM;
+  const int clusters = std::min(m_blocks, max_clusters[dev & 63]);
+  cfg.gridDim = dim3(C * clusters);
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  CK(cudaLaunchKernelEx(&cfg, kern, ta, tb, a));
+}
+
+template <typename T>
+void launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tb, const GemmLnArgs& a, cudaStream_t st) {
+  switch (a.N) {
+    case 256: launch_gemm_ln_inst<1, T>(ta, tb, a, st); break;
+    case 512: launch_gemm_ln_inst<2, T>(ta, tb, a, st); break;
+    case 768: launch_gemm_ln_inst<3, T>(ta, tb, a, st); break;
+    case 1024: launch_gemm_ln_inst<4, T>(ta, tb, a, st); break;
+    default: fail(LAYA_ERR_INVALID, "fused residual + LayerNorm needs N in {256, 512, 768, 1024}, got %d", a.N);
+  }
+}
+
+// The fused residual + LayerNorm GEMM (gemm_ln.cuh) serves classes that do not split K;
+// LAYA_GEMM_LN=0 in the environment falls back to the residual GEMM + norm kernel.
+bool gemm_ln_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("LAYA_GEMM_LN");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 // Rows from which GEMMs run as CTA pairs (256-row tiles); below, 1-CTA tiles (and split-K) fill
@@ -963,18 +1024,38 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
     return Pending{};
   };
 
+  // residual += A W^T + bias, then x = LN(residual): one fused kernel when the class does not
+  // split K, else the residual GEMM (or its split-K partials) followed by the norm kernel.
+  const bool fuse_ln = gemm_ln_enabled() && m > kSplitRowsMax && d % kLnBN == 0 && d <= 4 * kLnBN;
+  auto residual_ln = [&](int family, const CUtensorMap& ta, const std::string& wname, const float* bias,
+                         const float* gamma, const float* beta, float eps) {
+    if (!fuse_ln) {
+      const Pending pend = residual_gemm(family, ta, wname, m, residual, bias);
+      norm(residual, m, gamma, beta, eps, x, pend);
+      return;
+    }
+    const Tensor& w = W(e, wname);
+    GemmLnArgs a{};
+    a.M = m; a.N = (int)w.shape[0]; a.K = (int)w.shape[1];
+    a.residual = residual; a.ldr = d; a.bias = bias; a.gamma = gamma; a.beta = beta; a.eps = eps;
+    a.x = x; a.ldx = d; a.err = err;
+    const CUtensorMap tb = weight_map(e, wname, kLnBN);
+    launch(e, prof, family, 2.0 * m * a.N * a.K, [&] { launch_gemm_ln<T>(ta, tb, a, e.stream); });
+  };
+
   for (int i = 0; i < c.layers; ++i) {
     const std::string p = "encoder.layers." + std::to_string(i) + ".";
     const bool local = i % c.global_every != 0;
     gemm<T>(e, prof, FAM_GEMM_QKV, EPI_QKV, s.map_x, p + "attn.Wqkv.weight", m, qkv, 0, nullptr, 0, nullptr, err, local ? 1 : 0, positions);
     attention(local ? c.window : -1, false);
-    Pending pend = residual_gemm(FAM_GEMM_ATTN_OUT, s.map_attn, p + "attn.Wo.weight", m, residual, nullptr);
-    norm(residual, m, Wf(e, p + "mlp_norm.weight"), nullptr, c.eps, x, pend);
+    residual_ln(FAM_GEMM_ATTN_OUT, s.map_attn, p + "attn.Wo.weight", nullptr, Wf(e, p + "mlp_norm.weight"), nullptr,
+                c.eps);
     gemm<T>(e, prof, FAM_GEMM_FFN_UP, EPI_GEGLU, s.map_x, p + "mlp.Wi.weight", m, ff, e.F(), nullptr, 0, nullptr, err);
-    pend = residual_gemm(FAM_GEMM_FFN_DOWN, s.map_ff, p + "mlp.Wo.weight", m, residual, nullptr);
     if (i + 1 < c.layers) {
-      norm(residual, m, Wf(e, "encoder.layers." + std::to_string(i + 1) + ".attn_norm.weight"), nullptr, c.eps, x, pend);
+      residual_ln(FAM_GEMM_FFN_DOWN, s.map_ff, p + "mlp.Wo.weight", nullptr,
+                  Wf(e, "encoder.layers." + std::to_string(i + 1) + ".attn_norm.weight"), nullptr, c.eps);
     } else {
+      const Pending pend = residual_gemm(FAM_GEMM_FFN_DOWN, s.map_ff, p + "mlp.Wo.weight", m, residual, nullptr);
       // encoder.final_norm -> residual; residual += type_emb[kind]; x = head.layers.0.norm1(residual)
       NormArgs a{};
       a.residual = residual;
@@ -1541,6 +1622,24 @@ int laya_op_gemm(int precision, int epi, const void* x, const void* w, int M, in
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (bf) launch_gemm<__nv_bfloat16>(epi, bn, ta, tb, a, sms, st, pair);
   else launch_gemm<__half>(epi, bn, ta, tb, a, sms, st, pair);
+  API_END(nullptr)
+}
+
+int laya_op_gemm_ln(int precision, const void* x, const void* w, int M, int N, int K, float* residual, int ldr,
+                    const float* bias, const float* gamma, const float* beta, float eps, void* out, int ldo, int* err,
+                    void* stream) {
+  API_BEGIN
+  if (!residual || !gamma || !out) fail(LAYA_ERR_INVALID, "null argument");
+  const bool bf = precision == LAYA_PRECISION_BF16;
+  GemmLnArgs a{};
+  a.M = M; a.N = N; a.K = K;
+  a.residual = residual; a.ldr = ldr; a.bias = bias; a.gamma = gamma; a.beta = beta; a.eps = eps;
+  a.x = out; a.ldx = ldo; a.err = err;
+  const CUtensorMap ta = make_map(x, M, K, kBM, bf);
+  const CUtensorMap tb = make_map(w, N, K, kLnBN, bf);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (bf) launch_gemm_ln<__nv_bfloat16>(ta, tb, a, st);
+  else launch_gemm_ln<__half>(ta, tb, a, st);
   API_END(nullptr)
 }
 

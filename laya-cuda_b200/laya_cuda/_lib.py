@@ -19,7 +19,7 @@ EXPORTS = (
     "laya_shape_class",
     "laya_forward_device", "laya_packed_ints", "laya_pack", "laya_reserve", "laya_stream", "laya_set_profiling",
     "laya_profile_read", "laya_read_tensor", "laya_cached_shapes", "laya_pool_bytes", "laya_destroy",
-    "laya_last_error", "laya_op_gemm", "laya_interleave_geglu", "laya_op_attention", "laya_op_attention_gathered",
+    "laya_last_error", "laya_op_gemm", "laya_op_gemm_ln", "laya_interleave_geglu", "laya_op_attention", "laya_op_attention_gathered",
     "laya_attention_tiles", "laya_op_embed_norm", "laya_op_norm", "laya_op_gemm_residual_static",
 )
 STATIC_SCRATCH_FLOATS = 4 * 1024 * 1024
@@ -73,6 +73,7 @@ def load():
         "laya_destroy": (i, [p]),
         "laya_last_error": (ct.c_char_p, [p]),
         "laya_op_gemm": (i, [i, i, p, p, i, i, i, p, i, p, i, p, i, p, p, i, p, i, i, p, p]),
+        "laya_op_gemm_ln": (i, [i, p, p, i, i, i, p, i, p, p, p, ct.c_float, p, i, p, p]),
         "laya_interleave_geglu": (i, [p, p, i, i]),
         "laya_op_attention": (i, [i, i, p, p, p, i, p, p, i, i, i, i, p, p]),
         "laya_op_attention_gathered": (i, [i, p, p, p, i, p, p, i, i, i, p, p]),

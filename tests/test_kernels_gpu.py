@@ -376,3 +376,34 @@ def test_gathered_query_attention_matches_oracle(lib, prec, lengths, q_per_row):
             worst = max(worst, float(np.max(np.abs(got[t] - e) - ROUND[prec] * np.abs(e))))
     assert worst < ATTN_LIMIT[(prec, 0)], worst
     np.testing.assert_array_equal(got[~written], 7.0)
+
+
+@pytest.mark.parametrize("prec", ["f16", "bf16"])
+@pytest.mark.parametrize("M,N,K,with_bias", [(300, 768, 768, False), (4099, 768, 3072, False), (200, 256, 128, True),
+                                             (513, 512, 768, True), (130, 1024, 256, False)])
+def test_gemm_residual_layernorm_matches_fp64(lib, prec, M, N, K, with_bias):
+    """Fused residual GEMM + LayerNorm (clusters of N/256 CTAs exchanging row statistics):
+    residual += x W^T + bias and out = LN(residual) * gamma (+ beta) against float64."""
+    rng = np.random.default_rng(M + N + K)
+    x, xd = rand16((M, K), prec, rng)
+    w, wd = rand16((N, K), prec, rng, 0.02)
+    base = rng.normal(0, 1, (M, N)).astype(np.float32) + rng.normal(0, 0.5, (M, 1)).astype(np.float32)
+    bias = rng.normal(0, 0.1, N).astype(np.float32) if with_bias else None
+    gamma = (1 + rng.normal(0, 0.1, N)).astype(np.float32)
+    beta = rng.normal(0, 0.1, N).astype(np.float32) if with_bias else None
+    residual = torch.from_numpy(base.copy()).cuda()
+    out = torch.full((M, N), float("nan"), dtype=PRECISIONS[prec][1], device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    dev = lambda a: torch.from_numpy(a).cuda() if a is not None else None  # noqa: E731
+    b_t, g_t, be_t = dev(bias), dev(gamma), dev(beta)
+    _lib.check(lib.laya_op_gemm_ln(PRECISIONS[prec][0], ptr(x), ptr(w), M, N, K, ptr(residual), N, ptr(b_t), ptr(g_t),
+                                   ptr(be_t), 1e-5, ptr(out), N, ptr(err), stream()))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    want_r = base.astype(np.float64) + xd @ wd.T + (bias if with_bias else 0)
+    assert np.max(np.abs(residual.cpu().numpy() - want_r)) < 2e-4 * math.sqrt(K)
+    mean = want_r.mean(1, keepdims=True)
+    var = ((want_r - mean) ** 2).mean(1, keepdims=True)
+    want = (want_r - mean) / np.sqrt(var + 1e-5) * gamma + (beta if with_bias else 0)
+    got = out.double().cpu().numpy()
+    assert np.max(np.abs(got - want) - ROUND[prec] * np.abs(want)) < 2e-3
