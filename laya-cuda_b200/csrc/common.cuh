@@ -372,7 +372,30 @@ __device__ __forceinline__ float2 unpack2_f32(uint32_t v, __half*) {
   return __half22float2(p);
 }
 
-// Exact (erf-based) GELU, as the checkpoint's "gelu" activation specifies.
-__device__ __forceinline__ float gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+// 1/x on the special-function unit (PTX rcp.approx.ftz.f32).
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// The checkpoint's "gelu" activation, x * Phi(x) = x/2 (1 + erf(x / sqrt 2)), with erf from
+// Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26:
+//   erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-z^2),  t = 1 / (1 + p z),  z >= 0,
+// |error| <= 1.5e-7 (the GELU's absolute error stays below 5e-7 for every x, far under the
+// 16-bit rounding of its output).  Two special-function operations and nine FMA-pipe ones,
+// against ~6% of the FFN-up GEMM's time for the library erff.
+__device__ __forceinline__ float gelu_erf(float x) {
+  const float z = fabsf(x) * 0.70710678118654752f;
+  const float t = rcp_approx(fmaf(0.3275911f, z, 1.0f));
+  float poly = fmaf(1.061405429f, t, -1.453152027f);
+  poly = fmaf(poly, t, 1.421413741f);
+  poly = fmaf(poly, t, -0.284496736f);
+  poly = fmaf(poly, t, 0.254829592f);
+  poly *= t;
+  const float e = ex2_approx(-z * z * 1.4426950408889634f);  // exp(-z^2)
+  const float erf_v = copysignf(fmaf(-poly, e, 1.0f), x);
+  return 0.5f * x * (1.0f + erf_v);
+}
 
 }  // namespace laya

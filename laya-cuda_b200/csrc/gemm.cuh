@@ -54,7 +54,7 @@ struct GemmArgs {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kGemmThreads = 320;
+constexpr int kGemmThreads = 320;  // 10 warps: the busiest scheduler holds 3, so <= 168 registers
 constexpr int kEpiWarps = 8;
 
 // Per epilogue warp: a [32 rows][128 B] staging block in shared memory.  The warp's lanes own

@@ -6,19 +6,26 @@
 // (reference: runtime.py:96-108 calling linear, add and layer_norm, kernels.cu:20-49), so the
 // updated residual never makes a second trip through HBM for its normalisation.
 //
-// A LayerNorm needs whole rows, and a row of N = C x 256 fp32 accumulators does not fit one
+// A LayerNorm needs whole rows, and a row of N = C x BN fp32 accumulators does not fit one
 // SM's TMEM next to a second accumulator buffer, so C CTAs form a cluster that owns a 128-row
-// block: CTA `rank` computes columns [256 rank, 256 rank + 256) of it.  The row statistics are
-// combined through distributed shared memory: every epilogue warp writes its partial row sums
-// into every CTA of the cluster and arrives on that CTA's exchange mbarrier (release at cluster
-// scope; the waiter acquires at cluster scope).  Two rounds: the sum (mean), then the centred
-// sum of squares (variance), as the reference's two-pass LayerNorm.
+// block: CTA `rank` computes columns [BN rank, BN rank + BN) of it (d = 768: C = 3, BN = 256
+// with a 3-stage operand ring for short K, where the longer MMA per tile hides the epilogue;
+// C = 4, BN = 192 with a 4-stage ring for long K, where load latency matters more).  The row
+// statistics are combined through distributed shared memory: every epilogue thread computes,
+// for its row and its BN/2 columns, the partial sum and the partial centred sum of squares and
+// sends both to every CTA of the cluster with st.async, which counts its bytes on the
+// receiving CTA's exchange mbarrier (armed once per tile with the expected byte count).  No
+// release fence is involved, so the exchange does not wait for the epilogue's outstanding
+// global stores.  The partials are merged with Chan's parallel-variance formula,
+// M2 = sum M2_i + n sum (mean_i - mean)^2, so the result is the centred (two-pass) variance of
+// the reference's LayerNorm, with one exchange per tile.
 //
 // Per CTA the roles are those of gemm_kernel (warp 0 TMA, warp 1 TMEM + MMA, warps 2-9
-// epilogue; two 256-column TMEM accumulators so tile i's epilogue overlaps tile i+1's MMAs).
+// epilogue; two BN-column TMEM accumulators so tile i's epilogue overlaps tile i+1's MMAs).
 // The epilogue keeps the updated residual in the accumulator's TMEM columns between its three
-// passes: (A) v = acc + bias + residual, written to HBM and back to TMEM, row sums; (B) centred
-// squares; (C) x = (v - mean) * rstd * gamma (+ beta), rounded once.  Global traffic goes
+// passes: (A) v = acc + bias + residual, written to HBM and back to TMEM, with this thread's
+// partial sum and centred M2 (per 32-column chunk in registers, merged with Chan's formula);
+// exchange; (C) x = (v - mean) * rstd * gamma (+ beta), rounded once.  Global traffic goes
 // through the per-warp swizzled staging block of gemm.cuh, so it covers whole 128-byte lines.
 // Clusters walk the row blocks in lock step (same order in every CTA of a cluster).
 #pragma once
@@ -27,7 +34,7 @@
 namespace laya {
 
 struct GemmLnArgs {
-  int M, N, K;              // N = C * 256
+  int M, N, K;              // N = C * BN
   float* residual;          // [M][ldr] fp32, updated in place
   int ldr;
   const float* bias;        // [N] or nullptr
@@ -39,54 +46,29 @@ struct GemmLnArgs {
   int* err;
 };
 
-constexpr int kLnBN = 256;
-
-template <int C>
+template <int C, int BN>
 struct GemmLnCfg {
+  static_assert(BN == 192 || BN == 256, "column block of 192 or 256");
   static constexpr int kStageA = kBM * kBK * 2;
-  static constexpr int kStageB = kLnBN * kBK * 2;
+  static constexpr int kStageB = BN * kBK * 2;
   static constexpr int kStageBytes = kStageA + kStageB;
-  static constexpr int kStages = 3;
+  static constexpr int kStages = BN == 256 ? 3 : 4;
   static constexpr int kOffEpi = kStages * kStageBytes;
-  // Exchange: [2 parity][2 round][2C partials][128 rows] fp32.
+  static constexpr int kChunks = BN / 64;  // 32-column chunks per epilogue warp
+  // Exchange: [2 parity][2C partials][128 rows][sum, M2] fp32.
   static constexpr int kOffX = kOffEpi + kEpiSmemBytes;
-  static constexpr int kXBytes = 2 * 2 * 2 * C * kBM * 4;
+  static constexpr int kXBytes = 2 * 2 * C * kBM * 2 * 4;
+  static constexpr uint32_t kXTxBytes = C * kEpiWarps * 32 * 8;  // received per CTA per tile
   static constexpr int kOffBar = kOffX + kXBytes;
   static constexpr int kSmemBytes = kOffBar + 256 + 1024;
 };
 
-__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.b32 %0, 1, 0, p;\n\t}"
-      : "=r"(done)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
-// mbar_wait with cluster-scope acquire (the arrivals come from the cluster's other CTAs).
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* err, int code,
-                                                  volatile int* abort) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  const unsigned long long start = global_ns();
-  for (uint32_t spin = 1;; ++spin) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((spin & 63) == 0) {
-      if (*abort) return false;
-      if (global_ns() - start > kWaitTimeoutNs) {
-        *abort = 1;
-        if (err) atomicCAS(err, 0, code);
-        return false;
-      }
-    }
-  }
+// Asynchronous store of two floats into a cluster CTA's shared memory (cluster address `addr`,
+// 8-byte aligned) whose 8 bytes complete on the mbarrier at cluster address `bar`.
+__device__ __forceinline__ void st_async_f32x2(uint32_t addr, float a, float b, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+               "f"(a), "f"(b), "r"(bar)
+               : "memory");
 }
 
 // Staging-block accessors for the coalesced <-> row-per-lane transposes (see gemm.cuh).
@@ -97,11 +79,12 @@ __device__ __forceinline__ uint4 stage_get_row(const uint8_t* buf, int lane, int
   return *reinterpret_cast<const uint4*>(buf + stage_off(lane, j));
 }
 
-template <int C, typename T>
+template <int C, int BN, typename T>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_ln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const GemmLnArgs args) {
-  using Cfg = GemmLnCfg<C>;
+  using Cfg = GemmLnCfg<C, BN>;
+  constexpr int NCH = Cfg::kChunks;
   constexpr int S = Cfg::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -113,9 +96,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* empty = bars + S;
   uint64_t* tfull = bars + 2 * S;
   uint64_t* tempty = bars + 2 * S + 2;
-  uint64_t* xbar = bars + 2 * S + 4;   // [2 parity][2 round]
-  uint64_t* drain = bars + 2 * S + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 9);
+  uint64_t* xbar = bars + 2 * S + 4;   // [2 parity]
+  uint64_t* drain = bars + 2 * S + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 7);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -124,18 +107,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int cid = blockIdx.x / C, n_clusters = gridDim.x / C;
   const int m_blocks = (args.M + kBM - 1) / kBM;
   const int k_blocks = args.K / kBK;
-  const int nb = rank;  // this CTA's 256-column block
+  const int nb = rank;  // this CTA's BN-column block
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], kEpiWarps); }
-    for (int i = 0; i < 4; ++i) mbar_init(&xbar[i], kEpiWarps * C);
+    for (int i = 0; i < 2; ++i) mbar_init(&xbar[i], 1);  // armed with expect_tx once per tile
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) { tma_prefetch_desc(&tmA); tma_prefetch_desc(&tmB); }
-  if (warp == 1) { tmem_alloc(tmem_slot, 2 * kLnBN); tmem_relinquish(); }
+  if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
   tc_fence_before();
   cluster_sync();  // every CTA's exchange barriers exist before the first remote arrival
   tc_fence_after();
@@ -154,7 +137,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         pre = k_blocks < S ? k_blocks : S;
         for (int kb = 0; kb < pre; ++kb) {
           mbar_arrive_expect_tx(&full[kb], Cfg::kStageBytes);
-          tma_load_2d(sB + kb * Cfg::kStageB, &tmB, &full[kb], kb * kBK, nb * kLnBN);
+          tma_load_2d(sB + kb * Cfg::kStageB, &tmB, &full[kb], kb * kBK, nb * BN);
         }
       }
       pdl_wait();
@@ -166,7 +149,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrGemmProducerWait, abort_flag)) { ok = false; break; }
             mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
             tma_load_2d(sA + stage * Cfg::kStageA, &tmA, &full[stage], kb * kBK, mb * kBM);
-            tma_load_2d(sB + stage * Cfg::kStageB, &tmB, &full[stage], kb * kBK, nb * kLnBN);
+            tma_load_2d(sB + stage * Cfg::kStageB, &tmB, &full[stage], kb * kBK, nb * BN);
           }
           issued |= 1u << stage;
           last_par = (last_par & ~(1u << stage)) | (phase << stage);
@@ -183,14 +166,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     pdl_wait();
     if (lane == 0) {
-      const uint32_t idesc = mma_idesc<std::is_same<T, __nv_bfloat16>::value>(kBM, kLnBN);
+      const uint32_t idesc = mma_idesc<std::is_same<T, __nv_bfloat16>::value>(kBM, BN);
       int stage = 0; uint32_t phase = 0;
       int acc = 0; uint32_t acc_phase = 0;
       bool ok = true;
       for (int mb = cid; mb < m_blocks && ok; mb += n_clusters) {
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, args.err, kErrGemmMmaWait, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * kLnBN;
+        const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&full[stage], phase, args.err, kErrGemmMmaWait, abort_flag)) { ok = false; break; }
           tc_fence_after();
@@ -213,39 +196,48 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     pdl_wait();
     // Epilogue warp: TMEM lane quarter q (tile rows 32q..32q+31, one per lane) and column half h
-    // (this CTA's columns [128h, 128h + 128), four 32-column chunks).
+    // (this CTA's columns [h BN/2, (h+1) BN/2), NCH 32-column chunks).
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
     uint8_t* stage = smem + Cfg::kOffEpi + (warp - 2) * kEpiStageBytes;
-    const int col0 = nb * kLnBN + half * 128;         // first global column of this warp
+    const int col0 = nb * BN + half * (BN / 2);       // first global column of this warp
+    constexpr float kPart = (float)(BN / 2);          // columns per partial
     const float inv_n = 1.f / (float)args.N;
     T* xout = reinterpret_cast<T*>(args.x);
-    // Exchange: publish this thread's partial (its row, this warp's 128 columns) into every CTA
-    // of the cluster, then wait for all C * 8 warps and return the row total.
-    auto exchange = [&](int par, int round, int lt, float partial, bool& fine) -> float {
-      const int slot = ((par * 2 + round) * 2 * C + rank * 2 + half) * kBM + quarter * 32 + lane;
-      const uint32_t local = smem_u32(xbuf + slot);
-      const uint32_t bar_local = smem_u32(&xbar[par * 2 + round]);
+    // Exchange: send this thread's partials (sum and centred M2 of its row over this warp's
+    // columns) to every CTA of the cluster, wait until all C * 8 warps' partials have landed
+    // here, and merge them.  The tile's exchange barrier was armed at the start of the tile.
+    auto exchange = [&](int par, int lt, float sum, float m2, float& mean, float& var, bool& fine) {
+      const int slot = (par * 2 * C + rank * 2 + half) * kBM + quarter * 32 + lane;
+      const uint32_t local = smem_u32(xbuf + 2 * slot);
+      const uint32_t bar_local = smem_u32(&xbar[par]);
 #pragma unroll
-      for (int c = 0; c < C; ++c) st_cluster_f32(cluster_addr(local, c), partial);
-      __syncwarp();
-      if (lane == 0) {
-#pragma unroll
-        for (int c = 0; c < C; ++c) mbar_arrive_cluster(cluster_addr(bar_local, c));
-      }
-      fine = mbar_wait_cluster(&xbar[par * 2 + round], (lt >> 1) & 1, args.err, kErrGemmEpilogueWait, abort_flag);
+      for (int c = 0; c < C; ++c) st_async_f32x2(cluster_addr(local, c), sum, m2, cluster_addr(bar_local, c));
+      fine = mbar_wait(&xbar[par], (lt >> 1) & 1, args.err, kErrGemmEpilogueWait, abort_flag);
+      const float2* part = reinterpret_cast<const float2*>(xbuf) + (par * 2 * C) * kBM + quarter * 32 + lane;
       float total = 0.f;
-      const float* row = xbuf + ((par * 2 + round) * 2 * C) * kBM + quarter * 32 + lane;
 #pragma unroll
-      for (int i = 0; i < 2 * C; ++i) total += row[i * kBM];
-      return total;
+      for (int i = 0; i < 2 * C; ++i) total += part[i * kBM].x;
+      mean = total * inv_n;
+      float acc_m2 = 0.f, spread = 0.f;
+#pragma unroll
+      for (int i = 0; i < 2 * C; ++i) {
+        const float2 pi = part[i * kBM];
+        const float d = pi.x * (1.f / kPart) - mean;
+        acc_m2 += pi.y;
+        spread = fmaf(d, d, spread);
+      }
+      var = (acc_m2 + kPart * spread) * inv_n;
     };
     int acc = 0; uint32_t acc_phase = 0;
     int lt = 0;  // local tile count
     for (int mb = cid; mb < m_blocks; mb += n_clusters, ++lt) {
       const int row0 = mb * kBM + quarter * 32;
-      const int rows = min(32, args.M - row0);  // may be <= 0: the warp still takes part in the exchanges
+      const int rows = min(32, args.M - row0);  // may be <= 0: the warp still takes part in the exchange
       const int par = lt & 1;
+      // Arm this tile's exchange barrier with the bytes every CTA of the cluster will send here.
+      // (The previous use of this parity completed: this warp waited for it.)
+      if (warp == 2 && lane == 0) mbar_arrive_expect_tx(&xbar[par], Cfg::kXTxBytes);
       // Residual chunks, coalesced (lane -> row 4k + lane/8, columns 4(lane%8)..+3), loaded two
       // ahead; the first two before the accumulator is waited on.
       float4 res[2][8];
@@ -262,11 +254,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       load_res(1);
       if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag)) break;
       tc_fence_after();
-      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * kLnBN + half * 128;
-      // Pass A: v = acc + bias + residual -> HBM (residual) and TMEM (in place); row sums.
-      float sum = 0.f;
+      const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + half * (BN / 2);
+      // Pass A: v = acc + bias + residual -> HBM (residual) and TMEM (in place).  Each chunk's
+      // sum and centred M2 come from its 32 values in registers (two passes) and are merged into
+      // this thread's partial with Chan's formula, so no second pass over TMEM is needed.
+      float pm = 0.f, pm2 = 0.f;  // running mean and M2 of this thread's partial
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < NCH; ++j) {
         uint32_t v[32];
         tmem_ld32_async(tbase + 32 * j, v);
         tmem_wait_ld(v);
@@ -291,62 +285,69 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           stage_put_co(stage, k, lane, make_uint4(__float_as_uint(nv.x), __float_as_uint(nv.y), __float_as_uint(nv.z),
                                                   __float_as_uint(nv.w)));
         }
-        if (j + 2 < 4) load_res(j + 2);
+        if (j + 2 < NCH) load_res(j + 2);
         __syncwarp();
+        float cs = 0.f;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const uint4 w = stage_get_row(stage, lane, q);
           v[4 * q] = w.x; v[4 * q + 1] = w.y; v[4 * q + 2] = w.z; v[4 * q + 3] = w.w;
-          sum += (__uint_as_float(w.x) + __uint_as_float(w.y)) + (__uint_as_float(w.z) + __uint_as_float(w.w));
+          cs += (__uint_as_float(w.x) + __uint_as_float(w.y)) + (__uint_as_float(w.z) + __uint_as_float(w.w));
         }
         tmem_st32(tbase + 32 * j, v);
-      }
-      tmem_wait_st();
-      bool fine;
-      const float mean = exchange(par, 0, lt, sum, fine) * inv_n;
-      if (!__all_sync(0xffffffffu, fine)) break;
-      // Pass B: centred squares.
-      float sq = 0.f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t v[32];
-        tmem_ld32_async(tbase + 32 * j, v);
-        tmem_wait_ld(v);
+        const float cm = cs * (1.f / 32.f);
+        float cm2 = 0.f;
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float d = __uint_as_float(v[i]) - mean;
-          sq = fmaf(d, d, sq);
+          const float d = __uint_as_float(v[i]) - cm;
+          cm2 = fmaf(d, d, cm2);
         }
+        // Merge (32 j values, mean pm, M2 pm2) with (32 values, mean cm, M2 cm2).
+        const float delta = cm - pm;
+        pm += delta * (1.f / (float)(j + 1));
+        pm2 += cm2 + delta * delta * (32.f * (float)j / (float)(j + 1));
       }
-      const float var = exchange(par, 1, lt, sq, fine) * inv_n;
+      tmem_wait_st();
+      const float sum = pm * kPart, m2 = pm2;
+      bool fine;
+      float mean, var;
+      exchange(par, lt, sum, m2, mean, var, fine);
       if (!__all_sync(0xffffffffu, fine)) break;
       const float rstd = rsqrtf(var + args.eps);
-      // Pass C: x = (v - mean) * rstd * gamma (+ beta), 64 columns (128 bytes of T) per block.
+      // Pass C: x = (v - mean) * rstd * gamma (+ beta): 64 columns (128 bytes of T) per staged
+      // block, and a last 32-column block (64 bytes per row) when NCH is odd.
+      auto normalise = [&](int j, uint32_t (&v)[32], uint4* p) {
+        tmem_wait_ld(v);
+        const int c0 = col0 + 32 * j;
 #pragma unroll
-      for (int pj = 0; pj < 2; ++pj) {
-        uint4 p[8];
+        for (int i = 0; i < 32; i += 8) {
+          float y[8];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int j = 2 * pj + h;
-          uint32_t v[32];
-          tmem_ld32_async(tbase + 32 * j, v);
-          tmem_wait_ld(v);
-          const int c0 = col0 + 32 * j;
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            float y[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              y[e] = (__uint_as_float(v[i + e]) - mean) * rstd * args.gamma[c0 + i + e];
-              if (args.beta) y[e] += args.beta[c0 + i + e];
-            }
-            p[h * 4 + i / 8] = make_uint4(pack2<T>(y[0], y[1]), pack2<T>(y[2], y[3]), pack2<T>(y[4], y[5]),
-                                          pack2<T>(y[6], y[7]));
+          for (int e = 0; e < 8; ++e) {
+            y[e] = (__uint_as_float(v[i + e]) - mean) * rstd * args.gamma[c0 + i + e];
+            if (args.beta) y[e] += args.beta[c0 + i + e];
           }
+          p[i / 8] = make_uint4(pack2<T>(y[0], y[1]), pack2<T>(y[2], y[3]), pack2<T>(y[4], y[5]), pack2<T>(y[6], y[7]));
         }
+      };
+#pragma unroll
+      for (int j = 0; j < NCH; j += 2) {
+        uint4 p[8];
+        const int pieces = j + 1 < NCH ? 8 : 4;
+        uint32_t vb[2][32];
+        tmem_ld32_async(tbase + 32 * j, vb[0]);
+        if (pieces == 8) tmem_ld32_async(tbase + 32 * (j + 1), vb[1]);
+        normalise(j, vb[0], p);
+        if (pieces == 8) normalise(j + 1, vb[1], p + 4);
+        else p[4] = p[5] = p[6] = p[7] = make_uint4(0, 0, 0, 0);
         stage_put(stage, lane, p);
-        T* xo = xout + col0 + 64 * pj;
-        stage_store16(stage, lane, rows, [&](int r) { return xo + (size_t)(row0 + r) * args.ldx; });
+        T* xo = xout + col0 + 32 * j;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int r = 4 * k + (lane >> 3);
+          if (r < rows && (lane & 7) < pieces)
+            *reinterpret_cast<uint4*>(xo + (size_t)(row0 + r) * args.ldx + (lane & 7) * 8) = stage_get(stage, k, lane);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -358,7 +359,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   cluster_sync();  // no CTA leaves while a peer may still write its exchange buffer
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, 2 * kLnBN);
+  if (warp == 1) tmem_dealloc(tmem_base, 512);
 }
 
 }  // namespace laya

@@ -195,18 +195,18 @@ void launch_gemm_pair_bn(int epi, const CUtensorMap& ta, const CUtensorMap& tb, 
   }
 }
 
-// Residual GEMM + LayerNorm: clusters of C = N/256 CTAs own 128-row blocks (persistent, as many
+// Residual GEMM + LayerNorm: clusters of C = N/BN CTAs own 128-row blocks (persistent, as many
 // clusters as can be resident at once, at most one per row block).
-template <int C, typename T>
+template <int C, int BN, typename T>
 void launch_gemm_ln_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmLnArgs& a, cudaStream_t st) {
   static uint64_t configured = 0;  // one bit per device
   static int max_clusters[64] = {};
-  auto kern = gemm_ln_kernel<C, T>;
+  auto kern = gemm_ln_kernel<C, BN, T>;
   int dev = 0;
   CK(cudaGetDevice(&dev));
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(kGemmThreads);
-  cfg.dynamicSmemBytes = GemmLnCfg<C>::kSmemBytes;
+  cfg.dynamicSmemBytes = GemmLnCfg<C, BN>::kSmemBytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -217,7 +217,7 @@ void launch_gemm_ln_inst(const CUtensorMap& ta, const CUtensorMap& tb, const Gem
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   if (!(configured & (1ull << dev))) {
-    CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmLnCfg<C>::kSmemBytes));
+    CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GemmLnCfg<C, BN>::kSmemBytes));
     int sms = 0;
     CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     cfg.gridDim = dim3(C * (sms / C));
@@ -234,15 +234,27 @@ void launch_gemm_ln_inst(const CUtensorMap& ta, const CUtensorMap& tb, const Gem
   CK(cudaLaunchKernelEx(&cfg, kern, ta, tb, a));
 }
 
+// Column block of the fused residual + LayerNorm GEMM for row width N and depth K (0: not
+// supported).  256-column blocks (3-stage ring) for short K; 192 (4-stage ring) for long K.
+int ln_block_n(int N, int K) {
+  const bool b256 = N % 256 == 0 && N / 256 <= 4, b192 = N % 192 == 0 && N / 192 <= 4;
+  if (b256 && (K <= 1024 || !b192)) return 256;
+  if (b192) return 192;
+  return 0;
+}
+
 template <typename T>
-void launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tb, const GemmLnArgs& a, cudaStream_t st) {
-  switch (a.N) {
-    case 256: launch_gemm_ln_inst<1, T>(ta, tb, a, st); break;
-    case 512: launch_gemm_ln_inst<2, T>(ta, tb, a, st); break;
-    case 768: launch_gemm_ln_inst<3, T>(ta, tb, a, st); break;
-    case 1024: launch_gemm_ln_inst<4, T>(ta, tb, a, st); break;
-    default: fail(LAYA_ERR_INVALID, "fused residual + LayerNorm needs N in {256, 512, 768, 1024}, got %d", a.N);
-  }
+void launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tb, const GemmLnArgs& a, int bn, cudaStream_t st) {
+  const int c = a.N / bn;
+  if (bn == 256 && c == 1) launch_gemm_ln_inst<1, 256, T>(ta, tb, a, st);
+  else if (bn == 256 && c == 2) launch_gemm_ln_inst<2, 256, T>(ta, tb, a, st);
+  else if (bn == 256 && c == 3) launch_gemm_ln_inst<3, 256, T>(ta, tb, a, st);
+  else if (bn == 256 && c == 4) launch_gemm_ln_inst<4, 256, T>(ta, tb, a, st);
+  else if (bn == 192 && c == 1) launch_gemm_ln_inst<1, 192, T>(ta, tb, a, st);
+  else if (bn == 192 && c == 2) launch_gemm_ln_inst<2, 192, T>(ta, tb, a, st);
+  else if (bn == 192 && c == 3) launch_gemm_ln_inst<3, 192, T>(ta, tb, a, st);
+  else if (bn == 192 && c == 4) launch_gemm_ln_inst<4, 192, T>(ta, tb, a, st);
+  else fail(LAYA_ERR_INVALID, "fused residual + LayerNorm: N=%d is not 1-4 blocks of 192 or 256 columns", a.N);
 }
 
 // The fused residual + LayerNorm GEMM (gemm_ln.cuh) serves classes that do not split K;
@@ -1026,21 +1038,22 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
 
   // residual += A W^T + bias, then x = LN(residual): one fused kernel when the class does not
   // split K, else the residual GEMM (or its split-K partials) followed by the norm kernel.
-  const bool fuse_ln = gemm_ln_enabled() && m > kSplitRowsMax && d % kLnBN == 0 && d <= 4 * kLnBN;
+  const bool fuse_ln = gemm_ln_enabled() && m > kSplitRowsMax;
   auto residual_ln = [&](int family, const CUtensorMap& ta, const std::string& wname, const float* bias,
                          const float* gamma, const float* beta, float eps) {
-    if (!fuse_ln) {
+    const Tensor& w = W(e, wname);
+    const int bn = ln_block_n((int)w.shape[0], (int)w.shape[1]);
+    if (!fuse_ln || !bn) {
       const Pending pend = residual_gemm(family, ta, wname, m, residual, bias);
       norm(residual, m, gamma, beta, eps, x, pend);
       return;
     }
-    const Tensor& w = W(e, wname);
     GemmLnArgs a{};
     a.M = m; a.N = (int)w.shape[0]; a.K = (int)w.shape[1];
     a.residual = residual; a.ldr = d; a.bias = bias; a.gamma = gamma; a.beta = beta; a.eps = eps;
     a.x = x; a.ldx = d; a.err = err;
-    const CUtensorMap tb = weight_map(e, wname, kLnBN);
-    launch(e, prof, family, 2.0 * m * a.N * a.K, [&] { launch_gemm_ln<T>(ta, tb, a, e.stream); });
+    const CUtensorMap tb = weight_map(e, wname, bn);
+    launch(e, prof, family, 2.0 * m * a.N * a.K, [&] { launch_gemm_ln<T>(ta, tb, a, bn, e.stream); });
   };
 
   for (int i = 0; i < c.layers; ++i) {
@@ -1636,10 +1649,12 @@ int laya_op_gemm_ln(int precision, const void* x, const void* w, int M, int N, i
   a.residual = residual; a.ldr = ldr; a.bias = bias; a.gamma = gamma; a.beta = beta; a.eps = eps;
   a.x = out; a.ldx = ldo; a.err = err;
   const CUtensorMap ta = make_map(x, M, K, kBM, bf);
-  const CUtensorMap tb = make_map(w, N, K, kLnBN, bf);
+  const int bn = ln_block_n(N, K);
+  if (!bn) fail(LAYA_ERR_INVALID, "fused residual + LayerNorm: N=%d is not 1-4 blocks of 192 or 256 columns", N);
+  const CUtensorMap tb = make_map(w, N, K, bn, bf);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (bf) launch_gemm_ln<__nv_bfloat16>(ta, tb, a, st);
-  else launch_gemm_ln<__half>(ta, tb, a, st);
+  if (bf) launch_gemm_ln<__nv_bfloat16>(ta, tb, a, bn, st);
+  else launch_gemm_ln<__half>(ta, tb, a, bn, st);
   API_END(nullptr)
 }
 

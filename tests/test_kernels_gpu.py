@@ -380,9 +380,10 @@ def test_gathered_query_attention_matches_oracle(lib, prec, lengths, q_per_row):
 
 @pytest.mark.parametrize("prec", ["f16", "bf16"])
 @pytest.mark.parametrize("M,N,K,with_bias", [(300, 768, 768, False), (4099, 768, 3072, False), (200, 256, 128, True),
-                                             (513, 512, 768, True), (130, 1024, 256, False)])
+                                             (513, 512, 768, True), (130, 1024, 256, False), (257, 384, 256, True),
+                                             (300, 576, 512, False)])
 def test_gemm_residual_layernorm_matches_fp64(lib, prec, M, N, K, with_bias):
-    """Fused residual GEMM + LayerNorm (clusters of N/256 CTAs exchanging row statistics):
+    """Fused residual GEMM + LayerNorm (clusters of CTAs exchanging row statistics):
     residual += x W^T + bias and out = LN(residual) * gamma (+ beta) against float64."""
     rng = np.random.default_rng(M + N + K)
     x, xd = rand16((M, K), prec, rng)
