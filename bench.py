@@ -395,9 +395,9 @@ def run_engine(args, rank, world, local_rank):
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one FFN-up GEMM launch per token (ncu capture
-# of a 28,617-token launch, summarised in profiles/gemm_ffn_up_geglu_config5.md: 179.8 MB);
+# of a 39,518-token launch, summarised in profiles/gemm_ffn_up_geglu_config5.md: 266.0 MB);
 # traffic grows in proportion to the rows, so a full launch is this times its tokens.
-TRAFFIC_FFN_UP_BYTES_PER_TOKEN = 179.8e6 / 28617
+TRAFFIC_FFN_UP_BYTES_PER_TOKEN = 266.0e6 / 39518
 
 
 def main():

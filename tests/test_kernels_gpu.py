@@ -116,7 +116,8 @@ def rope_tables(theta, rows):
 
 
 @pytest.mark.parametrize("prec", ["bf16", "f16"])
-@pytest.mark.parametrize("rope,M,block_n", [(True, 208, 0), (False, 208, 0), (True, 2320, -256), (False, 2320, -128)])
+@pytest.mark.parametrize("rope,M,block_n", [(True, 208, 0), (False, 208, 0), (True, 2320, -256), (False, 2320, -128),
+                                            (True, 203, 0)])
 def test_gemm_qkv_rope_layout(lib, prec, rope, M, block_n):
     """Encoder QKV (RoPE, no bias) and head in_proj (bias, no RoPE) epilogues, 1-CTA and CTA-pair
     kernels; cf. tests/test_gpu.py:36-53."""
