@@ -284,6 +284,13 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 
+// Arrival without release semantics: for signals that order nothing but work the arriving
+// thread has already completed synchronously (e.g. TMEM reads finished by tcgen05.wait::ld), so
+// the arrival does not wait for the thread's outstanding global stores.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
 // TMA load into this CTA's shared memory whose completion is counted on an mbarrier of the pair
 // leader (cluster address).  No multicast.
 __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, uint32_t leader_bar, int x,

@@ -606,7 +606,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       else epilogue_tile<BN, EPI, T>(args, tbase, row0, nb * BN, 0, half, lane, stage);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(acc == 0 ? leader_tempty0 : leader_tempty1);
+      // The accumulator's TMEM columns were read to completion (tcgen05.wait::ld) before this
+      // point; the tile's global stores need no ordering with the next MMAs, so the arrival is
+      // relaxed and does not wait for them.
+      if (lane == 0) mbar_arrive_cluster_relaxed(acc == 0 ? leader_tempty0 : leader_tempty1);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
   }

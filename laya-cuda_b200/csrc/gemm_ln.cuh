@@ -229,6 +229,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       var = (acc_m2 + kPart * spread) * inv_n;
     };
+    // Residual chunks, coalesced (lane -> row 4k + lane/8, columns 4(lane%8)..+3), loaded two
+    // ahead.  The first two chunks of the next tile are loaded as soon as this tile's pass A has
+    // consumed its own, so their latency overlaps the exchange and pass C.
+    float4 res[2][8];
+    auto load_res = [&](int row0, int rows, int j) {
+      const float* base = args.residual + col0 + 32 * j + (lane & 7) * 4;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int r = 4 * k + (lane >> 3);
+        res[j & 1][k] = r < rows ? *reinterpret_cast<const float4*>(base + (size_t)(row0 + r) * args.ldr)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    };
+    if (cid < m_blocks) {
+      const int row0 = cid * kBM + quarter * 32;
+      load_res(row0, min(32, args.M - row0), 0);
+      load_res(row0, min(32, args.M - row0), 1);
+    }
     int acc = 0; uint32_t acc_phase = 0;
     int lt = 0;  // local tile count
     for (int mb = cid; mb < m_blocks; mb += n_clusters, ++lt) {
@@ -238,20 +256,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // Arm this tile's exchange barrier with the bytes every CTA of the cluster will send here.
       // (The previous use of this parity completed: this warp waited for it.)
       if (warp == 2 && lane == 0) mbar_arrive_expect_tx(&xbar[par], Cfg::kXTxBytes);
-      // Residual chunks, coalesced (lane -> row 4k + lane/8, columns 4(lane%8)..+3), loaded two
-      // ahead; the first two before the accumulator is waited on.
-      float4 res[2][8];
-      auto load_res = [&](int j) {
-        const float* base = args.residual + col0 + 32 * j + (lane & 7) * 4;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int r = 4 * k + (lane >> 3);
-          res[j & 1][k] = r < rows ? *reinterpret_cast<const float4*>(base + (size_t)(row0 + r) * args.ldr)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-      };
-      load_res(0);
-      load_res(1);
       if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + half * (BN / 2);
@@ -285,7 +289,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           stage_put_co(stage, k, lane, make_uint4(__float_as_uint(nv.x), __float_as_uint(nv.y), __float_as_uint(nv.z),
                                                   __float_as_uint(nv.w)));
         }
-        if (j + 2 < NCH) load_res(j + 2);
+        if (j + 2 < NCH) load_res(row0, rows, j + 2);
         __syncwarp();
         float cs = 0.f;
 #pragma unroll
@@ -308,6 +312,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         pm2 += cm2 + delta * delta * (32.f * (float)j / (float)(j + 1));
       }
       tmem_wait_st();
+      if (mb + n_clusters < m_blocks) {
+        const int next0 = (mb + n_clusters) * kBM + quarter * 32;
+        load_res(next0, min(32, args.M - next0), 0);
+        load_res(next0, min(32, args.M - next0), 1);
+      }
       const float sum = pm * kPart, m2 = pm2;
       bool fine;
       float mean, var;

@@ -4,10 +4,13 @@ The library is built in-tree next to this file (see build.py).  There is no fall
 library is missing, importing the runtime raises, so a run never silently executes elsewhere.
 """
 import ctypes as ct
+import os
 from pathlib import Path
 
 LIB_NAME = "liblaya_b200.so"
-LIB_PATH = Path(__file__).with_name(LIB_NAME)
+# LAYA_LIB points at another build of the library (an alternative configuration to compare
+# against); by default the in-tree build next to this file.
+LIB_PATH = Path(os.environ["LAYA_LIB"]) if os.environ.get("LAYA_LIB") else Path(__file__).with_name(LIB_NAME)
 
 OK, ERR_INVALID, ERR_CUDA, ERR_DEVICE, ERR_STATE, ERR_NO_DEVICE = range(6)
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
