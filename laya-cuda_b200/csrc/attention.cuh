@@ -79,7 +79,6 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnArgs 
   __shared__ __align__(128) uint8_t sK[2][kAttnKB * 128];
   __shared__ __align__(128) uint8_t sV[2][kAttnKB * 128];
 
-  pdl_trigger();
   pdl_wait();
   const int4 tile = a.tiles[blockIdx.y];  // grid: (heads, tiles), all heads of a tile together
   const int head = blockIdx.x;

@@ -341,7 +341,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   // The prologue above touches no predecessor output.
-  pdl_trigger();
 
   // Tile order: split outermost, then row block, then column block, so CTAs running together
   // share an A row block (it stays in L2 while all its column blocks are computed).
@@ -525,7 +524,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   cluster_sync();  // both CTAs' barriers initialised before any cross-CTA arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  pdl_trigger();
   pdl_wait();
 
   if (warp == 0) {

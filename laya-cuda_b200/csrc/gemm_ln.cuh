@@ -123,7 +123,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   cluster_sync();  // every CTA's exchange barriers exist before the first remote arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {

@@ -94,7 +94,6 @@ template <int NPL, typename T>
 __global__ void __launch_bounds__(kRowWarps * 32) embed_norm_kernel(const int* ids, const float* table,
                                                                     const float* gamma, float eps, int rows, int d,
                                                                     int vocab, float* residual, T* x, int* err) {
-  pdl_trigger();
   pdl_wait();
   const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -130,7 +129,6 @@ struct NormArgs {
 // variant's register footprint small.  Replaces kernels.cu:20-49 and kernels.cu:155-158.
 template <int NPL, typename T, bool PARTIALS>
 __global__ void __launch_bounds__(kRowWarps * 32) norm_kernel(const NormArgs a) {
-  pdl_trigger();
   pdl_wait();
   const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= a.rows) return;
@@ -190,7 +188,6 @@ template <typename T>
 __global__ void __launch_bounds__(256) gather_rows_kernel(const float* residual, const T* attention,
                                                           const int* indices, int count, int d, int rows,
                                                           float* selected, T* scored, int* err) {
-  pdl_trigger();
   pdl_wait();
   const int i = blockIdx.x;
   if (i >= count) return;
@@ -239,7 +236,6 @@ __device__ __forceinline__ float warp_max(float x) {
 // Dynamic shared memory: features [d+4], hidden [256], logits [k+1].
 template <typename T>
 __global__ void __launch_bounds__(kTailThreads) head_tail_kernel(const TailArgs a) {
-  pdl_trigger();
   pdl_wait();
   extern __shared__ float sh[];
   __shared__ int s_last;

@@ -151,8 +151,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
   T* out = reinterpret_cast<T*>(a.out);
   if (row < 0) {
     // Tokens past the last row: zeros (8 x 16 bytes per token and head).
-    pdl_trigger();
-    pdl_wait();
+      pdl_wait();
     for (int i = threadIdx.x; i < (t1 - t0) * 8; i += kTcThreads) {
       const int t = t0 + (i >> 3);
       *reinterpret_cast<uint4*>(out + (size_t)t * width + head * 64 + (i & 7) * 8) = make_uint4(0, 0, 0, 0);
@@ -203,7 +202,6 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  pdl_trigger();
   pdl_wait();
 
   if (warp == 0) {
