@@ -6,21 +6,23 @@
 //
 // Work unit: one CTA per (128-query tile of one row, head); the host's tile table never lets a
 // tile straddle rows.  Two CTAs share an SM (82 KB shared memory and 256 TMEM columns each).
-// 6 warps:
-//   warp 0     TMA: the Q tile once, then per 128-key block the K tile and the V^T tile into
-//              double-buffered stages (128-byte swizzle, no multicast).
-//   warp 1     TMEM allocation + MMA issue (one thread):
-//                S_j = Q K_j^T        (M=128, N=128, K=64)   TMEM columns [0,128), fp32
-//                O  += P_j V_j        (M=128, N=64,  K=128)  A = P from TMEM, O in [192,256)
-//              S_{j+1} is issued as soon as the softmax has read S_j, so the tensor core works on
-//              the next block while the softmax computes this one.
-//   warps 2-5  softmax, one thread per query row (its TMEM lane): loads its row of S_j with all
-//              loads in flight before one wait, masks only the 32-key chunks that straddle a
-//              boundary and skips chunks no query of the warp can see, keeps the running
-//              maximum m and sum l in fp32, and writes P = 2^(s*log2e/8 - m) as 16-bit pairs
-//              into TMEM columns [128,192) for the P V product.  O stays in TMEM: it is rescaled
-//              (read, scaled, written back) only when the row maximum grows by more than 2^8, so
-//              P is at most 256 and the final O / l is unchanged.
+// 4 warps, one thread per query row (warp w owns TMEM lanes [32w, 32w + 32)).  Every warp runs
+// the softmax: it loads its rows of S_j with all loads in flight before one wait, masks only the
+// 32-key chunks that straddle a boundary and skips chunks no query of the warp can see, keeps
+// the running maximum m and sum l in fp32 (paired fp32 instructions for the scale-and-subtract
+// and the sums), and writes P = 2^(s*log2e/8 - m) as 16-bit pairs into TMEM columns [128,192).
+// O stays in TMEM: it is rescaled (read, scaled, written back) only when the row maximum grows
+// by more than 2^8, so P is at most 256 and the final O / l is unchanged.  Warp 0 also controls
+// the pipeline (TMEM allocation; one lane issues copies and MMAs):
+//   TMA   the Q tile, then per 128-key block the K tile and the V^T tile into double-buffered
+//         stages (128-byte swizzle, no multicast), each refilled once warp 0 has observed the
+//         completion of the MMA that last read it;
+//   S_j = Q K_j^T   (M=128, N=128, K=64)  TMEM columns [0,128), fp32, issued as soon as every
+//         warp has read S_{j-1}, so the tensor core works on the next block during the softmax;
+//   O += P_j V_j    (M=128, N=64, K=128)  A = P from TMEM, O in [192,256), issued as soon as
+//         every warp has written P_j.
+// Without separate copy and MMA warps the CTA has 128 threads, so two CTAs per SM leave each
+// thread 255 registers (the softmax keeps a 128-key row of S in registers without spilling).
 // Key blocks start at the window's first key (rounded down to 16 tokens), not at a multiple of
 // 128, so a 128-query tile of a window-64 layer reads two blocks.
 // Inputs (from the QKV GEMM epilogue): Q, K [heads][M][64] (K-major rows of 128 bytes) and V
@@ -33,7 +35,7 @@ namespace laya {
 
 constexpr int kTcQ = 128;              // queries per CTA
 constexpr int kTcKB = 128;             // keys per block
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 128;
 constexpr int kTcTmemCols = 256;       // S: [0,128), P: [128,192), O: [192,256)
 constexpr float kTcRescaleLog2 = 8.f;  // O is rescaled when the row maximum grows by more than 2^8
 
@@ -89,7 +91,8 @@ __device__ __forceinline__ float tc_block_max(uint32_t (&sx)[4][32], uint32_t vi
         if ((uint32_t)(d + i) > span_keys) sx[c][i] = __float_as_uint(-INFINITY);
     }
 #pragma unroll
-    for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(sx[c][i]));
+    for (int i = 0; i < 32; i += 2)
+      mx[(i >> 1) & 7] = max3(mx[(i >> 1) & 7], __uint_as_float(sx[c][i]), __uint_as_float(sx[c][i + 1]));
   }
 #pragma unroll
   for (int w = 4; w >= 1; w >>= 1)
@@ -103,17 +106,18 @@ __device__ __forceinline__ float tc_block_max(uint32_t (&sx)[4][32], uint32_t vi
 template <bool kAll, typename T>
 __device__ __forceinline__ float tc_block_probs(const uint32_t (&sx)[4][32], uint32_t vis, float scale, float sub,
                                                 uint32_t p_tmem) {
-  float sm[4] = {0.f, 0.f, 0.f, 0.f};
+  float2 sm[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+  const float2 sc = make_float2(scale, scale), ns = make_float2(-sub, -sub);
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
     uint32_t pk[16];
     if (kAll || ((vis >> c) & 1)) {
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
-        const float p0 = ex2_approx(fmaf(__uint_as_float(sx[c][i]), scale, -sub));
-        const float p1 = ex2_approx(fmaf(__uint_as_float(sx[c][i + 1]), scale, -sub));
-        sm[(i >> 1) & 3] += p0 + p1;
-        pk[i >> 1] = pack2<T>(p0, p1);
+        const float2 x = fma2(make_float2(__uint_as_float(sx[c][i]), __uint_as_float(sx[c][i + 1])), sc, ns);
+        const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+        sm[(i >> 1) & 3] = add2(sm[(i >> 1) & 3], p);
+        pk[i >> 1] = pack2<T>(p.x, p.y);
       }
     } else {
 #pragma unroll
@@ -121,7 +125,8 @@ __device__ __forceinline__ float tc_block_probs(const uint32_t (&sx)[4][32], uin
     }
     tmem_st16(p_tmem + 16 * c, pk);
   }
-  return (sm[0] + sm[1]) + (sm[2] + sm[3]);
+  const float2 t = add2(add2(sm[0], sm[1]), add2(sm[2], sm[3]));
+  return t.x + t.y;
 }
 
 template <typename T>
@@ -151,7 +156,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
   T* out = reinterpret_cast<T*>(a.out);
   if (row < 0) {
     // Tokens past the last row: zeros (8 x 16 bytes per token and head).
-      pdl_wait();
+    pdl_wait();
     for (int i = threadIdx.x; i < (t1 - t0) * 8; i += kTcThreads) {
       const int t = t0 + (i >> 3);
       *reinterpret_cast<uint4*>(out + (size_t)t * width + head * 64 + (i & 7) * 8) = make_uint4(0, 0, 0, 0);
@@ -175,239 +180,248 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + TcAttnSmem::kOffBar);
   uint64_t* q_full = bar + 0;
   uint64_t* k_full = bar + 1;   // [2]
-  uint64_t* k_empty = bar + 3;  // [2]
-  uint64_t* v_full = bar + 5;   // [2]
-  uint64_t* v_empty = bar + 7;  // [2]
-  uint64_t* s_full = bar + 9;
-  uint64_t* s_free = bar + 10;
-  uint64_t* p_full = bar + 11;
-  uint64_t* o_full = bar + 12;
-  uint64_t* drain = bar + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
+  uint64_t* v_full = bar + 3;   // [2]
+  uint64_t* s_full = bar + 5;
+  uint64_t* s_free = bar + 6;
+  uint64_t* p_full = bar + 7;
+  uint64_t* o_full = bar + 8;
+  uint64_t* drain = bar + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 10);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
+  // Thread <-> query row r = TMEM lane r: warp w owns lanes [32w, 32w + 32).
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = threadIdx.x;
+  const bool ctl = warp == 0;  // the control warp: TMEM allocation, copies and MMA issue (lane 0)
   if (threadIdx.x == 0) {
-    mbar_init(q_full, gathered ? 4 : 1);  // gathered: the four softmax warps write Q
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(k_full + s, 1); mbar_init(k_empty + s, 1); mbar_init(v_full + s, 1); mbar_init(v_empty + s, 1);
-    }
+    mbar_init(q_full, gathered ? 4 : 1);  // gathered: the four warps write Q
+    for (int s = 0; s < 2; ++s) { mbar_init(k_full + s, 1); mbar_init(v_full + s, 1); }
     mbar_init(s_full, 1); mbar_init(s_free, 4); mbar_init(p_full, 4); mbar_init(o_full, 1); mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
+    tma_prefetch_desc(&tmQK);
+    tma_prefetch_desc(&tmVt);
   }
-  if (warp == 0 && lane == 0) { tma_prefetch_desc(&tmQK); tma_prefetch_desc(&tmVt); }
-  if (warp == 1) { tmem_alloc(tmem_slot, kTcTmemCols); tmem_relinquish(); }
+  if (ctl) { tmem_alloc(tmem_slot, kTcTmemCols); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();
 
-  if (warp == 0) {
+  constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
+  const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
+  const uint32_t s_tmem = tmem_base + lane_addr, p_tmem = s_tmem + 128, o_tmem = s_tmem + 192;
+  const int plane_rows = a.heads * a.M;
+  int k_issued = 0, v_issued = 0;  // copies issued (control lane)
+  // Copies into stage j & 1; the control warp issues one only after observing the completion of
+  // the MMA that last read the stage (S_{j-2} for K, P_{j-2} V_{j-2} for V).
+  auto load_k = [&](int j) {
+    const int st = j & 1;
+    mbar_arrive_expect_tx(k_full + st, TcAttnSmem::kK);
+    tma_load_2d(sK + st * TcAttnSmem::kK, &tmQK, k_full + st, 0, plane_rows + head * a.M + first + k_lo + j * kTcKB);
+    k_issued = j + 1;
+  };
+  auto load_v = [&](int j) {
+    const int st = j & 1;
+    mbar_arrive_expect_tx(v_full + st, TcAttnSmem::kV);
+    uint8_t* v = sV + st * TcAttnSmem::kV;
+    const int key0 = first + k_lo + j * kTcKB;  // absolute token of the block's first key
+    tma_load_2d(v, &tmVt, v_full + st, key0, head * 64);
+    tma_load_2d(v + 64 * 128, &tmVt, v_full + st, key0 + 64, head * 64);
+    v_issued = j + 1;
+  };
+  // S_j = Q K_j^T into TMEM columns [0, 128) once K_j has landed (control warp).
+  auto issue_s = [&](int j) -> bool {
+    if (!mbar_wait(k_full + (j & 1), (j >> 1) & 1, a.err, kErrAttnWait, abort_flag)) return false;
+    tc_fence_after();
     if (lane == 0) {
-      const int plane_rows = a.heads * a.M;
-      int k_issued = 0, v_issued = 0;
-      if (!gathered) {
-        mbar_arrive_expect_tx(q_full, TcAttnSmem::kQ);
-        tma_load_2d(sQ, &tmQK, q_full, 0, head * a.M + t0);
-      }
-      for (int j = 0; j < n_blocks; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        const int key0 = first + k_lo + j * kTcKB;  // absolute token of the block's first key
-        if (!mbar_wait(k_empty + st, ph ^ 1, a.err, kErrAttnWait, abort_flag)) break;
-        mbar_arrive_expect_tx(k_full + st, TcAttnSmem::kK);
-        tma_load_2d(sK + st * TcAttnSmem::kK, &tmQK, k_full + st, 0, plane_rows + head * a.M + key0);
-        k_issued = j + 1;
-        if (!mbar_wait(v_empty + st, ph ^ 1, a.err, kErrAttnWait, abort_flag)) break;
-        mbar_arrive_expect_tx(v_full + st, TcAttnSmem::kV);
-        uint8_t* v = sV + st * TcAttnSmem::kV;
-        tma_load_2d(v, &tmVt, v_full + st, key0, head * 64);
-        tma_load_2d(v + 64 * 128, &tmVt, v_full + st, key0 + 64, head * 64);
-        v_issued = j + 1;
-      }
-      if (*abort_flag) {
-        // Let the copies already issued land before the CTA exits.
-        if (!gathered) mbar_drain(q_full, 0);
-        for (int j = max(0, k_issued - 2); j < k_issued; ++j) mbar_drain(k_full + (j & 1), (j >> 1) & 1);
-        for (int j = max(0, v_issued - 2); j < v_issued; ++j) mbar_drain(v_full + (j & 1), (j >> 1) & 1);
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
       const uint32_t idesc_s = mma_idesc<bf>(kTcQ, kTcKB);
+      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK + (j & 1) * TcAttnSmem::kK);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        tc_mma_f16(tmem_base, smem_desc_sw128(q_addr + k * 32), smem_desc_sw128(k_addr + k * 32), idesc_s, k > 0);
+      tc_commit(s_full);
+    }
+    __syncwarp();
+    return true;
+  };
+  // O (+)= P_j V_j, A = P from TMEM columns [128, 192), once V_j has landed (control warp).
+  auto issue_pv = [&](int j) -> bool {
+    if (!mbar_wait(v_full + (j & 1), (j >> 1) & 1, a.err, kErrAttnWait, abort_flag)) return false;
+    tc_fence_after();
+    if (lane == 0) {
       const uint32_t idesc_o = mma_idesc<bf>(kTcQ, 64);
-      const uint32_t s_tmem = tmem_base, p_tmem = tmem_base + 128, o_tmem = tmem_base + 192;
-      const uint32_t q_addr = smem_u32(sQ);
-      // O += P_i V_i once the softmax has written P_i and V_i has landed.
-      auto issue_pv = [&](int i) -> bool {
-        if (!mbar_wait(p_full, i & 1, a.err, kErrAttnWait, abort_flag)) return false;
-        if (!mbar_wait(v_full + (i & 1), (i >> 1) & 1, a.err, kErrAttnWait, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t v_addr = smem_u32(sV + (i & 1) * TcAttnSmem::kV);
+      const uint32_t v_addr = smem_u32(sV + (j & 1) * TcAttnSmem::kV);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          tc_mma_f16_ts(o_tmem, p_tmem + 8 * k, smem_desc_sw128(v_addr + (k >> 2) * 64 * 128 + (k & 3) * 32),
-                        idesc_o, (i | k) != 0);
-        tc_commit(o_full);
-        tc_commit(v_empty + (i & 1));
-        return true;
-      };
-      bool ok = mbar_wait(q_full, 0, a.err, kErrAttnWait, abort_flag);
-      for (int j = 0; j < n_blocks && ok; ++j) {
-        const int st = j & 1;
-        // S_j = Q K_j^T once K_j has landed and the softmax has read S_{j-1}.
-        if (!mbar_wait(k_full + st, (j >> 1) & 1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
-        if (j > 0 && !mbar_wait(s_free, (j - 1) & 1, a.err, kErrAttnWait, abort_flag)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t k_addr = smem_u32(sK + st * TcAttnSmem::kK);
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          tc_mma_f16(s_tmem, smem_desc_sw128(q_addr + k * 32), smem_desc_sw128(k_addr + k * 32), idesc_s, k > 0);
-        tc_commit(s_full);
-        tc_commit(k_empty + st);
-        if (j > 0 && !issue_pv(j - 1)) { ok = false; break; }
-      }
-      if (ok && n_blocks > 0) issue_pv(n_blocks - 1);
-      // Every MMA issued by this thread completes before the TMEM is released.
-      tc_commit(drain);
-      mbar_drain(drain, 0);
+      for (int k = 0; k < 8; ++k)
+        tc_mma_f16_ts(tmem_base + 192, tmem_base + 128 + 8 * k,
+                      smem_desc_sw128(v_addr + (k >> 2) * 64 * 128 + (k & 3) * 32), idesc_o, (j | k) != 0);
+      tc_commit(o_full);
     }
-  } else {
-    // Softmax warps: thread <-> query row r (TMEM lane r).
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;
-    const int q = q0 + r;                  // row-relative query index of this thread
-    const int qa = q0 + quarter * 32;      // the warp's first query
-    const uint32_t lane_addr = (uint32_t)(quarter * 32) << 16;
-    const uint32_t s_tmem = tmem_base + lane_addr, p_tmem = s_tmem + 128, o_tmem = s_tmem + 192;
-    constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;
-    // Keys this query may see: row-relative [lo_key, lo_key + span_keys]; an empty range (a
-    // padding query of a windowed layer) sees nothing.
-    int lo_key = a.window >= 0 ? q - a.window : 0;
-    const int hi_key = a.window >= 0 ? min(valid - 1, q + a.window) : valid - 1;
-    uint32_t span_keys = (uint32_t)(hi_key - lo_key);
-    if (hi_key < lo_key) { lo_key = 1 << 30; span_keys = 0; }
-    const bool warp_live = gathered ? quarter * 32 < nq : qa < valid;
-    if (gathered) {
-      // Q row r <- token qidx[r] (zeros past nq), written in the 128-byte swizzled K-major layout
-      // the TMA would produce, then handed to the async proxy.
-      const T* qsrc = reinterpret_cast<const T*>(a.qk) + ((size_t)head * a.M + (r < nq ? qidx[r] : 0)) * 64;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 v = r < nq ? *reinterpret_cast<const uint4*>(qsrc + c * 8) : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(sQ + r * 128 + ((c ^ (r & 7)) << 4)) = v;
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(q_full);
+    __syncwarp();
+    return true;
+  };
+
+  bool ok = true;
+  if (ctl && lane == 0 && n_blocks > 0) {
+    if (!gathered) {
+      mbar_arrive_expect_tx(q_full, TcAttnSmem::kQ);
+      tma_load_2d(sQ, &tmQK, q_full, 0, head * a.M + t0);
     }
-    float m_used = -INFINITY, l = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_blocks; ++j) {
-      const int kb = k_lo + j * kTcKB;
-      ok = mbar_wait(s_full, j & 1, a.err, kErrAttnWait, abort_flag);
+    for (int j = 0; j < n_blocks && j < 2; ++j) { load_k(j); load_v(j); }
+  }
+
+  const int q = q0 + r;              // row-relative query index of this thread
+  const int qa = q0 + warp * 32;     // the warp's first query
+  constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;
+  // Keys this query may see: row-relative [lo_key, lo_key + span_keys]; an empty range (a
+  // padding query of a windowed layer) sees nothing.
+  int lo_key = a.window >= 0 ? q - a.window : 0;
+  const int hi_key = a.window >= 0 ? min(valid - 1, q + a.window) : valid - 1;
+  uint32_t span_keys = (uint32_t)(hi_key - lo_key);
+  if (hi_key < lo_key) { lo_key = 1 << 30; span_keys = 0; }
+  const bool warp_live = gathered ? warp * 32 < nq : qa < valid;
+  if (gathered && n_blocks > 0) {
+    // Q row r <- token qidx[r] (zeros past nq), written in the 128-byte swizzled K-major layout
+    // the TMA would produce, then handed to the async proxy.
+    const T* qsrc = reinterpret_cast<const T*>(a.qk) + ((size_t)head * a.M + (r < nq ? qidx[r] : 0)) * 64;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const uint4 v = r < nq ? *reinterpret_cast<const uint4*>(qsrc + c * 8) : make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(sQ + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(q_full);
+  }
+  if (ctl && n_blocks > 0) ok = mbar_wait(q_full, 0, a.err, kErrAttnWait, abort_flag) && issue_s(0);
+
+  float m_used = -INFINITY, l = 0.f;
+  for (int j = 0; j < n_blocks; ++j) {
+    const int kb = k_lo + j * kTcKB;
+    ok = ok && mbar_wait(s_full, j & 1, a.err, kErrAttnWait, abort_flag);
+    if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+    tc_fence_after();
+    // Chunk c holds keys [kb + 32c, kb + 32c + 32).  vis bit c: some query of the warp sees a
+    // key of the chunk; full bit c: every query of the warp sees every key.  Warp-uniform.
+    uint32_t vis = 0, full = 0;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int ck = kb + 32 * c;
+      if (warp_live && ck < valid && (a.window < 0 || (ck + 31 >= qa - a.window && ck <= qa + 31 + a.window)))
+        vis |= 1u << c;
+      if (ck + 31 < valid && (a.window < 0 || (ck >= qa + 31 - a.window && ck + 31 <= qa + a.window)))
+        full |= 1u << c;
+    }
+    full &= vis;
+    uint32_t sx[4][32];
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      if ((vis >> c) & 1) tmem_ld32_async(s_tmem + 32 * c, sx[c]);
+#pragma unroll
+    for (int c = 0; c < 4; ++c)
+      if ((vis >> c) & 1) tmem_wait_ld(sx[c]);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(s_free);
+    if (ctl && j + 1 < n_blocks) {
+      // Once every warp has read S_j: S_{j+1} into the same columns, and K_{j+2} into the stage
+      // S_j has finished reading.
+      ok = mbar_wait(s_free, j & 1, a.err, kErrAttnWait, abort_flag) && issue_s(j + 1);
+      if (ok && lane == 0 && j + 2 < n_blocks) load_k(j + 2);
+    }
+    const bool all = full == 0xFu;
+    const float bmax = all ? tc_block_max<true>(sx, vis, full, kb, lo_key, span_keys)
+                           : tc_block_max<false>(sx, vis, full, kb, lo_key, span_keys);
+    const float m_new = bmax * kScaleLog2;
+    float alpha = 1.f;
+    bool o_dirty = false;
+    if (m_new > m_used + kTcRescaleLog2) {  // false while every visible key is masked
+      if (m_used != -INFINITY) { alpha = ex2_approx(m_used - m_new); o_dirty = true; }
+      m_used = m_new;
+    }
+    const float sub = m_used == -INFINITY ? 0.f : m_used;
+    // P_j overwrites P_{j-1}: wait for the previous P V product.
+    if (j > 0) {
+      ok = ok && mbar_wait(o_full, (j - 1) & 1, a.err, kErrAttnWait, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      // Chunk c holds keys [kb + 32c, kb + 32c + 32).  vis bit c: some query of the warp sees a
-      // key of the chunk; full bit c: every query of the warp sees every key.  Warp-uniform.
-      uint32_t vis = 0, full = 0;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int ck = kb + 32 * c;
-        if (warp_live && ck < valid && (a.window < 0 || (ck + 31 >= qa - a.window && ck <= qa + 31 + a.window)))
-          vis |= 1u << c;
-        if (ck + 31 < valid && (a.window < 0 || (ck >= qa + 31 - a.window && ck + 31 <= qa + a.window)))
-          full |= 1u << c;
-      }
-      full &= vis;
-      uint32_t sx[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        if ((vis >> c) & 1) tmem_ld32_async(s_tmem + 32 * c, sx[c]);
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        if ((vis >> c) & 1) tmem_wait_ld(sx[c]);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_free);
-      const bool all = full == 0xFu;
-      const float bmax = all ? tc_block_max<true>(sx, vis, full, kb, lo_key, span_keys)
-                             : tc_block_max<false>(sx, vis, full, kb, lo_key, span_keys);
-      const float m_new = bmax * kScaleLog2;
-      float alpha = 1.f;
-      bool o_dirty = false;
-      if (m_new > m_used + kTcRescaleLog2) {  // false while every visible key is masked
-        if (m_used != -INFINITY) { alpha = ex2_approx(m_used - m_new); o_dirty = true; }
-        m_used = m_new;
-      }
-      const float sub = m_used == -INFINITY ? 0.f : m_used;
-      // P_j overwrites P_{j-1}: wait for the previous P V product.
-      if (j > 0) {
-        ok = mbar_wait(o_full, (j - 1) & 1, a.err, kErrAttnWait, abort_flag);
-        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-        tc_fence_after();
-      }
-      const float sum = all ? tc_block_probs<true, T>(sx, vis, kScaleLog2, sub, p_tmem)
-                            : tc_block_probs<false, T>(sx, vis, kScaleLog2, sub, p_tmem);
-      l = l * alpha + sum;
-      // Rows whose maximum grew by more than 2^8 rescale O before P_j V_j accumulates into it.
-      if (__any_sync(0xffffffffu, o_dirty)) {
+    }
+    const float sum = all ? tc_block_probs<true, T>(sx, vis, kScaleLog2, sub, p_tmem)
+                          : tc_block_probs<false, T>(sx, vis, kScaleLog2, sub, p_tmem);
+    l = l * alpha + sum;
+    // Rows whose maximum grew by more than 2^8 rescale O before P_j V_j accumulates into it.
+    if (__any_sync(0xffffffffu, o_dirty)) {
 #pragma unroll 1
-        for (int h = 0; h < 2; ++h) {
-          uint32_t o[32];
-          tmem_ld32_async(o_tmem + 32 * h, o);
-          tmem_wait_ld(o);
+      for (int h = 0; h < 2; ++h) {
+        uint32_t o[32];
+        tmem_ld32_async(o_tmem + 32 * h, o);
+        tmem_wait_ld(o);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(o_tmem + 32 * h, o);
+        for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+        tmem_st32(o_tmem + 32 * h, o);
+      }
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(p_full);
+    if (ctl) {
+      // Once every warp has written P_j: P_j V_j, and V_{j+1} into the stage P_{j-1} V_{j-1}
+      // has finished reading (observed through o_full above).
+      ok = ok && mbar_wait(p_full, j & 1, a.err, kErrAttnWait, abort_flag) && issue_pv(j);
+      if (ok && lane == 0 && j >= 1 && j + 1 < n_blocks) load_v(j + 1);
+    }
+  }
+  // Normalise and store this row (zeros for padding queries); rows past the tile belong to
+  // other tiles and are not written.
+  if (ok && n_blocks > 0) {
+    ok = mbar_wait(o_full, (n_blocks - 1) & 1, a.err, kErrAttnWait, abort_flag);
+    ok = __all_sync(0xffffffffu, ok);
+  }
+  if (ok) {
+    const int token = gathered ? (r < nq ? qidx[r] : -1) : t0 + r;
+    uint32_t o[2][32];
+    tc_fence_after();
+    tmem_ld32_async(o_tmem, o[0]);
+    tmem_ld32_async(o_tmem + 32, o[1]);
+    tmem_wait_ld(o[0]);
+    tmem_wait_ld(o[1]);
+    if (gathered ? token >= 0 : token < t1) {
+      const bool live = n_blocks > 0 && (gathered || q < valid) && l > 0.f;
+      const float inv = live ? 1.f / l : 0.f;
+      T* dst = out + (size_t)token * width + head * 64;
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          float v[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = live ? __uint_as_float(o[h][i + e]) * inv : 0.f;
+          uint4 w;
+          w.x = pack2<T>(v[0], v[1]); w.y = pack2<T>(v[2], v[3]);
+          w.z = pack2<T>(v[4], v[5]); w.w = pack2<T>(v[6], v[7]);
+          *reinterpret_cast<uint4*>(dst + h * 32 + i) = w;
         }
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
     }
-    // Normalise and store this row (zeros for padding queries); rows past the tile belong to
-    // other tiles and are not written.
-    if (ok && n_blocks > 0) {
-      ok = mbar_wait(o_full, (n_blocks - 1) & 1, a.err, kErrAttnWait, abort_flag);
-      ok = __all_sync(0xffffffffu, ok);
-    }
-    if (ok) {
-      const int token = gathered ? (r < nq ? qidx[r] : -1) : t0 + r;
-      uint32_t o[2][32];
-      tc_fence_after();
-      tmem_ld32_async(o_tmem, o[0]);
-      tmem_ld32_async(o_tmem + 32, o[1]);
-      tmem_wait_ld(o[0]);
-      tmem_wait_ld(o[1]);
-      if (gathered ? token >= 0 : token < t1) {
-        const bool live = n_blocks > 0 && (gathered || q < valid) && l > 0.f;
-        const float inv = live ? 1.f / l : 0.f;
-        T* dst = out + (size_t)token * width + head * 64;
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            float v[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = live ? __uint_as_float(o[h][i + e]) * inv : 0.f;
-            uint4 w;
-            w.x = pack2<T>(v[0], v[1]); w.y = pack2<T>(v[2], v[3]);
-            w.z = pack2<T>(v[4], v[5]); w.w = pack2<T>(v[6], v[7]);
-            *reinterpret_cast<uint4*>(dst + h * 32 + i) = w;
-          }
-      }
+  }
+  if (ctl && lane == 0) {
+    // Every MMA issued completes before the TMEM is released, and every copy lands before the
+    // CTA exits (bounded waits).
+    tc_commit(drain);
+    mbar_drain(drain, 0);
+    if (*abort_flag) {
+      if (!gathered && n_blocks > 0) mbar_drain(q_full, 0);
+      for (int j = max(0, k_issued - 2); j < k_issued; ++j) mbar_drain(k_full + (j & 1), (j >> 1) & 1);
+      for (int j = max(0, v_issued - 2); j < v_issued; ++j) mbar_drain(v_full + (j & 1), (j >> 1) & 1);
     }
   }
 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, kTcTmemCols);
+  if (ctl) tmem_dealloc(tmem_base, kTcTmemCols);
 }
 
 }  // namespace laya
