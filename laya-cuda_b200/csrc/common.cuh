@@ -393,6 +393,15 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
       : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
   return d;
 }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -432,6 +441,28 @@ __device__ __forceinline__ float gelu_erf(float x) {
   const float e = ex2_approx(-z * z * 1.4426950408889634f);  // exp(-z^2)
   const float erf_v = copysignf(fmaf(-poly, e, 1.0f), x);
   return 0.5f * x * (1.0f + erf_v);
+}
+
+// gelu_erf of two values with paired fp32 instructions: the same approximation (the Horner
+// coefficients negated so 1 - poly e is one fma; 1 - poly e >= 0, so the sign of x is OR-ed in),
+// about 11 instructions per value instead of 18.
+__device__ __forceinline__ float2 gelu_erf2(float2 x) {
+  const float2 ax = make_float2(fabsf(x.x), fabsf(x.y));
+  const float2 z = mul2(ax, make_float2(0.70710678118654752f, 0.70710678118654752f));
+  const float2 d = fma2(z, make_float2(0.3275911f, 0.3275911f), make_float2(1.0f, 1.0f));
+  const float2 t = make_float2(rcp_approx(d.x), rcp_approx(d.y));
+  float2 np = fma2(make_float2(-1.061405429f, -1.061405429f), t, make_float2(1.453152027f, 1.453152027f));
+  np = fma2(np, t, make_float2(-1.421413741f, -1.421413741f));
+  np = fma2(np, t, make_float2(0.284496736f, 0.284496736f));
+  np = fma2(np, t, make_float2(-0.254829592f, -0.254829592f));
+  np = mul2(np, t);  // -poly
+  const float2 w = mul2(mul2(z, make_float2(-1.4426950408889634f, -1.4426950408889634f)), z);
+  const float2 e = make_float2(ex2_approx(w.x), ex2_approx(w.y));  // exp(-z^2)
+  const float2 r = fma2(np, e, make_float2(1.0f, 1.0f));           // |erf(x / sqrt 2)|
+  const float2 erf_v = make_float2(__uint_as_float(__float_as_uint(r.x) | (__float_as_uint(x.x) & 0x80000000u)),
+                                   __uint_as_float(__float_as_uint(r.y) | (__float_as_uint(x.y) & 0x80000000u)));
+  const float2 hx = mul2(x, make_float2(0.5f, 0.5f));
+  return fma2(hx, erf_v, hx);
 }
 
 }  // namespace laya

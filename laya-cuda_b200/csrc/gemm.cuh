@@ -184,10 +184,14 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tba
         tmem_ld32(tbase + c * 128 + 64 + h * 32, u);
 #pragma unroll
         for (int i = 0; i < 32; i += 8) {
-          p[h * 4 + i / 8] = make_uint4(pack2<T>(gelu_erf(g[i + 0]) * u[i + 0], gelu_erf(g[i + 1]) * u[i + 1]),
-                                        pack2<T>(gelu_erf(g[i + 2]) * u[i + 2], gelu_erf(g[i + 3]) * u[i + 3]),
-                                        pack2<T>(gelu_erf(g[i + 4]) * u[i + 4], gelu_erf(g[i + 5]) * u[i + 5]),
-                                        pack2<T>(gelu_erf(g[i + 6]) * u[i + 6], gelu_erf(g[i + 7]) * u[i + 7]));
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 y = mul2(gelu_erf2(make_float2(g[i + 2 * e], g[i + 2 * e + 1])),
+                                  make_float2(u[i + 2 * e], u[i + 2 * e + 1]));
+            w[e] = pack2<T>(y.x, y.y);
+          }
+          p[h * 4 + i / 8] = make_uint4(w[0], w[1], w[2], w[3]);
         }
       }
       stage_put(stage, lane, p);
