@@ -162,15 +162,17 @@ const char* laya_last_error(laya_engine* e);
  * ------------------------------------------------------------------------------------------ */
 
 /* out/residual = epilogue(x[M][K] @ w[N][K]^T).  epi: 0 store, 1 relu, 2 gelu, 3 geglu (w rows
- * pre-interleaved by laya_interleave_geglu; out is [M][N/2]), 4 qkv (RoPE when cos/sin given,
- * tables transposed [32][rope_rows] indexed by positions[row]; out is [3][heads][M][64]),
+ * pre-interleaved by laya_interleave_geglu; out is [M][N/2]), 4 qkv (RoPE when rope_tab is
+ * given: 16-byte aligned fp32 [16][rope_rows][4] holding (cos f_2k, cos f_2k+1, sin f_2k,
+ * sin f_2k+1) of position p at [k][p], indexed by positions[row]; q and k are written
+ * [heads][M][64], v transposed [heads][64][M], all in `out`),
  * 5 residual += (fp32), 6 split-K partials ([splits][M][N] fp32 in `residual`).  bias: fp32 [N]
  * or NULL.  block_n: column tile (64, 128, 256), 0 to choose, or -128 / -256 for the CTA-pair
  * (cta_group::2, 256-row tile) kernel.  Replaces cublasGemmEx + bias/activate/layout
  * (ops.py:58-66; kernels.cu:50-82). */
 int laya_op_gemm(int precision, int epi, const void* x, const void* w, int M, int N, int K, void* out, int ldo,
-                 float* residual, int ldr, const float* bias, int heads, const float* cos_tab, const float* sin_tab,
-                 int rope_rows, const int32_t* positions, int splits, int block_n, int* err, void* stream);
+                 float* residual, int ldr, const float* bias, int heads, const float* rope_tab, int rope_rows,
+                 const int32_t* positions, int splits, int block_n, int* err, void* stream);
 
 /* Residual GEMM with the following LayerNorm fused (runtime.py:96-108: linear, add, layer_norm
  * of kernels.cu:20-49): residual[M][N] (fp32, row stride ldr) += x W^T + bias, then

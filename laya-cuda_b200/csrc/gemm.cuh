@@ -45,8 +45,10 @@ struct GemmArgs {
   const float* bias;      // fp32 [N] (GeGLU: unused) or nullptr
   // EPI_QKV
   int heads;
-  const float* cos_tab;   // [32][rope_rows] (transposed, so a warp's rows read contiguously) or nullptr
-  const float* sin_tab;
+  // RoPE table or nullptr: [16][rope_rows] of (cos f_2k, cos f_2k+1, sin f_2k, sin f_2k+1) at a
+  // position, frequency-pair major so a warp's rows (mostly consecutive positions) read one
+  // contiguous run per pair, one 16-byte load per two rotations.
+  const float4* rope_tab;
   int rope_rows;
   const int* positions;   // [M]
   int* err;               // device error word
@@ -218,20 +220,20 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tba
 #pragma unroll
         for (int i = 0; i < 64; ++i) x[i] += args.bias[n + i];
       }
-      if (part < 2 && args.cos_tab && live) {
+      if (part < 2 && args.rope_tab && live) {
         // Rotate-half RoPE: out[d] = x[d] cos - x[d+32] sin (d < 32),
-        //                   out[d] = x[d] cos + x[d-32] sin (d >= 32).
-        // Tables are [32][rope_rows]: the 32 lanes (consecutive rows, mostly consecutive
-        // positions) read one contiguous run per frequency.
-        const int pos = args.positions[row];
-        const float* cs = args.cos_tab + pos;
-        const float* sn = args.sin_tab + pos;
+        //                   out[d] = x[d] cos + x[d-32] sin (d >= 32),
+        // two frequencies (d, d+1) per table load and per paired instruction.
+        const float4* rt = args.rope_tab + args.positions[row];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float c0 = __ldg(cs + (size_t)i * args.rope_rows), s0 = __ldg(sn + (size_t)i * args.rope_rows);
-          const float a = x[i], b = x[i + 32];
-          x[i] = a * c0 - b * s0;
-          x[i + 32] = b * c0 + a * s0;
+        for (int k = 0; k < 16; ++k) {
+          const float4 t = __ldg(rt + (size_t)k * args.rope_rows);
+          const float2 c = make_float2(t.x, t.y), s = make_float2(t.z, t.w);
+          const float2 lo = make_float2(x[2 * k], x[2 * k + 1]), hi = make_float2(x[2 * k + 32], x[2 * k + 33]);
+          const float2 nlo = sub2(mul2(lo, c), mul2(hi, s));
+          const float2 nhi = fma2(hi, c, mul2(lo, s));
+          x[2 * k] = nlo.x; x[2 * k + 1] = nlo.y;
+          x[2 * k + 32] = nhi.x; x[2 * k + 33] = nhi.y;
         }
       }
       if (part < 2) {

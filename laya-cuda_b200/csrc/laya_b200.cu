@@ -612,8 +612,7 @@ struct Engine {
   cudaStream_t stream = nullptr;
   std::unordered_map<std::string, Tensor> weights;
   std::map<std::string, std::vector<int64_t>> expected;
-  float* rope_cos[2] = {nullptr, nullptr};
-  float* rope_sin[2] = {nullptr, nullptr};
+  float4* rope_tab[2] = {nullptr, nullptr};  // global / local theta, [16][rope_rows] (see GemmArgs)
   int rope_rows = 0;
   uint8_t* ws = nullptr;
   size_t ws_bytes = 0;
@@ -642,7 +641,7 @@ struct Engine {
   size_t owned() const {
     size_t s = ws_bytes;
     for (auto& kv : weights) s += kv.second.bytes;
-    for (int i = 0; i < 2; ++i) if (rope_cos[i]) s += 2 * (size_t)rope_rows * 32 * sizeof(float);
+    for (int i = 0; i < 2; ++i) if (rope_tab[i]) s += (size_t)rope_rows * 16 * sizeof(float4);
     return s;
   }
 };
@@ -931,7 +930,7 @@ void gemm(Engine& e, bool prof, int family, int epi, const CUtensorMap& ta, cons
   a.M = M; a.N = N; a.K = K; a.splits = 1;
   a.out = out; a.ldo = ldo; a.residual = residual; a.ldr = ldr; a.bias = bias;
   a.heads = e.cfg.heads;
-  if (rope >= 0) { a.cos_tab = e.rope_cos[rope]; a.sin_tab = e.rope_sin[rope]; a.rope_rows = e.rope_rows; }
+  if (rope >= 0) { a.rope_tab = e.rope_tab[rope]; a.rope_rows = e.rope_rows; }
   a.positions = positions;
   a.err = err;
   const CUtensorMap& tb = weight_map(e, wname, pair ? bn / 2 : bn);
@@ -1334,22 +1333,21 @@ int laya_finalize(laya_engine* h) {
   e.rope_rows = span16(e.cfg.max_len);
   const float thetas[2] = {e.cfg.theta_global, e.cfg.theta_local};
   for (int t = 0; t < 2; ++t) {
-    // Stored transposed, [32][rope_rows], so the QKV epilogue's lanes read contiguously.
-    std::vector<float> cs((size_t)e.rope_rows * 32), sn((size_t)e.rope_rows * 32);
+    // [16][rope_rows] x (cos f_2k, cos f_2k+1, sin f_2k, sin f_2k+1): see GemmArgs::rope_tab.
+    std::vector<float> tab((size_t)e.rope_rows * 64);
     for (int j = 0; j < 32; ++j) {
       const float expo = (float)(2 * j) / 64.0f;
       const float freq = 1.0f / powf(thetas[t], expo);
       for (int pos = 0; pos < e.rope_rows; ++pos) {
         const float angle = (float)pos * freq;
-        cs[(size_t)j * e.rope_rows + pos] = (float)cos((double)angle);
-        sn[(size_t)j * e.rope_rows + pos] = (float)sin((double)angle);
+        float* q = &tab[((size_t)(j >> 1) * e.rope_rows + pos) * 4];
+        q[j & 1] = (float)cos((double)angle);
+        q[2 + (j & 1)] = (float)sin((double)angle);
       }
     }
-    if (e.rope_cos[t]) { cudaFree(e.rope_cos[t]); cudaFree(e.rope_sin[t]); }
-    e.rope_cos[t] = static_cast<float*>(dev_alloc(cs.size() * 4));
-    e.rope_sin[t] = static_cast<float*>(dev_alloc(sn.size() * 4));
-    CK(cudaMemcpy(e.rope_cos[t], cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(e.rope_sin[t], sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+    if (e.rope_tab[t]) cudaFree(e.rope_tab[t]);
+    e.rope_tab[t] = static_cast<float4*>(dev_alloc(tab.size() * 4));
+    CK(cudaMemcpy(e.rope_tab[t], tab.data(), tab.size() * 4, cudaMemcpyHostToDevice));
   }
   drop_graphs(e);
   e.finalized = true;
@@ -1593,8 +1591,7 @@ int laya_destroy(laya_engine* h) {
     if (kv.second.ptr) cudaFree(kv.second.ptr);
   e.weights.clear();
   for (int i = 0; i < 2; ++i) {
-    if (e.rope_cos[i]) cudaFree(e.rope_cos[i]);
-    if (e.rope_sin[i]) cudaFree(e.rope_sin[i]);
+    if (e.rope_tab[i]) cudaFree(e.rope_tab[i]);
   }
   if (e.ws) cudaFree(e.ws);
   for (auto& r : e.inflight) {
@@ -1618,8 +1615,8 @@ const char* laya_last_error(laya_engine* h) { return h ? h->impl.error.c_str() :
 // Kernel-level entry points
 // ---------------------------------------------------------------------------------------------
 int laya_op_gemm(int precision, int epi, const void* x, const void* w, int M, int N, int K, void* out, int ldo,
-                 float* residual, int ldr, const float* bias, int heads, const float* cos_tab, const float* sin_tab,
-                 int rope_rows, const int32_t* positions, int splits, int block_n, int* err, void* stream) {
+                 float* residual, int ldr, const float* bias, int heads, const float* rope_tab, int rope_rows,
+                 const int32_t* positions, int splits, int block_n, int* err, void* stream) {
   API_BEGIN
   int dev = 0;
   CK(cudaGetDevice(&dev));
@@ -1632,7 +1629,9 @@ int laya_op_gemm(int precision, int epi, const void* x, const void* w, int M, in
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K; a.splits = splits;
   a.out = out; a.ldo = ldo; a.residual = residual; a.ldr = ldr; a.bias = bias;
-  a.heads = heads; a.cos_tab = cos_tab; a.sin_tab = sin_tab; a.rope_rows = rope_rows; a.positions = positions;
+  a.heads = heads; a.rope_tab = reinterpret_cast<const float4*>(rope_tab); a.rope_rows = rope_rows;
+  a.positions = positions;
+  if (rope_tab && (reinterpret_cast<uintptr_t>(rope_tab) & 15)) fail(LAYA_ERR_INVALID, "rope_tab must be 16-byte aligned");
   a.err = err;
   const CUtensorMap ta = make_map(x, M, K, kBM, bf);
   const CUtensorMap tb = make_map(w, N, K, pair ? bn / 2 : bn, bf);

@@ -75,7 +75,7 @@ def load():
         "laya_pool_bytes": (i, [p, ct.POINTER(ct.c_uint64), ct.POINTER(ct.c_uint64)]),
         "laya_destroy": (i, [p]),
         "laya_last_error": (ct.c_char_p, [p]),
-        "laya_op_gemm": (i, [i, i, p, p, i, i, i, p, i, p, i, p, i, p, p, i, p, i, i, p, p]),
+        "laya_op_gemm": (i, [i, i, p, p, i, i, i, p, i, p, i, p, i, p, i, p, i, i, p, p]),
         "laya_op_gemm_ln": (i, [i, p, p, i, i, i, p, i, p, p, p, ct.c_float, p, i, p, p]),
         "laya_interleave_geglu": (i, [p, p, i, i]),
         "laya_op_attention": (i, [i, i, p, p, p, i, p, p, i, i, i, i, p, p]),

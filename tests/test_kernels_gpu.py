@@ -37,15 +37,15 @@ def stream():
     return ct.c_void_p(torch.cuda.current_stream().cuda_stream)
 
 
-def gemm(lib, prec, epi, x, w, out=None, ldo=0, residual=None, ldr=0, bias=None, heads=0, cos=None, sin=None,
+def gemm(lib, prec, epi, x, w, out=None, ldo=0, residual=None, ldr=0, bias=None, heads=0, rope_tab=None,
          positions=None, splits=1, block_n=0):
-    """cos/sin: transposed RoPE tables [32][rope_rows] (or None)."""
+    """rope_tab: RoPE table [16][rope_rows][4] = (cos f_2k, cos f_2k+1, sin f_2k, sin f_2k+1), or None."""
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     M, K = x.shape
     N = w.shape[0]
-    rope_rows = cos.shape[1] if cos is not None else 0
+    rope_rows = rope_tab.shape[1] if rope_tab is not None else 0
     _lib.check(lib.laya_op_gemm(PRECISIONS[prec][0], epi, ptr(x), ptr(w), M, N, K, ptr(out), ldo, ptr(residual), ldr,
-                                ptr(bias), heads, ptr(cos), ptr(sin), rope_rows, ptr(positions), splits, block_n,
+                                ptr(bias), heads, ptr(rope_tab), rope_rows, ptr(positions), splits, block_n,
                                 ptr(err), stream()))
     torch.cuda.synchronize()
     assert int(err.item()) == 0
@@ -115,6 +115,13 @@ def rope_tables(theta, rows):
     return np.cos(angle).astype(np.float32), np.sin(angle).astype(np.float32)
 
 
+def rope_table_device(cos, sin):
+    """[rows][32] cos/sin -> the kernel's table [16][rows][4] = (cos 2k, cos 2k+1, sin 2k, sin 2k+1)."""
+    rows = cos.shape[0]
+    tab = np.stack([cos[:, 0::2], cos[:, 1::2], sin[:, 0::2], sin[:, 1::2]], -1)  # [rows][16][4]
+    return torch.from_numpy(np.ascontiguousarray(tab.transpose(1, 0, 2))).cuda()
+
+
 @pytest.mark.parametrize("prec", ["bf16", "f16"])
 @pytest.mark.parametrize("rope,M,block_n", [(True, 208, 0), (False, 208, 0), (True, 2320, -256), (False, 2320, -128),
                                             (True, 203, 0)])
@@ -130,9 +137,7 @@ def test_gemm_qkv_rope_layout(lib, prec, rope, M, block_n):
     cos, sin = rope_tables(10000, 128)
     bias = None if rope else torch.from_numpy(rng.normal(0, 0.1, N).astype(np.float32)).cuda()
     out = torch.full((3, heads, M, 64), float("nan"), dtype=PRECISIONS[prec][1], device="cuda")
-    gemm(lib, prec, 4, x, w, out, heads=heads,
-         cos=torch.from_numpy(cos.T.copy()).cuda() if rope else None,
-         sin=torch.from_numpy(sin.T.copy()).cuda() if rope else None,
+    gemm(lib, prec, 4, x, w, out, heads=heads, rope_tab=rope_table_device(cos, sin) if rope else None,
          positions=torch.from_numpy(positions).cuda(), bias=bias, block_n=block_n)
     h = xd @ wd.T
     if bias is not None:

@@ -46,7 +46,7 @@ def allocating(lib, x, w, base, bias):
     N = w.shape[0]
     stream = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
     _lib.check(lib.laya_op_gemm(_lib.PRECISION_F16, 5, ptr(x), ptr(w), M, N, K, None, 0, ptr(out), N, ptr(bias), 0,
-                                None, None, 0, None, 1, 0, ptr(err), stream))
+                                None, 0, None, 1, 0, ptr(err), stream))
     torch.cuda.synchronize()
     assert int(err.item()) == 0
     return out
