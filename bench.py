@@ -195,6 +195,21 @@ def percentiles(values):
     return {"p50_ms": round(float(np.percentile(values, 50)), 4), "p95_ms": round(float(np.percentile(values, 95)), 4)}
 
 
+def run_latency_only(args):
+    """--latency-only: configurations 1/2 (+1024 tokens) on the `laya` geometry through
+    Engine.predict, nothing else (a small command for profiler captures of the batch-1 path)."""
+    from laya_cuda import Engine
+    from laya_cuda import synthetic as S
+    arch = S.architecture("laya", max_len=1024)
+    CACHE.mkdir(parents=True, exist_ok=True)
+    path = S.cached_checkpoint(CACHE, "laya", seed=0, max_len=1024)
+    lengths = tuple(int(v) for v in args.lengths.split(","))
+    with Engine(path, device="cuda:0") as engine:
+        lat = latency(engine, arch, np.random.default_rng(0), lengths, repeats=args.repeats,
+                      warmup=max(3, min(20, args.repeats)), tag="laya_")
+    print(json.dumps({"latency_batch1": lat}), flush=True)
+
+
 def latency(engine, arch, rng, lengths, repeats=200, warmup=20, zipf=None, tag=""):
     """Batch-1 latency of Engine.predict(text) at the given sequence lengths (one question with
     4 options): p50/p95 of the API time and of the device time."""
@@ -417,7 +432,13 @@ def main():
     parser.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of oracle time for cpu_baseline")
     parser.add_argument("--requests", type=int, default=REQUESTS,
                         help="requests per rank (4096 = configuration 5; smaller only for profiler captures)")
+    parser.add_argument("--latency-only", action="store_true",
+                        help="only the batch-1 latencies of the laya geometry (for profiler captures)")
+    parser.add_argument("--lengths", default="83,512,1024", help="sequence lengths of --latency-only")
+    parser.add_argument("--repeats", type=int, default=200, help="timed repeats per length of --latency-only")
     args = parser.parse_args()
+    if args.latency_only:
+        return run_latency_only(args)
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
     rank = int(os.environ.get("RANK", 0))

@@ -115,6 +115,14 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+// Brings one tensor-map box into L2 (no shared-memory destination, no barrier to complete).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 // ---------------------------------------------------------------------------------------------
 // tcgen05
 // ---------------------------------------------------------------------------------------------
@@ -175,6 +183,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 32 lanes x 16 consecutive 32-bit columns, waited on.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // The same load without the wait: several loads can be in flight before one tmem_wait_ld.
@@ -332,15 +354,17 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
 
 // ---------------------------------------------------------------------------------------------
 // Programmatic dependent launch.  Every kernel of the forward pass is launched with programmatic
-// stream serialisation and none triggers its dependents early, so a kernel is launched once every
-// CTA of its predecessor has exited: its launch and prologue (barrier init, TMEM allocation,
-// descriptor and weight prefetch) overlap the predecessor's memory flush, and it waits in
-// pdl_wait() for that flush before touching anything the predecessor wrote.  (An early
-// griddepcontrol.launch_dependents measured 5% slower on the throughput workload: dependents
-// resident beside a running kernel cost more than the launch latency they hide.)  Without the
-// launch attribute pdl_wait() is a no-op.
+// stream serialisation; it waits in pdl_wait() for its predecessor's completion (and memory
+// flush) before touching anything the predecessor wrote.  For large classes no kernel triggers
+// its dependents early, so a kernel is launched once every CTA of its predecessor has exited and
+// only its launch and prologue overlap the predecessor's flush (an early trigger measured 5%
+// slower there: dependents resident beside a running kernel cost more than the launch latency
+// they hide).  Small classes, whose grids leave SMs idle, trigger at kernel start (`early` launch
+// flag): the successor's CTAs become resident where resources allow and run their launch and
+// prologue while this kernel runs.  Without the launch attribute both instructions are no-ops.
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 // ---------------------------------------------------------------------------------------------
 // Element conversions

@@ -52,6 +52,7 @@ struct GemmArgs {
   int rope_rows;
   const int* positions;   // [M]
   int* err;               // device error word
+  int early;              // trigger dependents at kernel start (small classes)
 };
 
 constexpr int kBM = 128;
@@ -162,6 +163,92 @@ struct ResidualPipe {
         if (r < a.M) *reinterpret_cast<float4*>(base + (size_t)r * a.ldr) = t;
       }
       if (i + 2 < kChunks) load(a, row0, n0, half, lane, i + 2);
+    }
+  }
+};
+
+// QKV epilogue of a 64-column tile (one head of q, k or v), the tile width small classes use:
+// the two warps of a TMEM lane quarter split the head's 32 frequency pairs, warp `half` taking
+// pairs 8*half .. 8*half+7, i.e. columns [16 half, +16) and [32 + 16 half, +16), so all eight
+// epilogue warps work.  The row's RoPE entries (position, then table) do not depend on the
+// GEMM, so start() loads them before the accumulator is waited on.
+template <typename T>
+struct Qkv64Pipe {
+  float4 rope[8];
+  bool roped;
+
+  __device__ __forceinline__ void start(const GemmArgs& a, int row, int n0, int half) {
+    const int part = n0 / (a.heads * 64);
+    roped = part < 2 && a.rope_tab != nullptr && row < a.M;
+    if (roped) {
+      const float4* rt = a.rope_tab + a.positions[row];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) rope[k] = __ldg(rt + (size_t)(8 * half + k) * a.rope_rows);
+    }
+  }
+
+  __device__ __forceinline__ void finish(const GemmArgs& a, uint32_t tbase, int row0, int n0, int half, int lane,
+                                         uint8_t* stage) {
+    const int row = row0 + lane;
+    const int rows = min(32, a.M - row0);
+    const int width = a.heads * 64;
+    const int part = n0 / width;
+    const int head = (n0 - part * width) >> 6;
+    float lo[16], hi[16];
+    tmem_ld16(tbase + 16 * half, lo);
+    tmem_ld16(tbase + 32 + 16 * half, hi);
+    if (a.bias) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        lo[i] += a.bias[n0 + 16 * half + i];
+        hi[i] += a.bias[n0 + 32 + 16 * half + i];
+      }
+    }
+    if (roped) {
+      // Rotate-half RoPE: lo' = lo cos - hi sin, hi' = hi cos + lo sin (pairs of frequencies).
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float2 c = make_float2(rope[k].x, rope[k].y), s = make_float2(rope[k].z, rope[k].w);
+        const float2 l = make_float2(lo[2 * k], lo[2 * k + 1]), h = make_float2(hi[2 * k], hi[2 * k + 1]);
+        const float2 nl = sub2(mul2(l, c), mul2(h, s));
+        const float2 nh = fma2(h, c, mul2(l, s));
+        lo[2 * k] = nl.x; lo[2 * k + 1] = nl.y;
+        hi[2 * k] = nh.x; hi[2 * k + 1] = nh.y;
+      }
+    }
+    if (part < 2) {
+      // q, k -> [part][heads][M][64]: this warp's half of each of its 32 rows is two 32-byte
+      // runs (pieces 0,1 at byte 32 half, pieces 2,3 at byte 64 + 32 half), staged so that each
+      // store covers whole 32-byte sectors.
+      uint4 p[4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        p[j] = make_uint4(pack2<T>(lo[8 * j + 0], lo[8 * j + 1]), pack2<T>(lo[8 * j + 2], lo[8 * j + 3]),
+                          pack2<T>(lo[8 * j + 4], lo[8 * j + 5]), pack2<T>(lo[8 * j + 6], lo[8 * j + 7]));
+        p[2 + j] = make_uint4(pack2<T>(hi[8 * j + 0], hi[8 * j + 1]), pack2<T>(hi[8 * j + 2], hi[8 * j + 3]),
+                              pack2<T>(hi[8 * j + 4], hi[8 * j + 5]), pack2<T>(hi[8 * j + 6], hi[8 * j + 7]));
+      }
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(stage + stage_off(lane, j)) = p[j];
+      __syncwarp();
+      T* out = reinterpret_cast<T*>(a.out) + ((size_t)part * a.heads + head) * a.M * 64;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int r = 8 * k + (lane >> 2), j = lane & 3;
+        const int col = (j < 2 ? 16 * half + 8 * j : 32 + 16 * half + 8 * (j - 2));
+        if (r < rows)
+          *reinterpret_cast<uint4*>(out + (size_t)(row0 + r) * 64 + col) =
+              *reinterpret_cast<const uint4*>(stage + stage_off(r, j));
+      }
+    } else if (row < a.M) {
+      // V transposed, [heads][64][M]: each dimension's 32 stores fill one 64-byte run.
+      T* vt = reinterpret_cast<T*>(a.out) + ((size_t)2 * a.heads + head) * a.M * 64 + row;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        vt[(size_t)(16 * half + i) * a.M] = from_f32<T>(lo[i]);
+        vt[(size_t)(32 + 16 * half + i) * a.M] = from_f32<T>(hi[i]);
+      }
     }
   }
 };
@@ -326,6 +413,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
+  if (args.early && threadIdx.x == 0) pdl_trigger();
   const int m_blocks = (args.M + kBM - 1) / kBM;
   const int n_blocks = args.N / BN;
   const int splits = args.splits;
@@ -363,8 +451,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t issued = 0, last_par = 0;
       bool ok = true;
       // Weights do not depend on the previous kernel: the first tile's weight stages are loaded
-      // before waiting for it, so their HBM latency overlaps the predecessor's tail.
+      // before waiting for it, so their HBM latency overlaps the predecessor's tail.  A CTA
+      // launched early (while its predecessor still runs) waits first instead: its weight
+      // traffic would slow the predecessor, which is on the same critical path.
       int pre = 0;
+      if (args.early) pdl_wait();
       if ((int)blockIdx.x < tiles) {
         int split, mb, nb; decode(blockIdx.x, split, mb, nb);
         pre = k_blocks < S ? k_blocks : S;
@@ -372,8 +463,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           mbar_arrive_expect_tx(&full[kb], Cfg::kStageBytes);
           tma_load_2d(sB + kb * Cfg::kStageB, &tmB, &full[kb], (split * k_blocks + kb) * kBK, nb * BN);
         }
+        // The rest of the first tile's weights are requested into L2 at once, so the ring's
+        // refills hit L2 instead of each waiting out HBM latency (small classes, where every
+        // CTA runs one tile, are latency-bound on exactly that chain).
+        for (int kb = pre; kb < k_blocks; ++kb) tma_prefetch_l2_2d(&tmB, (split * k_blocks + kb) * kBK, nb * BN);
       }
-      pdl_wait();
+      if (!args.early) pdl_wait();
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         int split, mb, nb; decode(t, split, mb, nb);
         for (int kb = 0; kb < k_blocks; ++kb) {
@@ -442,12 +537,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
       int split, mb, nb; decode(t, split, mb, nb);
       const int row0 = mb * kBM + quarter * 32;
+      constexpr bool kQkv64 = EPI == EPI_QKV && BN == 64;
       ResidualPipe<BN> rp;
+      Qkv64Pipe<T> qp;
       if (EPI == EPI_RESIDUAL) rp.start(args, row0, nb * BN, half, lane);
+      if (kQkv64) qp.start(args, row0 + lane, nb * BN, half);
       if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       if (EPI == EPI_RESIDUAL) rp.finish(args, tbase, row0, nb * BN, half, lane, stage);
+      else if (kQkv64) qp.finish(args, tbase, row0, nb * BN, half, lane, stage);
       else epilogue_tile<BN, EPI, T>(args, tbase, row0, nb * BN, split, half, lane, stage);
       tc_fence_before();
       __syncwarp();

@@ -21,6 +21,7 @@
 #include <map>
 #include <memory>
 #include <mutex>
+#include <set>
 #include <string>
 #include <tuple>
 #include <unordered_map>
@@ -122,6 +123,42 @@ bool pdl_enabled() {
   return on;
 }
 
+// Every kernel of the library asks for the largest shared-memory carveout.  The GEMMs and the
+// attention need most of an SM's shared memory; a kernel that preferred another L1 / shared split
+// could not become resident on an SM running one of them (an SM changes its split only when
+// empty), which would keep programmatic dependent launches from overlapping there.
+void prefer_max_shared(const void* fn) {
+  static std::mutex mu;
+  static std::set<std::pair<int, const void*>> done;
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.insert({dev, fn}).second)
+    CK(cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared));
+}
+
+// Whether the kernels of a class of m rows trigger their dependents at kernel start: classes up
+// to kEarlyRowsMax rows (LAYA_PDL_EARLY=0 / 1 in the environment: never / always).
+constexpr int kEarlyRowsMax = 2048;
+bool early_launch(int m) {
+  static const int mode = [] {
+    const char* v = getenv("LAYA_PDL_EARLY");
+    return v && v[0] == '0' ? 0 : v && v[0] == '1' ? 1 : 2;
+  }();
+  return pdl_enabled() && (mode == 1 || (mode == 2 && m <= kEarlyRowsMax));
+}
+
+// Warps (= rows) per block of the row kernels: 8, or fewer when that leaves SMs idle, so that a
+// small class's rows spread over the whole GPU (one row per warp either way).
+int row_warps(int rows) {
+  int device = 0;
+  CK(cudaGetDevice(&device));
+  const int sms = sm_count(device);
+  int w = kRowWarps;
+  while (w > 1 && rows < w * sms) w /= 2;
+  return w;
+}
+
 template <typename... KArgs, typename... Args>
 void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
@@ -134,6 +171,7 @@ void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cuda
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  prefer_max_shared(reinterpret_cast<const void*>(kernel));
   CK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
 }
 
@@ -271,8 +309,8 @@ int gemm_ln_mode() {
   return mode;
 }
 
-// Rows from which GEMMs run as CTA pairs (256-row tiles); below, 1-CTA tiles (and split-K) fill
-// the SMs better.  LAYA_GEMM_PAIR=0 in the environment turns pairs off.
+// Rows from which GEMMs always run as CTA pairs with 256 x 256 tiles; below, plan_small picks the
+// tile (1-CTA or pair) and split-K.  LAYA_GEMM_PAIR=0 in the environment turns pairs off.
 constexpr int kPairMinRows = 2048;
 bool pair_enabled() {
   static const bool on = [] {
@@ -342,15 +380,45 @@ int pick_bn(int M, int N, int epi, int sms) {
   return best;
 }
 
-// Split-K factor for a GEMM whose output tiles leave most SMs idle: the largest divisor of the
-// k-block count that keeps at least 3 k-blocks per split and the tile count within one wave.
-int pick_splits(int M, int N, int K, int bn, int sms) {
-  const int tiles = ((M + kBM - 1) / kBM) * (N / bn);
+// Tile plan of a GEMM of a small class (fewer than kPairMinRows rows).  There every CTA runs about
+// one tile and the mainloop is bound by moving operand tiles from L2 into shared memory: a
+// per-CTA globaltimer trace of a 512-row pass measured ~10.5 TB/s over the GPU (the same for the
+// QKV, FFN-up and FFN-down GEMMs) and up to ~57 B per cycle into one SM.  The plan takes the tile
+// (1-CTA 128 x {64,128,256}, CTA pair 256 x {128,256}: the pair halves each CTA's weight rows)
+// and, where allowed, the split-K factor (one wave at most) with the smallest modelled time
+//   waves * max(per-CTA bytes / SM rate, concurrent bytes / L2 rate, per-CTA MMA time)
+// plus, for split-K, the fp32 partials written here and read back by the LayerNorm.
+struct TilePlan {
+  bool pair = false;
+  int bn = 0;
+  int splits = 1;
+};
+TilePlan plan_small(int M, int N, int K, int epi, bool split_ok, bool pair_ok, int sms) {
+  constexpr double kSmRate = 107e9, kL2Rate = 10.5e12, kSmFlops = 14e12;
   const int kb = K / kBK;
-  if (2 * tiles >= sms) return 1;
-  int best = 1;
-  for (int s = 2; s <= kMaxSplits; ++s)
-    if (kb % s == 0 && kb / s >= 3 && tiles * s <= sms) best = s;
+  TilePlan best;
+  double best_t = 1e30;
+  for (int pair = 0; pair <= (pair_ok ? 1 : 0); ++pair) {
+    for (int bn : {64, 128, 256}) {
+      if (N % bn || (epi == EPI_GEGLU && bn < 128) || (pair && bn < 128)) continue;
+      for (int s = 1; s <= (split_ok && !pair ? kMaxSplits : 1); ++s) {
+        if (kb % s || (s > 1 && kb / s < 3)) continue;
+        const int rows_tile = pair ? 2 * kBM : kBM;
+        const int tiles = ((M + rows_tile - 1) / rows_tile) * (N / bn) * s;
+        const int slots = pair ? sms / 2 : sms;
+        if (s > 1 && tiles > slots) continue;
+        const int waves = (tiles + slots - 1) / slots;
+        const double kk = (double)(K / s);
+        const double cta_bytes = (std::min(M, kBM) + (pair ? bn / 2 : bn)) * kk * 2.0;
+        const double concurrent = (double)std::min(tiles, slots) * (pair ? 2 : 1) * cta_bytes;
+        double t = std::max(std::max(cta_bytes / kSmRate, concurrent / kL2Rate), 2.0 * kBM * bn * kk / kSmFlops);
+        t *= waves;
+        if (s > 1) t += 2.0 * s * (double)M * N * 4.0 / kL2Rate;
+        if (t < best_t * (1 - 1e-9)) { best_t = t; best.pair = pair; best.bn = bn; best.splits = s; }
+      }
+    }
+  }
+  if (!best.bn) fail(LAYA_ERR_INVALID, "no column tile divides N=%d", N);
   return best;
 }
 
@@ -393,13 +461,14 @@ void launch_attention(const AttnArgs& a, int n_tiles, bool split_p, cudaStream_t
 
 template <typename T>
 void launch_embed(const int* ids, const float* table, const float* gamma, float eps, int rows, int d, int vocab,
-                  float* residual, T* x, int* err, cudaStream_t st) {
-  const int grid = (rows + kRowWarps - 1) / kRowWarps;
+                  float* residual, T* x, int* err, cudaStream_t st, int early = 0) {
+  const int warps = row_warps(rows);
+  const int grid = (rows + warps - 1) / warps;
   switch (d / 32) {
 #define LAYA_EMBED_CASE(N)                                                                                  \
   case N:                                                                                                   \
-    launch_k(embed_norm_kernel<N, T>, dim3(grid), dim3(kRowWarps * 32), 0, st, ids, table, gamma, eps, rows, d, \
-             vocab, residual, x, err);                                                                      \
+    launch_k(embed_norm_kernel<N, T>, dim3(grid), dim3(warps * 32), 0, st, ids, table, gamma, eps, rows, d,     \
+             vocab, residual, x, err, early);                                                               \
     break;
     LAYA_FOR_EACH_WIDTH(LAYA_EMBED_CASE)
 #undef LAYA_EMBED_CASE
@@ -410,13 +479,14 @@ void launch_embed(const int* ids, const float* table, const float* gamma, float 
 template <typename T>
 void launch_norm(const NormArgs& a, cudaStream_t st) {
   if (a.d % 64 || a.d > 1024) fail(LAYA_ERR_INVALID, "unsupported width %d", a.d);
-  const int grid = (a.rows + kRowWarps - 1) / kRowWarps;
+  const int warps = row_warps(a.rows);
+  const int grid = (a.rows + warps - 1) / warps;
   const bool partials = a.splits > 0;
   switch (a.d / 32) {
 #define LAYA_NORM_CASE(N)                                                                   \
   case N:                                                                                   \
-    if (partials) launch_k(norm_kernel<N, T, true>, dim3(grid), dim3(kRowWarps * 32), 0, st, a); \
-    else launch_k(norm_kernel<N, T, false>, dim3(grid), dim3(kRowWarps * 32), 0, st, a);         \
+    if (partials) launch_k(norm_kernel<N, T, true>, dim3(grid), dim3(warps * 32), 0, st, a); \
+    else launch_k(norm_kernel<N, T, false>, dim3(grid), dim3(warps * 32), 0, st, a);         \
     break;
     LAYA_FOR_EACH_WIDTH(LAYA_NORM_CASE)
 #undef LAYA_NORM_CASE
@@ -627,6 +697,7 @@ struct Engine {
   // Attention kernel of the forward pass: the tcgen05/TMEM kernel (default) or the mma.sync
   // kernel (LAYA_ATTENTION=mma_sync in the environment at engine creation).
   bool tc_attention = true;
+  int early = 0;  // kernels of the pass being enqueued trigger their dependents at start
   std::vector<ProfEvent> prof_pending;
   std::vector<cudaEvent_t> prof_pool;
   double prof_ms[kFamilies] = {};
@@ -921,11 +992,21 @@ void gemm(Engine& e, bool prof, int family, int epi, const CUtensorMap& ta, cons
           int ldo, float* residual, int ldr, const float* bias, int* err, int rope = -1, const int* positions = nullptr) {
   const Tensor& w = W(e, wname);
   const int N = (int)w.shape[0], K = (int)w.shape[1];
-  int bn = pick_bn(M, N, epi, e.sms);
   // The CTA pair wins for the 16-bit output epilogues; the fp32 residual read-modify-write is as
   // fast or faster on the 1-CTA kernel (measured at 41k rows).
-  const bool pair = M >= kPairMinRows && pair_enabled() && N % 256 == 0 && epi != EPI_RESIDUAL;
-  if (pair) bn = 256;
+  const bool pair_ok = pair_enabled() && epi != EPI_RESIDUAL;
+  int bn;
+  bool pair;
+  if (M < kPairMinRows) {
+    // Small classes: the pair's QKV epilogue (64-column chunks, RoPE loads after the accumulator
+    // wait) measured slower than the 1-CTA kernel's split 64-column tiles, so QKV stays 1-CTA.
+    const TilePlan plan = plan_small(M, N, K, epi, false, pair_ok && epi != EPI_QKV, e.sms);
+    bn = plan.bn;
+    pair = plan.pair;
+  } else {
+    pair = pair_ok && N % 256 == 0;
+    bn = pair ? 256 : pick_bn(M, N, epi, e.sms);
+  }
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K; a.splits = 1;
   a.out = out; a.ldo = ldo; a.residual = residual; a.ldr = ldr; a.bias = bias;
@@ -933,19 +1014,19 @@ void gemm(Engine& e, bool prof, int family, int epi, const CUtensorMap& ta, cons
   if (rope >= 0) { a.rope_tab = e.rope_tab[rope]; a.rope_rows = e.rope_rows; }
   a.positions = positions;
   a.err = err;
+  a.early = e.early;
   const CUtensorMap& tb = weight_map(e, wname, pair ? bn / 2 : bn);
   launch(e, prof, family, 2.0 * M * N * K, [&] { launch_gemm<T>(epi, bn, ta, tb, a, e.sms, e.stream, pair); });
 }
 
 template <typename T>
 void gemm_partial(Engine& e, bool prof, int family, const CUtensorMap& ta, const std::string& wname, int M, int splits,
-                  float* partials, int* err) {
+                  int bn, float* partials, int* err) {
   const Tensor& w = W(e, wname);
   const int N = (int)w.shape[0], K = (int)w.shape[1];
-  const int bn = pick_bn(M, N, EPI_PARTIAL, e.sms);
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K; a.splits = splits;
-  a.residual = partials; a.ldr = N; a.err = err;
+  a.residual = partials; a.ldr = N; a.err = err; a.early = e.early;
   const CUtensorMap& tb = weight_map(e, wname, bn);
   launch(e, prof, family, 2.0 * M * N * K, [&] { launch_gemm<T>(EPI_PARTIAL, bn, ta, tb, a, e.sms, e.stream); });
 }
@@ -984,11 +1065,12 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
   int* err = reinterpret_cast<int*>(acts + (size_t)L.b * c.n_act);
 
   int* arrivals = err + 1;
+  e.early = early_launch(m) ? 1 : 0;
   CK(cudaMemsetAsync(err, 0, sizeof(int) * (1 + (size_t)L.b), e.stream));
   const double rowbytes = (double)m * d;
   launch(e, prof, FAM_ROWS, 0, [&] {
     launch_embed<T>(ids, Wf(e, "encoder.embeddings.tok_embeddings.weight"), Wf(e, "encoder.embeddings.norm.weight"),
-                    c.eps, m, d, c.vocab, residual, x, err, e.stream);
+                    c.eps, m, d, c.vocab, residual, x, err, e.stream, e.early);
   });
   (void)rowbytes;
 
@@ -998,7 +1080,7 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
     if (e.tc_attention) {
       TcAttnArgs a{};
       a.qk = qkv; a.out = attn; a.tiles = tiles128; a.starts = starts; a.lengths = lengths;
-      a.M = m; a.heads = c.heads; a.window = window; a.err = err;
+      a.M = m; a.heads = c.heads; a.window = window; a.err = err; a.early = e.early;
       int n_tiles = L.tiles128;
       if (gathered) {
         a.q_index = indices; a.q_per_row = L.k + 1; a.q_tiles = (L.k + 1 + kTcQ - 1) / kTcQ;
@@ -1019,7 +1101,7 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
     a.residual = res; a.partials = pend.splits ? partials : nullptr; a.splits = pend.splits;
     a.partial_bias = pend.bias;
     a.gamma1 = g; a.beta1 = b; a.eps1 = eps; a.fused_final = 0;
-    a.x = out; a.rows = rows; a.d = d;
+    a.x = out; a.rows = rows; a.d = d; a.early = e.early;
     launch(e, prof, FAM_ROWS, 0, [&] { launch_norm<T>(a, e.stream); });
   };
   // residual += A W^T + bias: the fused residual epilogue, or, for small classes, split-K
@@ -1028,12 +1110,12 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
                            const float* bias) -> Pending {
     const Tensor& w = W(e, wname);
     const int N = (int)w.shape[0], K = (int)w.shape[1];
-    int splits = 1;
-    if (partials && rows <= kSplitRowsMax && N == d)
-      splits = pick_splits(rows, N, K, pick_bn(rows, N, EPI_PARTIAL, e.sms), e.sms);
-    if (splits > 1) {
-      gemm_partial<T>(e, prof, family, ta, wname, rows, splits, partials, err);
-      return Pending{splits, bias};
+    if (partials && rows <= kSplitRowsMax && N == d) {
+      const TilePlan plan = plan_small(rows, N, K, EPI_PARTIAL, true, false, e.sms);
+      if (plan.splits > 1) {
+        gemm_partial<T>(e, prof, family, ta, wname, rows, plan.splits, plan.bn, partials, err);
+        return Pending{plan.splits, bias};
+      }
     }
     gemm<T>(e, prof, family, EPI_RESIDUAL, ta, wname, rows, nullptr, 0, res, d, bias, err);
     return Pending{};
@@ -1079,7 +1161,7 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
       a.gamma1 = Wf(e, "encoder.final_norm.weight"); a.beta1 = nullptr; a.eps1 = c.eps;
       a.fused_final = 1; a.type_emb = Wf(e, "type_emb.weight"); a.kinds = kinds;
       a.gamma2 = Wf(e, "head.layers.0.norm1.weight"); a.beta2 = Wf(e, "head.layers.0.norm1.bias"); a.eps2 = 1e-5f;
-      a.x = x; a.rows = m; a.d = d;
+      a.x = x; a.rows = m; a.d = d; a.early = e.early;
       launch(e, prof, FAM_ROWS, 0, [&] { launch_norm<T>(a, e.stream); });
     }
   }

@@ -10,7 +10,8 @@
 
 namespace laya {
 
-constexpr int kRowWarps = 8;           // rows per 256-thread block
+constexpr int kRowWarps = 8;           // most rows per block (one warp per row); small classes launch
+                                       // fewer warps per block so that their rows spread over more SMs
 
 // A warp holds one row of width d = 32 * NPL (NPL even, 2..32: widths 64..1024): lane `lane`
 // keeps NPL floats, in vectors of CH consecutive columns at col = j*32*CH + lane*CH.
@@ -93,9 +94,11 @@ __device__ __forceinline__ void row_layernorm(float (&v)[NPL], int lane, const f
 template <int NPL, typename T>
 __global__ void __launch_bounds__(kRowWarps * 32) embed_norm_kernel(const int* ids, const float* table,
                                                                     const float* gamma, float eps, int rows, int d,
-                                                                    int vocab, float* residual, T* x, int* err) {
+                                                                    int vocab, float* residual, T* x, int* err,
+                                                                    int early) {
+  if (early && threadIdx.x == 0) pdl_trigger();
   pdl_wait();
-  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
   int id = ids[row];
   if (id < 0 || id >= vocab) {
@@ -121,6 +124,7 @@ struct NormArgs {
   const float* gamma2; const float* beta2; float eps2;
   void* x;                  // [rows][d] T output (may be nullptr)
   int rows, d;
+  int early;                // trigger dependents at kernel start (small classes)
 };
 
 // Normal:  residual += sum(partials) + bias; x = LN1(residual).
@@ -129,8 +133,9 @@ struct NormArgs {
 // variant's register footprint small.  Replaces kernels.cu:20-49 and kernels.cu:155-158.
 template <int NPL, typename T, bool PARTIALS>
 __global__ void __launch_bounds__(kRowWarps * 32) norm_kernel(const NormArgs a) {
+  if (a.early && threadIdx.x == 0) pdl_trigger();
   pdl_wait();
-  const int row = blockIdx.x * kRowWarps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= a.rows) return;
   const int d = 32 * NPL;
   float* r = a.residual + (size_t)row * d;
@@ -218,7 +223,7 @@ struct TailArgs {
 
 constexpr int kTailThreads = 256;
 constexpr int kTailWarps = kTailThreads / 32;
-constexpr int kTailParts = 8;            // CTAs per question, each owning 256/8 hidden units
+constexpr int kTailParts = 32;           // CTAs per question, each owning 256/32 hidden units (one per warp)
 constexpr int kActHidden = 256;
 
 __device__ __forceinline__ float warp_max(float x) {
@@ -236,11 +241,19 @@ __device__ __forceinline__ float warp_max(float x) {
 // Dynamic shared memory: features [d+4], hidden [256], logits [k+1].
 template <typename T>
 __global__ void __launch_bounds__(kTailThreads) head_tail_kernel(const TailArgs a) {
-  pdl_wait();
   extern __shared__ float sh[];
   __shared__ int s_last;
   const int q = blockIdx.x, part = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int k1 = a.k + 1, d = a.d;
+  {
+    // This part's act_head.0 rows do not depend on the previous kernel: start them towards L2.
+    constexpr int kUnitsPerPart = kActHidden / kTailParts;
+    const char* w = reinterpret_cast<const char*>(a.wa0 + (size_t)part * kUnitsPerPart * (d + 4));
+    const int lines = (int)(((size_t)kUnitsPerPart * (d + 4) * sizeof(float) + 127) / 128);
+    for (int i = threadIdx.x; i < lines; i += kTailThreads)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(w + (size_t)i * 128));
+  }
+  pdl_wait();
   float* feat = sh;                    // [d + 4]
   float* hidden = sh + d + 4;          // [256]
   float* logit = hidden + kActHidden;  // [k1]

@@ -265,7 +265,11 @@ class Laya:
         return shapes
 
     def fingerprint(self, items):
-        return hashlib.sha256(json.dumps(items, separators=(",", ":")).encode()).hexdigest()
+        """sha256 of the items' compact JSON (laya.py:192-193), built directly: for lists of
+        ints the text equals json.dumps(items, separators=(",", ":")) at a third of the cost."""
+        text = ",".join(f"[[{','.join(map(str, ids))}],[{','.join(map(str, markers))}],{int(kind)}]"
+                        for ids, markers, kind in items)
+        return hashlib.sha256(f"[{text}]".encode()).hexdigest()
 
     def official(self, device):
         from .official import Official

@@ -161,3 +161,18 @@ def test_synthetic_checkpoint_contract(tmp_path):
     assert len(markers) == 2 and all(seq[i] == a.mask for i in markers) and kind == 0
     with pytest.raises(ValueError):
         a.prepare("", {})
+
+
+def test_fingerprint_equals_compact_json_digest(adapter):
+    """The fingerprint is sha256 of json.dumps(items, separators=(",", ":")) (laya.py:192-193)."""
+    import hashlib
+    rng = np.random.default_rng(5)
+    for n in (1, 2, 7):
+        items = []
+        for _ in range(n):
+            ids = [int(v) for v in rng.integers(0, 250000, rng.integers(1, 600))]
+            markers = [int(v) for v in rng.integers(0, 500, rng.integers(1, 80))]
+            item = (ids, markers, int(rng.integers(0, 3)))
+            items.append(item if rng.random() < 0.5 else list(item))
+        want = hashlib.sha256(json.dumps(items, separators=(",", ":")).encode()).hexdigest()
+        assert adapter.fingerprint(items) == want
