@@ -167,19 +167,21 @@ struct ResidualPipe {
   }
 };
 
-// QKV epilogue of a 64-column tile (one head of q, k or v), the tile width small classes use:
-// the two warps of a TMEM lane quarter split the head's 32 frequency pairs, warp `half` taking
-// pairs 8*half .. 8*half+7, i.e. columns [16 half, +16) and [32 + 16 half, +16), so all eight
-// epilogue warps work.  The row's RoPE entries (position, then table) do not depend on the
-// GEMM, so start() loads them before the accumulator is waited on.
-template <typename T>
-struct Qkv64Pipe {
+// QKV epilogue (RoPE on q and k, head-major q/k, transposed v).  The tile's columns are 64-column
+// chunks, one head of q, k or v each.  The two
+// warps of a TMEM lane quarter split every chunk's 32 frequency pairs, warp `half` taking pairs
+// 8*half .. 8*half+7, i.e. columns [16 half, +16) and [32 + 16 half, +16) of each chunk, so all
+// eight epilogue warps work on every chunk.  A row's RoPE entries depend only on its position
+// and the frequency pair, not on the head, so start() loads the warp's eight entries once per
+// tile, before the accumulator is waited on.
+template <int BN, typename T>
+struct QkvPipe {
   float4 rope[8];
   bool roped;
 
   __device__ __forceinline__ void start(const GemmArgs& a, int row, int n0, int half) {
-    const int part = n0 / (a.heads * 64);
-    roped = part < 2 && a.rope_tab != nullptr && row < a.M;
+    // roped: the tile starts in q or k (its later chunks may reach v, which is not rotated).
+    roped = n0 / (a.heads * 64) < 2 && a.rope_tab != nullptr && row < a.M;
     if (roped) {
       const float4* rt = a.rope_tab + a.positions[row];
 #pragma unroll
@@ -192,62 +194,66 @@ struct Qkv64Pipe {
     const int row = row0 + lane;
     const int rows = min(32, a.M - row0);
     const int width = a.heads * 64;
-    const int part = n0 / width;
-    const int head = (n0 - part * width) >> 6;
-    float lo[16], hi[16];
-    tmem_ld16(tbase + 16 * half, lo);
-    tmem_ld16(tbase + 32 + 16 * half, hi);
-    if (a.bias) {
+#pragma unroll 1
+    for (int c = 0; c < BN / 64; ++c) {
+      const int n = n0 + 64 * c;
+      const int part = n / width;
+      const int head = (n - part * width) >> 6;
+      float lo[16], hi[16];
+      tmem_ld16(tbase + 64 * c + 16 * half, lo);
+      tmem_ld16(tbase + 64 * c + 32 + 16 * half, hi);
+      if (a.bias) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        lo[i] += a.bias[n0 + 16 * half + i];
-        hi[i] += a.bias[n0 + 32 + 16 * half + i];
+        for (int i = 0; i < 16; ++i) {
+          lo[i] += a.bias[n + 16 * half + i];
+          hi[i] += a.bias[n + 32 + 16 * half + i];
+        }
       }
-    }
-    if (roped) {
-      // Rotate-half RoPE: lo' = lo cos - hi sin, hi' = hi cos + lo sin (pairs of frequencies).
+      if (roped && part < 2) {
+        // Rotate-half RoPE: lo' = lo cos - hi sin, hi' = hi cos + lo sin (pairs of frequencies).
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const float2 c = make_float2(rope[k].x, rope[k].y), s = make_float2(rope[k].z, rope[k].w);
-        const float2 l = make_float2(lo[2 * k], lo[2 * k + 1]), h = make_float2(hi[2 * k], hi[2 * k + 1]);
-        const float2 nl = sub2(mul2(l, c), mul2(h, s));
-        const float2 nh = fma2(h, c, mul2(l, s));
-        lo[2 * k] = nl.x; lo[2 * k + 1] = nl.y;
-        hi[2 * k] = nh.x; hi[2 * k + 1] = nh.y;
+        for (int k = 0; k < 8; ++k) {
+          const float2 cs = make_float2(rope[k].x, rope[k].y), sn = make_float2(rope[k].z, rope[k].w);
+          const float2 l = make_float2(lo[2 * k], lo[2 * k + 1]), h = make_float2(hi[2 * k], hi[2 * k + 1]);
+          const float2 nl = sub2(mul2(l, cs), mul2(h, sn));
+          const float2 nh = fma2(h, cs, mul2(l, sn));
+          lo[2 * k] = nl.x; lo[2 * k + 1] = nl.y;
+          hi[2 * k] = nh.x; hi[2 * k + 1] = nh.y;
+        }
       }
-    }
-    if (part < 2) {
-      // q, k -> [part][heads][M][64]: this warp's half of each of its 32 rows is two 32-byte
-      // runs (pieces 0,1 at byte 32 half, pieces 2,3 at byte 64 + 32 half), staged so that each
-      // store covers whole 32-byte sectors.
-      uint4 p[4];
+      if (part < 2) {
+        // q, k -> [part][heads][M][64]: this warp's half of each of its 32 rows is two 32-byte
+        // runs (pieces 0,1 at byte 32 half, pieces 2,3 at byte 64 + 32 half), staged so that
+        // each store covers whole 32-byte sectors.
+        uint4 p[4];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        p[j] = make_uint4(pack2<T>(lo[8 * j + 0], lo[8 * j + 1]), pack2<T>(lo[8 * j + 2], lo[8 * j + 3]),
-                          pack2<T>(lo[8 * j + 4], lo[8 * j + 5]), pack2<T>(lo[8 * j + 6], lo[8 * j + 7]));
-        p[2 + j] = make_uint4(pack2<T>(hi[8 * j + 0], hi[8 * j + 1]), pack2<T>(hi[8 * j + 2], hi[8 * j + 3]),
-                              pack2<T>(hi[8 * j + 4], hi[8 * j + 5]), pack2<T>(hi[8 * j + 6], hi[8 * j + 7]));
-      }
-      __syncwarp();
+        for (int j = 0; j < 2; ++j) {
+          p[j] = make_uint4(pack2<T>(lo[8 * j + 0], lo[8 * j + 1]), pack2<T>(lo[8 * j + 2], lo[8 * j + 3]),
+                            pack2<T>(lo[8 * j + 4], lo[8 * j + 5]), pack2<T>(lo[8 * j + 6], lo[8 * j + 7]));
+          p[2 + j] = make_uint4(pack2<T>(hi[8 * j + 0], hi[8 * j + 1]), pack2<T>(hi[8 * j + 2], hi[8 * j + 3]),
+                                pack2<T>(hi[8 * j + 4], hi[8 * j + 5]), pack2<T>(hi[8 * j + 6], hi[8 * j + 7]));
+        }
+        __syncwarp();
 #pragma unroll
-      for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(stage + stage_off(lane, j)) = p[j];
-      __syncwarp();
-      T* out = reinterpret_cast<T*>(a.out) + ((size_t)part * a.heads + head) * a.M * 64;
+        for (int j = 0; j < 4; ++j) *reinterpret_cast<uint4*>(stage + stage_off(lane, j)) = p[j];
+        __syncwarp();
+        T* out = reinterpret_cast<T*>(a.out) + ((size_t)part * a.heads + head) * a.M * 64;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int r = 8 * k + (lane >> 2), j = lane & 3;
-        const int col = (j < 2 ? 16 * half + 8 * j : 32 + 16 * half + 8 * (j - 2));
-        if (r < rows)
-          *reinterpret_cast<uint4*>(out + (size_t)(row0 + r) * 64 + col) =
-              *reinterpret_cast<const uint4*>(stage + stage_off(r, j));
-      }
-    } else if (row < a.M) {
-      // V transposed, [heads][64][M]: each dimension's 32 stores fill one 64-byte run.
-      T* vt = reinterpret_cast<T*>(a.out) + ((size_t)2 * a.heads + head) * a.M * 64 + row;
+        for (int k = 0; k < 4; ++k) {
+          const int r = 8 * k + (lane >> 2), j = lane & 3;
+          const int col = (j < 2 ? 16 * half + 8 * j : 32 + 16 * half + 8 * (j - 2));
+          if (r < rows)
+            *reinterpret_cast<uint4*>(out + (size_t)(row0 + r) * 64 + col) =
+                *reinterpret_cast<const uint4*>(stage + stage_off(r, j));
+        }
+      } else if (row < a.M) {
+        // V transposed, [heads][64][M]: each dimension's 32 stores fill one 64-byte run.
+        T* vt = reinterpret_cast<T*>(a.out) + ((size_t)2 * a.heads + head) * a.M * 64 + row;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        vt[(size_t)(16 * half + i) * a.M] = from_f32<T>(lo[i]);
-        vt[(size_t)(32 + 16 * half + i) * a.M] = from_f32<T>(hi[i]);
+        for (int i = 0; i < 16; ++i) {
+          vt[(size_t)(16 * half + i) * a.M] = from_f32<T>(lo[i]);
+          vt[(size_t)(32 + 16 * half + i) * a.M] = from_f32<T>(hi[i]);
+        }
       }
     }
   }
@@ -255,11 +261,11 @@ struct Qkv64Pipe {
 
 // Epilogue of one accumulator tile for one warp: TMEM lanes row0 .. row0+31 of the tile (this
 // lane: row0 + lane), columns from `tbase`, output column base n0; `half` selects every other
-// column chunk (two warps share a TMEM lane quarter).  EPI_RESIDUAL is handled by ResidualPipe.
+// column chunk (two warps share a TMEM lane quarter).  EPI_RESIDUAL and EPI_QKV are handled by
+// ResidualPipe and QkvPipe.
 template <int BN, int EPI, typename T>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tbase, int row0, int n0, int split,
                                               int half, int lane, uint8_t* stage) {
-  const int row = row0 + lane;
   const int rows = min(32, args.M - row0);  // live rows of this warp's block
   if (EPI == EPI_GEGLU) {
     // Tile columns: [gate 64 | up 64] x (BN / 128); output columns n0/2 + 64c + [0, 64).
@@ -286,61 +292,6 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tba
       stage_put(stage, lane, p);
       T* out = reinterpret_cast<T*>(args.out) + n0 / 2 + c * 64;
       stage_store16(stage, lane, rows, [&](int r) { return out + (size_t)(row0 + r) * args.ldo; });
-    }
-  } else if (EPI == EPI_QKV) {
-    const int width = args.heads * 64;
-#pragma unroll 1
-    for (int c = half; c < BN / 64; c += 2) {
-      float x[64];
-      {
-        float lo[32], hi[32];
-        tmem_ld32(tbase + c * 64, lo);
-        tmem_ld32(tbase + c * 64 + 32, hi);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) { x[i] = lo[i]; x[32 + i] = hi[i]; }
-      }
-      const bool live = row < args.M;
-      const int n = n0 + c * 64;
-      const int part = n / width;
-      const int head = (n - part * width) >> 6;
-      if (args.bias) {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) x[i] += args.bias[n + i];
-      }
-      if (part < 2 && args.rope_tab && live) {
-        // Rotate-half RoPE: out[d] = x[d] cos - x[d+32] sin (d < 32),
-        //                   out[d] = x[d] cos + x[d-32] sin (d >= 32),
-        // two frequencies (d, d+1) per table load and per paired instruction.
-        const float4* rt = args.rope_tab + args.positions[row];
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float4 t = __ldg(rt + (size_t)k * args.rope_rows);
-          const float2 c = make_float2(t.x, t.y), s = make_float2(t.z, t.w);
-          const float2 lo = make_float2(x[2 * k], x[2 * k + 1]), hi = make_float2(x[2 * k + 32], x[2 * k + 33]);
-          const float2 nlo = sub2(mul2(lo, c), mul2(hi, s));
-          const float2 nhi = fma2(hi, c, mul2(lo, s));
-          x[2 * k] = nlo.x; x[2 * k + 1] = nlo.y;
-          x[2 * k + 32] = nhi.x; x[2 * k + 33] = nhi.y;
-        }
-      }
-      if (part < 2) {
-        // q, k -> [part][heads][M][64]: the warp's 32 rows are one contiguous 4 KB block.
-        uint4 p[8];
-#pragma unroll
-        for (int i = 0; i < 64; i += 8)
-          p[i / 8] = make_uint4(pack2<T>(x[i + 0], x[i + 1]), pack2<T>(x[i + 2], x[i + 3]),
-                                pack2<T>(x[i + 4], x[i + 5]), pack2<T>(x[i + 6], x[i + 7]));
-        stage_put(stage, lane, p);
-        T* out = reinterpret_cast<T*>(args.out) + ((size_t)part * args.heads + head) * args.M * 64;
-        stage_store16(stage, lane, rows, [&](int r) { return out + (size_t)(row0 + r) * 64; });
-      } else if (live) {
-        // V transposed, [heads][64][M]: the attention's P.V product reads it K-major
-        // (keys contiguous).  The warp's lanes are consecutive rows, so each dimension's
-        // 32 stores fill one contiguous 64-byte run.
-        T* vt = reinterpret_cast<T*>(args.out) + ((size_t)2 * args.heads + head) * args.M * 64 + row;
-#pragma unroll
-        for (int i = 0; i < 64; ++i) vt[(size_t)i * args.M] = from_f32<T>(x[i]);
-      }
     }
   } else if (EPI == EPI_PARTIAL) {
     // partial[split][row][col] = acc (fp32), 32 columns (128 B per row) per chunk.
@@ -537,16 +488,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
       int split, mb, nb; decode(t, split, mb, nb);
       const int row0 = mb * kBM + quarter * 32;
-      constexpr bool kQkv64 = EPI == EPI_QKV && BN == 64;
       ResidualPipe<BN> rp;
-      Qkv64Pipe<T> qp;
+      QkvPipe<BN, T> qp;
       if (EPI == EPI_RESIDUAL) rp.start(args, row0, nb * BN, half, lane);
-      if (kQkv64) qp.start(args, row0 + lane, nb * BN, half);
+      if (EPI == EPI_QKV) qp.start(args, row0 + lane, nb * BN, half);
       if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       if (EPI == EPI_RESIDUAL) rp.finish(args, tbase, row0, nb * BN, half, lane, stage);
-      else if (kQkv64) qp.finish(args, tbase, row0, nb * BN, half, lane, stage);
+      else if (EPI == EPI_QKV) qp.finish(args, tbase, row0, nb * BN, half, lane, stage);
       else epilogue_tile<BN, EPI, T>(args, tbase, row0, nb * BN, split, half, lane, stage);
       tc_fence_before();
       __syncwarp();
@@ -701,11 +651,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int mb = t / n_blocks, nb = t - mb * n_blocks;
       const int row0 = mb * 2 * kBM + (int)rank * kBM + quarter * 32;
       ResidualPipe<BN> rp;
+      QkvPipe<BN, T> qp;
       if (EPI == EPI_RESIDUAL) rp.start(args, row0, nb * BN, half, lane);
+      if (EPI == EPI_QKV) qp.start(args, row0 + lane, nb * BN, half);
       if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       if (EPI == EPI_RESIDUAL) rp.finish(args, tbase, row0, nb * BN, half, lane, stage);
+      else if (EPI == EPI_QKV) qp.finish(args, tbase, row0, nb * BN, half, lane, stage);
       else epilogue_tile<BN, EPI, T>(args, tbase, row0, nb * BN, 0, half, lane, stage);
       tc_fence_before();
       __syncwarp();

@@ -139,7 +139,7 @@ void prefer_max_shared(const void* fn) {
 
 // Whether the kernels of a class of m rows trigger their dependents at kernel start: classes up
 // to kEarlyRowsMax rows (LAYA_PDL_EARLY=0 / 1 in the environment: never / always).
-constexpr int kEarlyRowsMax = 2048;
+constexpr int kEarlyRowsMax = 256;
 bool early_launch(int m) {
   static const int mode = [] {
     const char* v = getenv("LAYA_PDL_EARLY");
@@ -998,9 +998,7 @@ void gemm(Engine& e, bool prof, int family, int epi, const CUtensorMap& ta, cons
   int bn;
   bool pair;
   if (M < kPairMinRows) {
-    // Small classes: the pair's QKV epilogue (64-column chunks, RoPE loads after the accumulator
-    // wait) measured slower than the 1-CTA kernel's split 64-column tiles, so QKV stays 1-CTA.
-    const TilePlan plan = plan_small(M, N, K, epi, false, pair_ok && epi != EPI_QKV, e.sms);
+    const TilePlan plan = plan_small(M, N, K, epi, false, pair_ok, e.sms);
     bn = plan.bn;
     pair = plan.pair;
   } else {
