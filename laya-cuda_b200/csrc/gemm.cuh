@@ -414,10 +414,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           mbar_arrive_expect_tx(&full[kb], Cfg::kStageBytes);
           tma_load_2d(sB + kb * Cfg::kStageB, &tmB, &full[kb], (split * k_blocks + kb) * kBK, nb * BN);
         }
-        // The rest of the first tile's weights are requested into L2 at once, so the ring's
-        // refills hit L2 instead of each waiting out HBM latency (small classes, where every
-        // CTA runs one tile, are latency-bound on exactly that chain).
-        for (int kb = pre; kb < k_blocks; ++kb) tma_prefetch_l2_2d(&tmB, (split * k_blocks + kb) * kBK, nb * BN);
+        // A CTA with a single tile (small classes) requests the rest of its weights into L2 at
+        // once, so the ring's refills hit L2 instead of each waiting out HBM latency.
+        if (tiles <= (int)gridDim.x)
+          for (int kb = pre; kb < k_blocks; ++kb) tma_prefetch_l2_2d(&tmB, (split * k_blocks + kb) * kBK, nb * BN);
       }
       if (!args.early) pdl_wait();
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {

@@ -380,21 +380,24 @@ int pick_bn(int M, int N, int epi, int sms) {
   return best;
 }
 
-// Tile plan of a GEMM of a small class (fewer than kPairMinRows rows).  There every CTA runs about
-// one tile and the mainloop is bound by moving operand tiles from L2 into shared memory: a
-// per-CTA globaltimer trace of a 512-row pass measured ~10.5 TB/s over the GPU (the same for the
-// QKV, FFN-up and FFN-down GEMMs) and up to ~57 B per cycle into one SM.  The plan takes the tile
-// (1-CTA 128 x {64,128,256}, CTA pair 256 x {128,256}: the pair halves each CTA's weight rows)
-// and, where allowed, the split-K factor (one wave at most) with the smallest modelled time
-//   waves * max(per-CTA bytes / SM rate, concurrent bytes / L2 rate, per-CTA MMA time)
-// plus, for split-K, the fp32 partials written here and read back by the LayerNorm.
+// Tile plan of a GEMM of a small class (fewer than kPairMinRows rows), where every CTA runs about
+// one tile, so latency and per-CTA work decide.  Per-CTA globaltimer traces of 512-row passes
+// fitted this model of one wave (all constants measured on B200 there):
+//   ~1.2 us from the dependency wait to the first full stage, then the operand tiles at
+//   max(per-CTA bytes / ~107 GB/s into one SM (~65 GB/s for a CTA of a pair),
+//       bytes of all running CTAs / ~10.5 TB/s from L2),
+//   then the epilogue, ~0.8 us + ~0.1 us per 1024 accumulators of the CTA;
+// plus, for split-K, the fp32 partials written here and read back by the LayerNorm.  Candidates:
+// 1-CTA tiles 128 x {64,128,256}, CTA pairs 256 x {128,256} (each CTA loads half of the weight
+// rows) and, where allowed, split-K factors with at most one wave.
 struct TilePlan {
   bool pair = false;
   int bn = 0;
   int splits = 1;
 };
 TilePlan plan_small(int M, int N, int K, int epi, bool split_ok, bool pair_ok, int sms) {
-  constexpr double kSmRate = 107e9, kL2Rate = 10.5e12, kSmFlops = 14e12;
+  constexpr double kSmRate = 107e9, kPairSmRate = 65e9, kL2Rate = 10.5e12, kSmFlops = 14e12;
+  constexpr double kLatency = 1.2e-6, kEpiFixed = 0.8e-6, kEpiPerAcc = 0.1e-6 / 1024;
   const int kb = K / kBK;
   TilePlan best;
   double best_t = 1e30;
@@ -411,8 +414,9 @@ TilePlan plan_small(int M, int N, int K, int epi, bool split_ok, bool pair_ok, i
         const double kk = (double)(K / s);
         const double cta_bytes = (std::min(M, kBM) + (pair ? bn / 2 : bn)) * kk * 2.0;
         const double concurrent = (double)std::min(tiles, slots) * (pair ? 2 : 1) * cta_bytes;
-        double t = std::max(std::max(cta_bytes / kSmRate, concurrent / kL2Rate), 2.0 * kBM * bn * kk / kSmFlops);
-        t *= waves;
+        const double load = std::max(std::max(cta_bytes / (pair ? kPairSmRate : kSmRate), concurrent / kL2Rate),
+                                     2.0 * kBM * bn * kk / kSmFlops);
+        double t = waves * (kLatency + load + kEpiFixed + kEpiPerAcc * kBM * bn);
         if (s > 1) t += 2.0 * s * (double)M * N * 4.0 / kL2Rate;
         if (t < best_t * (1 - 1e-9)) { best_t = t; best.pair = pair; best.bn = bn; best.splits = s; }
       }
@@ -1205,7 +1209,8 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
   t.hidden = reinterpret_cast<float*>(ws + L.hidden); t.arrivals = arrivals;
   const size_t tail_smem = ((size_t)(L.k + 1) + d + 4 + kActHidden) * sizeof(float);
   launch(e, prof, FAM_HEAD_TAIL, 0, [&] {
-    launch_k(head_tail_kernel<T>, dim3(L.b, kTailParts), dim3(kTailThreads), tail_smem, e.stream, t);
+    const int parts = L.b * kTailPartsSmall <= 4 * e.sms ? kTailPartsSmall : kTailPartsLarge;
+    launch_k(head_tail_kernel<T>, dim3(L.b, parts), dim3(kTailThreads), tail_smem, e.stream, t);
   });
 }
 

@@ -223,7 +223,9 @@ struct TailArgs {
 
 constexpr int kTailThreads = 256;
 constexpr int kTailWarps = kTailThreads / 32;
-constexpr int kTailParts = 32;           // CTAs per question, each owning 256/32 hidden units (one per warp)
+// CTAs per question (gridDim.y), each owning 256/parts hidden units: 32 (one unit per warp) for
+// small batches, whose few questions would otherwise leave most SMs idle; 8 for large ones.
+constexpr int kTailPartsSmall = 32, kTailPartsLarge = 8;
 constexpr int kActHidden = 256;
 
 __device__ __forceinline__ float warp_max(float x) {
@@ -232,7 +234,7 @@ __device__ __forceinline__ float warp_max(float x) {
   return x;
 }
 
-// Decision-head tail, kTailParts CTAs per question (blockIdx.x = question, blockIdx.y = part).
+// Decision-head tail, gridDim.y CTAs per question (blockIdx.x = question, blockIdx.y = part).
 // Restates laya.py:241-245 and kernels.cu:167-183 (features) in fp32:
 //   logits   = scored . w3 + b3                       (every part; part 0 stores them)
 //   features = [CLS row, p1, p1 - p2, H / log(max(c,2)), max(c,2)/255] over the option logits
@@ -247,9 +249,9 @@ __global__ void __launch_bounds__(kTailThreads) head_tail_kernel(const TailArgs 
   const int k1 = a.k + 1, d = a.d;
   {
     // This part's act_head.0 rows do not depend on the previous kernel: start them towards L2.
-    constexpr int kUnitsPerPart = kActHidden / kTailParts;
-    const char* w = reinterpret_cast<const char*>(a.wa0 + (size_t)part * kUnitsPerPart * (d + 4));
-    const int lines = (int)(((size_t)kUnitsPerPart * (d + 4) * sizeof(float) + 127) / 128);
+    const int units = kActHidden / (int)gridDim.y;
+    const char* w = reinterpret_cast<const char*>(a.wa0 + (size_t)part * units * (d + 4));
+    const int lines = (int)(((size_t)units * (d + 4) * sizeof(float) + 127) / 128);
     for (int i = threadIdx.x; i < lines; i += kTailThreads)
       asm volatile("prefetch.global.L2 [%0];" ::"l"(w + (size_t)i * 128));
   }
@@ -312,7 +314,7 @@ __global__ void __launch_bounds__(kTailThreads) head_tail_kernel(const TailArgs 
   }
   __syncthreads();
   // act_head.0 + GELU for this part's hidden units: one warp per unit, float4 over d+4.
-  constexpr int kUnits = kActHidden / kTailParts;
+  const int kUnits = kActHidden / (int)gridDim.y;
   const int n4 = (d + 4) / 4;
   const float4* f4 = reinterpret_cast<const float4*>(feat);
   for (int u = warp; u < kUnits; u += kTailWarps) {
@@ -329,7 +331,7 @@ __global__ void __launch_bounds__(kTailThreads) head_tail_kernel(const TailArgs 
   // The part that finishes last computes the action logits from all 256 hidden units.
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(&a.arrivals[q], 1) == kTailParts - 1;
+  if (threadIdx.x == 0) s_last = atomicAdd(&a.arrivals[q], 1) == (int)gridDim.y - 1;
   __syncthreads();
   if (!s_last) return;
   __threadfence();
