@@ -354,17 +354,16 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
 
 // ---------------------------------------------------------------------------------------------
 // Programmatic dependent launch.  Every kernel of the forward pass is launched with programmatic
-// stream serialisation; it waits in pdl_wait() for its predecessor's completion (and memory
-// flush) before touching anything the predecessor wrote.  For large classes no kernel triggers
-// its dependents early, so a kernel is launched once every CTA of its predecessor has exited and
-// only its launch and prologue overlap the predecessor's flush (an early trigger measured 5%
-// slower there: dependents resident beside a running kernel cost more than the launch latency
-// they hide).  Small classes, whose grids leave SMs idle, trigger at kernel start (`early` launch
-// flag): the successor's CTAs become resident where resources allow and run their launch and
-// prologue while this kernel runs.  Without the launch attribute both instructions are no-ops.
+// stream serialisation and none triggers its dependents early, so a kernel is launched once every
+// CTA of its predecessor has exited: its launch and prologue (barrier init, TMEM allocation,
+// descriptor and weight prefetch) overlap the predecessor's memory flush, and it waits in
+// pdl_wait() for that flush before touching anything the predecessor wrote.  (An early
+// griddepcontrol.launch_dependents measured 5% slower on the throughput workload: dependents
+// resident beside a running kernel cost more than the launch latency they hide.  On batch-1
+// passes it was no better either: early dependents crowd onto the few idle SMs, and a GEMM's
+// weight reads slow the kernel it waits for.)  Without the launch attribute pdl_wait() is a no-op.
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 // ---------------------------------------------------------------------------------------------
 // Element conversions

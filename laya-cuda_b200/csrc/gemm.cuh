@@ -52,7 +52,6 @@ struct GemmArgs {
   int rope_rows;
   const int* positions;   // [M]
   int* err;               // device error word
-  int early;              // trigger dependents at kernel start (small classes)
 };
 
 constexpr int kBM = 128;
@@ -364,7 +363,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  if (args.early && threadIdx.x == 0) pdl_trigger();
   const int m_blocks = (args.M + kBM - 1) / kBM;
   const int n_blocks = args.N / BN;
   const int splits = args.splits;
@@ -402,11 +400,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t issued = 0, last_par = 0;
       bool ok = true;
       // Weights do not depend on the previous kernel: the first tile's weight stages are loaded
-      // before waiting for it, so their HBM latency overlaps the predecessor's tail.  A CTA
-      // launched early (while its predecessor still runs) waits first instead: its weight
-      // traffic would slow the predecessor, which is on the same critical path.
+      // before waiting for it, so their HBM latency overlaps the predecessor's tail.
       int pre = 0;
-      if (args.early) pdl_wait();
       if ((int)blockIdx.x < tiles) {
         int split, mb, nb; decode(blockIdx.x, split, mb, nb);
         pre = k_blocks < S ? k_blocks : S;
@@ -419,7 +414,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (tiles <= (int)gridDim.x)
           for (int kb = pre; kb < k_blocks; ++kb) tma_prefetch_l2_2d(&tmB, (split * k_blocks + kb) * kBK, nb * BN);
       }
-      if (!args.early) pdl_wait();
+      pdl_wait();
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
         int split, mb, nb; decode(t, split, mb, nb);
         for (int kb = 0; kb < k_blocks; ++kb) {

@@ -21,7 +21,6 @@
 #include <map>
 #include <memory>
 #include <mutex>
-#include <set>
 #include <string>
 #include <tuple>
 #include <unordered_map>
@@ -123,31 +122,6 @@ bool pdl_enabled() {
   return on;
 }
 
-// Every kernel of the library asks for the largest shared-memory carveout.  The GEMMs and the
-// attention need most of an SM's shared memory; a kernel that preferred another L1 / shared split
-// could not become resident on an SM running one of them (an SM changes its split only when
-// empty), which would keep programmatic dependent launches from overlapping there.
-void prefer_max_shared(const void* fn) {
-  static std::mutex mu;
-  static std::set<std::pair<int, const void*>> done;
-  int dev = 0;
-  CK(cudaGetDevice(&dev));
-  std::lock_guard<std::mutex> lock(mu);
-  if (done.insert({dev, fn}).second)
-    CK(cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared));
-}
-
-// Whether the kernels of a class of m rows trigger their dependents at kernel start: classes up
-// to kEarlyRowsMax rows (LAYA_PDL_EARLY=0 / 1 in the environment: never / always).
-constexpr int kEarlyRowsMax = 256;
-bool early_launch(int m) {
-  static const int mode = [] {
-    const char* v = getenv("LAYA_PDL_EARLY");
-    return v && v[0] == '0' ? 0 : v && v[0] == '1' ? 1 : 2;
-  }();
-  return pdl_enabled() && (mode == 1 || (mode == 2 && m <= kEarlyRowsMax));
-}
-
 // Warps (= rows) per block of the row kernels: 8, or fewer when that leaves SMs idle, so that a
 // small class's rows spread over the whole GPU (one row per warp either way).
 int row_warps(int rows) {
@@ -171,7 +145,6 @@ void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cuda
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  prefer_max_shared(reinterpret_cast<const void*>(kernel));
   CK(cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...));
 }
 
@@ -465,14 +438,14 @@ void launch_attention(const AttnArgs& a, int n_tiles, bool split_p, cudaStream_t
 
 template <typename T>
 void launch_embed(const int* ids, const float* table, const float* gamma, float eps, int rows, int d, int vocab,
-                  float* residual, T* x, int* err, cudaStream_t st, int early = 0) {
+                  float* residual, T* x, int* err, cudaStream_t st) {
   const int warps = row_warps(rows);
   const int grid = (rows + warps - 1) / warps;
   switch (d / 32) {
 #define LAYA_EMBED_CASE(N)                                                                                  \
   case N:                                                                                                   \
     launch_k(embed_norm_kernel<N, T>, dim3(grid), dim3(warps * 32), 0, st, ids, table, gamma, eps, rows, d,     \
-             vocab, residual, x, err, early);                                                               \
+             vocab, residual, x, err);                                                                      \
     break;
     LAYA_FOR_EACH_WIDTH(LAYA_EMBED_CASE)
 #undef LAYA_EMBED_CASE
@@ -701,7 +674,6 @@ struct Engine {
   // Attention kernel of the forward pass: the tcgen05/TMEM kernel (default) or the mma.sync
   // kernel (LAYA_ATTENTION=mma_sync in the environment at engine creation).
   bool tc_attention = true;
-  int early = 0;  // kernels of the pass being enqueued trigger their dependents at start
   std::vector<ProfEvent> prof_pending;
   std::vector<cudaEvent_t> prof_pool;
   double prof_ms[kFamilies] = {};
@@ -1016,7 +988,6 @@ void gemm(Engine& e, bool prof, int family, int epi, const CUtensorMap& ta, cons
   if (rope >= 0) { a.rope_tab = e.rope_tab[rope]; a.rope_rows = e.rope_rows; }
   a.positions = positions;
   a.err = err;
-  a.early = e.early;
   const CUtensorMap& tb = weight_map(e, wname, pair ? bn / 2 : bn);
   launch(e, prof, family, 2.0 * M * N * K, [&] { launch_gemm<T>(epi, bn, ta, tb, a, e.sms, e.stream, pair); });
 }
@@ -1028,7 +999,7 @@ void gemm_partial(Engine& e, bool prof, int family, const CUtensorMap& ta, const
   const int N = (int)w.shape[0], K = (int)w.shape[1];
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K; a.splits = splits;
-  a.residual = partials; a.ldr = N; a.err = err; a.early = e.early;
+  a.residual = partials; a.ldr = N; a.err = err;
   const CUtensorMap& tb = weight_map(e, wname, bn);
   launch(e, prof, family, 2.0 * M * N * K, [&] { launch_gemm<T>(EPI_PARTIAL, bn, ta, tb, a, e.sms, e.stream); });
 }
@@ -1067,12 +1038,11 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
   int* err = reinterpret_cast<int*>(acts + (size_t)L.b * c.n_act);
 
   int* arrivals = err + 1;
-  e.early = early_launch(m) ? 1 : 0;
   CK(cudaMemsetAsync(err, 0, sizeof(int) * (1 + (size_t)L.b), e.stream));
   const double rowbytes = (double)m * d;
   launch(e, prof, FAM_ROWS, 0, [&] {
     launch_embed<T>(ids, Wf(e, "encoder.embeddings.tok_embeddings.weight"), Wf(e, "encoder.embeddings.norm.weight"),
-                    c.eps, m, d, c.vocab, residual, x, err, e.stream, e.early);
+                    c.eps, m, d, c.vocab, residual, x, err, e.stream);
   });
   (void)rowbytes;
 
@@ -1082,7 +1052,7 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
     if (e.tc_attention) {
       TcAttnArgs a{};
       a.qk = qkv; a.out = attn; a.tiles = tiles128; a.starts = starts; a.lengths = lengths;
-      a.M = m; a.heads = c.heads; a.window = window; a.err = err; a.early = e.early;
+      a.M = m; a.heads = c.heads; a.window = window; a.err = err;
       int n_tiles = L.tiles128;
       if (gathered) {
         a.q_index = indices; a.q_per_row = L.k + 1; a.q_tiles = (L.k + 1 + kTcQ - 1) / kTcQ;
@@ -1103,7 +1073,7 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
     a.residual = res; a.partials = pend.splits ? partials : nullptr; a.splits = pend.splits;
     a.partial_bias = pend.bias;
     a.gamma1 = g; a.beta1 = b; a.eps1 = eps; a.fused_final = 0;
-    a.x = out; a.rows = rows; a.d = d; a.early = e.early;
+    a.x = out; a.rows = rows; a.d = d;
     launch(e, prof, FAM_ROWS, 0, [&] { launch_norm<T>(a, e.stream); });
   };
   // residual += A W^T + bias: the fused residual epilogue, or, for small classes, split-K
@@ -1163,7 +1133,7 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
       a.gamma1 = Wf(e, "encoder.final_norm.weight"); a.beta1 = nullptr; a.eps1 = c.eps;
       a.fused_final = 1; a.type_emb = Wf(e, "type_emb.weight"); a.kinds = kinds;
       a.gamma2 = Wf(e, "head.layers.0.norm1.weight"); a.beta2 = Wf(e, "head.layers.0.norm1.bias"); a.eps2 = 1e-5f;
-      a.x = x; a.rows = m; a.d = d; a.early = e.early;
+      a.x = x; a.rows = m; a.d = d;
       launch(e, prof, FAM_ROWS, 0, [&] { launch_norm<T>(a, e.stream); });
     }
   }

@@ -94,9 +94,7 @@ __device__ __forceinline__ void row_layernorm(float (&v)[NPL], int lane, const f
 template <int NPL, typename T>
 __global__ void __launch_bounds__(kRowWarps * 32) embed_norm_kernel(const int* ids, const float* table,
                                                                     const float* gamma, float eps, int rows, int d,
-                                                                    int vocab, float* residual, T* x, int* err,
-                                                                    int early) {
-  if (early && threadIdx.x == 0) pdl_trigger();
+                                                                    int vocab, float* residual, T* x, int* err) {
   pdl_wait();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -124,7 +122,6 @@ struct NormArgs {
   const float* gamma2; const float* beta2; float eps2;
   void* x;                  // [rows][d] T output (may be nullptr)
   int rows, d;
-  int early;                // trigger dependents at kernel start (small classes)
 };
 
 // Normal:  residual += sum(partials) + bias; x = LN1(residual).
@@ -133,7 +130,6 @@ struct NormArgs {
 // variant's register footprint small.  Replaces kernels.cu:20-49 and kernels.cu:155-158.
 template <int NPL, typename T, bool PARTIALS>
 __global__ void __launch_bounds__(kRowWarps * 32) norm_kernel(const NormArgs a) {
-  if (a.early && threadIdx.x == 0) pdl_trigger();
   pdl_wait();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (row >= a.rows) return;

@@ -55,7 +55,6 @@ struct TcAttnArgs {
   const int* q_index;
   int q_per_row;
   int q_tiles;
-  int early;            // trigger dependents at kernel start (small classes)
 };
 
 struct TcAttnSmem {
@@ -135,7 +134,6 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
                                                                     const __grid_constant__ CUtensorMap tmVt,
                                                                     const TcAttnArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  if (a.early && threadIdx.x == 0) pdl_trigger();
   // The tile table, starts and lengths are written by the host before the forward pass, so they
   // are read before waiting on the previous kernel.
   const bool gathered = a.q_index != nullptr;
