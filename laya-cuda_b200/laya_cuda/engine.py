@@ -45,10 +45,16 @@ class Engine:
             metrics = {"precision": self.runtime.precision, "gpu_ms": self.runtime.gpu_ms}
         else:
             items = self.adapter.prepare(state, questions)
-            logits, acts, metrics = self.runtime.predict(items)
-            result = self.adapter.decode(logits, acts, questions, items)
+            ticket = self.runtime.submit(items)
+            try:
+                # Host work that needs no model output runs while the device pass does.
+                fingerprint = self.adapter.fingerprint(items)
+                plan = self.adapter.decode_plan(questions)
+            finally:
+                logits, acts, metrics = self.runtime.collect(ticket)
+            result = self.adapter.decode(logits, acts, questions, items, plan)
             metrics.update(precision=self.runtime.precision, tokens_per_question=[len(v[0]) for v in items],
-                           input_sha256=self.adapter.fingerprint(items))
+                           input_sha256=fingerprint)
         self.last_metrics = {**metrics, "backend": self.backend, "api_ms": (time.perf_counter() - started) * 1000}
         return result
 

@@ -203,15 +203,22 @@ class Laya:
             return 1.0
         return float(np.clip(value, .5, 5)) if math.isfinite(value) else 1.0
 
-    def decode(self, logits, acts, questions, items):
-        """Answer dict of the SDK (laya.py:137-165) from option logits [b, >=k] and action logits."""
+    def decode_plan(self, questions):
+        """The parts of decode() that need no model output: per question (id, kind, criteria,
+        option count, calibration temperature)."""
+        plan = []
+        for qid, definition in questions.items():
+            kind, _, criteria, options = question(definition)
+            plan.append((qid, kind, criteria, len(options), self._temperature(kind, len(options))))
+        return plan
+
+    def decode(self, logits, acts, questions, items, plan=None):
+        """Answer dict of the SDK (laya.py:137-165) from option logits [b, >=k] and action logits.
+        `plan` is decode_plan(questions), when the caller computed it already."""
         if not np.isfinite(logits).all() or not np.isfinite(acts).all():
             raise RuntimeError("Non-finite model output; no decision returned")
         actions, answers = softmax(acts), {}
-        for row, (qid, definition) in enumerate(questions.items()):
-            kind, _, criteria, options = question(definition)
-            count = len(options)
-            temp = self._temperature(kind, count)
+        for row, (qid, kind, criteria, count, temp) in enumerate(plan if plan is not None else self.decode_plan(questions)):
             prob = softmax(logits[row, :count].astype(np.float32) / np.float32(temp))
             if count > 1:
                 entropy = (prob * np.log(np.maximum(prob, 1e-12))).sum()

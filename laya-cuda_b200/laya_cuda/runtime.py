@@ -6,6 +6,7 @@ attributes its tests read (`slots`, `pool.used_bytes()/total_bytes()`, `weights[
 `span` and `classes` are importable without any GPU library (BatchEngine imports `span`).
 """
 import ctypes as ct
+from itertools import chain
 
 import numpy as np
 
@@ -32,8 +33,8 @@ def flatten(items):
     lengths = np.fromiter((len(item[0]) for item in items), np.int32, len(items))
     counts = np.fromiter((len(item[1]) for item in items), np.int32, len(items))
     kinds = np.fromiter((item[2] for item in items), np.int32, len(items))
-    tokens = np.fromiter((t for item in items for t in item[0]), np.int32, int(lengths.sum()))
-    markers = np.fromiter((p for item in items for p in item[1]), np.int32, int(counts.sum()))
+    tokens = np.fromiter(chain.from_iterable(item[0] for item in items), np.int32, int(lengths.sum()))
+    markers = np.fromiter(chain.from_iterable(item[1] for item in items), np.int32, int(counts.sum()))
     return tokens, lengths, markers, counts, kinds
 
 
