@@ -189,8 +189,10 @@ int laya_interleave_geglu(const uint16_t* src, uint16_t* dst, int F, int K);
 /* Packed attention (kernels.cu:90-154).  qkv: q, k [heads][M][64] each, then v transposed
  * [heads][64][M] (the layout the QKV GEMM epilogue writes); out [M][heads*64].  impl 0: mma.sync
  * kernel over 64-query tiles (split_p: probabilities as high + low 16-bit parts); impl 1: the
- * tcgen05/TMEM kernel the forward pass uses, over 128-query tiles.  Tiles from
- * laya_attention_tiles with the matching tile size; err: device error word (impl 1). */
+ * tcgen05/TMEM kernel the forward pass uses, over 128-query tiles, splitting each tile's keys
+ * over a CTA pair when heads * n_tiles <= the SM count (as the forward pass does); impl 2 / 3:
+ * the tcgen05 kernel never / always splitting keys.  Tiles from laya_attention_tiles with the
+ * matching tile size; err: device error word (impl 1-3). */
 int laya_op_attention(int precision, int impl, const void* qkv, void* out, const int32_t* tiles, int n_tiles,
                       const int32_t* starts, const int32_t* lengths, int M, int heads, int window, int split_p,
                       int* err, void* stream);
@@ -199,7 +201,7 @@ int laya_op_attention(int precision, int impl, const void* qkv, void* out, const
  * laya.py:214-245 followed by the gather of kernels.cu:159-166): row r attends from the tokens
  * q_index[r*q_per_row .. +q_per_row) (token indices into the packed rows, duplicates allowed)
  * to every key of the row; only those rows of `out` are written.  Rows with length 0 are
- * skipped.  Layouts as laya_op_attention; tcgen05 kernel. */
+ * skipped.  Layouts as laya_op_attention; tcgen05 kernel (key split as impl 1). */
 int laya_op_attention_gathered(int precision, const void* qkv, void* out, const int32_t* q_index, int q_per_row,
                                const int32_t* starts, const int32_t* lengths, int n_rows, int M, int heads, int* err,
                                void* stream);

@@ -295,6 +295,12 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// 16-byte store into another CTA's shared memory (a shared::cluster address from cluster_addr).
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+
 // Cluster address of the object at `local` (a shared::cta address) in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t cluster_addr(uint32_t local, uint32_t rank) {
   uint32_t r;

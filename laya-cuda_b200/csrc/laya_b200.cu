@@ -422,8 +422,31 @@ void launch_tc_attention(const AttnMaps& maps, const TcAttnArgs& a, int n_tiles,
     configured |= 1ull << dev;
   }
   if (n_tiles > 65535) fail(LAYA_ERR_INVALID, "%d attention tiles exceed the grid limit", n_tiles);
-  launch_k(tc_attention_kernel<T>, dim3(a.heads, n_tiles), dim3(kTcThreads), TcAttnSmem::kBytes, st, maps.qk, maps.vt, a);
+  if (a.splits != 1 && a.splits != 2) fail(LAYA_ERR_INVALID, "attention key split %d (1 or 2)", a.splits);
+  if (a.splits == 1) {
+    launch_k(tc_attention_kernel<T>, dim3(a.heads, n_tiles), dim3(kTcThreads), TcAttnSmem::kBytes, st, maps.qk, maps.vt, a);
+    return;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.heads, n_tiles, 2);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = TcAttnSmem::kBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 2;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  CK(cudaLaunchKernelEx(&cfg, tc_attention_kernel<T>, maps.qk, maps.vt, a));
 }
+
+// Key split of the tcgen05 attention: two CTAs per tile when one CTA per tile and head would
+// leave at least half of the SMs idle (batch-1 classes), one otherwise.
+int attention_splits(int heads, int n_tiles, int sms) { return heads * n_tiles <= sms ? 2 : 1; }
 
 template <typename T>
 void launch_attention(const AttnArgs& a, int n_tiles, bool split_p, cudaStream_t st) {
@@ -1058,6 +1081,7 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
         a.q_index = indices; a.q_per_row = L.k + 1; a.q_tiles = (L.k + 1 + kTcQ - 1) / kTcQ;
         n_tiles = L.b * a.q_tiles;
       }
+      a.splits = attention_splits(c.heads, n_tiles, e.sms);
       launch(e, prof, FAM_ATTENTION, 0, [&] { launch_tc_attention<T>(s.attn_maps, a, n_tiles, e.stream); });
     } else {
       AttnArgs a{};
@@ -1736,12 +1760,15 @@ int laya_op_attention(int precision, int impl, const void* qkv, void* out, const
                       const int32_t* starts, const int32_t* lengths, int M, int heads, int window, int split_p, int* err,
                       void* stream) {
   API_BEGIN
-  if (impl == 1) {
+  if (impl >= 1 && impl <= 3) {
     const bool bf = precision == LAYA_PRECISION_BF16;
     const AttnMaps maps = attn_maps(qkv, M, heads, bf);
     TcAttnArgs t{};
     t.qk = qkv; t.out = out; t.tiles = reinterpret_cast<const int4*>(tiles); t.starts = starts; t.lengths = lengths;
     t.M = M; t.heads = heads; t.window = window; t.err = err;
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    t.splits = impl == 2 ? 1 : impl == 3 ? 2 : attention_splits(heads, n_tiles, sm_count(dev));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (bf) launch_tc_attention<__nv_bfloat16>(maps, t, n_tiles, st);
     else launch_tc_attention<__half>(maps, t, n_tiles, st);
@@ -1767,6 +1794,9 @@ int laya_op_attention_gathered(int precision, const void* qkv, void* out, const 
   t.qk = qkv; t.out = out; t.starts = starts; t.lengths = lengths;
   t.M = M; t.heads = heads; t.window = -1; t.err = err;
   t.q_index = q_index; t.q_per_row = q_per_row; t.q_tiles = (q_per_row + kTcQ - 1) / kTcQ;
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  t.splits = attention_splits(heads, n_rows * t.q_tiles, sm_count(dev));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (bf) launch_tc_attention<__nv_bfloat16>(maps, t, n_rows * t.q_tiles, st);
   else launch_tc_attention<__half>(maps, t, n_rows * t.q_tiles, st);

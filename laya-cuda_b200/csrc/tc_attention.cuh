@@ -21,6 +21,7 @@
 //         warp has read S_{j-1}, so the tensor core works on the next block during the softmax;
 //   O += P_j V_j    (M=128, N=64, K=128)  A = P from TMEM, O in [192,256), issued as soon as
 //         every warp has written P_j.
+// Small grids (batch-1 classes) split each tile's key blocks over a CTA pair (TcAttnArgs::splits).
 // Without separate copy and MMA warps the CTA has 128 threads, so two CTAs per SM leave each
 // thread 255 registers (the softmax keeps a 128-key row of S in registers without spilling).
 // Key blocks start at the window's first key (rounded down to 16 tokens), not at a multiple of
@@ -55,6 +56,11 @@ struct TcAttnArgs {
   const int* q_index;
   int q_per_row;
   int q_tiles;
+  // 1, or 2: key split.  The grid is (heads, tiles, 2) in clusters of (1, 1, 2); CTA rank r of a
+  // cluster runs key blocks [r h, ...) of its tile (h = half the blocks, rounded up); rank 1 hands
+  // its unnormalised O row, running maximum and sum to rank 0 through distributed shared memory,
+  // and rank 0 merges and stores.  Halves the serial block chain of grids that leave SMs idle.
+  int splits;
 };
 
 struct TcAttnSmem {
@@ -171,7 +177,16 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
     k_lo = max(0, q0 - a.window) & ~15;  // 16-token aligned: the V^T copy's inner coordinate
     k_hi = min(valid, q0 + kTcQ + a.window);
   }
-  const int n_blocks = k_hi > k_lo ? (k_hi - k_lo + kTcKB - 1) / kTcKB : 0;
+  const int all_blocks = k_hi > k_lo ? (k_hi - k_lo + kTcKB - 1) / kTcKB : 0;
+  // Key split: this CTA's share of the tile's blocks (k_lo stays 16-aligned: 128-key steps).
+  const bool split = a.splits > 1;
+  const uint32_t rank = split ? cluster_rank() : 0;
+  int n_blocks = all_blocks;
+  if (split) {
+    const int h = (all_blocks + 1) / 2;
+    n_blocks = rank == 0 ? h : all_blocks - h;
+    if (rank == 1) k_lo += h * kTcKB;
+  }
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem + TcAttnSmem::kOffQ;
@@ -380,16 +395,62 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
     ok = mbar_wait(o_full, (n_blocks - 1) & 1, a.err, kErrAttnWait, abort_flag);
     ok = __all_sync(0xffffffffu, ok);
   }
-  if (ok) {
-    const int token = gathered ? (r < nq ? qidx[r] : -1) : t0 + r;
-    uint32_t o[2][32];
+  uint32_t o[2][32];
+  if (ok && n_blocks > 0) {
     tc_fence_after();
     tmem_ld32_async(o_tmem, o[0]);
     tmem_ld32_async(o_tmem + 32, o[1]);
     tmem_wait_ld(o[0]);
     tmem_wait_ld(o[1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) { o[0][i] = 0u; o[1][i] = 0u; }
+  }
+  if (split) {
+    // Every CTA of the cluster reaches both barriers on every path (the early returns above
+    // are taken by both CTAs of a cluster alike).  (1): both CTAs' last MMAs have completed,
+    // so rank 0's K/V stages are free; rank 1 then writes its row there: 64 O values, its
+    // running maximum (log2 units), its sum and its status.  (2): the rows have landed.
+    constexpr int kXRow = 68;  // floats per exchanged row (16-byte multiple)
+    static_assert(kTcQ * kXRow * 4 <= 2 * (TcAttnSmem::kK + TcAttnSmem::kV), "exchange buffer");
+    float* xrow = reinterpret_cast<float*>(sK) + r * kXRow;
+    cluster_sync();
+    if (rank == 1) {
+      const uint32_t dst = cluster_addr(smem_u32(xrow), 0);
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          st_cluster_v4(dst + (h * 32 + i) * 4, make_float4(__uint_as_float(o[h][i]), __uint_as_float(o[h][i + 1]),
+                                                            __uint_as_float(o[h][i + 2]), __uint_as_float(o[h][i + 3])));
+      st_cluster_v4(dst + 64 * 4, make_float4(m_used, l, ok ? 1.f : 0.f, 0.f));
+    }
+    cluster_sync();
+    if (rank == 0) {
+      const float4 ml = *reinterpret_cast<const float4*>(xrow + 64);
+      ok = ok && ml.z != 0.f;
+      // Rescale both partial results to the larger maximum (a side that saw no key has
+      // maximum -inf, sum 0 and O 0, and weight 0).
+      const float mx = fmaxf(m_used, ml.x);
+      const float w0 = m_used == -INFINITY ? 0.f : ex2_approx(m_used - mx);
+      const float w1 = ml.x == -INFINITY ? 0.f : ex2_approx(ml.x - mx);
+      l = l * w0 + ml.y * w1;
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+          const float4 p = *reinterpret_cast<const float4*>(xrow + h * 32 + i);
+          o[h][i] = __float_as_uint(__uint_as_float(o[h][i]) * w0 + p.x * w1);
+          o[h][i + 1] = __float_as_uint(__uint_as_float(o[h][i + 1]) * w0 + p.y * w1);
+          o[h][i + 2] = __float_as_uint(__uint_as_float(o[h][i + 2]) * w0 + p.z * w1);
+          o[h][i + 3] = __float_as_uint(__uint_as_float(o[h][i + 3]) * w0 + p.w * w1);
+        }
+    }
+  }
+  if (ok && rank == 0) {
+    const int token = gathered ? (r < nq ? qidx[r] : -1) : t0 + r;
     if (gathered ? token >= 0 : token < t1) {
-      const bool live = n_blocks > 0 && (gathered || q < valid) && l > 0.f;
+      const bool live = all_blocks > 0 && (gathered || q < valid) && l > 0.f;
       const float inv = live ? 1.f / l : 0.f;
       T* dst = out + (size_t)token * width + head * 64;
 #pragma unroll

@@ -217,16 +217,17 @@ def packed_case(lengths):
 
 
 @pytest.mark.parametrize("prec,impl,split_p", [("bf16", 0, 0), ("bf16", 0, 1), ("f16", 0, 1), ("f16", 1, 0),
-                                               ("bf16", 1, 0)])
+                                               ("bf16", 1, 0), ("f16", 2, 0), ("bf16", 3, 0)])
 @pytest.mark.parametrize("lengths,window", [([32], -1), ([7, 96], 64), ([128, 1], -1), ([250, 131], 64),
                                             ([256, 219, 145], -1), ([500], 64), ([1024, 333], -1), ([300, 77], 40)])
 def test_packed_attention_matches_oracle(lib, prec, impl, split_p, lengths, window):
     """Cases and float64 oracle of tests/test_attention.py:12-56 (h=2, seeded by M), for the
-    mma.sync kernel (impl 0, 64-query tiles) and the tcgen05 kernel (impl 1, 128-query tiles)."""
+    mma.sync kernel (impl 0, 64-query tiles) and the tcgen05 kernel (128-query tiles; impl 1:
+    key split chosen by grid size, which these small grids always take; 2: never; 3: always)."""
     check_packed_attention(lib, prec, impl, split_p, lengths, window, ramp=False)
 
 
-@pytest.mark.parametrize("prec,impl", [("f16", 0), ("f16", 1), ("bf16", 1)])
+@pytest.mark.parametrize("prec,impl", [("f16", 0), ("f16", 1), ("bf16", 1), ("f16", 2), ("bf16", 3)])
 @pytest.mark.parametrize("lengths,window", [([1024, 333], -1), ([700], 64), ([513, 200], -1)])
 def test_packed_attention_growing_scores(lib, prec, impl, lengths, window):
     """Scores that grow along the row (keys scaled up with position), so the running maximum
