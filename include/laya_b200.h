@@ -190,7 +190,8 @@ int laya_interleave_geglu(const uint16_t* src, uint16_t* dst, int F, int K);
  * [heads][64][M] (the layout the QKV GEMM epilogue writes); out [M][heads*64].  impl 0: mma.sync
  * kernel over 64-query tiles (split_p: probabilities as high + low 16-bit parts); impl 1: the
  * tcgen05/TMEM kernel the forward pass uses, over 128-query tiles, splitting each tile's keys
- * over a CTA pair when heads * n_tiles <= the SM count (as the forward pass does); impl 2 / 3:
+ * over a CTA pair for global attention (window < 0) when heads * n_tiles <= the SM count and
+ * M >= 384 (the forward pass's rule, with M for the row length); impl 2 / 3:
  * the tcgen05 kernel never / always splitting keys.  Tiles from laya_attention_tiles with the
  * matching tile size; err: device error word (impl 1-3). */
 int laya_op_attention(int precision, int impl, const void* qkv, void* out, const int32_t* tiles, int n_tiles,

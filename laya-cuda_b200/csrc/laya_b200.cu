@@ -445,8 +445,13 @@ void launch_tc_attention(const AttnMaps& maps, const TcAttnArgs& a, int n_tiles,
 }
 
 // Key split of the tcgen05 attention: two CTAs per tile when one CTA per tile and head would
-// leave at least half of the SMs idle (batch-1 classes), one otherwise.
-int attention_splits(int heads, int n_tiles, int sms) { return heads * n_tiles <= sms ? 2 : 1; }
+// leave at least half of the SMs idle (batch-1 classes) and a tile sees at least three key blocks
+// (global attention over rows of ~384+ keys).  Traces of 512-token passes: a global layer's
+// attention 11.0 -> 9.7 us after the dependency wait; split window-64 tiles (two blocks) were
+// 1 us slower, the merge costing more than the block it saves.
+int attention_splits(int heads, int n_tiles, int sms, int window, int row_keys) {
+  return window < 0 && row_keys >= 3 * kTcKB && heads * n_tiles <= sms ? 2 : 1;
+}
 
 template <typename T>
 void launch_attention(const AttnArgs& a, int n_tiles, bool split_p, cudaStream_t st) {
@@ -1081,7 +1086,7 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
         a.q_index = indices; a.q_per_row = L.k + 1; a.q_tiles = (L.k + 1 + kTcQ - 1) / kTcQ;
         n_tiles = L.b * a.q_tiles;
       }
-      a.splits = attention_splits(c.heads, n_tiles, e.sms);
+      a.splits = attention_splits(c.heads, n_tiles, e.sms, window, m / L.b);
       launch(e, prof, FAM_ATTENTION, 0, [&] { launch_tc_attention<T>(s.attn_maps, a, n_tiles, e.stream); });
     } else {
       AttnArgs a{};
@@ -1768,7 +1773,7 @@ int laya_op_attention(int precision, int impl, const void* qkv, void* out, const
     t.M = M; t.heads = heads; t.window = window; t.err = err;
     int dev = 0;
     CK(cudaGetDevice(&dev));
-    t.splits = impl == 2 ? 1 : impl == 3 ? 2 : attention_splits(heads, n_tiles, sm_count(dev));
+    t.splits = impl == 2 ? 1 : impl == 3 ? 2 : attention_splits(heads, n_tiles, sm_count(dev), window, M);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (bf) launch_tc_attention<__nv_bfloat16>(maps, t, n_tiles, st);
     else launch_tc_attention<__half>(maps, t, n_tiles, st);
@@ -1796,7 +1801,7 @@ int laya_op_attention_gathered(int precision, const void* qkv, void* out, const 
   t.q_index = q_index; t.q_per_row = q_per_row; t.q_tiles = (q_per_row + kTcQ - 1) / kTcQ;
   int dev = 0;
   CK(cudaGetDevice(&dev));
-  t.splits = attention_splits(heads, n_rows * t.q_tiles, sm_count(dev));
+  t.splits = attention_splits(heads, n_rows * t.q_tiles, sm_count(dev), -1, M / n_rows);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (bf) launch_tc_attention<__nv_bfloat16>(maps, t, n_rows * t.q_tiles, st);
   else launch_tc_attention<__half>(maps, t, n_rows * t.q_tiles, st);

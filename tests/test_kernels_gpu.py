@@ -223,7 +223,7 @@ def packed_case(lengths):
 def test_packed_attention_matches_oracle(lib, prec, impl, split_p, lengths, window):
     """Cases and float64 oracle of tests/test_attention.py:12-56 (h=2, seeded by M), for the
     mma.sync kernel (impl 0, 64-query tiles) and the tcgen05 kernel (128-query tiles; impl 1:
-    key split chosen by grid size, which these small grids always take; 2: never; 3: always)."""
+    key split chosen as the forward pass does; 2: never; 3: always)."""
     check_packed_attention(lib, prec, impl, split_p, lengths, window, ramp=False)
 
 
