@@ -167,9 +167,8 @@ const char* laya_last_error(laya_engine* e);
  * sin f_2k+1) of position p at [k][p], indexed by positions[row]; q and k are written
  * [heads][M][64], v transposed [heads][64][M], all in `out`),
  * 5 residual += (fp32), 6 split-K partials ([splits][M][N] fp32 in `residual`).  bias: fp32 [N]
- * or NULL.  block_n: column tile (64, 128, 256), 0 to choose, -128 / -256 for the CTA-pair
- * (cta_group::2, 256-row tile) kernel, or 1 for the CUDA-core kernel the decision head uses for
- * at most 16 rows (epilogues 0, 1, 2 and 5; K a multiple of 8, at most 4096).  Replaces cublasGemmEx + bias/activate/layout
+ * or NULL.  block_n: column tile (64, 128, 256), 0 to choose, or -128 / -256 for the CTA-pair
+ * (cta_group::2, 256-row tile) kernel.  Replaces cublasGemmEx + bias/activate/layout
  * (ops.py:58-66; kernels.cu:50-82). */
 int laya_op_gemm(int precision, int epi, const void* x, const void* w, int M, int N, int K, void* out, int ldo,
                  float* residual, int ldr, const float* bias, int heads, const float* rope_tab, int rope_rows,

@@ -32,7 +32,6 @@
 #include "rowops.cuh"
 #include "tc_attention.cuh"
 #include "gemm_ln.cuh"
-#include "skinny.cuh"
 
 using namespace laya;
 
@@ -411,38 +410,6 @@ AttnMaps attn_maps(const void* qkv, int M, int heads, bool bf) {
   m.qk = make_map(qkv, 3 * hm, 64, kTcQ, bf);
   m.vt = make_map(static_cast<const uint8_t*>(qkv) + (size_t)2 * hm * 64 * 2, (int64_t)heads * 64, M, 64, bf);
   return m;
-}
-
-// The CUDA-core GEMM serves a few rows: at most kSkinnyRows, K a multiple of 8 up to kSkinnyMaxK,
-// and the 16-bit output or fp32 residual epilogues.
-bool skinny_ok(int M, int K, int epi) {
-  return M >= 1 && M <= kSkinnyRows && K % 8 == 0 && K <= kSkinnyMaxK &&
-         (epi == EPI_STORE || epi == EPI_RELU || epi == EPI_GELU || epi == EPI_RESIDUAL);
-}
-
-template <typename T, int EPI>
-void launch_skinny_inst(const void* x, const void* w, const GemmArgs& a, cudaStream_t st) {
-  static uint64_t configured = 0;  // one bit per device
-  int dev = 0;
-  CK(cudaGetDevice(&dev));
-  if (!(configured & (1ull << dev))) {
-    CK(cudaFuncSetAttribute(skinny_gemm_kernel<EPI, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                            kSkinnyRows * kSkinnyMaxK * 2));
-    configured |= 1ull << dev;
-  }
-  launch_k(skinny_gemm_kernel<EPI, T>, dim3((a.N + kSkinnyWarps - 1) / kSkinnyWarps), dim3(kSkinnyWarps * 32),
-           (size_t)a.M * a.K * 2, st, static_cast<const T*>(x), static_cast<const T*>(w), a);
-}
-
-template <typename T>
-void launch_skinny(int epi, const void* x, const void* w, const GemmArgs& a, cudaStream_t st) {
-  if (!skinny_ok(a.M, a.K, epi)) fail(LAYA_ERR_INVALID, "skinny GEMM: %d rows, K %d, epilogue %d", a.M, a.K, epi);
-  switch (epi) {
-    case EPI_STORE: launch_skinny_inst<T, EPI_STORE>(x, w, a, st); break;
-    case EPI_RELU: launch_skinny_inst<T, EPI_RELU>(x, w, a, st); break;
-    case EPI_GELU: launch_skinny_inst<T, EPI_GELU>(x, w, a, st); break;
-    default: launch_skinny_inst<T, EPI_RESIDUAL>(x, w, a, st); break;
-  }
 }
 
 template <typename T>
@@ -1065,17 +1032,6 @@ void gemm_partial(Engine& e, bool prof, int family, const CUtensorMap& ta, const
   launch(e, prof, family, 2.0 * M * N * K, [&] { launch_gemm<T>(EPI_PARTIAL, bn, ta, tb, a, e.sms, e.stream); });
 }
 
-// A GEMM of at most kSkinnyRows rows on the CUDA cores (skinny.cuh): A given by its pointer.
-template <typename T>
-void gemm_skinny(Engine& e, bool prof, int family, int epi, const void* x, const std::string& wname, int M, void* out,
-                 int ldo, float* residual, int ldr, const float* bias, int* err) {
-  const Tensor& w = W(e, wname);
-  GemmArgs a{};
-  a.M = M; a.N = (int)w.shape[0]; a.K = (int)w.shape[1]; a.splits = 1;
-  a.out = out; a.ldo = ldo; a.residual = residual; a.ldr = ldr; a.bias = bias; a.err = err;
-  launch(e, prof, family, 2.0 * M * a.N * a.K, [&] { launch_skinny<T>(epi, x, w.ptr, a, e.stream); });
-}
-
 // The whole forward pass of one shape class (runtime.py:90-113 + laya.py:214-245), enqueued
 // on the engine stream.  Used eagerly and inside graph capture.
 template <typename T>
@@ -1152,13 +1108,9 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
   // residual += A W^T + bias: the fused residual epilogue, or, for small classes, split-K
   // partials that the following norm adds.
   auto residual_gemm = [&](int family, const CUtensorMap& ta, const std::string& wname, int rows, float* res,
-                           const float* bias, const void* a_ptr = nullptr) -> Pending {
+                           const float* bias) -> Pending {
     const Tensor& w = W(e, wname);
     const int N = (int)w.shape[0], K = (int)w.shape[1];
-    if (a_ptr && skinny_ok(rows, K, EPI_RESIDUAL)) {
-      gemm_skinny<T>(e, prof, family, EPI_RESIDUAL, a_ptr, wname, rows, nullptr, 0, res, d, bias, err);
-      return Pending{};
-    }
     if (partials && rows <= kSplitRowsMax && N == d) {
       const TilePlan plan = plan_small(rows, N, K, EPI_PARTIAL, true, false, e.sms);
       if (plan.splits > 1) {
@@ -1229,16 +1181,11 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
                  indices, count, d, m, sel, scored, err);
       });
       Pending pend = residual_gemm(FAM_GEMM_HEAD, s.map_scored, p + "self_attn.out_proj.weight", count, sel,
-                                   Wf(e, p + "self_attn.out_proj.bias"), scored);
+                                   Wf(e, p + "self_attn.out_proj.bias"));
       norm(sel, count, Wf(e, p + "norm2.weight"), Wf(e, p + "norm2.bias"), 1e-5f, selx, pend);
-      if (skinny_ok(count, d, EPI_RELU))
-        gemm_skinny<T>(e, prof, FAM_GEMM_HEAD, EPI_RELU, selx, p + "linear1.weight", count, ffsel, 4 * d, nullptr, 0,
-                       Wf(e, p + "linear1.bias"), err);
-      else
-        gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_RELU, s.map_selx, p + "linear1.weight", count, ffsel, 4 * d, nullptr, 0,
-                Wf(e, p + "linear1.bias"), err);
-      head_pend = residual_gemm(FAM_GEMM_HEAD, s.map_ffsel, p + "linear2.weight", count, sel, Wf(e, p + "linear2.bias"),
-                                ffsel);
+      gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_RELU, s.map_selx, p + "linear1.weight", count, ffsel, 4 * d, nullptr, 0,
+              Wf(e, p + "linear1.bias"), err);
+      head_pend = residual_gemm(FAM_GEMM_HEAD, s.map_ffsel, p + "linear2.weight", count, sel, Wf(e, p + "linear2.bias"));
     } else {
       Pending pend = residual_gemm(FAM_GEMM_HEAD, s.map_attn, p + "self_attn.out_proj.weight", m, residual,
                                    Wf(e, p + "self_attn.out_proj.bias"));
@@ -1251,12 +1198,7 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
     }
   }
   norm(sel, count, Wf(e, "scorer.0.weight"), Wf(e, "scorer.0.bias"), 1e-5f, selx, head_pend);
-  if (skinny_ok(count, d, EPI_GELU))
-    gemm_skinny<T>(e, prof, FAM_GEMM_HEAD, EPI_GELU, selx, "scorer.1.weight", count, scored, d, nullptr, 0,
-                   Wf(e, "scorer.1.bias"), err);
-  else
-    gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_GELU, s.map_selx, "scorer.1.weight", count, scored, d, nullptr, 0,
-            Wf(e, "scorer.1.bias"), err);
+  gemm<T>(e, prof, FAM_GEMM_HEAD, EPI_GELU, s.map_selx, "scorer.1.weight", count, scored, d, nullptr, 0, Wf(e, "scorer.1.bias"), err);
   TailArgs t{};
   t.selected = sel; t.scored = scored; t.counts = counts;
   t.w3 = Wf(e, "scorer.3.weight"); t.b3 = Wf(e, "scorer.3.bias");
@@ -1765,16 +1707,6 @@ int laya_op_gemm(int precision, int epi, const void* x, const void* w, int M, in
   const int sms = sm_count(dev);
   const bool bf = precision == LAYA_PRECISION_BF16;
   if (splits < 1) splits = 1;
-  if (block_n == 1) {
-    // The CUDA-core kernel for a few rows.
-    GemmArgs a{};
-    a.M = M; a.N = N; a.K = K; a.splits = 1;
-    a.out = out; a.ldo = ldo; a.residual = residual; a.ldr = ldr; a.bias = bias; a.err = err;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (bf) launch_skinny<__nv_bfloat16>(epi, x, w, a, st);
-    else launch_skinny<__half>(epi, x, w, a, st);
-    return LAYA_OK;
-  }
   // block_n < 0 selects the CTA-pair kernel with |block_n| columns per tile.
   const bool pair = block_n < 0;
   const int bn = block_n > 0 ? block_n : block_n < 0 ? -block_n : pick_bn(M, N, epi, sms);

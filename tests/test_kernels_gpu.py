@@ -90,33 +90,6 @@ def test_gemm_relu_gelu_epilogues(lib, prec, epi):
 
 
 @pytest.mark.parametrize("prec", ["bf16", "f16"])
-@pytest.mark.parametrize("epi", [0, 1, 2, 5])
-@pytest.mark.parametrize("M,N,K", [(1, 768, 768), (9, 3072, 768), (16, 768, 3072), (5, 200, 4096)])
-def test_gemm_skinny_cuda_core_kernel(lib, prec, epi, M, N, K):
-    """The CUDA-core kernel the decision head uses for its few gathered rows (block_n = 1)."""
-    rng = np.random.default_rng(M * 7 + N + K + epi)
-    x, xd = rand16((M, K), prec, rng)
-    w, wd = rand16((N, K), prec, rng, 0.05)
-    bias_np = rng.normal(0, 0.1, N).astype(np.float32)
-    bias = torch.from_numpy(bias_np).cuda()
-    pre = xd @ wd.T + bias_np
-    tol_acc = 1e-4 * math.sqrt(K)
-    if epi == 5:
-        base = rng.normal(0, 1, (M, N)).astype(np.float32)
-        residual = torch.from_numpy(base.copy()).cuda()
-        gemm(lib, prec, epi, x, w, residual=residual, ldr=N, bias=bias, block_n=1)
-        assert np.max(np.abs(residual.cpu().numpy() - (base + pre))) < tol_acc
-        return
-    out = torch.full((M, N), float("nan"), dtype=PRECISIONS[prec][1], device="cuda")
-    gemm(lib, prec, epi, x, w, out, N, bias=bias, block_n=1)
-    expected = pre if epi == 0 else np.maximum(pre, 0) if epi == 1 else \
-        0.5 * pre * (1 + np.vectorize(math.erf)(pre / math.sqrt(2)))
-    got = out.double().cpu().numpy()
-    assert np.all(np.abs(got - expected) <= ROUND[prec] * np.abs(expected) + tol_acc), \
-        float(np.max(np.abs(got - expected) - ROUND[prec] * np.abs(expected)))
-
-
-@pytest.mark.parametrize("prec", ["bf16", "f16"])
 @pytest.mark.parametrize("M,F", [(96, 3072), (333, 512)])
 def test_gemm_geglu_epilogue(lib, prec, M, F):
     rng = np.random.default_rng(M)
