@@ -68,11 +68,10 @@ __device__ __forceinline__ float warp_sum(float x) {
   return x;
 }
 
-// In-place LayerNorm of the lane's slice: v = (v - mean) * rsqrt(var + eps) * gamma (+ beta).
+// In-place LayerNorm of the lane's slice: v = (v - mean) * rsqrt(var + eps) * gamma + beta, with
+// the lane's gamma / beta slices already in registers (row_load's layout; beta zeros if absent).
 template <int NPL>
-__device__ __forceinline__ void row_layernorm(float (&v)[NPL], int lane, const float* gamma, const float* beta,
-                                              float eps) {
-  constexpr int CH = RowVec<NPL>::CH;
+__device__ __forceinline__ void row_layernorm(float (&v)[NPL], const float (&g)[NPL], const float (&b)[NPL], float eps) {
   constexpr float inv_d = 1.0f / (32 * NPL);
   float s = 0.f;
 #pragma unroll
@@ -83,9 +82,17 @@ __device__ __forceinline__ void row_layernorm(float (&v)[NPL], int lane, const f
   for (int i = 0; i < NPL; ++i) { const float t = v[i] - mean; q += t * t; }
   const float inv = rsqrtf(warp_sum(q) * inv_d + eps);
 #pragma unroll
-  for (int i = 0; i < NPL; ++i) {
-    const int col = (i / CH) * 32 * CH + lane * CH + i % CH;
-    v[i] = (v[i] - mean) * inv * gamma[col] + (beta ? beta[col] : 0.f);
+  for (int i = 0; i < NPL; ++i) v[i] = (v[i] - mean) * inv * g[i] + b[i];
+}
+
+// Loads the lane's slice of an optional [d] vector (zeros when absent).
+template <int NPL>
+__device__ __forceinline__ void row_load_opt(const float* src, int lane, float (&v)[NPL]) {
+  if (src) {
+    row_load<NPL>(src, lane, v);
+  } else {
+#pragma unroll
+    for (int i = 0; i < NPL; ++i) v[i] = 0.f;
   }
 }
 
@@ -95,8 +102,11 @@ template <int NPL, typename T>
 __global__ void __launch_bounds__(kRowWarps * 32) embed_norm_kernel(const int* ids, const float* table,
                                                                     const float* gamma, float eps, int rows, int d,
                                                                     int vocab, float* residual, T* x, int* err) {
-  pdl_wait();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  float g[NPL], z[NPL];
+  row_load<NPL>(gamma, lane, g);  // a weight: loaded before waiting on the previous kernel
+  row_load_opt<NPL>(nullptr, lane, z);
+  pdl_wait();
   if (row >= rows) return;
   int id = ids[row];
   if (id < 0 || id >= vocab) {
@@ -105,7 +115,7 @@ __global__ void __launch_bounds__(kRowWarps * 32) embed_norm_kernel(const int* i
   }
   float v[NPL];
   row_load<NPL>(table + (size_t)id * d, lane, v);
-  row_layernorm<NPL>(v, lane, gamma, nullptr, eps);
+  row_layernorm<NPL>(v, g, z, eps);
   row_store<NPL>(residual + (size_t)row * d, lane, v);
   row_store_t<NPL, T>(x + (size_t)row * d, lane, v);
 }
@@ -130,8 +140,15 @@ struct NormArgs {
 // variant's register footprint small.  Replaces kernels.cu:20-49 and kernels.cu:155-158.
 template <int NPL, typename T, bool PARTIALS>
 __global__ void __launch_bounds__(kRowWarps * 32) norm_kernel(const NormArgs a) {
-  pdl_wait();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  // Every independent load is issued up front, so a row costs about one memory round trip: the
+  // norm weights and the split GEMM's bias (weights) before waiting on the previous kernel, then
+  // the residual row and up to four partial rows together.
+  float g1[NPL], b1[NPL], pb[NPL];
+  row_load<NPL>(a.gamma1, lane, g1);
+  row_load_opt<NPL>(a.beta1, lane, b1);
+  if (PARTIALS) row_load_opt<NPL>(a.partial_bias, lane, pb);
+  pdl_wait();
   if (row >= a.rows) return;
   const int d = 32 * NPL;
   float* r = a.residual + (size_t)row * d;
@@ -139,46 +156,38 @@ __global__ void __launch_bounds__(kRowWarps * 32) norm_kernel(const NormArgs a) 
   row_load<NPL>(r, lane, v);
   if (PARTIALS) {
     // Partial sums in split order, then the GEMM bias, then the residual: a fixed order, so the
-    // result does not depend on the batch or on scheduling.  Three partial rows in flight per
-    // step: the reduction is latency-bound at the small batches that use it.
+    // result does not depend on the batch or on scheduling.
     float acc[NPL];
-    row_load<NPL>(a.partials + (size_t)row * d, lane, acc);
-    for (int s = 1; s < a.splits; s += 3) {
-      float p0[NPL], p1[NPL], p2[NPL];
-      row_load<NPL>(a.partials + ((size_t)s * a.rows + row) * d, lane, p0);
-      if (s + 1 < a.splits) row_load<NPL>(a.partials + ((size_t)(s + 1) * a.rows + row) * d, lane, p1);
-      if (s + 2 < a.splits) row_load<NPL>(a.partials + ((size_t)(s + 2) * a.rows + row) * d, lane, p2);
 #pragma unroll
-      for (int i = 0; i < NPL; ++i) acc[i] += p0[i];
-      if (s + 1 < a.splits) {
+    for (int i = 0; i < NPL; ++i) acc[i] = 0.f;
+    for (int s0 = 0; s0 < a.splits; s0 += 4) {
+      float p[4][NPL];
 #pragma unroll
-        for (int i = 0; i < NPL; ++i) acc[i] += p1[i];
-      }
-      if (s + 2 < a.splits) {
+      for (int q = 0; q < 4; ++q)
+        if (s0 + q < a.splits) row_load<NPL>(a.partials + ((size_t)(s0 + q) * a.rows + row) * d, lane, p[q]);
 #pragma unroll
-        for (int i = 0; i < NPL; ++i) acc[i] += p2[i];
-      }
-    }
-    if (a.partial_bias) {
-      float b[NPL];
-      row_load<NPL>(a.partial_bias, lane, b);
+      for (int q = 0; q < 4; ++q)
+        if (s0 + q < a.splits) {
 #pragma unroll
-      for (int i = 0; i < NPL; ++i) acc[i] += b[i];
+          for (int i = 0; i < NPL; ++i) acc[i] += p[q][i];
+        }
     }
 #pragma unroll
-    for (int i = 0; i < NPL; ++i) v[i] += acc[i];
+    for (int i = 0; i < NPL; ++i) v[i] += acc[i] + pb[i];
   }
   if (a.fused_final) {
-    row_layernorm<NPL>(v, lane, a.gamma1, a.beta1, a.eps1);
-    float t[NPL];
+    float g2[NPL], b2[NPL], t[NPL];
+    row_load<NPL>(a.gamma2, lane, g2);
+    row_load_opt<NPL>(a.beta2, lane, b2);
     row_load<NPL>(a.type_emb + (size_t)a.kinds[row] * d, lane, t);
+    row_layernorm<NPL>(v, g1, b1, a.eps1);
 #pragma unroll
     for (int i = 0; i < NPL; ++i) v[i] += t[i];
     row_store<NPL>(r, lane, v);
-    row_layernorm<NPL>(v, lane, a.gamma2, a.beta2, a.eps2);
+    row_layernorm<NPL>(v, g2, b2, a.eps2);
   } else {
     if (PARTIALS) row_store<NPL>(r, lane, v);
-    row_layernorm<NPL>(v, lane, a.gamma1, a.beta1, a.eps1);
+    row_layernorm<NPL>(v, g1, b1, a.eps1);
   }
   if (a.x) row_store_t<NPL, T>(reinterpret_cast<T*>(a.x) + (size_t)row * d, lane, v);
 }
