@@ -416,9 +416,8 @@ def run_engine(args, rank, world, local_rank):
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one FFN-up GEMM launch per token (ncu capture
-# of the first 64-sequence micro-batch, 39,518 tokens, of the current kernel, summarised in
-# profiles/row_kernels_head_and_gemms_config5.md: 71.1 + 190.7 MB); traffic grows in proportion
-# to the rows, so a full launch is this times its tokens.
+# of the first 64-sequence micro-batch, 39,518 tokens, of the current kernel: 71.1 + 190.7 MB);
+# traffic grows in proportion to the rows, so a full launch is this times its tokens.
 TRAFFIC_FFN_UP_BYTES_PER_TOKEN = 261.8e6 / 39518
 
 

@@ -155,6 +155,15 @@ int laya_destroy(laya_engine* e);
 /* Message of the last failing call on `e` (or of the last failing laya_create when e is NULL). */
 const char* laya_last_error(laya_engine* e);
 
+/* Process-wide launch options for tests of ordering and failure handling (no counterpart in the
+ * reference).  programmatic_launch (1, the default, or 0): kernels of a pass launch with
+ * programmatic stream serialisation, each waiting on the device for its predecessor's results.
+ * wait_limit_ns: the limit of every bounded pipeline wait inside the kernels (0 restores the
+ * default of 2 s); a wait that runs out makes the kernel unwind, drain what it issued and set its
+ * error word, so the call reports LAYA_ERR_DEVICE.  Applies to launches made after the call;
+ * CUDA graphs keep the options in effect when they were captured. */
+int laya_set_launch_options(int programmatic_launch, uint64_t wait_limit_ns);
+
 /* ------------------------------------------------------------------------------------------
  * Kernel-level entry points (device pointers, enqueued on `stream`), used by the parity tests
  * the way the reference's tests drive Ops directly (tests/test_gpu.py, tests/test_attention.py).
@@ -186,17 +195,15 @@ int laya_op_gemm_ln(int precision, const void* x, const void* w, int M, int N, i
 /* Reorders Wi [2F][K] (gate rows then up rows) into 64-row blocks [gate_i, up_i] (host memory). */
 int laya_interleave_geglu(const uint16_t* src, uint16_t* dst, int F, int K);
 
-/* Packed attention (kernels.cu:90-154).  qkv: q, k [heads][M][64] each, then v transposed
- * [heads][64][M] (the layout the QKV GEMM epilogue writes); out [M][heads*64].  impl 0: mma.sync
- * kernel over 64-query tiles (split_p: probabilities as high + low 16-bit parts); impl 1: the
- * tcgen05/TMEM kernel the forward pass uses, over 128-query tiles, splitting each tile's keys
- * over a CTA pair for global attention (window < 0) when heads * n_tiles <= the SM count and
- * M >= 384 (the forward pass's rule, with M for the row length); impl 2 / 3:
- * the tcgen05 kernel never / always splitting keys.  Tiles from laya_attention_tiles with the
- * matching tile size; err: device error word (impl 1-3). */
+/* Packed attention (kernels.cu:90-154) on the tcgen05/TMEM kernel the forward pass uses.
+ * qkv: q, k [heads][M][64] each, then v transposed [heads][64][M] (the layout the QKV GEMM
+ * epilogue writes); out [M][heads*64].  Tiles of 128 queries from laya_attention_tiles.
+ * impl 1: each tile's keys split over a CTA pair for global attention (window < 0) when
+ * heads * n_tiles <= the SM count and M >= 384 (the forward pass's rule, with M for the row
+ * length); impl 2 / 3: never / always split.  err: device error word. */
 int laya_op_attention(int precision, int impl, const void* qkv, void* out, const int32_t* tiles, int n_tiles,
-                      const int32_t* starts, const int32_t* lengths, int M, int heads, int window, int split_p,
-                      int* err, void* stream);
+                      const int32_t* starts, const int32_t* lengths, int M, int heads, int window, int* err,
+                      void* stream);
 
 /* Global attention for gathered queries only (the decision head's last layer,
  * laya.py:214-245 followed by the gather of kernels.cu:159-166): row r attends from the tokens
@@ -207,7 +214,7 @@ int laya_op_attention_gathered(int precision, const void* qkv, void* out, const 
                                const int32_t* starts, const int32_t* lengths, int n_rows, int M, int heads, int* err,
                                void* stream);
 
-/* Builds the attention tile table (tile_q = 64 or 128) for rows packed at `starts` with
+/* Builds the attention tile table (tile_q = 128) for rows packed at `starts` with
  * `lengths` into M tokens, rows longest first, then zero-fill tiles for tokens past the last
  * row, then unused slots.  Returns the number of tiles written (<= capacity) or -1. */
 int laya_attention_tiles(const int32_t* starts, const int32_t* lengths, int n_rows, int M, int tile_q,
@@ -216,6 +223,18 @@ int laya_attention_tiles(const int32_t* starts, const int32_t* lengths, int n_ro
 /* residual = LN(E[ids]); x = residual (16-bit).  (kernels.cu:16-19 + runtime.py:93-95) */
 int laya_op_embed_norm(int precision, const int32_t* ids, const float* table, const float* gamma, float eps, int rows,
                        int width, int vocab, float* residual, void* x, int* err, void* stream);
+
+/* Decision-head tail (laya.py:241-245 with the features of kernels.cu:167-183), one question per
+ * row of `batch`: logits[q][j] = scored[q][j] . w3 + b3 for the CLS slot and `options` option
+ * slots (scored: 16-bit [batch][options+1][width]); features over the first counts[q] option
+ * logits (p1, p1 - p2, entropy / log(max(c,2)), max(c,2)/255), written to features[q][4] when it
+ * is not NULL; acts[q] = act_head.2(gelu(act_head.0([selected[q][0], features]))) with selected
+ * fp32 [batch][options+1][width].  hidden: fp32 [batch][256] scratch; arrivals: int32 [batch],
+ * zero on entry (left zero).  width a multiple of 8. */
+int laya_op_head_tail(int precision, const float* selected, const void* scored, const int32_t* counts, int batch,
+                      int options, int width, const float* w3, const float* b3, const float* wa0, const float* ba0,
+                      const float* wa2, const float* ba2, int n_act, float* logits, float* acts, float* features,
+                      float* hidden, int32_t* arrivals, void* stream);
 
 /* residual += sum(partials[0..splits)); x = LN(residual; gamma, beta).  (kernels.cu:20-49) */
 int laya_op_norm(int precision, float* residual, const float* partials, int splits, const float* gamma,
@@ -237,7 +256,10 @@ int laya_op_norm(int precision, float* residual, const float* partials, int spli
  * overlap on the GPU (different streams, or different host threads on one device) race.  The
  * array keeps the last call's contents; every partial a call reads is written by the same call
  * first, so nothing needs clearing.  No cudaMalloc, cudaFree or allocating library routine is
- * called.  Enqueued on `stream` like the other kernel-level entry points. */
+ * called.  Enqueued on `stream` like the other kernel-level entry points; `stream` must belong
+ * to the current device (LAYA_ERR_INVALID otherwise), whose array the call uses.  `residual` and
+ * `bias` must be 16-byte aligned.  `err` (zero on entry, or NULL) receives a device error; when
+ * it is set, `residual` is left unchanged. */
 #define LAYA_STATIC_SCRATCH_FLOATS (4 * 1024 * 1024)
 int laya_op_gemm_residual_static(int precision, const void* x, const void* w, int M, int N, int K, int splits,
                                  float* residual, const float* bias, int* err, void* stream);

@@ -15,6 +15,12 @@ namespace laya {
 
 constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s: forward passes take ms
 
+// The wait limit a launch uses: its argument, or kWaitTimeoutNs when the argument is 0.  Drains
+// of work already issued (mbar_drain) always use kWaitTimeoutNs.
+__device__ __forceinline__ unsigned long long wait_limit(unsigned long long arg) {
+  return arg ? arg : kWaitTimeoutNs;
+}
+
 enum DeviceError : int {
   kErrNone = 0,
   kErrGemmProducerWait = 1,
@@ -72,17 +78,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete.  Returns false (and records `code`
-// in *err) when the wait runs past kWaitTimeoutNs or another role of the CTA already gave up
-// (*abort set), so that every role unwinds instead of spinning forever.
+// in *err) when the wait runs past `limit_ns` (the launch's wait limit, kWaitTimeoutNs unless a
+// caller asked for another) or another role of the CTA already gave up (*abort set), so that
+// every role unwinds instead of spinning forever.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
-                                          volatile int* abort) {
+                                          volatile int* abort, unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long start = global_ns();
   for (uint32_t spin = 1;; ++spin) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((spin & 63) == 0) {
       if (*abort) return false;
-      if (global_ns() - start > kWaitTimeoutNs) {
+      if (global_ns() - start > limit_ns) {
         *abort = 1;
         if (err) atomicCAS(err, 0, code);
         return false;

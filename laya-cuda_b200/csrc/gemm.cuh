@@ -52,6 +52,7 @@ struct GemmArgs {
   int rope_rows;
   const int* positions;   // [M]
   int* err;               // device error word
+  unsigned long long wait_ns;  // wait limit of this launch (0: kWaitTimeoutNs)
 };
 
 constexpr int kBM = 128;
@@ -359,6 +360,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* drain = bars + 2 * S + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const unsigned long long wait_ns = wait_limit(args.wait_ns);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -423,7 +425,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             // Stage `kb` already expects this k-block's bytes and holds its weights.
             tma_load_2d(sA + stage * Cfg::kStageA, &tmA, &full[stage], kx, mb * kBM);
           } else {
-            if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrGemmProducerWait, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrGemmProducerWait, abort_flag, wait_ns)) { ok = false; break; }
             mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
             tma_load_2d(sA + stage * Cfg::kStageA, &tmA, &full[stage], kx, mb * kBM);
             tma_load_2d(sB + stage * Cfg::kStageB, &tmB, &full[stage], kx, nb * BN);
@@ -433,11 +435,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
       }
-      if (!ok) {
-        // Let copies already in flight land before the CTA exits.
-        for (int s = 0; s < S; ++s)
-          if (issued & (1u << s)) mbar_wait(&full[s], (last_par >> s) & 1, nullptr, 0, abort_flag);
-      }
+      // Every copy issued lands before the CTA exits, also when this role finished its loads
+      // but another role gave up and will not consume them.  mbar_drain is bounded by time only:
+      // on an abort an abort-aware wait would return at once and leave TMA writes landing in
+      // shared memory the CTA no longer owns.  On the normal path every stage has completed.
+      (void)ok;
+      for (int s = 0; s < S; ++s)
+        if (issued & (1u << s)) mbar_drain(&full[s], (last_par >> s) & 1);
     } else {
       pdl_wait();
     }
@@ -449,11 +453,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int acc = 0; uint32_t acc_phase = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, args.err, kErrGemmMmaWait, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, args.err, kErrGemmMmaWait, abort_flag, wait_ns)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, args.err, kErrGemmMmaWait, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&full[stage], phase, args.err, kErrGemmMmaWait, abort_flag, wait_ns)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + stage * Cfg::kStageA);
           const uint32_t b0 = smem_u32(sB + stage * Cfg::kStageB);
@@ -469,9 +473,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tc_commit(&tfull[acc]);
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
-      // Drain: make sure no MMA is still writing TMEM when it is released.
+      // Drain: make sure no MMA is still writing TMEM when it is released (bounded by time
+      // only, so it also waits after an abort).
       tc_commit(drain);
-      mbar_wait(drain, 0, nullptr, 0, abort_flag);
+      mbar_drain(drain, 0);
     }
   } else {
     pdl_wait();
@@ -487,7 +492,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       QkvPipe<BN, T> qp;
       if (EPI == EPI_RESIDUAL) rp.start(args, row0, nb * BN, half, lane);
       if (EPI == EPI_QKV) qp.start(args, row0 + lane, nb * BN, half);
-      if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag)) break;
+      if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag, wait_ns)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       if (EPI == EPI_RESIDUAL) rp.finish(args, tbase, row0, nb * BN, half, lane, stage);
@@ -549,6 +554,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* drain = bars + 2 * S + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const unsigned long long wait_ns = wait_limit(args.wait_ns);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -586,7 +592,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int arow = mb * 2 * kBM + (int)rank * kBM;
         const int brow = nb * BN + (int)rank * (BN / 2);
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrGemmProducerWait, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrGemmProducerWait, abort_flag, wait_ns)) { ok = false; break; }
           const uint32_t leader_full = cluster_addr(smem_u32(&full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
           tma_load_2d_pair(sA + stage * Cfg::kStageA, &tmA, leader_full, kb * kBK, arow);
@@ -596,9 +602,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
       }
-      if (!ok && leader) {
+      if (leader) {
+        // Both CTAs' copies complete on the leader's full barriers: wait for them by time only,
+        // on every path (see gemm_kernel).
+        (void)ok;
         for (int s = 0; s < S; ++s)
-          if (issued & (1u << s)) mbar_wait(&full[s], (last_par >> s) & 1, nullptr, 0, abort_flag);
+          if (issued & (1u << s)) mbar_drain(&full[s], (last_par >> s) & 1);
       }
     }
   } else if (warp == 1) {
@@ -608,11 +617,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int acc = 0; uint32_t acc_phase = 0;
       bool ok = true;
       for (int t = pair; t < tiles && ok; t += pairs) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, args.err, kErrGemmMmaWait, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, args.err, kErrGemmMmaWait, abort_flag, wait_ns)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, args.err, kErrGemmMmaWait, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&full[stage], phase, args.err, kErrGemmMmaWait, abort_flag, wait_ns)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + stage * Cfg::kStageA);
           const uint32_t b0 = smem_u32(sB + stage * Cfg::kStageB);
@@ -633,7 +642,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
       tc_commit_pair(cluster_addr(smem_u32(drain), 0));
-      mbar_wait(drain, 0, nullptr, 0, abort_flag);
+      mbar_drain(drain, 0);
     }
   } else {
     const int quarter = warp & 3;
@@ -649,7 +658,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       QkvPipe<BN, T> qp;
       if (EPI == EPI_RESIDUAL) rp.start(args, row0, nb * BN, half, lane);
       if (EPI == EPI_QKV) qp.start(args, row0 + lane, nb * BN, half);
-      if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag)) break;
+      if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag, wait_ns)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       if (EPI == EPI_RESIDUAL) rp.finish(args, tbase, row0, nb * BN, half, lane, stage);

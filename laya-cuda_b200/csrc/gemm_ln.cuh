@@ -44,6 +44,7 @@ struct GemmLnArgs {
   void* x;                  // [M][ldx] T: the normalised rows
   int ldx;
   int* err;
+  unsigned long long wait_ns;  // wait limit of this launch (0: kWaitTimeoutNs)
 };
 
 template <int C, int BN>
@@ -100,6 +101,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* drain = bars + 2 * S + 6;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 7);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const unsigned long long wait_ns = wait_limit(args.wait_ns);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -145,7 +147,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (mb == cid && kb < pre) {
             tma_load_2d(sA + stage * Cfg::kStageA, &tmA, &full[stage], kb * kBK, mb * kBM);
           } else {
-            if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrGemmProducerWait, abort_flag)) { ok = false; break; }
+            if (!mbar_wait(&empty[stage], phase ^ 1, args.err, kErrGemmProducerWait, abort_flag, wait_ns)) { ok = false; break; }
             mbar_arrive_expect_tx(&full[stage], Cfg::kStageBytes);
             tma_load_2d(sA + stage * Cfg::kStageA, &tmA, &full[stage], kb * kBK, mb * kBM);
             tma_load_2d(sB + stage * Cfg::kStageB, &tmB, &full[stage], kb * kBK, nb * BN);
@@ -155,10 +157,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
       }
-      if (!ok) {
-        for (int s = 0; s < S; ++s)
-          if (issued & (1u << s)) mbar_drain(&full[s], (last_par >> s) & 1);
-      }
+      // Every copy issued lands before the CTA exits (bounded by time, on every path: another
+      // role may have given up without consuming them).
+      (void)ok;
+      for (int s = 0; s < S; ++s)
+        if (issued & (1u << s)) mbar_drain(&full[s], (last_par >> s) & 1);
     } else {
       pdl_wait();
     }
@@ -170,11 +173,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int acc = 0; uint32_t acc_phase = 0;
       bool ok = true;
       for (int mb = cid; mb < m_blocks && ok; mb += n_clusters) {
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, args.err, kErrGemmMmaWait, abort_flag)) { ok = false; break; }
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, args.err, kErrGemmMmaWait, abort_flag, wait_ns)) { ok = false; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, args.err, kErrGemmMmaWait, abort_flag)) { ok = false; break; }
+          if (!mbar_wait(&full[stage], phase, args.err, kErrGemmMmaWait, abort_flag, wait_ns)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + stage * Cfg::kStageA);
           const uint32_t b0 = smem_u32(sB + stage * Cfg::kStageB);
@@ -212,7 +215,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t bar_local = smem_u32(&xbar[par]);
 #pragma unroll
       for (int c = 0; c < C; ++c) st_async_f32x2(cluster_addr(local, c), sum, m2, cluster_addr(bar_local, c));
-      fine = mbar_wait(&xbar[par], (lt >> 1) & 1, args.err, kErrGemmEpilogueWait, abort_flag);
+      fine = mbar_wait(&xbar[par], (lt >> 1) & 1, args.err, kErrGemmEpilogueWait, abort_flag, wait_ns);
       const float2* part = reinterpret_cast<const float2*>(xbuf) + (par * 2 * C) * kBM + quarter * 32 + lane;
       float total = 0.f;
 #pragma unroll
@@ -255,7 +258,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // Arm this tile's exchange barrier with the bytes every CTA of the cluster will send here.
       // (The previous use of this parity completed: this warp waited for it.)
       if (warp == 2 && lane == 0) mbar_arrive_expect_tx(&xbar[par], Cfg::kXTxBytes);
-      if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag)) break;
+      if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag, wait_ns)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + half * (BN / 2);
       // Pass A: v = acc + bias + residual -> HBM (residual) and TMEM (in place).  Each chunk's

@@ -12,6 +12,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -27,7 +28,6 @@
 #include <vector>
 
 #include "../../include/laya_b200.h"
-#include "attention.cuh"
 #include "gemm.cuh"
 #include "rowops.cuh"
 #include "tc_attention.cuh"
@@ -113,14 +113,14 @@ int sm_count(int device) {
   return n;
 }
 
-// Programmatic dependent launch on every kernel (LAYA_PDL=0 in the environment turns it off).
-bool pdl_enabled() {
-  static const bool on = [] {
-    const char* v = getenv("LAYA_PDL");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
+// Process-wide launch options (laya_set_launch_options): programmatic dependent launch on every
+// kernel (on by default), and the wait limit every pipelined kernel's bounded waits use
+// (0: the kernels' default of 2 s).  Passes captured into CUDA graphs keep the options in effect
+// at capture.
+std::atomic<bool> g_pdl{true};
+std::atomic<unsigned long long> g_wait_ns{0};
+bool pdl_enabled() { return g_pdl.load(std::memory_order_relaxed); }
+unsigned long long wait_ns() { return g_wait_ns.load(std::memory_order_relaxed); }
 
 // Warps (= rows) per block of the row kernels: 8, or fewer when that leaves SMs idle, so that a
 // small class's rows spread over the whole GPU (one row per warp either way).
@@ -255,7 +255,9 @@ int ln_block_n(int N, int K) {
 }
 
 template <typename T>
-void launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tb, const GemmLnArgs& a, int bn, cudaStream_t st) {
+void launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tb, const GemmLnArgs& args, int bn, cudaStream_t st) {
+  GemmLnArgs a = args;
+  a.wait_ns = wait_ns();
   const int c = a.N / bn;
   if (bn == 256 && c == 1) launch_gemm_ln_inst<1, 256, T>(ta, tb, a, st);
   else if (bn == 256 && c == 2) launch_gemm_ln_inst<2, 256, T>(ta, tb, a, st);
@@ -268,30 +270,16 @@ void launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tb, const GemmLnAr
   else fail(LAYA_ERR_INVALID, "fused residual + LayerNorm: N=%d is not 1-4 blocks of 192 or 256 columns", a.N);
 }
 
-// The fused residual + LayerNorm GEMM (gemm_ln.cuh) serves classes that do not split K.
-// Which residual GEMMs carry the LayerNorm in their epilogue: 0 none, 1 all, 2 (default) those
-// with K <= 1024 (the attention output projection).  For the FFN-down GEMM (K = 3072) the
-// residual GEMM followed by the row LayerNorm measured about 3% faster than the fused kernel
-// on the throughput workload; for the attention output the fused kernel is about 4% faster.
-// LAYA_GEMM_LN overrides.
-int gemm_ln_mode() {
-  static const int mode = [] {
-    const char* v = getenv("LAYA_GEMM_LN");
-    return v && (v[0] == '0' || v[0] == '1') ? v[0] - '0' : 2;
-  }();
-  return mode;
-}
+// The fused residual + LayerNorm GEMM (gemm_ln.cuh) serves classes that do not split K, for the
+// residual GEMMs with K <= kLnMaxK (the attention output projection).  For the FFN-down GEMM
+// (K = 3072) the residual GEMM followed by the row LayerNorm measured about 3% faster than the
+// fused kernel on the throughput workload; for the attention output the fused kernel is about
+// 4% faster.
+constexpr int kLnMaxK = 1024;
 
 // Rows from which GEMMs always run as CTA pairs with 256 x 256 tiles; below, plan_small picks the
-// tile (1-CTA or pair) and split-K.  LAYA_GEMM_PAIR=0 in the environment turns pairs off.
+// tile (1-CTA or pair) and split-K.
 constexpr int kPairMinRows = 2048;
-bool pair_enabled() {
-  static const bool on = [] {
-    const char* v = getenv("LAYA_GEMM_PAIR");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
 
 template <typename T, int BN>
 void launch_gemm_bn(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t st) {
@@ -312,8 +300,10 @@ void launch_gemm_bn(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const
 
 // tb: W tensor map with BN-row boxes (1-CTA kernel) or BN/2-row boxes (pair kernel).
 template <typename T>
-void launch_gemm(int epi, int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int sms,
+void launch_gemm(int epi, int bn, const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int sms,
                  cudaStream_t st, bool pair = false) {
+  GemmArgs a = args;
+  a.wait_ns = wait_ns();
   if (a.K % kBK != 0 || a.N % bn != 0 || a.M <= 0) fail(LAYA_ERR_INVALID, "GEMM shape %dx%dx%d not tileable", a.M, a.N, a.K);
   if ((a.K / kBK) % a.splits != 0) fail(LAYA_ERR_INVALID, "split-K %d does not divide %d k-blocks", a.splits, a.K / kBK);
   if (pair) {
@@ -413,7 +403,9 @@ AttnMaps attn_maps(const void* qkv, int M, int heads, bool bf) {
 }
 
 template <typename T>
-void launch_tc_attention(const AttnMaps& maps, const TcAttnArgs& a, int n_tiles, cudaStream_t st) {
+void launch_tc_attention(const AttnMaps& maps, const TcAttnArgs& args, int n_tiles, cudaStream_t st) {
+  TcAttnArgs a = args;
+  a.wait_ns = wait_ns();
   static uint64_t configured = 0;  // one bit per device
   int dev = 0;
   CK(cudaGetDevice(&dev));
@@ -451,14 +443,6 @@ void launch_tc_attention(const AttnMaps& maps, const TcAttnArgs& a, int n_tiles,
 // 1 us slower, the merge costing more than the block it saves.
 int attention_splits(int heads, int n_tiles, int sms, int window, int row_keys) {
   return window < 0 && row_keys >= 3 * kTcKB && heads * n_tiles <= sms ? 2 : 1;
-}
-
-template <typename T>
-void launch_attention(const AttnArgs& a, int n_tiles, bool split_p, cudaStream_t st) {
-  if (n_tiles > 65535) fail(LAYA_ERR_INVALID, "%d attention tiles exceed the grid limit", n_tiles);
-  dim3 grid(a.heads, n_tiles);
-  if (split_p) launch_k(attention_kernel<T, true>, grid, dim3(kAttnThreads), 0, st, a);
-  else launch_k(attention_kernel<T, false>, grid, dim3(kAttnThreads), 0, st, a);
 }
 
 // Row kernels are instantiated per width (d = 32 * NPL, d a multiple of 64 up to 1024).
@@ -527,7 +511,7 @@ void shape_class(const int32_t* lengths, const int32_t* marker_counts, int n, in
 int tiles_capacity(int rows, int batch, int tile_q) { return (rows + (tile_q - 16) * batch + tile_q - 1) / tile_q + 1; }
 
 struct PackLayout {
-  int64_t ids, positions, rows_, kinds, starts, lengths, counts, indices, tiles64, tiles128, total;
+  int64_t ids, positions, rows_, kinds, starts, lengths, counts, indices, tiles128, total;
 };
 PackLayout pack_layout(int m, int b, int k) {
   PackLayout p;
@@ -541,7 +525,6 @@ PackLayout pack_layout(int m, int b, int k) {
   p.counts = o; o += b;
   p.indices = o; o += (int64_t)b * (k + 1);
   o = (o + 3) / 4 * 4;  // int4 alignment of the tile tables
-  p.tiles64 = o; o += 4LL * tiles_capacity(m, b, kAttnQ);    // mma.sync attention
   p.tiles128 = o; o += 4LL * tiles_capacity(m, b, kTcQ);     // tcgen05 attention
   p.total = o;
   return p;
@@ -611,8 +594,7 @@ void pack(const int32_t* tokens, const int32_t* lengths, const int32_t* markers,
     mk += cnt;
     offset = end;
   }
-  if (build_tiles(out + L.starts, out + L.lengths, n, m, kAttnQ, out + L.tiles64, tiles_capacity(m, b, kAttnQ)) < 0 ||
-      build_tiles(out + L.starts, out + L.lengths, n, m, kTcQ, out + L.tiles128, tiles_capacity(m, b, kTcQ)) < 0)
+  if (build_tiles(out + L.starts, out + L.lengths, n, m, kTcQ, out + L.tiles128, tiles_capacity(m, b, kTcQ)) < 0)
     fail(LAYA_ERR_INVALID, "attention tile table overflow");
 }
 
@@ -627,7 +609,7 @@ struct Tensor {
 };
 
 struct ClassLayout {
-  int m = 0, b = 0, k = 0, count = 0, tiles64 = 0, tiles128 = 0;
+  int m = 0, b = 0, k = 0, count = 0, tiles128 = 0;
   PackLayout pack{};
   size_t packed, residual, x, qkv, attn, ff, sel, selx, scored, ffsel, partials, hidden, out, total;
   bool has_partials = false;
@@ -699,9 +681,6 @@ struct Engine {
   std::map<std::tuple<const void*, int>, CUtensorMap> wmaps;
   std::string error;
   bool profiling = false;
-  // Attention kernel of the forward pass: the tcgen05/TMEM kernel (default) or the mma.sync
-  // kernel (LAYA_ATTENTION=mma_sync in the environment at engine creation).
-  bool tc_attention = true;
   std::vector<ProfEvent> prof_pending;
   std::vector<cudaEvent_t> prof_pool;
   double prof_ms[kFamilies] = {};
@@ -846,7 +825,6 @@ ClassLayout make_layout(const Engine& e, int m, int b, int k) {
   ClassLayout L;
   L.m = m; L.b = b; L.k = k;
   L.count = b * (k + 1);
-  L.tiles64 = tiles_capacity(m, b, kAttnQ);
   L.tiles128 = tiles_capacity(m, b, kTcQ);
   L.pack = pack_layout(m, b, k);
   const size_t d = e.d(), es = 2, A = 256;
@@ -998,7 +976,7 @@ void gemm(Engine& e, bool prof, int family, int epi, const CUtensorMap& ta, cons
   const int N = (int)w.shape[0], K = (int)w.shape[1];
   // The CTA pair wins for the 16-bit output epilogues; the fp32 residual read-modify-write is as
   // fast or faster on the 1-CTA kernel (measured at 41k rows).
-  const bool pair_ok = pair_enabled() && epi != EPI_RESIDUAL;
+  const bool pair_ok = epi != EPI_RESIDUAL;
   int bn;
   bool pair;
   if (M < kPairMinRows) {
@@ -1048,7 +1026,6 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
   const int* lengths = in + L.pack.lengths;
   const int* counts = in + L.pack.counts;
   const int* indices = in + L.pack.indices;
-  const int4* tiles64 = reinterpret_cast<const int4*>(in + L.pack.tiles64);
   const int4* tiles128 = reinterpret_cast<const int4*>(in + L.pack.tiles128);
   float* residual = reinterpret_cast<float*>(ws + L.residual);
   T* x = reinterpret_cast<T*>(ws + L.x);
@@ -1067,33 +1044,24 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
 
   int* arrivals = err + 1;
   CK(cudaMemsetAsync(err, 0, sizeof(int) * (1 + (size_t)L.b), e.stream));
-  const double rowbytes = (double)m * d;
   launch(e, prof, FAM_ROWS, 0, [&] {
     launch_embed<T>(ids, Wf(e, "encoder.embeddings.tok_embeddings.weight"), Wf(e, "encoder.embeddings.norm.weight"),
                     c.eps, m, d, c.vocab, residual, x, err, e.stream);
   });
-  (void)rowbytes;
 
   // gathered: only the rows gather_rows_kernel reads (each question's CLS and marker tokens)
   // attend; the other rows of `attn` are left as they are (global attention only).
   auto attention = [&](int window, bool gathered) {
-    if (e.tc_attention) {
-      TcAttnArgs a{};
-      a.qk = qkv; a.out = attn; a.tiles = tiles128; a.starts = starts; a.lengths = lengths;
-      a.M = m; a.heads = c.heads; a.window = window; a.err = err;
-      int n_tiles = L.tiles128;
-      if (gathered) {
-        a.q_index = indices; a.q_per_row = L.k + 1; a.q_tiles = (L.k + 1 + kTcQ - 1) / kTcQ;
-        n_tiles = L.b * a.q_tiles;
-      }
-      a.splits = attention_splits(c.heads, n_tiles, e.sms, window, m / L.b);
-      launch(e, prof, FAM_ATTENTION, 0, [&] { launch_tc_attention<T>(s.attn_maps, a, n_tiles, e.stream); });
-    } else {
-      AttnArgs a{};
-      a.qkv = qkv; a.out = attn; a.tiles = tiles64; a.starts = starts; a.lengths = lengths;
-      a.M = m; a.heads = c.heads; a.window = window;
-      launch(e, prof, FAM_ATTENTION, 0, [&] { launch_attention<T>(a, L.tiles64, false, e.stream); });
+    TcAttnArgs a{};
+    a.qk = qkv; a.out = attn; a.tiles = tiles128; a.starts = starts; a.lengths = lengths;
+    a.M = m; a.heads = c.heads; a.window = window; a.err = err;
+    int n_tiles = L.tiles128;
+    if (gathered) {
+      a.q_index = indices; a.q_per_row = L.k + 1; a.q_tiles = (L.k + 1 + kTcQ - 1) / kTcQ;
+      n_tiles = L.b * a.q_tiles;
     }
+    a.splits = attention_splits(c.heads, n_tiles, e.sms, window, m / L.b);
+    launch(e, prof, FAM_ATTENTION, 0, [&] { launch_tc_attention<T>(s.attn_maps, a, n_tiles, e.stream); });
   };
   // A residual GEMM whose sum the next norm must still add: split count and the GEMM bias.
   struct Pending { int splits = 0; const float* bias = nullptr; };
@@ -1124,12 +1092,11 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
 
   // residual += A W^T + bias, then x = LN(residual): one fused kernel when the class does not
   // split K, else the residual GEMM (or its split-K partials) followed by the norm kernel.
-  const int ln_mode = m > kSplitRowsMax ? gemm_ln_mode() : 0;
   auto residual_ln = [&](int family, const CUtensorMap& ta, const std::string& wname, const float* bias,
                          const float* gamma, const float* beta, float eps) {
     const Tensor& w = W(e, wname);
     const int bn = ln_block_n((int)w.shape[0], (int)w.shape[1]);
-    if (!bn || !(ln_mode == 1 || (ln_mode == 2 && w.shape[1] <= 1024))) {
+    if (!bn || m <= kSplitRowsMax || w.shape[1] > kLnMaxK) {
       const Pending pend = residual_gemm(family, ta, wname, m, residual, bias);
       norm(residual, m, gamma, beta, eps, x, pend);
       return;
@@ -1335,10 +1302,6 @@ int laya_create(const laya_config* cfg, int device, int max_cached_shapes, laya_
   e.device = device;
   e.limit = max_cached_shapes;
   e.sms = sm_count(device);
-  {
-    const char* v = getenv("LAYA_ATTENTION");
-    e.tc_attention = !(v && std::string(v) == "mma_sync");
-  }
   build_expected(e);
   CK(cudaStreamCreateWithFlags(&e.stream, cudaStreamNonBlocking));
 
@@ -1695,6 +1658,13 @@ int laya_destroy(laya_engine* h) {
 
 const char* laya_last_error(laya_engine* h) { return h ? h->impl.error.c_str() : g_create_error.c_str(); }
 
+int laya_set_launch_options(int programmatic_launch, uint64_t wait_limit_ns) {
+  if (programmatic_launch != 0 && programmatic_launch != 1) return LAYA_ERR_INVALID;
+  g_pdl.store(programmatic_launch != 0);
+  g_wait_ns.store(wait_limit_ns);
+  return LAYA_OK;
+}
+
 // ---------------------------------------------------------------------------------------------
 // Kernel-level entry points
 // ---------------------------------------------------------------------------------------------
@@ -1757,34 +1727,26 @@ int laya_interleave_geglu(const uint16_t* src, uint16_t* dst, int F, int K) {
 
 int laya_attention_tiles(const int32_t* starts, const int32_t* lengths, int n_rows, int M, int tile_q, int32_t* tiles,
                          int capacity) {
-  if (tile_q != kAttnQ && tile_q != kTcQ) return -1;
+  if (tile_q != kTcQ) return -1;
   return build_tiles(starts, lengths, n_rows, M, tile_q, tiles, capacity);
 }
 
 int laya_op_attention(int precision, int impl, const void* qkv, void* out, const int32_t* tiles, int n_tiles,
-                      const int32_t* starts, const int32_t* lengths, int M, int heads, int window, int split_p, int* err,
+                      const int32_t* starts, const int32_t* lengths, int M, int heads, int window, int* err,
                       void* stream) {
   API_BEGIN
-  if (impl >= 1 && impl <= 3) {
-    const bool bf = precision == LAYA_PRECISION_BF16;
-    const AttnMaps maps = attn_maps(qkv, M, heads, bf);
-    TcAttnArgs t{};
-    t.qk = qkv; t.out = out; t.tiles = reinterpret_cast<const int4*>(tiles); t.starts = starts; t.lengths = lengths;
-    t.M = M; t.heads = heads; t.window = window; t.err = err;
-    int dev = 0;
-    CK(cudaGetDevice(&dev));
-    t.splits = impl == 2 ? 1 : impl == 3 ? 2 : attention_splits(heads, n_tiles, sm_count(dev), window, M);
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (bf) launch_tc_attention<__nv_bfloat16>(maps, t, n_tiles, st);
-    else launch_tc_attention<__half>(maps, t, n_tiles, st);
-    return LAYA_OK;
-  }
-  AttnArgs a{};
-  a.qkv = qkv; a.out = out; a.tiles = reinterpret_cast<const int4*>(tiles); a.starts = starts; a.lengths = lengths;
-  a.M = M; a.heads = heads; a.window = window;
+  if (impl < 1 || impl > 3) fail(LAYA_ERR_INVALID, "attention impl %d (1: forward-pass rule, 2: no key split, 3: key split)", impl);
+  const bool bf = precision == LAYA_PRECISION_BF16;
+  const AttnMaps maps = attn_maps(qkv, M, heads, bf);
+  TcAttnArgs t{};
+  t.qk = qkv; t.out = out; t.tiles = reinterpret_cast<const int4*>(tiles); t.starts = starts; t.lengths = lengths;
+  t.M = M; t.heads = heads; t.window = window; t.err = err;
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  t.splits = impl == 2 ? 1 : impl == 3 ? 2 : attention_splits(heads, n_tiles, sm_count(dev), window, M);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (precision == LAYA_PRECISION_BF16) launch_attention<__nv_bfloat16>(a, n_tiles, split_p != 0, st);
-  else launch_attention<__half>(a, n_tiles, split_p != 0, st);
+  if (bf) launch_tc_attention<__nv_bfloat16>(maps, t, n_tiles, st);
+  else launch_tc_attention<__half>(maps, t, n_tiles, st);
   API_END(nullptr)
 }
 
@@ -1815,6 +1777,31 @@ int laya_op_embed_norm(int precision, const int32_t* ids, const float* table, co
   if (precision == LAYA_PRECISION_BF16)
     launch_embed<__nv_bfloat16>(ids, table, gamma, eps, rows, width, vocab, residual, static_cast<__nv_bfloat16*>(x), err, st);
   else launch_embed<__half>(ids, table, gamma, eps, rows, width, vocab, residual, static_cast<__half*>(x), err, st);
+  API_END(nullptr)
+}
+
+int laya_op_head_tail(int precision, const float* selected, const void* scored, const int32_t* counts, int batch,
+                      int options, int width, const float* w3, const float* b3, const float* wa0, const float* ba0,
+                      const float* wa2, const float* ba2, int n_act, float* logits, float* acts, float* features,
+                      float* hidden, int32_t* arrivals, void* stream) {
+  API_BEGIN
+  if (!selected || !scored || !counts || !w3 || !b3 || !wa0 || !ba0 || !wa2 || !ba2 || !logits || !acts || !hidden ||
+      !arrivals)
+    fail(LAYA_ERR_INVALID, "null argument");
+  if (batch <= 0 || options <= 0 || width <= 0 || width % 8 || n_act < 1) fail(LAYA_ERR_INVALID, "bad head shape");
+  TailArgs t{};
+  t.selected = selected; t.scored = scored; t.counts = counts;
+  t.w3 = w3; t.b3 = b3; t.wa0 = wa0; t.ba0 = ba0; t.wa2 = wa2; t.ba2 = ba2;
+  t.logits = logits; t.acts = acts; t.features = features; t.hidden = hidden; t.arrivals = arrivals;
+  t.k = options; t.d = width; t.n_act = n_act;
+  const size_t smem = ((size_t)(options + 1) + width + 4 + kActHidden) * sizeof(float);
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  const int parts = batch * kTailPartsSmall <= 4 * sm_count(dev) ? kTailPartsSmall : kTailPartsLarge;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (precision == LAYA_PRECISION_BF16)
+    launch_k(head_tail_kernel<__nv_bfloat16>, dim3(batch, parts), dim3(kTailThreads), smem, st, t);
+  else launch_k(head_tail_kernel<__half>, dim3(batch, parts), dim3(kTailThreads), smem, st, t);
   API_END(nullptr)
 }
 
@@ -1863,11 +1850,13 @@ float* static_partials_address() {
   return g_static_ptr[dev];
 }
 
-// residual[r][c] += bias[c] + sum_s partials[s][r][c], summed in split order.
+// residual[r][c] += bias[c] + sum_s partials[s][r][c], summed in split order.  Does nothing when
+// the split-K GEMM reported an error: its partials may then be only partly written.
 __global__ void __launch_bounds__(256) add_partials_kernel(float* residual, const float* partials, int splits,
-                                                           int rows, int cols, const float* bias) {
+                                                           int rows, int cols, const float* bias, const int* err) {
   // Launched with programmatic serialisation like every kernel here: wait for the split-K GEMM.
   pdl_wait();
+  if (err && *reinterpret_cast<const volatile int*>(err) != 0) return;
   const int64_t n4 = (int64_t)rows * cols / 4;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1892,15 +1881,26 @@ extern "C" int laya_op_gemm_residual_static(int precision, const void* x, const 
   API_BEGIN
   if (!x || !w || !residual) fail(LAYA_ERR_INVALID, "null argument");
   if (M <= 0 || N <= 0 || K <= 0 || splits < 1) fail(LAYA_ERR_INVALID, "bad GEMM shape %dx%dx%d split %d", M, N, K, splits);
+  // The partials are added to `residual` as float4, and to `bias` four columns at a time.
+  if (reinterpret_cast<uintptr_t>(residual) & 15) fail(LAYA_ERR_INVALID, "residual must be 16-byte aligned");
+  if (bias && (reinterpret_cast<uintptr_t>(bias) & 15)) fail(LAYA_ERR_INVALID, "bias must be 16-byte aligned");
   if (N % 64 || K % kBK) fail(LAYA_ERR_INVALID, "N must be a multiple of 64 and K of %d", kBK);
   if ((K / kBK) % splits) fail(LAYA_ERR_INVALID, "split-K %d does not divide %d k-blocks", splits, K / kBK);
   const int64_t need = (int64_t)M * N * splits;
   if (need > LAYA_STATIC_SCRATCH_FLOATS)
     fail(LAYA_ERR_INVALID, "M*N*splits = %lld partial sums exceed the static scratch of %d floats", (long long)need,
          LAYA_STATIC_SCRATCH_FLOATS);
-  float* partials = static_partials_address();
   int dev = 0;
   CK(cudaGetDevice(&dev));
+  // The scratch address is the current device's: a stream of another device would run the
+  // kernels there against this device's array.
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (st) {
+    int stream_dev = -1;
+    CK(cudaStreamGetDevice(st, &stream_dev));
+    if (stream_dev != dev) fail(LAYA_ERR_INVALID, "stream belongs to device %d, the current device is %d", stream_dev, dev);
+  }
+  float* partials = static_partials_address();
   const int sms = sm_count(dev);
   const bool bf = precision == LAYA_PRECISION_BF16;
   const int bn = pick_bn(M, N, EPI_PARTIAL, sms);
@@ -1909,13 +1909,13 @@ extern "C" int laya_op_gemm_residual_static(int precision, const void* x, const 
   a.residual = partials; a.ldr = N; a.err = err;
   const CUtensorMap ta = make_map(x, M, K, kBM, bf);
   const CUtensorMap tb = make_map(w, N, K, bn, bf);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   // Every partial element read below is written by this GEMM first, so the array needs no
   // clearing between calls.
   if (bf) launch_gemm<__nv_bfloat16>(EPI_PARTIAL, bn, ta, tb, a, sms, st);
   else launch_gemm<__half>(EPI_PARTIAL, bn, ta, tb, a, sms, st);
   const int64_t n4 = (int64_t)M * N / 4;
   const int grid = (int)std::min<int64_t>((n4 + 255) / 256, 4LL * sms);
-  launch_k(add_partials_kernel, dim3(grid), dim3(256), 0, st, residual, (const float*)partials, splits, M, N, bias);
+  launch_k(add_partials_kernel, dim3(grid), dim3(256), 0, st, residual, (const float*)partials, splits, M, N, bias,
+           (const int*)err);
   API_END(nullptr)
 }

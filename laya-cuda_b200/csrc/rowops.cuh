@@ -223,6 +223,7 @@ struct TailArgs {
   float* acts;             // [b][n_act]
   float* hidden;           // [b][256] scratch: act_head.0 outputs
   int* arrivals;           // [b] zero at launch: CTAs of the question that finished their part
+  float* features;         // [b][4] (p1, p1 - p2, H / log(max(c,2)), max(c,2)/255) or nullptr
   int k, d, n_act;
 };
 
@@ -288,7 +289,9 @@ __global__ void __launch_bounds__(kTailThreads) head_tail_kernel(const TailArgs 
   __syncthreads();
   if (warp == 0) {
     // Softmax over the question's options, its entropy and top-2 probabilities, warp-parallel.
-    const int count = a.counts[q];
+    // (The count is at most the class's option count; clamped so a bad count cannot read past
+    // the logits staged in shared memory.)
+    const int count = min(max(a.counts[q], 0), a.k);
     float top = -INFINITY;
     for (int j = lane; j < count; j += 32) top = fmaxf(top, logit[j + 1]);
     top = warp_max(top);
@@ -315,6 +318,8 @@ __global__ void __launch_bounds__(kTailThreads) head_tail_kernel(const TailArgs 
       feat[d + 1] = p1 - p2;
       feat[d + 2] = entropy / logf((float)c2);
       feat[d + 3] = (float)c2 / 255.f;
+      if (a.features && part == 0)
+        for (int i = 0; i < 4; ++i) a.features[(size_t)q * 4 + i] = feat[d + i];
     }
   }
   __syncthreads();

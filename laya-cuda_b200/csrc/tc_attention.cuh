@@ -1,8 +1,8 @@
 // Varlen packed attention on the 5th-generation tensor cores (tcgen05 + TMEM + TMA), used by the
-// forward pass.  Same semantics as attention.cuh, which restates the reference kernel
-// laya_cuda/kernels.cu:90-154: rows packed at 16-token alignment, key j visible to query i of
-// the same row iff j < length and (window < 0 or |i - j| <= window), scores scaled by 1/8,
-// fp32 softmax, padding queries and tokens past the last row produce zeros.
+// forward pass.  Same semantics as the reference kernel laya_cuda/kernels.cu:90-154: rows packed
+// at 16-token alignment, key j visible to query i of the same row iff j < length and
+// (window < 0 or |i - j| <= window), scores scaled by 1/8, fp32 softmax, padding queries and
+// tokens past the last row produce zeros.
 //
 // Work unit: one CTA per (128-query tile of one row, head); the host's tile table never lets a
 // tile straddle rows.  Two CTAs share an SM (82 KB shared memory and 256 TMEM columns each).
@@ -61,6 +61,7 @@ struct TcAttnArgs {
   // its unnormalised O row, running maximum and sum to rank 0 through distributed shared memory,
   // and rank 0 merges and stores.  Halves the serial block chain of grids that leave SMs idle.
   int splits;
+  unsigned long long wait_ns;  // wait limit of this launch (0: kWaitTimeoutNs)
 };
 
 struct TcAttnSmem {
@@ -203,6 +204,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
   uint64_t* drain = bar + 9;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 10);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const unsigned long long wait_ns = wait_limit(a.wait_ns);
 
   // Thread <-> query row r = TMEM lane r: warp w owns lanes [32w, 32w + 32).
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -248,7 +250,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
   };
   // S_j = Q K_j^T into TMEM columns [0, 128) once K_j has landed (control warp).
   auto issue_s = [&](int j) -> bool {
-    if (!mbar_wait(k_full + (j & 1), (j >> 1) & 1, a.err, kErrAttnWait, abort_flag)) return false;
+    if (!mbar_wait(k_full + (j & 1), (j >> 1) & 1, a.err, kErrAttnWait, abort_flag, wait_ns)) return false;
     tc_fence_after();
     if (lane == 0) {
       const uint32_t idesc_s = mma_idesc<bf>(kTcQ, kTcKB);
@@ -263,7 +265,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
   };
   // O (+)= P_j V_j, A = P from TMEM columns [128, 192), once V_j has landed (control warp).
   auto issue_pv = [&](int j) -> bool {
-    if (!mbar_wait(v_full + (j & 1), (j >> 1) & 1, a.err, kErrAttnWait, abort_flag)) return false;
+    if (!mbar_wait(v_full + (j & 1), (j >> 1) & 1, a.err, kErrAttnWait, abort_flag, wait_ns)) return false;
     tc_fence_after();
     if (lane == 0) {
       const uint32_t idesc_o = mma_idesc<bf>(kTcQ, 64);
@@ -297,25 +299,35 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
   uint32_t span_keys = (uint32_t)(hi_key - lo_key);
   if (hi_key < lo_key) { lo_key = 1 << 30; span_keys = 0; }
   const bool warp_live = gathered ? warp * 32 < nq : qa < valid;
+  // Gathered queries: this thread's token, or -1 past nq and for an index outside the packed
+  // rows (reported as kErrBadIndex; its Q row is zero and nothing is stored for it).
+  int qtok = -1;
+  if (gathered && r < nq) {
+    qtok = qidx[r];
+    if ((unsigned)qtok >= (unsigned)a.M) {
+      if (a.err) atomicCAS(a.err, 0, kErrBadIndex);
+      qtok = -1;
+    }
+  }
   if (gathered && n_blocks > 0) {
-    // Q row r <- token qidx[r] (zeros past nq), written in the 128-byte swizzled K-major layout
-    // the TMA would produce, then handed to the async proxy.
-    const T* qsrc = reinterpret_cast<const T*>(a.qk) + ((size_t)head * a.M + (r < nq ? qidx[r] : 0)) * 64;
+    // Q row r <- token qtok (zeros for -1), written in the 128-byte swizzled K-major layout the
+    // TMA would produce, then handed to the async proxy.
+    const T* qsrc = reinterpret_cast<const T*>(a.qk) + ((size_t)head * a.M + (qtok >= 0 ? qtok : 0)) * 64;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-      const uint4 v = r < nq ? *reinterpret_cast<const uint4*>(qsrc + c * 8) : make_uint4(0, 0, 0, 0);
+      const uint4 v = qtok >= 0 ? *reinterpret_cast<const uint4*>(qsrc + c * 8) : make_uint4(0, 0, 0, 0);
       *reinterpret_cast<uint4*>(sQ + r * 128 + ((c ^ (r & 7)) << 4)) = v;
     }
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(q_full);
   }
-  if (ctl && n_blocks > 0) ok = mbar_wait(q_full, 0, a.err, kErrAttnWait, abort_flag) && issue_s(0);
+  if (ctl && n_blocks > 0) ok = mbar_wait(q_full, 0, a.err, kErrAttnWait, abort_flag, wait_ns) && issue_s(0);
 
   float m_used = -INFINITY, l = 0.f;
   for (int j = 0; j < n_blocks; ++j) {
     const int kb = k_lo + j * kTcKB;
-    ok = ok && mbar_wait(s_full, j & 1, a.err, kErrAttnWait, abort_flag);
+    ok = ok && mbar_wait(s_full, j & 1, a.err, kErrAttnWait, abort_flag, wait_ns);
     if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
     tc_fence_after();
     // Chunk c holds keys [kb + 32c, kb + 32c + 32).  vis bit c: some query of the warp sees a
@@ -343,7 +355,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
     if (ctl && j + 1 < n_blocks) {
       // Once every warp has read S_j: S_{j+1} into the same columns, and K_{j+2} into the stage
       // S_j has finished reading.
-      ok = mbar_wait(s_free, j & 1, a.err, kErrAttnWait, abort_flag) && issue_s(j + 1);
+      ok = mbar_wait(s_free, j & 1, a.err, kErrAttnWait, abort_flag, wait_ns) && issue_s(j + 1);
       if (ok && lane == 0 && j + 2 < n_blocks) load_k(j + 2);
     }
     const bool all = full == 0xFu;
@@ -359,7 +371,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
     const float sub = m_used == -INFINITY ? 0.f : m_used;
     // P_j overwrites P_{j-1}: wait for the previous P V product.
     if (j > 0) {
-      ok = ok && mbar_wait(o_full, (j - 1) & 1, a.err, kErrAttnWait, abort_flag);
+      ok = ok && mbar_wait(o_full, (j - 1) & 1, a.err, kErrAttnWait, abort_flag, wait_ns);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
     }
@@ -385,14 +397,14 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
     if (ctl) {
       // Once every warp has written P_j: P_j V_j, and V_{j+1} into the stage P_{j-1} V_{j-1}
       // has finished reading (observed through o_full above).
-      ok = ok && mbar_wait(p_full, j & 1, a.err, kErrAttnWait, abort_flag) && issue_pv(j);
+      ok = ok && mbar_wait(p_full, j & 1, a.err, kErrAttnWait, abort_flag, wait_ns) && issue_pv(j);
       if (ok && lane == 0 && j >= 1 && j + 1 < n_blocks) load_v(j + 1);
     }
   }
   // Normalise and store this row (zeros for padding queries); rows past the tile belong to
   // other tiles and are not written.
   if (ok && n_blocks > 0) {
-    ok = mbar_wait(o_full, (n_blocks - 1) & 1, a.err, kErrAttnWait, abort_flag);
+    ok = mbar_wait(o_full, (n_blocks - 1) & 1, a.err, kErrAttnWait, abort_flag, wait_ns);
     ok = __all_sync(0xffffffffu, ok);
   }
   uint32_t o[2][32];
@@ -448,7 +460,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
     }
   }
   if (ok && rank == 0) {
-    const int token = gathered ? (r < nq ? qidx[r] : -1) : t0 + r;
+    const int token = gathered ? qtok : t0 + r;
     if (gathered ? token >= 0 : token < t1) {
       const bool live = all_blocks > 0 && (gathered || q < valid) && l > 0.f;
       const float inv = live ? 1.f / l : 0.f;

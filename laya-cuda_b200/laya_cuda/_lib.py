@@ -4,13 +4,10 @@ The library is built in-tree next to this file (see build.py).  There is no fall
 library is missing, importing the runtime raises, so a run never silently executes elsewhere.
 """
 import ctypes as ct
-import os
 from pathlib import Path
 
 LIB_NAME = "liblaya_b200.so"
-# LAYA_LIB points at another build of the library (an alternative configuration to compare
-# against); by default the in-tree build next to this file.
-LIB_PATH = Path(os.environ["LAYA_LIB"]) if os.environ.get("LAYA_LIB") else Path(__file__).with_name(LIB_NAME)
+LIB_PATH = Path(__file__).with_name(LIB_NAME)
 
 OK, ERR_INVALID, ERR_CUDA, ERR_DEVICE, ERR_STATE, ERR_NO_DEVICE = range(6)
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
@@ -22,8 +19,8 @@ EXPORTS = (
     "laya_shape_class",
     "laya_forward_device", "laya_packed_ints", "laya_pack", "laya_reserve", "laya_stream", "laya_set_profiling",
     "laya_profile_read", "laya_read_tensor", "laya_cached_shapes", "laya_pool_bytes", "laya_destroy",
-    "laya_last_error", "laya_op_gemm", "laya_op_gemm_ln", "laya_interleave_geglu", "laya_op_attention", "laya_op_attention_gathered",
-    "laya_attention_tiles", "laya_op_embed_norm", "laya_op_norm", "laya_op_gemm_residual_static",
+    "laya_last_error", "laya_set_launch_options", "laya_op_gemm", "laya_op_gemm_ln", "laya_interleave_geglu", "laya_op_attention", "laya_op_attention_gathered",
+    "laya_attention_tiles", "laya_op_embed_norm", "laya_op_head_tail", "laya_op_norm", "laya_op_gemm_residual_static",
 )
 STATIC_SCRATCH_FLOATS = 4 * 1024 * 1024
 
@@ -75,14 +72,16 @@ def load():
         "laya_pool_bytes": (i, [p, ct.POINTER(ct.c_uint64), ct.POINTER(ct.c_uint64)]),
         "laya_destroy": (i, [p]),
         "laya_last_error": (ct.c_char_p, [p]),
+        "laya_set_launch_options": (i, [i, ct.c_uint64]),
         "laya_op_gemm": (i, [i, i, p, p, i, i, i, p, i, p, i, p, i, p, i, p, i, i, p, p]),
         "laya_op_gemm_ln": (i, [i, p, p, i, i, i, p, i, p, p, p, ct.c_float, p, i, p, p]),
         "laya_interleave_geglu": (i, [p, p, i, i]),
-        "laya_op_attention": (i, [i, i, p, p, p, i, p, p, i, i, i, i, p, p]),
+        "laya_op_attention": (i, [i, i, p, p, p, i, p, p, i, i, i, p, p]),
         "laya_op_attention_gathered": (i, [i, p, p, p, i, p, p, i, i, i, p, p]),
         "laya_attention_tiles": (i, [p, p, i, i, i, p, i]),
         "laya_op_embed_norm": (i, [i, p, p, p, ct.c_float, i, i, i, p, p, p, p]),
         "laya_op_norm": (i, [i, p, p, i, p, p, ct.c_float, p, i, i, p]),
+        "laya_op_head_tail": (i, [i, p, p, p, i, i, i, p, p, p, p, p, p, i, p, p, p, p, p, p]),
         "laya_op_gemm_residual_static": (i, [i, p, p, i, i, i, i, p, p, p, p]),
     }
     for name, (res, args) in sig.items():

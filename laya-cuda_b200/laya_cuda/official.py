@@ -1,47 +1,111 @@
-"""backend="official": the unmodified official Laya SDK on a CUDA device.
+"""backend="official": the installed, unmodified Laya SDK as a comparison backend on CUDA.
 
-Kept for API parity with the reference (laya_cuda/official.py:8-72): the SDK runs its own
-model on the GPU, timed with CUDA events around its forward pass.  It is a comparison
-backend only; the product path is liblaya_b200.so.
+Engine(backend="official") dispatches here (the reference's engine.py:23-24 does the same).
+The SDK owns its model and its whole forward pass; this module only
+
+  * stages the checkpoint where the SDK may edit files (it rewrites its tokenizer settings on
+    load): small files are copied into a private directory, the weights file is linked;
+  * refuses anything that is not a CUDA run: the SDK's device, every model parameter and
+    buffer, and every tensor fed to the model's forward must live on a CUDA device, checked
+    at load, at every forward and after every prediction, so a silent CPU fallback can never
+    be reported as a GPU number;
+  * times the model forward with CUDA events on the SDK's stream (gpu_ms).
+
+It is not the product path: that is liblaya_b200.so behind backend="cuda".
 """
 import gc
+import os
 import shutil
 import tempfile
 from pathlib import Path
 
+# Files above this size are linked into the staging directory instead of copied.
+_LINK_BYTES = 1 << 20
+
+
+def _stage(checkpoint, into):
+    """Mirrors `checkpoint` under `into`: small files copied (the SDK may rewrite them), large
+    ones hard-linked when the filesystem allows, copied otherwise."""
+    for source in sorted(Path(checkpoint).rglob("*")):
+        target = into / source.relative_to(checkpoint)
+        if source.is_dir():
+            target.mkdir(parents=True, exist_ok=True)
+            continue
+        target.parent.mkdir(parents=True, exist_ok=True)
+        if source.stat().st_size >= _LINK_BYTES:
+            try:
+                os.link(source, target)
+                continue
+            except OSError:
+                pass
+        shutil.copy2(source, target)
+
+
+class _CudaProbe:
+    """Forward hooks on the SDK model: refuse non-CUDA inputs, record the forward's start and
+    end events on the model's device stream."""
+
+    def __init__(self, torch, model, device):
+        self.torch, self.device = torch, device
+        self.start = torch.cuda.Event(enable_timing=True)
+        self.end = torch.cuda.Event(enable_timing=True)
+        self.input_devices = set()
+        self.handles = [model.register_forward_pre_hook(self._enter), model.register_forward_hook(self._leave)]
+
+    def _enter(self, _module, inputs):
+        tensors = [x for x in inputs if self.torch.is_tensor(x)]
+        where = {x.device.type for x in tensors}
+        if not tensors or where != {"cuda"}:
+            raise RuntimeError(f"official SDK forward got inputs on {sorted(where) or 'no tensors'}; "
+                               "only CUDA runs are compared")
+        self.input_devices.update(str(x.device) for x in tensors)
+        self.start.record(self.torch.cuda.current_stream(self.device))
+
+    def _leave(self, *_):
+        self.end.record(self.torch.cuda.current_stream(self.device))
+
+    def elapsed_ms(self):
+        self.torch.cuda.synchronize(self.device)
+        return self.start.elapsed_time(self.end)
+
+    def remove(self):
+        for handle in self.handles:
+            handle.remove()
+        self.handles = []
+
 
 class Official:
+    """The SDK agent for one checkpoint on one CUDA device (`predict`, `precision`, `gpu_ms`)."""
+
     def __init__(self, path, device):
         try:
             import torch
             import laya
         except ImportError as error:
-            raise ImportError('The official backend needs the "laya" SDK and torch installed') from error
+            raise ImportError('backend="official" needs the official "laya" SDK and torch') from error
         if not torch.cuda.is_available():
-            raise RuntimeError("The official backend requires a CUDA-enabled torch build")
-        self.torch = torch
-        # The SDK may rewrite tokenizer files; give it a disposable copy of the checkpoint.
-        self.temp = tempfile.TemporaryDirectory(prefix="laya-b200-official-")
-        target = Path(self.temp.name)
+            raise RuntimeError('backend="official" needs a torch build with CUDA support and a CUDA device')
+        self.torch, self.gpu_ms, self.probe = torch, None, None
+        self._staging = tempfile.TemporaryDirectory(prefix="laya-b200-sdk-")
         try:
-            for sub in ("tokenizer", "encoder"):
-                shutil.copytree(path / sub, target / sub)
-            shutil.copy2(path / "rl_agent_config.json", target / "rl_agent_config.json")
-            try:
-                (target / "model.safetensors").hardlink_to(path / "model.safetensors")
-            except OSError:
-                shutil.copy2(path / "model.safetensors", target / "model.safetensors")
-            self.agent = laya.Agent(str(target), device=device)
-            if self.agent.device.type != "cuda":
-                raise RuntimeError("Official SDK unexpectedly fell back to CPU")
-            self.events = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
-            stream = lambda: torch.cuda.current_stream(self.agent.device)  # noqa: E731
-            self.hooks = [self.agent.model.register_forward_pre_hook(lambda *_: self.events[0].record(stream())),
-                          self.agent.model.register_forward_hook(lambda *_: self.events[1].record(stream()))]
-            self.gpu_ms = None
+            _stage(Path(path), Path(self._staging.name))
+            self.agent = laya.Agent(self._staging.name, device=device)
+            self._require_cuda("after loading")
+            tensors = [*self.agent.model.parameters(), *self.agent.model.buffers()]
+            self.device_info = {"torch_version": torch.__version__, "cuda_build": torch.version.cuda,
+                                "gpu": torch.cuda.get_device_name(self.agent.device),
+                                "model_devices": sorted({str(t.device) for t in tensors})}
+            self.probe = _CudaProbe(torch, self.agent.model, self.agent.device)
         except BaseException:
-            self.temp.cleanup()
+            self.close()
             raise
+
+    def _require_cuda(self, when):
+        if self.agent.device.type != "cuda":
+            raise RuntimeError(f"official SDK runs on {self.agent.device} {when}; only CUDA runs are compared")
+        tensors = [*self.agent.model.parameters(), *self.agent.model.buffers()]
+        if not tensors or any(t.device.type != "cuda" for t in tensors):
+            raise RuntimeError(f"official SDK model tensors are not all on CUDA {when}")
 
     @property
     def precision(self):
@@ -49,14 +113,19 @@ class Official:
 
     def predict(self, state, questions):
         result = self.agent.system_one(state, questions)
-        self.torch.cuda.synchronize(self.agent.device)
-        self.gpu_ms = self.events[0].elapsed_time(self.events[1])
+        self._require_cuda("after predicting")
+        self.device_info["input_devices"] = sorted(self.probe.input_devices)
+        self.gpu_ms = self.probe.elapsed_ms()
         return result
 
     def close(self):
-        for hook in self.hooks:
-            hook.remove()
-        self.agent = None
-        gc.collect()
-        self.torch.cuda.empty_cache()
-        self.temp.cleanup()
+        if self.probe is not None:
+            self.probe.remove()
+            self.probe = None
+        if getattr(self, "agent", None) is not None:
+            self.agent = None
+            gc.collect()
+            self.torch.cuda.empty_cache()
+        if self._staging is not None:
+            self._staging.cleanup()
+            self._staging = None

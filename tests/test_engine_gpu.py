@@ -77,22 +77,6 @@ def test_laya_geometry_matches_fp32_oracle(laya_ckpt, precision):
     assert max(r["logit"] for r in rows) <= (0.02 if precision == "bfloat16" else 0.005)
 
 
-def test_mma_sync_attention_forward_matches_fp32_oracle(laya_ckpt, monkeypatch):
-    """The forward pass with the mma.sync attention kernel (LAYA_ATTENTION=mma_sync) instead of
-    the default tcgen05 kernel meets the same parity bar."""
-    path, arch, weights = laya_ckpt
-    oracle = Oracle(weights, arch)
-    rng = np.random.default_rng(2)
-    items = [S.build_item(rng, n, k, arch["vocab"], kind=j % 3) for j, (n, k) in
-             enumerate([(83, 4), (512, 8), (300, 5), (129, 2)])]
-    monkeypatch.setenv("LAYA_ATTENTION", "mma_sync")
-    with Engine(path) as engine:
-        rows = compare(engine, oracle, items)
-    assert max(r["prob"] for r in rows) <= 2e-3
-    assert max(r["act"] for r in rows) <= 2e-3
-    assert max(r["logit"] for r in rows) <= 0.005
-
-
 @pytest.mark.parametrize("precision", ["bfloat16", "float16"])
 def test_decisive_checkpoint_argmax_and_probabilities(peaky_ckpt, precision):
     path, arch, weights = peaky_ckpt
@@ -265,33 +249,26 @@ def test_batch_engine_matches_engine(laya_ckpt):
 
 
 
-def test_programmatic_launch_does_not_change_results(laya_ckpt, tmp_path):
+def test_programmatic_launch_does_not_change_results(laya_ckpt):
     """Every kernel waits for its predecessor before reading its outputs, so results with
-    programmatic dependent launch equal those of plain stream order bit for bit."""
-    import subprocess
-    import sys
-    from pathlib import Path
+    programmatic dependent launch equal those of plain stream order bit for bit (a fresh
+    engine per mode, so no graph captured under the other mode is reused)."""
+    from laya_cuda import _lib
     path, arch, _ = laya_ckpt
-    root = Path(__file__).resolve().parents[1]
-    script = tmp_path / "run.py"
-    script.write_text(f"""
-import sys, numpy as np
-sys.path.insert(0, {str(root / 'laya-cuda_b200')!r})
-from laya_cuda import Engine, synthetic as S
-rng = np.random.default_rng(8)
-items = [S.build_item(rng, n, k, {arch['vocab']}, kind=j % 3) for j, (n, k) in enumerate([(83, 4), (512, 8), (300, 5)])]
-with Engine({str(path)!r}) as e:
-    outs = [e.runtime.predict(items, capture=c) for c in (True, False)] + [e.runtime.predict(items[:1])]
-np.savez(sys.argv[1], *[a for o in outs for a in o[:2]])
-""")
+    rng = np.random.default_rng(8)
+    items = [S.build_item(rng, n, k, arch["vocab"], kind=j % 3) for j, (n, k) in enumerate([(83, 4), (512, 8), (300, 5)])]
+    lib = _lib.load()
     results = []
-    for pdl in ("1", "0"):
-        out = tmp_path / f"pdl{pdl}.npz"
-        env = dict(__import__("os").environ, LAYA_PDL=pdl)
-        subprocess.run([sys.executable, str(script), str(out)], check=True, env=env)
-        results.append(np.load(out))
-    for key in results[0].files:
-        np.testing.assert_array_equal(results[0][key], results[1][key])
+    try:
+        for pdl in (1, 0):
+            assert lib.laya_set_launch_options(pdl, 0) == 0
+            with Engine(path) as e:
+                outs = [e.runtime.predict(items, capture=c) for c in (True, False)] + [e.runtime.predict(items[:1])]
+            results.append([a for o in outs for a in o[:2]])
+    finally:
+        lib.laya_set_launch_options(1, 0)
+    for a, b in zip(*results):
+        np.testing.assert_array_equal(a, b)
 
 
 def test_submit_collect_pipeline_matches_predict(laya_ckpt):

@@ -216,35 +216,34 @@ def packed_case(lengths):
     return starts, np.asarray(lengths, np.int32), M
 
 
-@pytest.mark.parametrize("prec,impl,split_p", [("bf16", 0, 0), ("bf16", 0, 1), ("f16", 0, 1), ("f16", 1, 0),
-                                               ("bf16", 1, 0), ("f16", 2, 0), ("bf16", 3, 0)])
+@pytest.mark.parametrize("prec,impl", [("f16", 1), ("bf16", 1), ("f16", 2), ("bf16", 2), ("f16", 3), ("bf16", 3)])
 @pytest.mark.parametrize("lengths,window", [([32], -1), ([7, 96], 64), ([128, 1], -1), ([250, 131], 64),
                                             ([256, 219, 145], -1), ([500], 64), ([1024, 333], -1), ([300, 77], 40)])
-def test_packed_attention_matches_oracle(lib, prec, impl, split_p, lengths, window):
+def test_packed_attention_matches_oracle(lib, prec, impl, lengths, window):
     """Cases and float64 oracle of tests/test_attention.py:12-56 (h=2, seeded by M), for the
-    mma.sync kernel (impl 0, 64-query tiles) and the tcgen05 kernel (128-query tiles; impl 1:
-    key split chosen as the forward pass does; 2: never; 3: always)."""
-    check_packed_attention(lib, prec, impl, split_p, lengths, window, ramp=False)
+    tcgen05 kernel over 128-query tiles (impl 1: key split chosen as the forward pass does;
+    2: never; 3: always)."""
+    check_packed_attention(lib, prec, impl, lengths, window, ramp=False)
 
 
-@pytest.mark.parametrize("prec,impl", [("f16", 0), ("f16", 1), ("bf16", 1), ("f16", 2), ("bf16", 3)])
+@pytest.mark.parametrize("prec,impl", [("f16", 1), ("bf16", 1), ("f16", 2), ("bf16", 3)])
 @pytest.mark.parametrize("lengths,window", [([1024, 333], -1), ([700], 64), ([513, 200], -1)])
 def test_packed_attention_growing_scores(lib, prec, impl, lengths, window):
     """Scores that grow along the row (keys scaled up with position), so the running maximum
     rises by far more than 2^8 between key blocks: exercises the rescaling of O."""
-    check_packed_attention(lib, prec, impl, 0, lengths, window, ramp=True)
+    check_packed_attention(lib, prec, impl, lengths, window, ramp=True)
 
 
-# Worst |error| - 16-bit output rounding, by (precision, split_p): probability rounding (split_p
-# keeps fp32-level probabilities).  Scores that grow along the row concentrate the softmax on a
-# few keys, so one rounded bf16 probability weighs more.
-ATTN_LIMIT = {("bf16", 0): 6e-3, ("bf16", 1): 1.5e-3, ("f16", 1): 6e-4, ("f16", 0): 1.5e-3}
-ATTN_LIMIT_RAMP = {("bf16", 0): 1e-2, ("f16", 0): 1.5e-3}
+# Worst |error| - 16-bit output rounding, by precision: the 16-bit rounding of the
+# probabilities.  Scores that grow along the row concentrate the softmax on a few keys, so one
+# rounded bf16 probability weighs more.
+ATTN_LIMIT = {"bf16": 6e-3, "f16": 1.5e-3}
+ATTN_LIMIT_RAMP = {"bf16": 1e-2, "f16": 1.5e-3}
 
 
-def check_packed_attention(lib, prec, impl, split_p, lengths, window, ramp):
+def check_packed_attention(lib, prec, impl, lengths, window, ramp):
     h = 2
-    tile_q = 64 if impl == 0 else 128
+    tile_q = 128
     starts, lens, M = packed_case(lengths)
     cap = (M + (tile_q - 16) * len(lengths) + tile_q - 1) // tile_q + 1
     tiles = np.zeros((cap, 4), np.int32)
@@ -265,7 +264,7 @@ def check_packed_attention(lib, prec, impl, split_p, lengths, window, ramp):
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     dev = [torch.from_numpy(v).cuda() for v in (tiles, starts, lens)]
     _lib.check(lib.laya_op_attention(PRECISIONS[prec][0], impl, ptr(layout), ptr(out), ptr(dev[0]), cap, ptr(dev[1]),
-                                     ptr(dev[2]), M, h, window, split_p, ptr(err), stream()))
+                                     ptr(dev[2]), M, h, window, ptr(err), stream()))
     torch.cuda.synchronize()
     assert int(err.item()) == 0
     got = out.double().cpu().numpy()
@@ -282,7 +281,7 @@ def check_packed_attention(lib, prec, impl, split_p, lengths, window, ramp):
         expected = (p @ v).transpose(1, 0, 2).reshape(n, h * 64)
         err_ = np.abs(got[start:start + n] - expected) - ROUND[prec] * np.abs(expected)
         worst = max(worst, float(err_.max()))
-    limit = (ATTN_LIMIT_RAMP if ramp else ATTN_LIMIT)[(prec, split_p)]
+    limit = (ATTN_LIMIT_RAMP if ramp else ATTN_LIMIT)[prec]
     assert worst < limit, worst
     np.testing.assert_array_equal(got[~real], 0)
 
@@ -381,7 +380,7 @@ def test_gathered_query_attention_matches_oracle(lib, prec, lengths, q_per_row):
             written[t] = True
             e = expected[t - s0]
             worst = max(worst, float(np.max(np.abs(got[t] - e) - ROUND[prec] * np.abs(e))))
-    assert worst < ATTN_LIMIT[(prec, 0)], worst
+    assert worst < ATTN_LIMIT[prec], worst
     np.testing.assert_array_equal(got[~written], 7.0)
 
 
@@ -415,3 +414,95 @@ def test_gemm_residual_layernorm_matches_fp64(lib, prec, M, N, K, with_bias):
     want = (want_r - mean) / np.sqrt(var + 1e-5) * gamma + (beta if with_bias else 0)
     got = out.double().cpu().numpy()
     assert np.max(np.abs(got - want) - ROUND[prec] * np.abs(want)) < 2e-3
+
+
+@pytest.mark.parametrize("prec", ["f16", "bf16"])
+@pytest.mark.parametrize("width", [128, 768])
+def test_head_tail_features_logits_and_actions(lib, prec, width):
+    """The decision-head tail against the oracle's features (kernels.cu:167-183, laya.py:241-245):
+    option counts 0, 1, 2, a tied top-2, 77 options and a random question in a k = 128 class.
+    scorer.3 is the unit vector e0 so the option logits are chosen values (16-bit exact), and p1,
+    p1 - p2, entropy / log(max(c, 2)) and max(c, 2) / 255 are compared directly."""
+    import types
+    from oracle.laya_oracle import Oracle, gelu
+    rng = np.random.default_rng(width)
+    counts = np.array([0, 1, 2, 2, 77, 5], np.int32)
+    b, k, d, n_act = len(counts), 128, width, 3
+    option_logits = np.zeros((b, k + 1), np.float32)
+    for q, c in enumerate(counts):
+        option_logits[q, 1:c + 1] = rng.normal(0, 2, c)
+    option_logits[3, 1:3] = 1.5                                     # tied top-2
+    t16 = PRECISIONS[prec][1]
+    option_logits = torch.from_numpy(option_logits).to(t16).float().numpy()
+    scored = np.zeros((b, k + 1, d), np.float32)
+    scored[:, :, 0] = option_logits
+    scored[:, :, 1:] = rng.normal(0, 1, (b, k + 1, d - 1))          # ignored by w3 = e0
+    selected = rng.normal(0, 1, (b, k + 1, d)).astype(np.float32)
+    w3 = np.zeros(d, np.float32); w3[0] = 1.0
+    b3 = np.array([0.25], np.float32)
+    wa0 = rng.normal(0, 0.05, (256, d + 4)).astype(np.float32)
+    ba0 = rng.normal(0, 0.1, 256).astype(np.float32)
+    wa2 = rng.normal(0, 0.05, (n_act, 256)).astype(np.float32)
+    ba2 = rng.normal(0, 0.1, n_act).astype(np.float32)
+    dev = {name: torch.from_numpy(v).cuda() for name, v in dict(selected=selected, w3=w3, b3=b3, wa0=wa0, ba0=ba0,
+                                                                 wa2=wa2, ba2=ba2, counts=counts).items()}
+    dev["scored"] = torch.from_numpy(scored).to(t16).cuda()
+    logits = torch.full((b, k + 1), float("nan"), device="cuda")
+    acts = torch.full((b, n_act), float("nan"), device="cuda")
+    feats = torch.full((b, 4), float("nan"), device="cuda")
+    hidden = torch.zeros((b, 256), device="cuda")
+    arrivals = torch.zeros(b, dtype=torch.int32, device="cuda")
+    _lib.check(lib.laya_op_head_tail(PRECISIONS[prec][0], ptr(dev["selected"]), ptr(dev["scored"]), ptr(dev["counts"]),
+                                     b, k, d, ptr(dev["w3"]), ptr(dev["b3"]), ptr(dev["wa0"]), ptr(dev["ba0"]),
+                                     ptr(dev["wa2"]), ptr(dev["ba2"]), n_act, ptr(logits), ptr(acts), ptr(feats),
+                                     ptr(hidden), ptr(arrivals), stream()))
+    torch.cuda.synchronize()
+    want_logits = option_logits.astype(np.float64) + 0.25
+    np.testing.assert_allclose(logits.cpu().numpy(), want_logits, atol=1e-6, rtol=0)
+    shim = types.SimpleNamespace(dtype=np.float64)
+    for q, c in enumerate(counts):
+        want_f = Oracle.features(shim, want_logits[q, 1:c + 1])
+        got_f = feats[q].cpu().numpy()
+        np.testing.assert_allclose(got_f, want_f, atol=2e-6, rtol=1e-5, err_msg=f"question {q}, {c} options")
+        feat = np.concatenate([selected[q, 0].astype(np.float64), want_f])
+        want_a = gelu(wa0.astype(np.float64) @ feat + ba0) @ wa2.astype(np.float64).T + ba2
+        np.testing.assert_allclose(acts[q].cpu().numpy(), want_a, atol=1e-4, rtol=0)
+    assert feats[3, 1].item() == 0.0                                 # tie: p1 - p2 exactly 0
+    np.testing.assert_array_equal(arrivals.cpu().numpy(), 0)         # left zero for the next launch
+
+
+def test_gathered_attention_reports_out_of_range_indices(lib):
+    """Gathered query indices outside the packed rows set the error word (kErrBadIndex = 4),
+    are not stored, and leave the valid rows exact: the kernel clamps instead of reading or
+    writing out of bounds."""
+    prec, h, q_per_row = "f16", 2, 4
+    starts, lens, M = packed_case([300, 77])
+    s1 = int(starts[1])
+    index = np.array([[0, 5, M + 7, 299], [s1, -3, s1 + 10, s1 + 76]], np.int32)
+    rng = np.random.default_rng(17)
+    x = rng.normal(0, 1, (M, 3, h, 64)).astype(np.float32)
+    xt = torch.from_numpy(x).to(torch.float16)
+    xd = xt.double().numpy()
+    layout = xt.permute(1, 2, 0, 3).contiguous()
+    layout[2] = layout[2].transpose(1, 2).reshape(h, M, 64)
+    out = torch.full((M, h * 64), 7.0, dtype=torch.float16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    dev = [torch.from_numpy(np.ascontiguousarray(v)).cuda() for v in (index, starts, lens)]
+    _lib.check(lib.laya_op_attention_gathered(PRECISIONS[prec][0], ptr(layout.cuda()), ptr(out), ptr(dev[0]), q_per_row,
+                                              ptr(dev[1]), ptr(dev[2]), 2, M, h, ptr(err), stream()))
+    torch.cuda.synchronize()
+    assert int(err.item()) == 4
+    got = out.double().cpu().numpy()
+    written = np.zeros(M, bool)
+    for r, (s0, n) in enumerate(zip(starts, lens)):
+        q, k, v = xd[s0:s0 + n].transpose(1, 2, 0, 3)
+        s = q @ k.transpose(0, 2, 1) / 8
+        p = np.exp(s - s.max(-1, keepdims=True))
+        p /= p.sum(-1, keepdims=True)
+        expected = (p @ v).transpose(1, 0, 2).reshape(n, h * 64)
+        for t in index[r]:
+            if 0 <= t < M:
+                written[t] = True
+                e = expected[t - s0]
+                assert np.max(np.abs(got[t] - e) - ROUND[prec] * np.abs(e)) < ATTN_LIMIT[prec]
+    np.testing.assert_array_equal(got[~written], 7.0)

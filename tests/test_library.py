@@ -95,11 +95,10 @@ def test_pack_matches_reference_fill(lib, seed):
     for field, size in zip(want, (m, m, m, m, b, b, b, b * (k + 1))):
         np.testing.assert_array_equal(out[o:o + size], field)
         o += size
-    # Attention tile tables (64 then 128 queries): every token of every row span is covered
-    # exactly once by a tile of its row; tokens past the last row by zero-fill tiles; no tile
-    # straddles rows.
+    # Attention tile table (128 queries): every token of every row span is covered exactly once
+    # by a tile of its row; tokens past the last row by zero-fill tiles; no tile straddles rows.
     o = (o + 3) // 4 * 4
-    for tile_q in (64, 128):
+    for tile_q in (128,):
         cap = (m + (tile_q - 16) * b + tile_q - 1) // tile_q + 1
         tiles = out[o:o + 4 * cap].reshape(-1, 4)
         o += 4 * cap
