@@ -3,8 +3,9 @@
 Workload (one "step"): configuration 5 of the benchmark plan -- the `laya` encoder geometry
 (12 layers, d 768, 12 heads, F 3072, vocab 50368) with positions extended to 1024, 4096
 requests of uniform length in [256, 1024], 3 questions x 8 options each (12,288 packed
-sequences), run as micro-batches of 64 sequences.  Under torchrun every rank processes its own
-4096-request set (per-GPU work fixed: weak scaling) on its own weight replica; nothing is
+sequences), run as micro-batches of 64 sequences.  Under torchrun the one 4096-request set is
+split across the ranks by modelled device work (laya_cuda.sharding.shard, the same partition on
+every rank: strong scaling); each rank runs its share on its own weight replica and nothing is
 exchanged between ranks (the NCCL group only carries the timing barrier and the max-reduction).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--latency none|basic]
@@ -106,11 +107,20 @@ class Clocks:
                 "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
 
 
-def rank_workload(rank, requests, vocab):
-    """This rank's sequences: its own seeded request set (weak scaling: per-rank work is fixed)."""
+def rank_workload(rank, world, requests, vocab):
+    """This rank's sequences: its share of the one seeded request set, partitioned across the
+    `world` ranks by modelled device work (strong scaling: the job's work is fixed).  Every rank
+    computes the same partition.  Returns (items, partition statistics)."""
     from laya_cuda import synthetic as S
-    reqs = S.throughput_requests(1000 + rank, requests, vocab, LENGTHS, QUESTIONS, OPTIONS)
-    return [item for req in reqs for item in req]
+    from laya_cuda.sharding import imbalance, request_cost, shard
+    reqs = S.throughput_requests(1000, requests, vocab, LENGTHS, QUESTIONS, OPTIONS)
+    costs = [request_cost(r) for r in reqs]
+    parts = shard(costs, world)
+    items = [item for i in parts[rank] for item in reqs[i]]
+    stats = {"requests_per_rank": [len(p) for p in parts],
+             "tokens_per_rank": [sum(len(it[0]) for i in p for it in reqs[i]) for p in parts],
+             "cost_imbalance": round(imbalance(costs, parts), 5)}
+    return items, stats
 
 
 def job_rate(local_ms, local_sequences, steps, world, device):
@@ -180,7 +190,7 @@ def run_reference(args, rank, world):
     sample = f"{per_step} sequences per step (lengths 256-1024, 8 options) of the config-5 workload"
     line = {"impl": "reference", "metric": "sequences/s", "value": round(value, 3), "unit": "sequences/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(elapsed / args.steps * 1000, 2), "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": round(elapsed / args.steps * 1000, 2), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "config5-throughput laya 12L d768 F3072 V50368 ctx1024, 3q x 8 options",
                        "sample": sample},
@@ -277,7 +287,7 @@ def run_engine(args, rank, world, local_rank):
     rt, lib = engine.runtime, engine.runtime._lib
     h = rt._handle
 
-    items = rank_workload(rank, args.requests, arch["vocab"])
+    items, sharding = rank_workload(rank, world, args.requests, arch["vocab"])
     batches = build_micro_batches(items)
     tokens = sum(len(i[0]) for i in items)
     packed, shapes, maxes = [], [], [0, 0, 0]
@@ -395,13 +405,14 @@ def run_engine(args, rank, world, local_rank):
                    "sample": f"first {n} sequences of the rank-0 workload, FP32 numpy oracle, all host threads"}
         line = {"metric": "sequences/s", "value": round(value, 2), "unit": "sequences/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
                 "data": "synthetic (seeded random-init weights, uniform token ids)",
                 "config": {"workload": "config5-throughput: laya 12L d768 h12 F3072 V50368, positions 1024; "
                                        f"{args.requests} requests x 3 questions x 8 options, lengths U[256,1024], "
-                                       "64-sequence micro-batches, per rank",
-                           "sequences_per_rank": len(items), "tokens_per_rank": tokens, "micro_batches": len(batches),
-                           "parallelism": f"replicas{world}", "l2": "inputs larger than L2 (no flush)"},
+                                       "64-sequence micro-batches, split across the GPUs by modelled work",
+                           "sequences_rank0": len(items), "tokens_rank0": tokens, "micro_batches_rank0": len(batches),
+                           "sharding": sharding, "parallelism": f"dp{world} (request shards, no collective)",
+                           "l2": "inputs larger than L2 (no flush)"},
                 "gpu_launches": launches * args.steps, "kernels": fam,
                 "kernels_note": "per family over one profiled step (event pair around every launch), after the timed steps",
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,

@@ -3,9 +3,14 @@
 Same contract as the reference BatchEngine (laya_cuda/batching.py:17-157): bounded pending
 queue, collection for up to max_wait_ms after the oldest request, whole requests packed into
 batches under max_batch_size questions and max_batch_tokens packed tokens (16-token row spans),
-one Runtime.predict per batch, per-request futures with metrics.  A failing request fails only
-its own future, a failing batch only that batch's futures, and a fatal worker error fails every
-accepted request before the worker releases the GPU.
+per-request futures with metrics.  A failing request fails only its own future, a failing batch
+only that batch's futures, and a fatal worker error fails every accepted request before the
+worker releases the GPU.
+
+Unlike the reference's worker, which runs one synchronous Runtime.predict per batch
+(batching.py:122), this one pipelines through Runtime.submit / collect: batch i+1 is packed and
+launched before batch i is collected and decoded, and requests that arrive while a batch runs
+are tokenised before it is collected, so tokenisation, packing and decoding overlap the device.
 """
 from concurrent.futures import Future
 from copy import deepcopy
@@ -80,24 +85,30 @@ class BatchEngine:
         else:
             future.set_exception(error)
 
-    def _collect(self):
-        """Waits for work; returns the requests to run, or None when closed and drained."""
+    def _collect(self, block):
+        """Takes the queued requests.  block=True waits for work and then up to max_wait_ms after
+        the oldest request (the batching window); returns None when closed and drained.
+        block=False (a batch is on the device) takes only what is queued now, possibly []."""
         with self._cv:
-            self._cv.wait_for(lambda: self._queue or self._closed)
+            if block:
+                self._cv.wait_for(lambda: self._queue or self._closed)
             if not self._queue:
-                return None
-            deadline = self._queue[0][3] + self.wait
-            while not self._closed and len(self._queue) < self.max_batch_size:
-                remaining = deadline - time.perf_counter()
-                if remaining <= 0:
-                    break
-                self._cv.wait(remaining)
+                return None if self._closed else []
+            if block:
+                deadline = self._queue[0][3] + self.wait
+                while not self._closed and len(self._queue) < self.max_batch_size:
+                    remaining = deadline - time.perf_counter()
+                    if remaining <= 0:
+                        break
+                    self._cv.wait(remaining)
             taken, self._queue = self._queue, []
             return taken
 
-    def _prepare(self, engine, active):
+    def _prepare(self, engine, active, taken):
+        """Tokenises newly taken requests (while a previous batch may still run on the device)."""
         prepared = []
-        for request in list(active):
+        active.extend(taken)
+        for request in taken:
             if not request[0].set_running_or_notify_cancel():
                 self._finish(request)
                 active.remove(request)
@@ -114,7 +125,8 @@ class BatchEngine:
         return prepared
 
     def _next_batch(self, prepared):
-        """First-fit in arrival order under both budgets; returns (batch, rest, questions)."""
+        """First-fit in arrival order under both budgets (questions and packed 16-token row spans);
+        returns (batch, rest, questions)."""
         batch, rest, questions, tokens = [], [], 0, 0
         for entry in prepared:
             size = len(entry[1])
@@ -126,47 +138,78 @@ class BatchEngine:
                 rest.append(entry)
         return batch, rest, questions
 
-    def _run(self, engine, active, prepared):
-        while prepared:
-            batch, prepared, questions = self._next_batch(prepared)
-            items = [item for _, rows, _ in batch for item in rows]
-            executed = time.perf_counter()
+    def _fail(self, active, batch, error):
+        for request, _, _ in batch:
+            if request in active:
+                active.remove(request)
+                self._finish(request, error=error)
+
+    def _launch(self, engine, active, batch, questions):
+        """Packs and launches one batch without waiting for it; returns its in-flight record."""
+        items = [item for _, rows, _ in batch for item in rows]
+        executed = time.perf_counter()
+        try:
+            return batch, questions, executed, engine.runtime.submit(items)
+        except Exception as error:
+            self._fail(active, batch, error)
+            return None
+
+    def _complete(self, engine, active, batch, questions, executed, ticket):
+        """Waits for a launched batch and resolves its requests' futures."""
+        try:
+            logits, acts, metrics = engine.runtime.collect(ticket)
+        except Exception as error:
+            self._fail(active, batch, error)
+            return
+        offset = 0
+        for request, rows, _ in batch:
+            future, _, questions_def, started = request
             try:
-                logits, acts, metrics = engine.runtime.predict(items)
+                end = offset + len(rows)
+                result = engine.adapter.decode(logits[offset:end], acts[offset:end], questions_def, rows)
+                future.metrics = {**metrics, "batch_questions": questions, "batch_requests": len(batch),
+                                  "queue_ms": (executed - started) * 1000,
+                                  "api_ms": (time.perf_counter() - started) * 1000,
+                                  "tokens_per_question": [len(x[0]) for x in rows], "backend": "cuda",
+                                  "precision": getattr(engine.runtime, "precision", "float16")}
+                active.remove(request)
+                self._finish(request, result)
             except Exception as error:
-                for request, _, _ in batch:
+                if request in active:
                     active.remove(request)
                     self._finish(request, error=error)
-                continue
-            offset = 0
-            for request, rows, _ in batch:
-                future, _, questions_def, started = request
-                try:
-                    end = offset + len(rows)
-                    result = engine.adapter.decode(logits[offset:end], acts[offset:end], questions_def, rows)
-                    future.metrics = {**metrics, "batch_questions": questions, "batch_requests": len(batch),
-                                      "queue_ms": (executed - started) * 1000,
-                                      "api_ms": (time.perf_counter() - started) * 1000,
-                                      "tokens_per_question": [len(x[0]) for x in rows], "backend": "cuda",
-                                      "precision": getattr(engine.runtime, "precision", "float16")}
-                    active.remove(request)
-                    self._finish(request, result)
-                except Exception as error:
-                    if request in active:
-                        active.remove(request)
-                        self._finish(request, error=error)
-                offset += len(rows)
+            offset += len(rows)
+
+    def _run(self, engine, active, prepared, pending):
+        """Launches the prepared requests batch by batch.  Each batch is launched before the
+        previous one is collected and decoded, so host work overlaps the device (at most two
+        batches in flight).  Returns the last launched batch, still in flight, or None."""
+        while prepared:
+            batch, prepared, questions = self._next_batch(prepared)
+            launched = self._launch(engine, active, batch, questions)
+            if pending is not None:
+                self._complete(engine, active, *pending)
+            pending = launched
+        return pending
 
     def _worker(self, model, options, ready):
-        engine, active = None, []
+        engine, active, pending = None, [], None
         try:
             engine = Engine(model, **options)
             ready.set_result(None)
             while True:
-                active = self._collect()
-                if active is None:
+                # With a batch in flight, requests queued meanwhile are tokenised before it is
+                # collected; with none, wait for work and the batching window.
+                taken = self._collect(block=pending is None)
+                if taken is None:
                     break
-                self._run(engine, active, self._prepare(engine, active))
+                if not taken:
+                    self._complete(engine, active, *pending)
+                    pending = None
+                    continue
+                pending = self._run(engine, active, self._prepare(engine, active, taken), pending)
+            if pending is not None:
+                self._complete(engine, active, *pending)
         except BaseException as error:
             with self._cv:
                 self._closed = True

@@ -41,6 +41,17 @@ def fake(monkeypatch):
                 raise RuntimeError("device failure")
             return [x[0][0] for x in items], [0] * len(items), {"gpu_ms": 1}
 
+        # The worker launches a batch (submit) before collecting the previous one; the fake runs
+        # the pass at submit and hands the result back at collect.
+        def submit(self, items):
+            self.tickets = getattr(self, "tickets", {})
+            self.issued = ticket = getattr(self, "issued", 0) + 1
+            self.tickets[ticket] = self.predict(items)
+            return ticket
+
+        def collect(self, ticket):
+            return self.tickets.pop(ticket)
+
         def decode(self, logits, acts, questions, items):
             return dict(zip(questions, logits))
 
@@ -147,3 +158,45 @@ def test_split_results_follow_batch_order(fake):
         futures = [engine.submit(s, {"x": n, "y": n + 1}) for s, n in (("p", 10), ("q", 30), ("r", 50))]
         assert [f.result(5) for f in futures] == [{"x": s, "y": s} for s in "pqr"]
         assert all(f.metrics["batch_questions"] == 6 for f in futures)
+
+
+def test_next_batch_launches_before_the_previous_is_collected(monkeypatch):
+    """Pipelining: with one question per batch, batch i+1 is submitted before batch i is
+    collected and decoded, and no more than two batches are ever in flight."""
+    events = []
+
+    class Engine:
+        def __init__(self, *args, **kwargs):
+            self.adapter = self
+            self.runtime = self
+            self.inflight = 0
+
+        def prepare(self, state, questions):
+            return [([state], [0], 0) for _ in questions]
+
+        def submit(self, items):
+            self.inflight += 1
+            assert self.inflight <= 2
+            events.append(("submit", items[0][0][0]))
+            return items[0][0][0]
+
+        def collect(self, ticket):
+            self.inflight -= 1
+            events.append(("collect", ticket))
+            return [ticket], [0], {"gpu_ms": 1}
+
+        def decode(self, logits, acts, questions, items):
+            events.append(("decode", logits[0]))
+            return dict(zip(questions, logits))
+
+        def close(self):
+            pass
+
+    monkeypatch.setattr(batching, "Engine", Engine)
+    with BatchEngine(max_batch_size=1, max_wait_ms=50) as engine:
+        futures = [engine.submit(s, {"q": 1}) for s in "abc"]
+        assert [f.result(5) for f in futures] == [{"q": s} for s in "abc"]
+    order = [e for e in events if e[0] != "decode"]
+    assert order == [("submit", "a"), ("submit", "b"), ("collect", "a"), ("submit", "c"), ("collect", "b"),
+                     ("collect", "c")]
+    assert events.index(("decode", "a")) > events.index(("submit", "b"))

@@ -1,6 +1,7 @@
-"""The multi-GPU bench logic on CPU: two gloo ranks, each with its own seeded workload
-(request-level data parallelism, no data exchanged), and the whole-job rate as all ranks'
-sequences over the slowest rank's time."""
+"""The multi-GPU bench logic on CPU: two gloo ranks split the one seeded request set by modelled
+device work (request-level data parallelism, no data exchanged): every request runs on exactly
+one rank, the ranks' modelled work is balanced, and the whole-job rate is all ranks' sequences
+over the slowest rank's time."""
 import os
 import sys
 from pathlib import Path
@@ -20,23 +21,33 @@ def _rank(rank, world, port, out):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         import bench
-        items = bench.rank_workload(rank, 8, 50368)
+        items, stats = bench.rank_workload(rank, world, 64, 50368)
+        keys = [tuple(item[0][:12]) + (len(item[0]),) for item in items]
+        everyone = [None] * world
+        dist.all_gather_object(everyone, keys)
         local_ms = 100.0 * (rank + 1)              # rank 1 is the slow one
         rate, ms_max, total = bench.job_rate(local_ms, len(items), 3, world, "cpu")
-        out[rank] = (len(items), sum(len(i[0]) for i in items), rate, ms_max, total, items[0][0][:8])
+        out[rank] = (everyone, stats, rate, ms_max, total)
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-def test_two_rank_weak_scaling_rate():
+def test_two_rank_request_shards():
     world, port = 2, 29611
     with mp.Manager() as manager:
         out = manager.dict()
         mp.spawn(_rank, args=(world, port, out), nprocs=world, join=True)
         results = dict(out)
-    (n0, t0, r0, m0, tot0, head0), (n1, t1, r1, m1, tot1, head1) = results[0], results[1]
-    assert n0 == n1 == 8 * 3                       # 8 requests x 3 questions per rank
-    assert head0 != head1                          # independent per-rank request sets
-    assert m0 == m1 == 200.0 and tot0 == tot1 == 48
-    assert r0 == r1 == pytest.approx(48 * 3 / 0.2)
+    everyone, stats, rate, ms_max, total = results[0]
+    assert results[1][0] == everyone and results[1][1] == stats      # the same partition on both ranks
+    import bench
+    all_items, _ = bench.rank_workload(0, 1, 64, 50368)
+    want = sorted(tuple(item[0][:12]) + (len(item[0]),) for item in all_items)
+    got = sorted(everyone[0] + everyone[1])
+    assert got == want                                               # every sequence exactly once
+    assert not set(everyone[0]) & set(everyone[1])
+    assert stats["requests_per_rank"] and sum(stats["requests_per_rank"]) == 64
+    assert stats["cost_imbalance"] < 1.02
+    assert ms_max == 200.0 and total == 64 * 3
+    assert rate == pytest.approx(64 * 3 * 3 / 0.2)
