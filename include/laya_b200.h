@@ -81,6 +81,22 @@ int laya_create(const laya_config* cfg, int device, int max_cached_shapes, laya_
 int laya_load_tensor(laya_engine* e, const char* name, int dtype, const int64_t* shape, int ndim,
                      const void* host);
 
+/* Replaces the whole weight load of runtime.py:147-158 (safetensors read, name and shape checks,
+ * per-tensor upload): reads the safetensors file at `path` (F32, F16 or BF16 tensors), checks
+ * that its tensor names are exactly Laya.weight_shapes() ("Checkpoint tensor names do not match
+ * the Laya adapter") and every shape ("Incompatible tensor shape: <name>"), both
+ * LAYA_ERR_INVALID, and places every tensor in one device allocation.  The file is memory-mapped
+ * and streamed through pinned staging chunks copied by several host threads; uploads are
+ * asynchronous and the conversion to the stored type (16-bit GEMM operands in the engine's
+ * precision, fp32 for norms, biases, embeddings and the head tail) and the GeGLU row interleave
+ * run on the device.  Replaces any tensors loaded before; call laya_finalize afterwards. */
+int laya_load_checkpoint(laya_engine* e, const char* path);
+
+/* Host only: parses the safetensors header at `path` and checks every tensor's byte range
+ * against the file, as laya_load_checkpoint does before uploading; returns the tensor count and
+ * their total element count.  LAYA_ERR_INVALID for a malformed or truncated file. */
+int laya_scan_checkpoint(const char* path, int64_t* tensors, int64_t* elements);
+
 /* After all tensors are loaded: checks completeness and builds the RoPE tables
  * (runtime.py:159-165) and the device-side weight layouts. */
 int laya_finalize(laya_engine* e);

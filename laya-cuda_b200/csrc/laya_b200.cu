@@ -10,8 +10,13 @@
 // (head buffers and forward), laya_cuda/ops.py (launch glue).
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
 
 #include <algorithm>
+#include <cerrno>
 #include <atomic>
 #include <cmath>
 #include <cstdarg>
@@ -22,7 +27,9 @@
 #include <map>
 #include <memory>
 #include <mutex>
+#include <set>
 #include <string>
+#include <thread>
 #include <tuple>
 #include <unordered_map>
 #include <vector>
@@ -32,6 +39,7 @@
 #include "rowops.cuh"
 #include "tc_attention.cuh"
 #include "gemm_ln.cuh"
+#include "checkpoint.cuh"
 
 using namespace laya;
 
@@ -606,6 +614,7 @@ struct Tensor {
   int dtype = LAYA_DTYPE_F32;  // storage dtype
   std::vector<int64_t> shape;
   size_t bytes = 0;
+  bool arena = false;          // inside the engine's weight arena (laya_load_checkpoint), not freed alone
 };
 
 struct ClassLayout {
@@ -672,6 +681,7 @@ struct Engine {
   float4* rope_tab[2] = {nullptr, nullptr};  // global / local theta, [16][rope_rows] (see GemmArgs)
   int rope_rows = 0;
   uint8_t* ws = nullptr;
+  void* arena = nullptr;       // every weight of the last laya_load_checkpoint, one allocation
   size_t ws_bytes = 0;
   size_t ws_generation = 0;
   Inflight inflight[2];
@@ -811,6 +821,205 @@ void* dev_alloc(size_t bytes) {
   void* p = nullptr;
   CK(cudaMalloc(&p, std::max<size_t>(bytes, 256)));
   return p;
+}
+
+void drop_graphs(Engine& e);
+
+// ---------------------------------------------------------------------------------------------
+// Checkpoint load (replaces runtime.py:147-158: safetensors read, per-tensor checks, upload)
+// ---------------------------------------------------------------------------------------------
+struct MappedFile {
+  int fd = -1;
+  void* base = nullptr;
+  size_t size = 0;
+  ~MappedFile() {
+    if (base) munmap(base, size);
+    if (fd >= 0) close(fd);
+  }
+};
+
+// Pinned host chunk, the device chunk it is uploaded into when the values need converting, and
+// the event that says both are free again.
+struct LoadStage {
+  void* host = nullptr;
+  void* dev = nullptr;
+  cudaEvent_t done = nullptr;
+  ~LoadStage() {
+    if (done) cudaEventDestroy(done);
+    if (host) cudaFreeHost(host);
+    if (dev) cudaFree(dev);
+  }
+};
+
+// memcpy split over host threads (a single thread copies from the page cache at a fraction of
+// what the host can do).
+void parallel_copy(void* dst, const void* src, size_t n) {
+  static const int threads = std::max(1, std::min(16, (int)std::thread::hardware_concurrency()));
+  if (n < (size_t(4) << 20) || threads == 1) {
+    memcpy(dst, src, n);
+    return;
+  }
+  const size_t per = (n / threads + 4095) & ~size_t(4095);
+  std::vector<std::thread> pool;
+  for (size_t off = 0; off < n; off += per) {
+    const size_t len = std::min(per, n - off);
+    pool.emplace_back([=] { memcpy(static_cast<char*>(dst) + off, static_cast<const char*>(src) + off, len); });
+  }
+  for (auto& t : pool) t.join();
+}
+
+void release_weights(Engine& e) {
+  CK(cudaStreamSynchronize(e.stream));
+  drop_graphs(e);
+  for (auto& kv : e.weights)
+    if (kv.second.ptr && !kv.second.arena) cudaFree(kv.second.ptr);
+  e.weights.clear();
+  e.wmaps.clear();
+  if (e.arena) CK(cudaFree(e.arena));
+  e.arena = nullptr;
+  e.finalized = false;
+}
+
+// The parsed header of a mapped safetensors file (offsets checked against the file size).
+struct Checkpoint {
+  MappedFile file;
+  std::map<std::string, StEntry> entries;
+  uint64_t data0 = 0;
+  const uint8_t* bytes() const { return static_cast<const uint8_t*>(file.base); }
+};
+
+void open_checkpoint(const char* path, Checkpoint& c) {
+  MappedFile& f = c.file;
+  f.fd = open(path, O_RDONLY | O_CLOEXEC);
+  if (f.fd < 0) fail(LAYA_ERR_INVALID, "cannot open %s: %s", path, strerror(errno));
+  struct stat sb;
+  if (fstat(f.fd, &sb) != 0) fail(LAYA_ERR_INVALID, "cannot stat %s", path);
+  f.size = (size_t)sb.st_size;
+  if (f.size < 8) fail(LAYA_ERR_INVALID, "%s is not a safetensors file", path);
+  f.base = mmap(nullptr, f.size, PROT_READ, MAP_PRIVATE, f.fd, 0);
+  if (f.base == MAP_FAILED) {
+    f.base = nullptr;
+    fail(LAYA_ERR_INVALID, "cannot map %s", path);
+  }
+  madvise(f.base, f.size, MADV_SEQUENTIAL);
+  const uint8_t* file = c.bytes();
+  uint64_t header = 0;
+  for (int i = 7; i >= 0; --i) header = (header << 8) | file[i];  // little-endian length
+  if (header > f.size - 8) fail(LAYA_ERR_INVALID, "%s: header length %llu exceeds the file", path, (unsigned long long)header);
+  try {
+    c.entries = StHeaderParser(reinterpret_cast<const char*>(file + 8), (size_t)header).parse();
+  } catch (const std::exception& x) {
+    fail(LAYA_ERR_INVALID, "%s: %s", path, x.what());
+  }
+  c.data0 = 8 + header;
+  for (auto& kv : c.entries) {
+    const StEntry& en = kv.second;
+    uint64_t elems = 1;
+    for (int64_t v : en.shape) elems *= (uint64_t)v;
+    if (en.end - en.begin != elems * st_dtype_bytes(en.dtype) || c.data0 + en.end > f.size)
+      fail(LAYA_ERR_INVALID, "%s: data of tensor %s is out of range", path, kv.first.c_str());
+  }
+}
+
+// Reads a safetensors checkpoint into the engine: checks names and shapes against the
+// adapter's tensor list (the reference's messages), places every tensor in one device arena,
+// and streams the file through two pinned chunks: while chunk i uploads (and converts on the
+// device), chunk i+1 is copied out of the mapped file by several host threads.
+void load_checkpoint(Engine& e, const char* path) {
+  Checkpoint ck;
+  open_checkpoint(path, ck);
+  const std::map<std::string, StEntry>& entries = ck.entries;
+  const uint8_t* file = ck.bytes();
+  const uint64_t data0 = ck.data0;
+  std::set<std::string> want, got;
+  for (auto& kv : e.expected) want.insert(kv.first);
+  for (auto& kv : entries) got.insert(kv.first);
+  if (want != got) fail(LAYA_ERR_INVALID, "Checkpoint tensor names do not match the Laya adapter");
+  struct Planned {
+    std::string name;
+    const StEntry* src;
+    int64_t elems, rows, cols;
+    int store;         // kStoreF32 / F16 / BF16
+    int64_t interleave;
+    size_t offset, bytes;
+  };
+  std::vector<Planned> plan;
+  size_t arena_bytes = 0;
+  for (auto& kv : entries) {
+    const StEntry& en = kv.second;
+    if (en.shape != e.expected[kv.first]) fail(LAYA_ERR_INVALID, "Incompatible tensor shape: %s", kv.first.c_str());
+    int64_t elems = 1;
+    for (int64_t v : en.shape) elems *= v;
+    if (kv.first == "temperature") continue;  // calibration is read by the adapter (laya.py:145-150)
+    Planned p;
+    p.name = kv.first;
+    p.src = &en;
+    p.elems = elems;
+    p.rows = en.shape.size() >= 2 ? en.shape[0] : 1;
+    p.cols = elems / std::max<int64_t>(p.rows, 1);
+    const bool is16 = stored_16bit(kv.first);
+    p.store = !is16 ? kStoreF32 : e.bf16() ? kStoreBF16 : kStoreF16;
+    p.interleave = kv.first.find("mlp.Wi.weight") != std::string::npos ? p.rows / 2 : 0;
+    if (p.interleave % 64) fail(LAYA_ERR_INVALID, "intermediate size must be a multiple of 64");
+    p.bytes = (size_t)elems * (is16 ? 2 : 4);
+    p.offset = arena_bytes;
+    arena_bytes = align_up(arena_bytes + p.bytes, 256);
+    plan.push_back(p);
+  }
+  // Stream the file in order, so the page cache and the disk read sequentially.
+  std::sort(plan.begin(), plan.end(), [](const Planned& a, const Planned& b) { return a.src->begin < b.src->begin; });
+
+  release_weights(e);
+  e.arena = dev_alloc(arena_bytes);
+  constexpr size_t kChunk = size_t(32) << 20;
+  LoadStage stage[2];
+  for (auto& s : stage) {
+    CK(cudaHostAlloc(&s.host, kChunk, cudaHostAllocDefault));
+    s.dev = dev_alloc(kChunk);
+    CK(cudaEventCreateWithFlags(&s.done, cudaEventDisableTiming));
+  }
+  bool used[2] = {false, false};
+  int next = 0;
+  for (const Planned& p : plan) {
+    const int esz = st_dtype_bytes(p.src->dtype);
+    const bool direct = p.interleave == 0 && ((p.store == kStoreF32 && p.src->dtype == StDtype::F32) ||
+                                              (p.store == kStoreF16 && p.src->dtype == StDtype::F16) ||
+                                              (p.store == kStoreBF16 && p.src->dtype == StDtype::BF16));
+    uint8_t* dst = static_cast<uint8_t*>(e.arena) + p.offset;
+    const int64_t row_bytes = p.cols * esz;
+    const int64_t rows_per_chunk = std::max<int64_t>(1, (int64_t)kChunk / row_bytes);
+    if (row_bytes > (int64_t)kChunk) fail(LAYA_ERR_INVALID, "tensor %s has rows longer than the staging chunk", p.name.c_str());
+    for (int64_t r0 = 0; r0 < p.rows; r0 += rows_per_chunk) {
+      const int64_t nr = std::min(rows_per_chunk, p.rows - r0);
+      const size_t nbytes = (size_t)(nr * row_bytes);
+      LoadStage& s = stage[next];
+      if (used[next]) CK(cudaEventSynchronize(s.done));
+      used[next] = true;
+      next ^= 1;
+      parallel_copy(s.host, file + data0 + p.src->begin + (size_t)(r0 * row_bytes), nbytes);
+      if (direct) {
+        CK(cudaMemcpyAsync(dst + (size_t)(r0 * row_bytes), s.host, nbytes, cudaMemcpyHostToDevice, e.stream));
+      } else {
+        CK(cudaMemcpyAsync(s.dev, s.host, nbytes, cudaMemcpyHostToDevice, e.stream));
+        const int64_t n = nr * p.cols;
+        const int grid = (int)std::min<int64_t>((n + 255) / 256, (int64_t)e.sms * 8);
+        convert_rows_kernel<<<grid, 256, 0, e.stream>>>(s.dev, (int)p.src->dtype, dst, p.store, r0, nr, p.cols,
+                                                         p.interleave);
+        CK(cudaGetLastError());
+      }
+      CK(cudaEventRecord(s.done, e.stream));
+    }
+  }
+  CK(cudaStreamSynchronize(e.stream));
+  for (const Planned& p : plan) {
+    Tensor t;
+    t.ptr = static_cast<uint8_t*>(e.arena) + p.offset;
+    t.shape = p.src->shape;
+    t.bytes = p.bytes;
+    t.arena = true;
+    t.dtype = p.store == kStoreF32 ? LAYA_DTYPE_F32 : p.store == kStoreBF16 ? LAYA_DTYPE_BF16 : LAYA_DTYPE_F16;
+    e.weights[p.name] = t;
+  }
 }
 
 void drop_graphs(Engine& e) {
@@ -1357,13 +1566,38 @@ int laya_load_tensor(laya_engine* h, const char* name, int dtype, const int64_t*
   }
   auto old = e.weights.find(n);
   if (old != e.weights.end() && old->second.ptr) {
-    CK(cudaFree(old->second.ptr));
+    if (!old->second.arena) CK(cudaFree(old->second.ptr));
     e.wmaps.clear();
   }
   t.ptr = dev_alloc(t.bytes);
   CK(cudaMemcpy(t.ptr, src, t.bytes, cudaMemcpyHostToDevice));
   e.weights[n] = t;
   e.finalized = false;
+  API_END(h)
+}
+
+int laya_scan_checkpoint(const char* path, int64_t* tensors, int64_t* elements) {
+  API_BEGIN
+  if (!path || !tensors || !elements) fail(LAYA_ERR_INVALID, "null argument");
+  Checkpoint ck;
+  open_checkpoint(path, ck);
+  int64_t n = 0;
+  for (auto& kv : ck.entries) {
+    int64_t c = 1;
+    for (int64_t v : kv.second.shape) c *= v;
+    n += c;
+  }
+  *tensors = (int64_t)ck.entries.size();
+  *elements = n;
+  API_END(nullptr)
+}
+
+int laya_load_checkpoint(laya_engine* h, const char* path) {
+  API_BEGIN
+  if (!h || !path) fail(LAYA_ERR_INVALID, "null argument");
+  Engine& e = h->impl;
+  CK(cudaSetDevice(e.device));
+  load_checkpoint(e, path);
   API_END(h)
 }
 
@@ -1635,12 +1869,13 @@ int laya_destroy(laya_engine* h) {
     if (kv.second->graph) cudaGraphExecDestroy(kv.second->graph);
   e.slots.clear();
   for (auto& kv : e.weights)
-    if (kv.second.ptr) cudaFree(kv.second.ptr);
+    if (kv.second.ptr && !kv.second.arena) cudaFree(kv.second.ptr);
   e.weights.clear();
   for (int i = 0; i < 2; ++i) {
     if (e.rope_tab[i]) cudaFree(e.rope_tab[i]);
   }
   if (e.ws) cudaFree(e.ws);
+  if (e.arena) cudaFree(e.arena);
   for (auto& r : e.inflight) {
     if (r.h_packed) cudaFreeHost(r.h_packed);
     if (r.h_out) cudaFreeHost(r.h_out);

@@ -15,7 +15,7 @@ PRECISION_BF16, PRECISION_F16 = 0, 1
 
 # Every symbol declared in include/laya_b200.h.
 EXPORTS = (
-    "laya_create", "laya_load_tensor", "laya_finalize", "laya_predict", "laya_submit", "laya_collect",
+    "laya_create", "laya_load_tensor", "laya_load_checkpoint", "laya_scan_checkpoint", "laya_finalize", "laya_predict", "laya_submit", "laya_collect",
     "laya_shape_class",
     "laya_forward_device", "laya_packed_ints", "laya_pack", "laya_reserve", "laya_stream", "laya_set_profiling",
     "laya_profile_read", "laya_read_tensor", "laya_cached_shapes", "laya_pool_bytes", "laya_destroy",
@@ -55,6 +55,8 @@ def load():
     sig = {
         "laya_create": (i, [ct.POINTER(Config), i, i, ct.POINTER(p)]),
         "laya_load_tensor": (i, [p, ct.c_char_p, i, i64p, i, p]),
+        "laya_load_checkpoint": (i, [p, ct.c_char_p]),
+        "laya_scan_checkpoint": (i, [ct.c_char_p, i64p, i64p]),
         "laya_finalize": (i, [p]),
         "laya_predict": (i, [p, p, p, p, p, p, i, i, p, p, ct.POINTER(Metrics)]),
         "laya_submit": (i, [p, p, p, p, p, p, i, i, i64p]),

@@ -122,7 +122,6 @@ class _Slots:
 
 class Runtime:
     def __init__(self, adapter, device, max_cached_shapes=16, precision="float16"):
-        from safetensors import safe_open
         from . import _lib
         if precision not in PRECISIONS:
             raise ValueError("precision must be 'bfloat16' or 'float16'")
@@ -137,31 +136,15 @@ class Runtime:
         self._handle = handle
         try:
             shapes = adapter.weight_shapes()
-            with safe_open(str(adapter.path / "model.safetensors"), framework="numpy") as f:
-                if set(f.keys()) != set(shapes):
-                    raise ValueError("Checkpoint tensor names do not match the Laya adapter")
-                for name, shape in shapes.items():
-                    if tuple(f.get_slice(name).get_shape()) != shape:
-                        raise ValueError(f"Incompatible tensor shape: {name}")
-                for name, shape in shapes.items():
-                    if name == "temperature":
-                        continue
-                    self._upload(name, f.get_tensor(name))
+            # The library maps the file, checks names and shapes (the reference's ValueErrors) and
+            # streams it to the device (runtime.py:147-158 of the reference).
+            path = str(adapter.path / "model.safetensors").encode()
+            _lib.check(self._lib.laya_load_checkpoint(self._handle, path), self._handle)
             _lib.check(self._lib.laya_finalize(self._handle), self._handle)
             self.weights = _Weights(self, shapes)
         except BaseException:
             self.close()
             raise
-
-    def _upload(self, name, array):
-        from . import _lib
-        if array.dtype == np.float16:
-            dtype, host = _lib.DTYPE_F16, np.ascontiguousarray(array)
-        else:
-            dtype, host = _lib.DTYPE_F32, np.ascontiguousarray(array, dtype=np.float32)
-        shape = (ct.c_int64 * host.ndim)(*host.shape)
-        _lib.check(self._lib.laya_load_tensor(self._handle, name.encode(), dtype, shape, host.ndim, _ptr(host)),
-                   self._handle)
 
     def predict(self, items, capture=True):
         """capture=True runs the class's CUDA graph (captured on first use) for classes of up

@@ -180,3 +180,58 @@ def test_gelu_erf_approximation_restated():
     xd = x.astype(np.float64)
     want = 0.5 * xd * (1 + np.array([math.erf(v / math.sqrt(2)) for v in xd]))
     assert np.max(np.abs(got - want)) < 6e-7
+
+
+def _scan(lib, path):
+    n, elems = ct.c_int64(), ct.c_int64()
+    code = lib.laya_scan_checkpoint(str(path).encode(), ct.byref(n), ct.byref(elems))
+    return code, n.value, elems.value
+
+
+def test_checkpoint_header_parser_matches_safetensors(lib, tmp_path):
+    """laya_scan_checkpoint parses the safetensors header the native loader uses: tensor count
+    and elements agree with the safetensors library on a synthetic checkpoint with metadata,
+    F32/F16/BF16 tensors and escaped names."""
+    from safetensors.numpy import save_file
+    from laya_cuda import synthetic as S
+    arch = S.architecture("tiny", layers=2)
+    weights = S.make_weights(arch, seed=1)
+    weights["encoder.final_norm.weight"] = weights["encoder.final_norm.weight"].astype(np.float16)
+    weights['odd "name"\\é'] = np.zeros((2, 3), np.float32)
+    path = tmp_path / "model.safetensors"
+    save_file(weights, str(path), metadata={"format": "pt", "note": 'a "quoted" {value}'})
+    code, n, elems = _scan(lib, path)
+    assert code == 0, lib.laya_last_error(None)
+    assert n == len(weights) and elems == sum(v.size for v in weights.values())
+    # bfloat16 through the torch writer, when present.
+    torch = pytest.importorskip("torch")
+    from safetensors.torch import save_file as save_torch
+    save_torch({"a": torch.zeros(4, 5, dtype=torch.bfloat16), "b": torch.ones(7)}, str(tmp_path / "bf.safetensors"))
+    assert _scan(lib, tmp_path / "bf.safetensors") == (0, 2, 27)
+
+
+@pytest.mark.parametrize("damage", ["truncated", "header", "offsets", "json", "dtype", "empty"])
+def test_checkpoint_header_parser_rejects_malformed_files(lib, tmp_path, damage):
+    import json as _json
+    import struct
+    header = {"w": {"dtype": "F32", "shape": [2, 2], "data_offsets": [0, 16]}}
+    body = b"\0" * 16
+    if damage == "offsets":
+        header["w"]["data_offsets"] = [0, 20]
+    if damage == "dtype":
+        header["w"]["dtype"] = "I64"
+    text = _json.dumps(header).encode()
+    if damage == "json":
+        text = text[:-3]
+    blob = struct.pack("<Q", len(text)) + text + body
+    if damage == "truncated":
+        blob = blob[:-4]
+    if damage == "header":
+        blob = struct.pack("<Q", 1 << 40) + blob[8:]
+    if damage == "empty":
+        blob = b"\0\0"
+    path = tmp_path / "bad.safetensors"
+    path.write_bytes(blob)
+    code, _, _ = _scan(lib, path)
+    assert code == _lib.ERR_INVALID
+    assert lib.laya_last_error(None)
