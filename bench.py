@@ -201,6 +201,43 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_cold_load(args):
+    """--cold-load NAME: in this fresh process, the wall time of Engine(checkpoint) (CUDA
+    context, library, tokenizer, weight load and finalize) and of the first request after it (a
+    512-token question with 4 options: cold shape class, graph capture included).  The checkpoint
+    file is written beforehand, so it is read from the page cache, not from disk."""
+    from laya_cuda import synthetic as S
+    name = args.cold_load
+    overrides = {"max_len": 1024} if name == "laya" else {}
+    arch = S.architecture(name, **overrides)
+    CACHE.mkdir(parents=True, exist_ok=True)
+    path = S.cached_checkpoint(CACHE, name, seed=0, **overrides)
+    state, questions, _ = S.request_texts(np.random.default_rng(7), 512, 4, arch["vocab"])
+    size = (path / "model.safetensors").stat().st_size
+    t0 = time.perf_counter()
+    from laya_cuda import Engine
+    engine = Engine(path, device="cuda:0")
+    t1 = time.perf_counter()
+    engine.predict(state, questions)
+    t2 = time.perf_counter()
+    engine.predict(state, questions)
+    t3 = time.perf_counter()
+    engine.close()
+    print(json.dumps({"model": name, "load_s": round(t1 - t0, 3), "first_request_ms": round((t2 - t1) * 1000, 2),
+                      "second_request_ms": round((t3 - t2) * 1000, 3), "checkpoint_bytes": size}), flush=True)
+
+
+def cold_loads(names):
+    """Cold Engine construction and first request per model, each in a fresh process."""
+    out = {}
+    for name in names:
+        run = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--cold-load", name], capture_output=True,
+                             text=True, timeout=600)
+        lines = [l for l in run.stdout.splitlines() if l.startswith("{")]
+        out[name] = json.loads(lines[-1]) if run.returncode == 0 and lines else {"error": run.stderr[-300:]}
+    return out
+
+
 def percentiles(values):
     return {"p50_ms": round(float(np.percentile(values, 50)), 4), "p95_ms": round(float(np.percentile(values, 95)), 4)}
 
@@ -397,6 +434,7 @@ def run_engine(args, rank, world, local_rank):
                 # Configuration 4: the typed-decisions geometry (1024 context) through BatchEngine.
                 typed = S.architecture("laya-typed-decisions")
                 stream = stream_latency(S.cached_checkpoint(CACHE, "laya-typed-decisions", seed=0), typed)
+        loads = cold_loads(["laya", "laya-multilingual"]) if world == 1 and args.latency != "none" else None
         cpu = None
         if world == 1 and args.cpu_budget > 0:
             weights = S.make_weights(arch, seed=0)
@@ -416,7 +454,7 @@ def run_engine(args, rank, world, local_rank):
                 "gpu_launches": launches * args.steps, "kernels": fam,
                 "kernels_note": "per family over one profiled step (event pair around every launch), after the timed steps",
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
-                "clocks": clocks.summary(), "latency_batch1": lat, "stream_config4": stream,
+                "clocks": clocks.summary(), "latency_batch1": lat, "stream_config4": stream, "cold_load": loads,
                 "attention_flops_per_step": attention_flops([len(i[0]) for i in items], arch)}
     engine.close()
     if world > 1:
@@ -447,9 +485,13 @@ def main():
                         help="only the batch-1 latencies of the laya geometry (for profiler captures)")
     parser.add_argument("--lengths", default="83,512,1024", help="sequence lengths of --latency-only")
     parser.add_argument("--repeats", type=int, default=200, help="timed repeats per length of --latency-only")
+    parser.add_argument("--cold-load", default=None, help="time Engine construction + first request of this model "
+                                                          "in this fresh process (used by the main run)")
     args = parser.parse_args()
     if args.latency_only:
         return run_latency_only(args)
+    if args.cold_load:
+        return run_cold_load(args)
     if args.warmup < 3:
         parser.error("--warmup must be at least 3")
     rank = int(os.environ.get("RANK", 0))

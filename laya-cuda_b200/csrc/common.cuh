@@ -84,16 +84,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
                                           volatile int* abort, unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
+  // try_wait may suspend the thread for a while before it reports an incomplete phase, so the
+  // limit and the abort flag are checked after every attempt.
   const unsigned long long start = global_ns();
-  for (uint32_t spin = 1;; ++spin) {
+  for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((spin & 63) == 0) {
-      if (*abort) return false;
-      if (global_ns() - start > limit_ns) {
-        *abort = 1;
-        if (err) atomicCAS(err, 0, code);
-        return false;
-      }
+    if (*abort) return false;
+    if (global_ns() - start > limit_ns) {
+      *abort = 1;
+      if (err) atomicCAS(err, 0, code);
+      return false;
     }
   }
 }

@@ -57,16 +57,18 @@ def gemm_store(lib, x, w, out):
     M, K = x.shape
     N = w.shape[0]
     stream = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
-    # 1-CTA kernel with 128-column tiles (block_n 128), plain store epilogue.
+    # 1-CTA kernel with 64-column tiles (block_n 64), plain store epilogue.
     _lib.check(lib.laya_op_gemm(_lib.PRECISION_F16, 0, ptr(x), ptr(w), M, N, K, ptr(out), N, None, 0, None, 0, None,
-                                0, None, 1, 128, ptr(err), stream))
+                                0, None, 1, 64, ptr(err), stream))
     torch.cuda.synchronize()
     return int(err.item())
 
 
 def test_gemm_wait_limit_runs_out_then_recovers(lib):
+    """One 128 x 64 tile over K = 65536 (1024 k-blocks): its epilogue waits for the accumulator
+    for well over 100 us, far past a 1 ns limit however long one try_wait suspends."""
     rng = np.random.default_rng(6)
-    M, N, K = 1024, 768, 3072
+    M, N, K = 128, 64, 65536
     x = torch.from_numpy(rng.normal(0, 1, (M, K)).astype(np.float32)).half().cuda()
     w = torch.from_numpy(rng.normal(0, 0.02, (N, K)).astype(np.float32)).half().cuda()
     expected = x.double().cpu().numpy() @ w.double().cpu().numpy().T
