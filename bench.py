@@ -155,6 +155,47 @@ def oracle_rate(arch, weights, items, budget_s):
     return done / (time.perf_counter() - t0), done
 
 
+def oracle_answer(adapter, oracle, state, questions):
+    """The answer dict of one request with the FP32 oracle as the forward pass: the adapter's
+    request contract and decoding around the CPU restatement."""
+    items = adapter.prepare(state, questions)
+    outs = [oracle.item(*item) for item in items]
+    logits = np.zeros((len(items), max(len(item[1]) for item in items)), np.float32)
+    for i, (option_logits, _) in enumerate(outs):
+        logits[i, :len(option_logits)] = option_logits
+    return adapter.decode(logits, np.stack([acts for _, acts in outs]).astype(np.float32), questions, items)
+
+
+def cpu_checks(engine, arch, weights, repeats=30):
+    """The cpu_baseline leg's other two parts, both with the FP32 oracle on the host cores:
+    configuration 1 (batch 1, one 83-token question with 4 options: tokenise, forward, decode)
+    as p50/p95 latency; and the reference's answer gates (laya_cuda.gates, benchmarks/run.py:23
+    of the reference) between this engine and the oracle on the frozen request set."""
+    from laya_cuda import gates
+    from laya_cuda import synthetic as S
+    sys.path.insert(0, str(ROOT))
+    from oracle.laya_oracle import Oracle
+    oracle = Oracle(weights, arch)
+    state, questions, _ = S.request_texts(np.random.default_rng(0), 83, 4, arch["vocab"])
+    times = []
+    for i in range(repeats + 3):
+        t0 = time.perf_counter()
+        oracle_answer(engine.adapter, oracle, state, questions)
+        if i >= 3:
+            times.append((time.perf_counter() - t0) * 1000)
+    config1 = {"p50_ms": round(float(np.percentile(times, 50)), 2), "p95_ms": round(float(np.percentile(times, 95)), 2),
+               "repeats": repeats, "cores": os.cpu_count(), "kind": "port",
+               "sample": "83-token request, 1 question x 4 options, FP32 numpy oracle (all host threads)"}
+    requests = list(gates.frozen_requests(engine.adapter))
+    candidate = gates.answers(engine, requests)
+    reference = [{"id": rid, "answers": oracle_answer(engine.adapter, oracle, st, qs)["answers"]}
+                 for rid, st, qs in requests]
+    stats = gates.compare(candidate, reference)
+    gate = {"requests": len(requests), "reference": "FP32 oracle", "thresholds": gates.GATES,
+            **{k: (round(v, 8) if isinstance(v, float) else v) for k, v in stats.items()}, "passed": gates.passes(stats)}
+    return config1, gate
+
+
 def run_reference(args, rank, world):
     """--impl reference: the CPU implementation of this path (the oracle restatement; the
     reference's own path needs CuPy and a GPU), timed on this host's cores."""
@@ -441,6 +482,7 @@ def run_engine(args, rank, world, local_rank):
             rate, n = oracle_rate(arch, weights, items, args.cpu_budget)
             cpu = {"value": round(rate, 3), "unit": "sequences/s", "cores": os.cpu_count(), "kind": "port",
                    "sample": f"first {n} sequences of the rank-0 workload, FP32 numpy oracle, all host threads"}
+            cpu["config1_batch1"], cpu["gates"] = cpu_checks(engine, arch, weights)
         line = {"metric": "sequences/s", "value": round(value, 2), "unit": "sequences/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
