@@ -397,16 +397,17 @@ TilePlan plan_small(int M, int N, int K, int epi, bool split_ok, bool pair_ok, i
   return best;
 }
 
-// Tensor maps of the tcgen05 attention over a qkv buffer of M tokens: 128-row tiles of the q/k
-// planes, and 64 dims x 64 keys tiles of V^T.
+// Tensor maps of the tcgen05 attention over a qkv buffer of M tokens: 128-row (query tile) and
+// 64-row (key block) boxes of the q/k planes, and 64 dims x 64 keys boxes of V^T.
 struct AttnMaps {
-  CUtensorMap qk, vt;
+  CUtensorMap q, k, vt;
 };
 AttnMaps attn_maps(const void* qkv, int M, int heads, bool bf) {
   const int64_t hm = (int64_t)heads * M;
   AttnMaps m;
-  m.qk = make_map(qkv, 3 * hm, 64, kTcQ, bf);
-  m.vt = make_map(static_cast<const uint8_t*>(qkv) + (size_t)2 * hm * 64 * 2, (int64_t)heads * 64, M, 64, bf);
+  m.q = make_map(qkv, 3 * hm, 64, kTcQ, bf);
+  m.k = make_map(qkv, 3 * hm, 64, kTcKB, bf);
+  m.vt = make_map(static_cast<const uint8_t*>(qkv) + (size_t)2 * hm * 64 * 2, (int64_t)heads * 64, M, kTcKB, bf);
   return m;
 }
 
@@ -424,7 +425,8 @@ void launch_tc_attention(const AttnMaps& maps, const TcAttnArgs& args, int n_til
   if (n_tiles > 65535) fail(LAYA_ERR_INVALID, "%d attention tiles exceed the grid limit", n_tiles);
   if (a.splits != 1 && a.splits != 2) fail(LAYA_ERR_INVALID, "attention key split %d (1 or 2)", a.splits);
   if (a.splits == 1) {
-    launch_k(tc_attention_kernel<T>, dim3(a.heads, n_tiles), dim3(kTcThreads), TcAttnSmem::kBytes, st, maps.qk, maps.vt, a);
+    launch_k(tc_attention_kernel<T>, dim3(a.heads, n_tiles), dim3(kTcThreads), TcAttnSmem::kBytes, st, maps.q, maps.k,
+             maps.vt, a);
     return;
   }
   cudaLaunchConfig_t cfg = {};
@@ -441,7 +443,7 @@ void launch_tc_attention(const AttnMaps& maps, const TcAttnArgs& args, int n_til
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  CK(cudaLaunchKernelEx(&cfg, tc_attention_kernel<T>, maps.qk, maps.vt, a));
+  CK(cudaLaunchKernelEx(&cfg, tc_attention_kernel<T>, maps.q, maps.k, maps.vt, a));
 }
 
 // Key split of the tcgen05 attention: two CTAs per tile when one CTA per tile and head would
@@ -450,7 +452,7 @@ void launch_tc_attention(const AttnMaps& maps, const TcAttnArgs& args, int n_til
 // attention 11.0 -> 9.7 us after the dependency wait; split window-64 tiles (two blocks) were
 // 1 us slower, the merge costing more than the block it saves.
 int attention_splits(int heads, int n_tiles, int sms, int window, int row_keys) {
-  return window < 0 && row_keys >= 3 * kTcKB && heads * n_tiles <= sms ? 2 : 1;
+  return window < 0 && row_keys >= 384 && heads * n_tiles <= sms ? 2 : 1;
 }
 
 // Row kernels are instantiated per width (d = 32 * NPL, d a multiple of 64 up to 1024).

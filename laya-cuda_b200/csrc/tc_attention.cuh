@@ -5,27 +5,30 @@
 // tokens past the last row produce zeros.
 //
 // Work unit: one CTA per (128-query tile of one row, head); the host's tile table never lets a
-// tile straddle rows.  Two CTAs share an SM (82 KB shared memory and 256 TMEM columns each).
-// 4 warps, one thread per query row (warp w owns TMEM lanes [32w, 32w + 32)).  Every warp runs
-// the softmax: it loads its rows of S_j with all loads in flight before one wait, masks only the
-// 32-key chunks that straddle a boundary and skips chunks no query of the warp can see, keeps
-// the running maximum m and sum l in fp32 (paired fp32 instructions for the scale-and-subtract
-// and the sums), and writes P = 2^(s*log2e/8 - m) as 16-bit pairs into TMEM columns [128,192).
-// O stays in TMEM: it is rescaled (read, scaled, written back) only when the row maximum grows
-// by more than 2^8, so P is at most 256 and the final O / l is unchanged.  Warp 0 also controls
-// the pipeline (TMEM allocation; one lane issues copies and MMAs):
-//   TMA   the Q tile, then per 128-key block the K tile and the V^T tile into double-buffered
-//         stages (128-byte swizzle, no multicast), each refilled once warp 0 has observed the
-//         completion of the MMA that last read it;
-//   S_j = Q K_j^T   (M=128, N=128, K=64)  TMEM columns [0,128), fp32, issued as soon as every
-//         warp has read S_{j-1}, so the tensor core works on the next block during the softmax;
-//   O += P_j V_j    (M=128, N=64, K=128)  A = P from TMEM, O in [192,256), issued as soon as
-//         every warp has written P_j.
+// tile straddle rows.  4 warps, one thread per query row (warp w owns TMEM lanes [32w, 32w+32)).
+// The kernel is bound by instruction latency in the softmax, not by a pipe's throughput, so it
+// is laid out for many resident warps: a CTA holds 128 TMEM columns and ~50 KB of shared memory,
+// so four CTAs (16 warps) share an SM and hide each other's waits.
+//
+// TMEM per CTA: S_j = Q K_j^T for a block of 64 keys in columns [0, 64) (fp32); the softmax
+// reads S_j into registers and writes P_j = 2^(s log2e / 8 - m) as 16-bit pairs over its first
+// 32 columns; O in columns [64, 128).  The tensor core executes a CTA's MMAs in issue order, so
+// the control lane issues O += P_j V_j and S_{j+1} = Q K_{j+1}^T back to back: S_{j+1} overwrites
+// P_j only after the P V product has read it, and the single commit after S_{j+1} tells the
+// softmax warps both that S_{j+1} is ready and that O is settled (for the rare rescale).  Per
+// block the warps wait on one barrier (s_full) and arrive on one (p_full).
+//
+// Warp 0 also controls the pipeline (TMEM allocation; one lane issues copies and MMAs):
+//   TMA   the Q tile once, then per 64-key block the K tile and the V^T tile into double-buffered
+//         stages (128-byte swizzle, no multicast); a stage is refilled once the commit that
+//         covers the MMA reading it has been observed;
+//   MMA   S_j (M=128, N=64, K=64), O += P_j V_j (M=128, N=64, K=64, A = P from TMEM).
+// The softmax masks only 32-key chunks that straddle the window or row end and skips chunks no
+// query of its warp can see; it keeps the running maximum m and sum l in fp32 (paired fp32
+// instructions for the scale-and-subtract and the sums); O stays in TMEM and is rescaled (read,
+// scaled, written back) only when a row maximum grows by more than 2^8, so P <= 256 and the final
+// O / l is unchanged.  Key blocks start at the window's first key (rounded down to 16 tokens).
 // Small grids (batch-1 classes) split each tile's key blocks over a CTA pair (TcAttnArgs::splits).
-// Without separate copy and MMA warps the CTA has 128 threads, so two CTAs per SM leave each
-// thread 255 registers (the softmax keeps a 128-key row of S in registers without spilling).
-// Key blocks start at the window's first key (rounded down to 16 tokens), not at a multiple of
-// 128, so a 128-query tile of a window-64 layer reads two blocks.
 // Inputs (from the QKV GEMM epilogue): Q, K [heads][M][64] (K-major rows of 128 bytes) and V
 // transposed [heads][64][M], so every shared-memory operand is K-major, as in gemm.cuh.  Every
 // wait is bounded and reports through the error word.
@@ -35,9 +38,10 @@
 namespace laya {
 
 constexpr int kTcQ = 128;              // queries per CTA
-constexpr int kTcKB = 128;             // keys per block
+constexpr int kTcKB = 64;              // keys per block
 constexpr int kTcThreads = 128;
-constexpr int kTcTmemCols = 256;       // S: [0,128), P: [128,192), O: [192,256)
+constexpr int kTcCtasPerSm = 4;
+constexpr int kTcTmemCols = 128;       // S / P: [0, 64), O: [64, 128)
 constexpr float kTcRescaleLog2 = 8.f;  // O is rescaled when the row maximum grows by more than 2^8
 
 struct TcAttnArgs {
@@ -66,30 +70,32 @@ struct TcAttnArgs {
 
 struct TcAttnSmem {
   static constexpr int kQ = kTcQ * 128;            // 16 KB: [128 queries][64 dims]
-  static constexpr int kK = kTcKB * 128;           // 16 KB per stage: [128 keys][64 dims]
-  static constexpr int kV = 2 * 64 * 128;          // 16 KB per stage: two [64 dims][64 keys] tiles
+  static constexpr int kK = kTcKB * 128;           // 8 KB per stage: [64 keys][64 dims]
+  static constexpr int kV = 64 * kTcKB * 2;        // 8 KB per stage: [64 dims][64 keys]
   static constexpr int kStages = 2;
   static constexpr int kOffQ = 0, kOffK = kQ, kOffV = kQ + kStages * kK;
   static constexpr int kOffBar = kOffV + kStages * kV;
   static constexpr int kBytes = kOffBar + 256 + 1024;  // barriers + alignment slack
 };
+static_assert(kTcCtasPerSm * (TcAttnSmem::kBytes + 1024) <= 228 * 1024, "shared memory of the resident CTAs");
+static_assert(kTcCtasPerSm * kTcTmemCols <= 512, "TMEM of the resident CTAs");
 
-// Softmax helpers for one thread's row of a 128-key block held in registers as four 32-key
-// chunks (raw fp32 scores).  `vis` bit c: chunk c is loaded (some query of the warp sees one of
-// its keys); `full` bit c: every query of the warp sees every key of chunk c (no mask).  Both
-// are warp-uniform; kAll = every chunk visible and full (the common case of global layers),
-// which compiles without a branch.
+// Softmax helpers for one thread's row of a 64-key block held in registers as two 32-key chunks
+// (raw fp32 scores).  `vis` bit c: chunk c is loaded (some query of the warp sees one of its
+// keys); `full` bit c: every query of the warp sees every key of chunk c (no mask).  Both are
+// warp-uniform; kAll = both chunks visible and full (the common case of global layers), which
+// compiles without a branch.
 //
 // Masks the scores this thread's query may not see to -inf and returns the block maximum.
 // Key ck + i is visible iff (unsigned)(ck + i - lo_key) <= span_keys.
 template <bool kAll>
-__device__ __forceinline__ float tc_block_max(uint32_t (&sx)[4][32], uint32_t vis, uint32_t full, int kb, int lo_key,
+__device__ __forceinline__ float tc_block_max(uint32_t (&sx)[2][32], uint32_t vis, uint32_t full, int kb, int lo_key,
                                               uint32_t span_keys) {
   float mx[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < 2; ++c) {
     if (!kAll && !((vis >> c) & 1)) continue;
     if (!kAll && !((full >> c) & 1)) {
       const int d = kb + 32 * c - lo_key;
@@ -111,12 +117,12 @@ __device__ __forceinline__ float tc_block_max(uint32_t (&sx)[4][32], uint32_t vi
 // P = 2^(s * scale - sub) for the loaded chunks (zeros for the others), stored as 16-bit pairs
 // into TMEM columns p_tmem + 16c; returns the row sum of the fp32 probabilities.
 template <bool kAll, typename T>
-__device__ __forceinline__ float tc_block_probs(const uint32_t (&sx)[4][32], uint32_t vis, float scale, float sub,
+__device__ __forceinline__ float tc_block_probs(const uint32_t (&sx)[2][32], uint32_t vis, float scale, float sub,
                                                 uint32_t p_tmem) {
   float2 sm[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
   const float2 sc = make_float2(scale, scale), ns = make_float2(-sub, -sub);
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < 2; ++c) {
     uint32_t pk[16];
     if (kAll || ((vis >> c) & 1)) {
 #pragma unroll
@@ -137,9 +143,9 @@ __device__ __forceinline__ float tc_block_probs(const uint32_t (&sx)[4][32], uin
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __grid_constant__ CUtensorMap tmQK,
-                                                                    const __grid_constant__ CUtensorMap tmVt,
-                                                                    const TcAttnArgs a) {
+__global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
+    tc_attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmVt, const TcAttnArgs a) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // The tile table, starts and lengths are written by the host before the forward pass, so they
   // are read before waiting on the previous kernel.
@@ -179,7 +185,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
     k_hi = min(valid, q0 + kTcQ + a.window);
   }
   const int all_blocks = k_hi > k_lo ? (k_hi - k_lo + kTcKB - 1) / kTcKB : 0;
-  // Key split: this CTA's share of the tile's blocks (k_lo stays 16-aligned: 128-key steps).
+  // Key split: this CTA's share of the tile's blocks (k_lo stays 16-aligned: 64-key steps).
   const bool split = a.splits > 1;
   const uint32_t rank = split ? cluster_rank() : 0;
   int n_blocks = all_blocks;
@@ -197,12 +203,11 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
   uint64_t* q_full = bar + 0;
   uint64_t* k_full = bar + 1;   // [2]
   uint64_t* v_full = bar + 3;   // [2]
-  uint64_t* s_full = bar + 5;
-  uint64_t* s_free = bar + 6;
-  uint64_t* p_full = bar + 7;
-  uint64_t* o_full = bar + 8;
-  uint64_t* drain = bar + 9;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 10);
+  uint64_t* s_full = bar + 5;   // S_j ready, and every earlier MMA (so O) complete
+  uint64_t* p_full = bar + 6;   // every warp wrote P_j
+  uint64_t* o_full = bar + 7;   // the last P V product complete
+  uint64_t* drain = bar + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const unsigned long long wait_ns = wait_limit(a.wait_ns);
 
@@ -213,10 +218,11 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
   if (threadIdx.x == 0) {
     mbar_init(q_full, gathered ? 4 : 1);  // gathered: the four warps write Q
     for (int s = 0; s < 2; ++s) { mbar_init(k_full + s, 1); mbar_init(v_full + s, 1); }
-    mbar_init(s_full, 1); mbar_init(s_free, 4); mbar_init(p_full, 4); mbar_init(o_full, 1); mbar_init(drain, 1);
+    mbar_init(s_full, 1); mbar_init(p_full, 4); mbar_init(o_full, 1); mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
-    tma_prefetch_desc(&tmQK);
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmVt);
   }
   if (ctl) { tmem_alloc(tmem_slot, kTcTmemCols); tmem_relinquish(); }
@@ -228,27 +234,24 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
 
   constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
   const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
-  const uint32_t s_tmem = tmem_base + lane_addr, p_tmem = s_tmem + 128, o_tmem = s_tmem + 192;
+  const uint32_t s_tmem = tmem_base + lane_addr, p_tmem = s_tmem, o_tmem = s_tmem + 64;
   const int plane_rows = a.heads * a.M;
   int k_issued = 0, v_issued = 0;  // copies issued (control lane)
-  // Copies into stage j & 1; the control warp issues one only after observing the completion of
-  // the MMA that last read the stage (S_{j-2} for K, P_{j-2} V_{j-2} for V).
+  // Copies into stage j & 1 (control lane), issued once the commit covering the MMA that last
+  // read the stage has been observed (S_{j-2} for K, P_{j-2} V_{j-2} for V).
   auto load_k = [&](int j) {
     const int st = j & 1;
     mbar_arrive_expect_tx(k_full + st, TcAttnSmem::kK);
-    tma_load_2d(sK + st * TcAttnSmem::kK, &tmQK, k_full + st, 0, plane_rows + head * a.M + first + k_lo + j * kTcKB);
+    tma_load_2d(sK + st * TcAttnSmem::kK, &tmK, k_full + st, 0, plane_rows + head * a.M + first + k_lo + j * kTcKB);
     k_issued = j + 1;
   };
   auto load_v = [&](int j) {
     const int st = j & 1;
     mbar_arrive_expect_tx(v_full + st, TcAttnSmem::kV);
-    uint8_t* v = sV + st * TcAttnSmem::kV;
-    const int key0 = first + k_lo + j * kTcKB;  // absolute token of the block's first key
-    tma_load_2d(v, &tmVt, v_full + st, key0, head * 64);
-    tma_load_2d(v + 64 * 128, &tmVt, v_full + st, key0 + 64, head * 64);
+    tma_load_2d(sV + st * TcAttnSmem::kV, &tmVt, v_full + st, first + k_lo + j * kTcKB, head * 64);
     v_issued = j + 1;
   };
-  // S_j = Q K_j^T into TMEM columns [0, 128) once K_j has landed (control warp).
+  // S_j = Q K_j^T into TMEM columns [0, 64) once K_j has landed, then commit s_full (control warp).
   auto issue_s = [&](int j) -> bool {
     if (!mbar_wait(k_full + (j & 1), (j >> 1) & 1, a.err, kErrAttnWait, abort_flag, wait_ns)) return false;
     tc_fence_after();
@@ -263,7 +266,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
     __syncwarp();
     return true;
   };
-  // O (+)= P_j V_j, A = P from TMEM columns [128, 192), once V_j has landed (control warp).
+  // O (+)= P_j V_j, A = P from TMEM columns [0, 32), once V_j has landed (control warp).  Not
+  // committed: the commit after the next S (or o_full after the last block) covers it.
   auto issue_pv = [&](int j) -> bool {
     if (!mbar_wait(v_full + (j & 1), (j >> 1) & 1, a.err, kErrAttnWait, abort_flag, wait_ns)) return false;
     tc_fence_after();
@@ -271,10 +275,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
       const uint32_t idesc_o = mma_idesc<bf>(kTcQ, 64);
       const uint32_t v_addr = smem_u32(sV + (j & 1) * TcAttnSmem::kV);
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        tc_mma_f16_ts(tmem_base + 192, tmem_base + 128 + 8 * k,
-                      smem_desc_sw128(v_addr + (k >> 2) * 64 * 128 + (k & 3) * 32), idesc_o, (j | k) != 0);
-      tc_commit(o_full);
+      for (int k = 0; k < 4; ++k)
+        tc_mma_f16_ts(tmem_base + 64, tmem_base + 8 * k, smem_desc_sw128(v_addr + k * 32), idesc_o, (j | k) != 0);
     }
     __syncwarp();
     return true;
@@ -284,7 +286,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
   if (ctl && lane == 0 && n_blocks > 0) {
     if (!gathered) {
       mbar_arrive_expect_tx(q_full, TcAttnSmem::kQ);
-      tma_load_2d(sQ, &tmQK, q_full, 0, head * a.M + t0);
+      tma_load_2d(sQ, &tmQ, q_full, 0, head * a.M + t0);
     }
     for (int j = 0; j < n_blocks && j < 2; ++j) { load_k(j); load_v(j); }
   }
@@ -327,14 +329,21 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
   float m_used = -INFINITY, l = 0.f;
   for (int j = 0; j < n_blocks; ++j) {
     const int kb = k_lo + j * kTcKB;
+    // S_j is ready, and every MMA issued before it (P_{j-1} V_{j-1}) has completed.
     ok = ok && mbar_wait(s_full, j & 1, a.err, kErrAttnWait, abort_flag, wait_ns);
     if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
     tc_fence_after();
+    if (ctl && lane == 0) {
+      // S_j completed: its K stage takes K_{j+2}.  P_{j-1} V_{j-1} completed: its V stage takes
+      // V_{j+1} (V_0 and V_1 were loaded up front).
+      if (j + 2 < n_blocks) load_k(j + 2);
+      if (j >= 1 && j + 1 < n_blocks) load_v(j + 1);
+    }
     // Chunk c holds keys [kb + 32c, kb + 32c + 32).  vis bit c: some query of the warp sees a
     // key of the chunk; full bit c: every query of the warp sees every key.  Warp-uniform.
     uint32_t vis = 0, full = 0;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
       const int ck = kb + 32 * c;
       if (warp_live && ck < valid && (a.window < 0 || (ck + 31 >= qa - a.window && ck <= qa + 31 + a.window)))
         vis |= 1u << c;
@@ -342,23 +351,14 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
         full |= 1u << c;
     }
     full &= vis;
-    uint32_t sx[4][32];
+    uint32_t sx[2][32];
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
+    for (int c = 0; c < 2; ++c)
       if ((vis >> c) & 1) tmem_ld32_async(s_tmem + 32 * c, sx[c]);
 #pragma unroll
-    for (int c = 0; c < 4; ++c)
+    for (int c = 0; c < 2; ++c)
       if ((vis >> c) & 1) tmem_wait_ld(sx[c]);
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(s_free);
-    if (ctl && j + 1 < n_blocks) {
-      // Once every warp has read S_j: S_{j+1} into the same columns, and K_{j+2} into the stage
-      // S_j has finished reading.
-      ok = mbar_wait(s_free, j & 1, a.err, kErrAttnWait, abort_flag, wait_ns) && issue_s(j + 1);
-      if (ok && lane == 0 && j + 2 < n_blocks) load_k(j + 2);
-    }
-    const bool all = full == 0xFu;
+    const bool all = full == 0x3u;
     const float bmax = all ? tc_block_max<true>(sx, vis, full, kb, lo_key, span_keys)
                            : tc_block_max<false>(sx, vis, full, kb, lo_key, span_keys);
     const float m_new = bmax * kScaleLog2;
@@ -369,16 +369,12 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
       m_used = m_new;
     }
     const float sub = m_used == -INFINITY ? 0.f : m_used;
-    // P_j overwrites P_{j-1}: wait for the previous P V product.
-    if (j > 0) {
-      ok = ok && mbar_wait(o_full, (j - 1) & 1, a.err, kErrAttnWait, abort_flag, wait_ns);
-      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      tc_fence_after();
-    }
+    // P_j goes over S_j's first columns, which this warp has read (the loads above completed).
     const float sum = all ? tc_block_probs<true, T>(sx, vis, kScaleLog2, sub, p_tmem)
                           : tc_block_probs<false, T>(sx, vis, kScaleLog2, sub, p_tmem);
     l = l * alpha + sum;
-    // Rows whose maximum grew by more than 2^8 rescale O before P_j V_j accumulates into it.
+    // Rows whose maximum grew by more than 2^8 rescale O before P_j V_j accumulates into it (O
+    // is settled: s_full covered every earlier MMA, and P_j V_j waits for p_full).
     if (__any_sync(0xffffffffu, o_dirty)) {
 #pragma unroll 1
       for (int h = 0; h < 2; ++h) {
@@ -395,16 +391,23 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
     __syncwarp();
     if (lane == 0) mbar_arrive(p_full);
     if (ctl) {
-      // Once every warp has written P_j: P_j V_j, and V_{j+1} into the stage P_{j-1} V_{j-1}
-      // has finished reading (observed through o_full above).
+      // Once every warp has written P_j: O += P_j V_j, then S_{j+1}, whose commit covers both
+      // (after the last block, o_full is committed instead).
       ok = ok && mbar_wait(p_full, j & 1, a.err, kErrAttnWait, abort_flag, wait_ns) && issue_pv(j);
-      if (ok && lane == 0 && j >= 1 && j + 1 < n_blocks) load_v(j + 1);
+      if (ok) {
+        if (j + 1 < n_blocks) {
+          ok = issue_s(j + 1);
+        } else {
+          if (lane == 0) tc_commit(o_full);
+          __syncwarp();
+        }
+      }
     }
   }
   // Normalise and store this row (zeros for padding queries); rows past the tile belong to
   // other tiles and are not written.
   if (ok && n_blocks > 0) {
-    ok = mbar_wait(o_full, (n_blocks - 1) & 1, a.err, kErrAttnWait, abort_flag, wait_ns);
+    ok = mbar_wait(o_full, 0, a.err, kErrAttnWait, abort_flag, wait_ns);
     ok = __all_sync(0xffffffffu, ok);
   }
   uint32_t o[2][32];
@@ -421,11 +424,11 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_attention_kernel(const __gri
   if (split) {
     // Every CTA of the cluster reaches both barriers on every path (the early returns above
     // are taken by both CTAs of a cluster alike).  (1): both CTAs' last MMAs have completed,
-    // so rank 0's K/V stages are free; rank 1 then writes its row there: 64 O values, its
-    // running maximum (log2 units), its sum and its status.  (2): the rows have landed.
+    // so rank 0's Q, K and V buffers are free; rank 1 then writes its row there: 64 O values,
+    // its running maximum (log2 units), its sum and its status.  (2): the rows have landed.
     constexpr int kXRow = 68;  // floats per exchanged row (16-byte multiple)
-    static_assert(kTcQ * kXRow * 4 <= 2 * (TcAttnSmem::kK + TcAttnSmem::kV), "exchange buffer");
-    float* xrow = reinterpret_cast<float*>(sK) + r * kXRow;
+    static_assert(kTcQ * kXRow * 4 <= TcAttnSmem::kOffBar, "exchange buffer");
+    float* xrow = reinterpret_cast<float*>(sQ) + r * kXRow;
     cluster_sync();
     if (rank == 1) {
       const uint32_t dst = cluster_addr(smem_u32(xrow), 0);
