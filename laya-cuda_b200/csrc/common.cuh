@@ -453,6 +453,27 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return d;
 }
 
+// 2^x of two values on the FMA pipe, for a share of the softmax exponentials (x <= 8), so the
+// special-function unit is not the only unit computing them.  Range reduction: adding
+// 1.5 * 2^23 rounds x to the nearest integer n, held in the sum's low mantissa bits; f = x - n is
+// in [-0.5, 0.5].  2^f is a degree-3 polynomial fitted to minimax relative error on [-0.5, 0.5]
+// by the Remez exchange algorithm (relative error 7.5e-5 with the coefficients rounded to fp32,
+// under the 2^-11 rounding of the 16-bit probabilities it feeds); n is then added to the
+// exponent field.  Inputs below -64 are raised to -64 (2^-64 is far below the smallest 16-bit
+// probability and the row sum's precision); callers pass no -inf (masked) values.
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  x = make_float2(fmaxf(x.x, -64.f), fmaxf(x.y, -64.f));
+  const float2 t = add2(x, make_float2(kMagic, kMagic));
+  const float2 n = sub2(t, make_float2(kMagic, kMagic));
+  const float2 f = sub2(x, n);
+  float2 p = fma2(make_float2(0.0551716685f, 0.0551716685f), f, make_float2(0.2426111251f, 0.2426111251f));
+  p = fma2(p, f, make_float2(0.6932609677f, 0.6932609677f));
+  p = fma2(p, f, make_float2(0.9999280572f, 0.9999280572f));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
 __device__ __forceinline__ float2 unpack2_f32(uint32_t v, __nv_bfloat16*) {
   __nv_bfloat162 p = *reinterpret_cast<__nv_bfloat162*>(&v);
   return __bfloat1622float2(p);

@@ -114,6 +114,11 @@ __device__ __forceinline__ float tc_block_max(uint32_t (&sx)[2][32], uint32_t vi
   return mx[0];
 }
 
+// Block-relative key from which blocks every query of the warp sees in full compute their
+// exponentials on the FMA pipe (exp2_poly2) rather than the special-function unit: keys 56..63,
+// an eighth of such a block (larger shares measured slower: the polynomial costs issue slots).
+constexpr int kTcPolyKey = 56;
+
 // P = 2^(s * scale - sub) for the loaded chunks (zeros for the others), stored as 16-bit pairs
 // into TMEM columns p_tmem + 16c; returns the row sum of the fp32 probabilities.
 template <bool kAll, typename T>
@@ -128,7 +133,7 @@ __device__ __forceinline__ float tc_block_probs(const uint32_t (&sx)[2][32], uin
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
         const float2 x = fma2(make_float2(__uint_as_float(sx[c][i]), __uint_as_float(sx[c][i + 1])), sc, ns);
-        const float2 p = make_float2(ex2_approx(x.x), ex2_approx(x.y));
+        const float2 p = kAll && 32 * c + i >= kTcPolyKey ? exp2_poly2(x) : make_float2(ex2_approx(x.x), ex2_approx(x.y));
         sm[(i >> 1) & 3] = add2(sm[(i >> 1) & 3], p);
         pk[i >> 1] = pack2<T>(p.x, p.y);
       }
