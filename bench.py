@@ -242,6 +242,61 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_attention_only(args):
+    """--attention-only: the attention kernel alone (laya_op_attention, the forward pass's
+    key-split rule) on the first 64 sequences of the config-5 workload, 12 heads, f16, random
+    q/k/v: 5 untimed + 30 timed launches of a global layer, then of a window-64 layer (CUDA
+    events on the launching stream).  The command of the attention profile captures."""
+    import torch
+    from laya_cuda import _lib
+    from laya_cuda import synthetic as S
+    from laya_cuda.runtime import span
+    lib = _lib.load()
+    reqs = S.throughput_requests(1000, 22, 50368, LENGTHS, QUESTIONS, OPTIONS)
+    lengths = [len(item[0]) for req in reqs for item in req][:MICRO]
+    starts = np.cumsum([0] + [span(n) for n in lengths])[:-1].astype(np.int32)
+    rows = int(span(sum(span(n) for n in lengths)) // 128 * 128 + 128)
+    heads = 12
+    lens = np.asarray(lengths, np.int32)
+    cap = (rows + (128 - 16) * len(lengths) + 127) // 128 + 1
+    tiles = np.zeros((cap, 4), np.int32)
+    n_tiles = lib.laya_attention_tiles(starts.ctypes.data, lens.ctypes.data, len(lengths), rows, 128,
+                                       tiles.ctypes.data, cap)
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    qkv = torch.randn(3 * heads * rows * 64, dtype=torch.float16, device="cuda", generator=gen)
+    out = torch.empty(rows * heads * 64, dtype=torch.float16, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    dev = [torch.from_numpy(v).cuda() for v in (tiles, starts, lens)]
+    stream = torch.cuda.current_stream()
+
+    def run(window):
+        _lib.check(lib.laya_op_attention(_lib.PRECISION_F16, 1, ct.c_void_p(qkv.data_ptr()), ct.c_void_p(out.data_ptr()),
+                                         ct.c_void_p(dev[0].data_ptr()), cap, ct.c_void_p(dev[1].data_ptr()),
+                                         ct.c_void_p(dev[2].data_ptr()), rows, heads, window,
+                                         ct.c_void_p(err.data_ptr()), ct.c_void_p(stream.cuda_stream)))
+    result = {"tokens": int(sum(lengths)), "rows": rows, "tiles": n_tiles}
+    for window in (-1, 64):
+        for _ in range(5):
+            run(window)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(30):
+            run(window)
+        b.record(stream)
+        torch.cuda.synchronize()
+        us = a.elapsed_time(b) / 30 * 1000
+        useful = 0
+        for n in lengths:
+            q = np.arange(n)
+            keys = n * n if window < 0 else int((np.minimum(n, q + window + 1) - np.maximum(0, q - window)).sum())
+            useful += 4 * 64 * heads * keys
+        result["global" if window < 0 else "window64"] = {"us": round(us, 1), "useful_tflops": round(useful / us / 1e6, 1)}
+    if int(err.item()) != 0:
+        raise RuntimeError(f"attention reported device error {int(err.item())}")
+    print(json.dumps({"attention_only": result}), flush=True)
+
+
 def run_cold_load(args):
     """--cold-load NAME: in this fresh process, the wall time of Engine(checkpoint) (CUDA
     context, library, tokenizer, weight load and finalize) and of the first request after it (a
@@ -268,14 +323,25 @@ def run_cold_load(args):
                       "second_request_ms": round((t3 - t2) * 1000, 3), "checkpoint_bytes": size}), flush=True)
 
 
-def cold_loads(names):
-    """Cold Engine construction and first request per model, each in a fresh process."""
+def cold_loads(names, runs=3):
+    """Cold Engine construction and first request per model, each in `runs` fresh processes
+    (the first process on a box also pays one-time driver work): the median run by load time,
+    with every run's load time."""
     out = {}
     for name in names:
-        run = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--cold-load", name], capture_output=True,
-                             text=True, timeout=600)
-        lines = [l for l in run.stdout.splitlines() if l.startswith("{")]
-        out[name] = json.loads(lines[-1]) if run.returncode == 0 and lines else {"error": run.stderr[-300:]}
+        results = []
+        for _ in range(runs):
+            run = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--cold-load", name], capture_output=True,
+                                 text=True, timeout=600)
+            lines = [l for l in run.stdout.splitlines() if l.startswith("{")]
+            if run.returncode != 0 or not lines:
+                results = None
+                out[name] = {"error": run.stderr[-300:]}
+                break
+            results.append(json.loads(lines[-1]))
+        if results:
+            results.sort(key=lambda r: r["load_s"])
+            out[name] = {**results[len(results) // 2], "load_s_runs": [r["load_s"] for r in results]}
     return out
 
 
@@ -529,9 +595,13 @@ def main():
     parser.add_argument("--repeats", type=int, default=200, help="timed repeats per length of --latency-only")
     parser.add_argument("--cold-load", default=None, help="time Engine construction + first request of this model "
                                                           "in this fresh process (used by the main run)")
+    parser.add_argument("--attention-only", action="store_true",
+                        help="only the attention kernel on one config-5 micro-batch (for profiler captures)")
     args = parser.parse_args()
     if args.latency_only:
         return run_latency_only(args)
+    if args.attention_only:
+        return run_attention_only(args)
     if args.cold_load:
         return run_cold_load(args)
     if args.warmup < 3:

@@ -53,15 +53,20 @@ struct GemmLnCfg {
   static constexpr int kStageA = kBM * kBK * 2;
   static constexpr int kStageB = BN * kBK * 2;
   static constexpr int kStageBytes = kStageA + kStageB;
-  static constexpr int kStages = BN == 256 ? 3 : 4;
+  static constexpr int kStages = 3;
   static constexpr int kOffEpi = kStages * kStageBytes;
   static constexpr int kChunks = BN / 64;  // 32-column chunks per epilogue warp
+  // Per epilogue warp, two 4 KB blocks (1024-byte aligned: the 128-byte swizzle pattern) for its
+  // 32 x 32 fp32 residual chunks; the second doubles as the staging block of the LayerNorm pass.
+  static constexpr int kRingBlock = 32 * 32 * 4;
+  static constexpr int kRingBytes = kEpiWarps * 2 * kRingBlock;
   // Exchange: [2 parity][2C partials][128 rows][sum, M2] fp32.
-  static constexpr int kOffX = kOffEpi + kEpiSmemBytes;
+  static constexpr int kOffX = kOffEpi + kRingBytes;
   static constexpr int kXBytes = 2 * 2 * C * kBM * 2 * 4;
   static constexpr uint32_t kXTxBytes = C * kEpiWarps * 32 * 8;  // received per CTA per tile
   static constexpr int kOffBar = kOffX + kXBytes;
-  static constexpr int kSmemBytes = kOffBar + 256 + 1024;
+  static constexpr int kSmemBytes = kOffBar + 512 + 1024;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory of one CTA");
 };
 
 // Asynchronous store of two floats into a cluster CTA's shared memory (cluster address `addr`,
@@ -83,7 +88,7 @@ __device__ __forceinline__ uint4 stage_get_row(const uint8_t* buf, int lane, int
 template <int C, int BN, typename T>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_ln_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmLnArgs args) {
+                   const __grid_constant__ CUtensorMap tmR, const GemmLnArgs args) {
   using Cfg = GemmLnCfg<C, BN>;
   constexpr int NCH = Cfg::kChunks;
   constexpr int S = Cfg::kStages;
@@ -99,7 +104,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tempty = bars + 2 * S + 2;
   uint64_t* xbar = bars + 2 * S + 4;   // [2 parity]
   uint64_t* drain = bars + 2 * S + 6;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 7);
+  uint64_t* rbar = bars + 2 * S + 7;   // [8 epilogue warps][2 blocks]: residual chunk landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 7 + 2 * kEpiWarps);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const unsigned long long wait_ns = wait_limit(args.wait_ns);
 
@@ -115,11 +121,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], kEpiWarps); }
     for (int i = 0; i < 2; ++i) mbar_init(&xbar[i], 1);  // armed with expect_tx once per tile
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(&rbar[i], 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 0 && lane == 0) { tma_prefetch_desc(&tmA); tma_prefetch_desc(&tmB); }
+  if (warp == 0 && lane == 0) { tma_prefetch_desc(&tmA); tma_prefetch_desc(&tmB); tma_prefetch_desc(&tmR); }
   if (warp == 1) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
   tc_fence_before();
   cluster_sync();  // every CTA's exchange barriers exist before the first remote arrival
@@ -201,7 +208,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // (this CTA's columns [h BN/2, (h+1) BN/2), NCH 32-column chunks).
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
-    uint8_t* stage = smem + Cfg::kOffEpi + (warp - 2) * kEpiStageBytes;
+    // Residual chunk j (32 rows x 32 fp32 columns) goes through ring block j & 1: a TMA load, the
+    // update in place by the lanes (row-per-lane, the swizzled layout of stage_off), a TMA store.
+    uint8_t* ring = smem + Cfg::kOffEpi + (warp - 2) * 2 * Cfg::kRingBlock;
+    uint64_t* rb = rbar + (warp - 2) * 2;
+    uint8_t* stage = ring + Cfg::kRingBlock;           // LayerNorm pass staging (ring block 1)
+    uint32_t rphase = 0, rpending = 0;                 // per ring block: phase, load in flight
     const int col0 = nb * BN + half * (BN / 2);       // first global column of this warp
     constexpr float kPart = (float)(BN / 2);          // columns per partial
     const float inv_n = 1.f / (float)args.N;
@@ -231,23 +243,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       var = (acc_m2 + kPart * spread) * inv_n;
     };
-    // Residual chunks, coalesced (lane -> row 4k + lane/8, columns 4(lane%8)..+3), loaded two
-    // ahead.  The first two chunks of the next tile are loaded as soon as this tile's pass A has
-    // consumed its own, so their latency overlaps the exchange and pass C.
-    float4 res[2][8];
-    auto load_res = [&](int row0, int rows, int j) {
-      const float* base = args.residual + col0 + 32 * j + (lane & 7) * 4;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int r = 4 * k + (lane >> 3);
-        res[j & 1][k] = r < rows ? *reinterpret_cast<const float4*>(base + (size_t)(row0 + r) * args.ldr)
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    // Loads residual chunk j of the block at row0 into ring block b (lane 0; rows past M read
+    // as zeros).  The block must be free: no store from it still reading.
+    auto res_load = [&](int b, int row0, int j) {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&rb[b], Cfg::kRingBlock);
+        tma_load_2d(ring + b * Cfg::kRingBlock, &tmR, &rb[b], col0 + 32 * j, row0);
       }
+      rpending |= 1u << b;
+    };
+    auto res_wait = [&](int b) -> bool {
+      const bool fine = mbar_wait(&rb[b], (rphase >> b) & 1, args.err, kErrGemmEpilogueWait, abort_flag, wait_ns);
+      rphase ^= 1u << b;
+      rpending &= ~(1u << b);
+      return fine;
+    };
+    // Every TMA store this warp issued has finished reading its ring block.
+    auto stores_read = [&]() {
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
     };
     if (cid < m_blocks) {
       const int row0 = cid * kBM + quarter * 32;
-      load_res(row0, min(32, args.M - row0), 0);
-      load_res(row0, min(32, args.M - row0), 1);
+      res_load(0, row0, 0);
+      res_load(1, row0, 1);
     }
     int acc = 0; uint32_t acc_phase = 0;
     int lt = 0;  // local tile count
@@ -265,40 +284,39 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // sum and centred M2 come from its 32 values in registers (two passes) and are merged into
       // this thread's partial with Chan's formula, so no second pass over TMEM is needed.
       float pm = 0.f, pm2 = 0.f;  // running mean and M2 of this thread's partial
+      bool landed = true;
 #pragma unroll
       for (int j = 0; j < NCH; ++j) {
+        const int b = j & 1;
+        uint8_t* blk = ring + b * Cfg::kRingBlock;
         uint32_t v[32];
         tmem_ld32_async(tbase + 32 * j, v);
+        landed = res_wait(b);
         tmem_wait_ld(v);
-        uint4 p[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float4 b = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (args.bias) b = *reinterpret_cast<const float4*>(args.bias + col0 + 32 * j + 4 * q);
-          p[q] = u4(__uint_as_float(v[4 * q]) + b.x, __uint_as_float(v[4 * q + 1]) + b.y,
-                    __uint_as_float(v[4 * q + 2]) + b.z, __uint_as_float(v[4 * q + 3]) + b.w);
-        }
-        stage_put(stage, lane, p);  // row layout in
-        float* rbase = args.residual + col0 + 32 * j + (lane & 7) * 4;
-        // Each staged piece is read and rewritten by the same lane, so the update is in place.
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const int r = 4 * k + (lane >> 3);
-          const float4 a = f4(stage_get(stage, k, lane));
-          const float4 t = res[j & 1][k];
-          const float4 nv = make_float4(t.x + a.x, t.y + a.y, t.z + a.z, t.w + a.w);
-          if (r < rows) *reinterpret_cast<float4*>(rbase + (size_t)(row0 + r) * args.ldr) = nv;
-          stage_put_co(stage, k, lane, make_uint4(__float_as_uint(nv.x), __float_as_uint(nv.y), __float_as_uint(nv.z),
-                                                  __float_as_uint(nv.w)));
-        }
-        if (j + 2 < NCH) load_res(row0, rows, j + 2);
-        __syncwarp();
+        if (!__all_sync(0xffffffffu, landed)) break;
+        // v = residual + (acc + bias), in place in the block (this lane's row, 8 x 16 bytes).
         float cs = 0.f;
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          const uint4 w = stage_get_row(stage, lane, q);
-          v[4 * q] = w.x; v[4 * q + 1] = w.y; v[4 * q + 2] = w.z; v[4 * q + 3] = w.w;
-          cs += (__uint_as_float(w.x) + __uint_as_float(w.y)) + (__uint_as_float(w.z) + __uint_as_float(w.w));
+          float4 bb = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (args.bias) bb = *reinterpret_cast<const float4*>(args.bias + col0 + 32 * j + 4 * q);
+          const float4 rr = f4(*reinterpret_cast<const uint4*>(blk + stage_off(lane, q)));
+          const float4 nv = make_float4(rr.x + (__uint_as_float(v[4 * q]) + bb.x),
+                                        rr.y + (__uint_as_float(v[4 * q + 1]) + bb.y),
+                                        rr.z + (__uint_as_float(v[4 * q + 2]) + bb.z),
+                                        rr.w + (__uint_as_float(v[4 * q + 3]) + bb.w));
+          *reinterpret_cast<uint4*>(blk + stage_off(lane, q)) = u4(nv.x, nv.y, nv.z, nv.w);
+          v[4 * q] = __float_as_uint(nv.x); v[4 * q + 1] = __float_as_uint(nv.y);
+          v[4 * q + 2] = __float_as_uint(nv.z); v[4 * q + 3] = __float_as_uint(nv.w);
+          cs += (nv.x + nv.y) + (nv.z + nv.w);
+        }
+        // The updated chunk goes back to HBM from the block (TMA store; the lanes' writes are
+        // handed to the async proxy first) and to TMEM for the LayerNorm pass.
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && rows > 0) {
+          tma_store_2d(&tmR, blk, col0 + 32 * j, row0);
+          bulk_commit();
         }
         tmem_st32(tbase + 32 * j, v);
         const float cm = cs * (1.f / 32.f);
@@ -312,13 +330,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const float delta = cm - pm;
         pm += delta * (1.f / (float)(j + 1));
         pm2 += cm2 + delta * delta * (32.f * (float)j / (float)(j + 1));
+        if (j + 2 < NCH) {
+          stores_read();
+          res_load(b, row0, j + 2);
+        }
       }
+      if (!__all_sync(0xffffffffu, landed)) break;
       tmem_wait_st();
-      if (mb + n_clusters < m_blocks) {
-        const int next0 = (mb + n_clusters) * kBM + quarter * 32;
-        load_res(next0, min(32, args.M - next0), 0);
-        load_res(next0, min(32, args.M - next0), 1);
-      }
+      // Ring block 0 takes the next tile's chunk 0 now; block 1 is the staging block of the
+      // LayerNorm pass below and takes chunk 1 after it.
+      const int next0 = (mb + n_clusters) * kBM + quarter * 32;
+      stores_read();
+      if (mb + n_clusters < m_blocks) res_load(0, next0, 0);
       const float sum = pm * kPart, m2 = pm2;
       bool fine;
       float mean, var;
@@ -364,7 +387,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      // The staging block takes the next tile's chunk 1 (the lanes' staging writes are ordered
+      // before the copy's writes).
+      if (mb + n_clusters < m_blocks) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        res_load(1, next0, 1);
+      }
     }
+    // Stores complete and loads landed before the CTA exits (on every path; bounded drains).
+    if (lane == 0) {
+      bulk_wait_all();
+      for (int b = 0; b < 2; ++b)
+        if ((rpending >> b) & 1) mbar_drain(&rb[b], (rphase >> b) & 1);
+    }
+    __syncwarp();
   }
 
   tc_fence_before();

@@ -111,6 +111,23 @@ CUtensorMap make_map(const void* ptr, int64_t rows, int64_t cols, int box_rows, 
   return m;
 }
 
+// 2-D fp32 tensor [rows][cols] with row stride ld elements, box {32 columns, 32 rows}, 128-byte
+// swizzle: the residual chunks of the fused residual + LayerNorm epilogue.
+CUtensorMap make_map_f32(const float* ptr, int64_t rows, int64_t cols, int64_t ld) {
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 != 0 || (ld * 4) % 16 != 0 || cols % 32 != 0)
+    fail(LAYA_ERR_INVALID, "residual must be 16-byte aligned, its row stride and width multiples of 4 and 32 floats");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail(LAYA_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return m;
+}
+
 int sm_count(int device) {
   static std::map<int, int> cache;
   auto it = cache.find(device);
@@ -217,7 +234,8 @@ void launch_gemm_pair_bn(int epi, const CUtensorMap& ta, const CUtensorMap& tb, 
 // Residual GEMM + LayerNorm: clusters of C = N/BN CTAs own 128-row blocks (persistent, as many
 // clusters as can be resident at once, at most one per row block).
 template <int C, int BN, typename T>
-void launch_gemm_ln_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmLnArgs& a, cudaStream_t st) {
+void launch_gemm_ln_inst(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tr, const GemmLnArgs& a,
+                         cudaStream_t st) {
   static uint64_t configured = 0;  // one bit per device
   static int max_clusters[64] = {};
   auto kern = gemm_ln_kernel<C, BN, T>;
@@ -250,7 +268,7 @@ void launch_gemm_ln_inst(const CUtensorMap& ta, const CUtensorMap& tb, const Gem
   const int clusters = std::min(m_blocks, max_clusters[dev & 63]);
   cfg.gridDim = dim3(C * clusters);
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  CK(cudaLaunchKernelEx(&cfg, kern, ta, tb, a));
+  CK(cudaLaunchKernelEx(&cfg, kern, ta, tb, tr, a));
 }
 
 // Column block of the fused residual + LayerNorm GEMM for row width N and depth K (0: not
@@ -263,18 +281,19 @@ int ln_block_n(int N, int K) {
 }
 
 template <typename T>
-void launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tb, const GemmLnArgs& args, int bn, cudaStream_t st) {
+void launch_gemm_ln(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tr, const GemmLnArgs& args, int bn,
+                    cudaStream_t st) {
   GemmLnArgs a = args;
   a.wait_ns = wait_ns();
   const int c = a.N / bn;
-  if (bn == 256 && c == 1) launch_gemm_ln_inst<1, 256, T>(ta, tb, a, st);
-  else if (bn == 256 && c == 2) launch_gemm_ln_inst<2, 256, T>(ta, tb, a, st);
-  else if (bn == 256 && c == 3) launch_gemm_ln_inst<3, 256, T>(ta, tb, a, st);
-  else if (bn == 256 && c == 4) launch_gemm_ln_inst<4, 256, T>(ta, tb, a, st);
-  else if (bn == 192 && c == 1) launch_gemm_ln_inst<1, 192, T>(ta, tb, a, st);
-  else if (bn == 192 && c == 2) launch_gemm_ln_inst<2, 192, T>(ta, tb, a, st);
-  else if (bn == 192 && c == 3) launch_gemm_ln_inst<3, 192, T>(ta, tb, a, st);
-  else if (bn == 192 && c == 4) launch_gemm_ln_inst<4, 192, T>(ta, tb, a, st);
+  if (bn == 256 && c == 1) launch_gemm_ln_inst<1, 256, T>(ta, tb, tr, a, st);
+  else if (bn == 256 && c == 2) launch_gemm_ln_inst<2, 256, T>(ta, tb, tr, a, st);
+  else if (bn == 256 && c == 3) launch_gemm_ln_inst<3, 256, T>(ta, tb, tr, a, st);
+  else if (bn == 256 && c == 4) launch_gemm_ln_inst<4, 256, T>(ta, tb, tr, a, st);
+  else if (bn == 192 && c == 1) launch_gemm_ln_inst<1, 192, T>(ta, tb, tr, a, st);
+  else if (bn == 192 && c == 2) launch_gemm_ln_inst<2, 192, T>(ta, tb, tr, a, st);
+  else if (bn == 192 && c == 3) launch_gemm_ln_inst<3, 192, T>(ta, tb, tr, a, st);
+  else if (bn == 192 && c == 4) launch_gemm_ln_inst<4, 192, T>(ta, tb, tr, a, st);
   else fail(LAYA_ERR_INVALID, "fused residual + LayerNorm: N=%d is not 1-4 blocks of 192 or 256 columns", a.N);
 }
 
@@ -633,7 +652,7 @@ struct Slot {
   cudaGraphExec_t graph = nullptr;
   bool maps_ready = false;
   size_t maps_ws = 0;  // workspace generation the maps point into
-  CUtensorMap map_x, map_attn, map_ff, map_selx, map_scored, map_ffsel;
+  CUtensorMap map_x, map_attn, map_ff, map_selx, map_scored, map_ffsel, map_residual;
   AttnMaps attn_maps;
   int launches = 0;
 };
@@ -1130,6 +1149,7 @@ void prepare_maps(Engine& e, Slot& s) {
   s.map_selx = make_map(e.ws + L.selx, L.count, d, kBM, bf);
   s.map_scored = make_map(e.ws + L.scored, L.count, d, kBM, bf);
   s.map_ffsel = make_map(e.ws + L.ffsel, L.count, 4 * d, kBM, bf);
+  s.map_residual = make_map_f32(reinterpret_cast<const float*>(e.ws + L.residual), L.m, d, d);
   // Attention: Q/K rows of the qkv buffer ([3*heads*m][64], 128-row boxes) and V^T
   // ([heads*64][m], 64x64 boxes), both 128-byte swizzled.
   s.attn_maps = attn_maps(e.ws + L.qkv, L.m, e.cfg.heads, bf);
@@ -1317,7 +1337,7 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
     a.residual = residual; a.ldr = d; a.bias = bias; a.gamma = gamma; a.beta = beta; a.eps = eps;
     a.x = x; a.ldx = d; a.err = err;
     const CUtensorMap tb = weight_map(e, wname, bn);
-    launch(e, prof, family, 2.0 * m * a.N * a.K, [&] { launch_gemm_ln<T>(ta, tb, a, bn, e.stream); });
+    launch(e, prof, family, 2.0 * m * a.N * a.K, [&] { launch_gemm_ln<T>(ta, tb, s.map_residual, a, bn, e.stream); });
   };
 
   for (int i = 0; i < c.layers; ++i) {
@@ -1947,8 +1967,9 @@ int laya_op_gemm_ln(int precision, const void* x, const void* w, int M, int N, i
   if (!bn) fail(LAYA_ERR_INVALID, "fused residual + LayerNorm: N=%d is not 1-4 blocks of 192 or 256 columns", N);
   const CUtensorMap tb = make_map(w, N, K, bn, bf);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (bf) launch_gemm_ln<__nv_bfloat16>(ta, tb, a, bn, st);
-  else launch_gemm_ln<__half>(ta, tb, a, bn, st);
+  const CUtensorMap tr = make_map_f32(residual, M, N, ldr);
+  if (bf) launch_gemm_ln<__nv_bfloat16>(ta, tb, tr, a, bn, st);
+  else launch_gemm_ln<__half>(ta, tb, tr, a, bn, st);
   API_END(nullptr)
 }
 
