@@ -214,9 +214,10 @@ int laya_interleave_geglu(const uint16_t* src, uint16_t* dst, int F, int K);
 /* Packed attention (kernels.cu:90-154) on the tcgen05/TMEM kernel the forward pass uses.
  * qkv: q, k [heads][M][64] each, then v transposed [heads][64][M] (the layout the QKV GEMM
  * epilogue writes); out [M][heads*64].  Tiles of 128 queries from laya_attention_tiles.
- * impl 1: each tile's keys split over a CTA pair for global attention (window < 0) when
- * heads * n_tiles <= the SM count and M >= 384 (the forward pass's rule, with M for the row
- * length); impl 2 / 3: never / always split.  err: device error word. */
+ * impl 1: the forward pass's rule for splitting each tile's keys over a cluster of 2 or 4 CTAs
+ * (global attention, window < 0, with M >= 384 taken as the row length, while the split grid
+ * fits 4 CTAs per SM); impl 2: never split; impl 3 / 4: always split over 2 / 4 CTAs.
+ * err: device error word. */
 int laya_op_attention(int precision, int impl, const void* qkv, void* out, const int32_t* tiles, int n_tiles,
                       const int32_t* starts, const int32_t* lengths, int M, int heads, int window, int* err,
                       void* stream);

@@ -416,62 +416,82 @@ TilePlan plan_small(int M, int N, int K, int epi, bool split_ok, bool pair_ok, i
   return best;
 }
 
-// Tensor maps of the tcgen05 attention over a qkv buffer of M tokens: 128-row (query tile) and
-// 64-row (key block) boxes of the q/k planes, and 64 dims x 64 keys boxes of V^T.
+// Tensor maps of the tcgen05 attention over a qkv buffer of M tokens: 128-row boxes of the q/k
+// planes (query tiles, and key blocks of 128), 64-row boxes (key blocks of 64), and 64 dims x
+// 64 keys boxes of V^T.
 struct AttnMaps {
-  CUtensorMap q, k, vt;
+  CUtensorMap q, k64, vt;
 };
 AttnMaps attn_maps(const void* qkv, int M, int heads, bool bf) {
   const int64_t hm = (int64_t)heads * M;
   AttnMaps m;
   m.q = make_map(qkv, 3 * hm, 64, kTcQ, bf);
-  m.k = make_map(qkv, 3 * hm, 64, kTcKB, bf);
-  m.vt = make_map(static_cast<const uint8_t*>(qkv) + (size_t)2 * hm * 64 * 2, (int64_t)heads * 64, M, kTcKB, bf);
+  m.k64 = make_map(qkv, 3 * hm, 64, 64, bf);
+  m.vt = make_map(static_cast<const uint8_t*>(qkv) + (size_t)2 * hm * 64 * 2, (int64_t)heads * 64, M, 64, bf);
   return m;
 }
 
-template <typename T>
-void launch_tc_attention(const AttnMaps& maps, const TcAttnArgs& args, int n_tiles, cudaStream_t st) {
-  TcAttnArgs a = args;
-  a.wait_ns = wait_ns();
+template <typename T, int KB>
+void launch_tc_attention_kb(const AttnMaps& maps, const TcAttnArgs& a, int n_tiles, cudaStream_t st) {
+  using Cfg = TcAttnCfg<KB>;
   static uint64_t configured = 0;  // one bit per device
+  auto kern = tc_attention_kernel<T, KB>;
   int dev = 0;
   CK(cudaGetDevice(&dev));
   if (!(configured & (1ull << dev))) {
-    CK(cudaFuncSetAttribute(tc_attention_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcAttnSmem::kBytes));
+    CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kBytes));
     configured |= 1ull << dev;
   }
-  if (n_tiles > 65535) fail(LAYA_ERR_INVALID, "%d attention tiles exceed the grid limit", n_tiles);
-  if (a.splits != 1 && a.splits != 2) fail(LAYA_ERR_INVALID, "attention key split %d (1 or 2)", a.splits);
+  const CUtensorMap& tk = KB == 64 ? maps.k64 : maps.q;
   if (a.splits == 1) {
-    launch_k(tc_attention_kernel<T>, dim3(a.heads, n_tiles), dim3(kTcThreads), TcAttnSmem::kBytes, st, maps.q, maps.k,
-             maps.vt, a);
+    launch_k(kern, dim3(a.heads, n_tiles), dim3(kTcThreads), Cfg::kBytes, st, maps.q, tk, maps.vt, a);
     return;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.heads, n_tiles, 2);
+  cfg.gridDim = dim3(a.heads, n_tiles, a.splits);
   cfg.blockDim = dim3(kTcThreads);
-  cfg.dynamicSmemBytes = TcAttnSmem::kBytes;
+  cfg.dynamicSmemBytes = Cfg::kBytes;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 2;
+  attr[0].val.clusterDim.z = a.splits;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  CK(cudaLaunchKernelEx(&cfg, tc_attention_kernel<T>, maps.q, maps.k, maps.vt, a));
+  CK(cudaLaunchKernelEx(&cfg, kern, maps.q, tk, maps.vt, a));
 }
 
-// Key split of the tcgen05 attention: two CTAs per tile when one CTA per tile and head would
-// leave at least half of the SMs idle (batch-1 classes) and a tile sees at least three key blocks
-// (global attention over rows of ~384+ keys).  Traces of 512-token passes: a global layer's
-// attention 11.0 -> 9.7 us after the dependency wait; split window-64 tiles (two blocks) were
-// 1 us slower, the merge costing more than the block it saves.
+// Key-block size of the tcgen05 attention: 128 keys (two CTAs per SM, half the serial chain of
+// blocks per tile) for grids that fit the SMs' resident slots at that occupancy, the batch-1
+// classes; 64 keys (four CTAs per SM to hide latency) for the rest.  Measured on 512-token
+// passes: 64-key blocks cost ~20 us per pass; on the throughput workload 128-key blocks cost 30%.
+int attention_block_keys(int heads, int n_tiles, int splits, int sms) {
+  return heads * n_tiles * splits <= TcAttnCfg<128>::kCtasPerSm * sms ? 128 : 64;
+}
+
+template <typename T>
+void launch_tc_attention(const AttnMaps& maps, const TcAttnArgs& args, int n_tiles, cudaStream_t st, int sms) {
+  TcAttnArgs a = args;
+  a.wait_ns = wait_ns();
+  if (n_tiles > 65535) fail(LAYA_ERR_INVALID, "%d attention tiles exceed the grid limit", n_tiles);
+  if (a.splits != 1 && a.splits != 2 && a.splits != 4) fail(LAYA_ERR_INVALID, "attention key split %d (1, 2 or 4)", a.splits);
+  if (attention_block_keys(a.heads, n_tiles, a.splits, sms) == 128) launch_tc_attention_kb<T, 128>(maps, a, n_tiles, st);
+  else launch_tc_attention_kb<T, 64>(maps, a, n_tiles, st);
+}
+
+// Key split of the tcgen05 attention for grids that leave SMs idle (batch-1 classes): global
+// attention over rows of 384+ keys runs each tile's key blocks on 2 CTAs while the split grid
+// still fits the SMs' resident CTA slots.
+// Window-64 tiles (at most four blocks) stay whole: a split costs a merge through distributed
+// shared memory that measured more than the blocks it saves there.
 int attention_splits(int heads, int n_tiles, int sms, int window, int row_keys) {
-  return window < 0 && row_keys >= 384 && heads * n_tiles <= sms ? 2 : 1;
+  if (window >= 0 || row_keys < 384) return 1;
+  // Four CTAs per tile measured slower than two at batch 1 (512 tokens: 0.696 vs 0.681 ms per
+  // pass): the second merge round costs more than the blocks it saves.
+  return heads * n_tiles * 2 <= TcAttnCfg<128>::kCtasPerSm * sms ? 2 : 1;
 }
 
 // Row kernels are instantiated per width (d = 32 * NPL, d a multiple of 64 up to 1024).
@@ -1292,7 +1312,7 @@ void enqueue_forward(Engine& e, Slot& s, bool prof) {
       n_tiles = L.b * a.q_tiles;
     }
     a.splits = attention_splits(c.heads, n_tiles, e.sms, window, m / L.b);
-    launch(e, prof, FAM_ATTENTION, 0, [&] { launch_tc_attention<T>(s.attn_maps, a, n_tiles, e.stream); });
+    launch(e, prof, FAM_ATTENTION, 0, [&] { launch_tc_attention<T>(s.attn_maps, a, n_tiles, e.stream, e.sms); });
   };
   // A residual GEMM whose sum the next norm must still add: split count and the GEMM bias.
   struct Pending { int splits = 0; const float* bias = nullptr; };
@@ -1993,7 +2013,8 @@ int laya_op_attention(int precision, int impl, const void* qkv, void* out, const
                       const int32_t* starts, const int32_t* lengths, int M, int heads, int window, int* err,
                       void* stream) {
   API_BEGIN
-  if (impl < 1 || impl > 3) fail(LAYA_ERR_INVALID, "attention impl %d (1: forward-pass rule, 2: no key split, 3: key split)", impl);
+  if (impl < 1 || impl > 4)
+    fail(LAYA_ERR_INVALID, "attention impl %d (1: forward-pass rule, 2: no key split, 3: 2-way, 4: 4-way key split)", impl);
   const bool bf = precision == LAYA_PRECISION_BF16;
   const AttnMaps maps = attn_maps(qkv, M, heads, bf);
   TcAttnArgs t{};
@@ -2001,10 +2022,10 @@ int laya_op_attention(int precision, int impl, const void* qkv, void* out, const
   t.M = M; t.heads = heads; t.window = window; t.err = err;
   int dev = 0;
   CK(cudaGetDevice(&dev));
-  t.splits = impl == 2 ? 1 : impl == 3 ? 2 : attention_splits(heads, n_tiles, sm_count(dev), window, M);
+  t.splits = impl == 2 ? 1 : impl == 3 ? 2 : impl == 4 ? 4 : attention_splits(heads, n_tiles, sm_count(dev), window, M);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (bf) launch_tc_attention<__nv_bfloat16>(maps, t, n_tiles, st);
-  else launch_tc_attention<__half>(maps, t, n_tiles, st);
+  if (bf) launch_tc_attention<__nv_bfloat16>(maps, t, n_tiles, st, sm_count(dev));
+  else launch_tc_attention<__half>(maps, t, n_tiles, st, sm_count(dev));
   API_END(nullptr)
 }
 
@@ -2023,8 +2044,8 @@ int laya_op_attention_gathered(int precision, const void* qkv, void* out, const 
   CK(cudaGetDevice(&dev));
   t.splits = attention_splits(heads, n_rows * t.q_tiles, sm_count(dev), -1, M / n_rows);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (bf) launch_tc_attention<__nv_bfloat16>(maps, t, n_rows * t.q_tiles, st);
-  else launch_tc_attention<__half>(maps, t, n_rows * t.q_tiles, st);
+  if (bf) launch_tc_attention<__nv_bfloat16>(maps, t, n_rows * t.q_tiles, st, sm_count(dev));
+  else launch_tc_attention<__half>(maps, t, n_rows * t.q_tiles, st, sm_count(dev));
   API_END(nullptr)
 }
 

@@ -6,23 +6,25 @@
 //
 // Work unit: one CTA per (128-query tile of one row, head); the host's tile table never lets a
 // tile straddle rows.  4 warps, one thread per query row (warp w owns TMEM lanes [32w, 32w+32)).
-// The kernel is bound by instruction latency in the softmax, not by a pipe's throughput, so it
-// is laid out for many resident warps: a CTA holds 128 TMEM columns and ~50 KB of shared memory,
-// so four CTAs (16 warps) share an SM and hide each other's waits.
+// The kernel is bound by instruction latency in the softmax, not by a pipe's throughput, so for
+// large grids it is laid out for many resident warps: with 64-key blocks (KB = 64) a CTA holds
+// 128 TMEM columns and ~50 KB of shared memory, so four CTAs (16 warps) share an SM and hide each
+// other's waits.  Small grids (batch 1), where the serial chain of blocks per tile decides,
+// take 128-key blocks (KB = 128: 256 TMEM columns, two CTAs per SM, half as many blocks).
 //
-// TMEM per CTA: S_j = Q K_j^T for a block of 64 keys in columns [0, 64) (fp32); the softmax
+// TMEM per CTA: S_j = Q K_j^T for a block of KB keys in columns [0, KB) (fp32); the softmax
 // reads S_j into registers and writes P_j = 2^(s log2e / 8 - m) as 16-bit pairs over its first
-// 32 columns; O in columns [64, 128).  The tensor core executes a CTA's MMAs in issue order, so
+// KB / 2 columns; O in columns [KB, KB + 64).  The tensor core executes a CTA's MMAs in issue order, so
 // the control lane issues O += P_j V_j and S_{j+1} = Q K_{j+1}^T back to back: S_{j+1} overwrites
 // P_j only after the P V product has read it, and the single commit after S_{j+1} tells the
 // softmax warps both that S_{j+1} is ready and that O is settled (for the rare rescale).  Per
 // block the warps wait on one barrier (s_full) and arrive on one (p_full).
 //
 // Warp 0 also controls the pipeline (TMEM allocation; one lane issues copies and MMAs):
-//   TMA   the Q tile once, then per 64-key block the K tile and the V^T tile into double-buffered
+//   TMA   the Q tile once, then per block the K tile and the V^T tile(s) into double-buffered
 //         stages (128-byte swizzle, no multicast); a stage is refilled once the commit that
 //         covers the MMA reading it has been observed;
-//   MMA   S_j (M=128, N=64, K=64), O += P_j V_j (M=128, N=64, K=64, A = P from TMEM).
+//   MMA   S_j (M=128, N=KB, K=64), O += P_j V_j (M=128, N=64, K=KB, A = P from TMEM).
 // The softmax masks only 32-key chunks that straddle the window or row end and skips chunks no
 // query of its warp can see; it keeps the running maximum m and sum l in fp32 (paired fp32
 // instructions for the scale-and-subtract and the sums); O stays in TMEM and is rescaled (read,
@@ -38,10 +40,7 @@
 namespace laya {
 
 constexpr int kTcQ = 128;              // queries per CTA
-constexpr int kTcKB = 64;              // keys per block
 constexpr int kTcThreads = 128;
-constexpr int kTcCtasPerSm = 4;
-constexpr int kTcTmemCols = 128;       // S / P: [0, 64), O: [64, 128)
 constexpr float kTcRescaleLog2 = 8.f;  // O is rescaled when the row maximum grows by more than 2^8
 
 struct TcAttnArgs {
@@ -60,42 +59,53 @@ struct TcAttnArgs {
   const int* q_index;
   int q_per_row;
   int q_tiles;
-  // 1, or 2: key split.  The grid is (heads, tiles, 2) in clusters of (1, 1, 2); CTA rank r of a
-  // cluster runs key blocks [r h, ...) of its tile (h = half the blocks, rounded up); rank 1 hands
-  // its unnormalised O row, running maximum and sum to rank 0 through distributed shared memory,
-  // and rank 0 merges and stores.  Halves the serial block chain of grids that leave SMs idle.
+  // 1, 2 or 4: key split.  The grid is (heads, tiles, splits) in clusters of (1, 1, splits); CTA
+  // rank r of a cluster runs key blocks [r h, r h + h) of its tile (h = the blocks / splits,
+  // rounded up).  The partial results merge pairwise through distributed shared memory (rank r
+  // hands its unnormalised O row, running maximum and sum to rank r - step, step = 1, 2), and
+  // rank 0 stores.  Shortens the serial block chain of grids that leave SMs idle.
   int splits;
   unsigned long long wait_ns;  // wait limit of this launch (0: kWaitTimeoutNs)
 };
 
-struct TcAttnSmem {
-  static constexpr int kQ = kTcQ * 128;            // 16 KB: [128 queries][64 dims]
-  static constexpr int kK = kTcKB * 128;           // 8 KB per stage: [64 keys][64 dims]
-  static constexpr int kV = 64 * kTcKB * 2;        // 8 KB per stage: [64 dims][64 keys]
+// Layout of the kernel with KB-key blocks.
+template <int KB>
+struct TcAttnCfg {
+  static_assert(KB == 64 || KB == 128, "64- or 128-key blocks");
+  static constexpr int kChunks = KB / 32;                 // 32-key chunks per block
+  static constexpr int kCtasPerSm = KB == 64 ? 4 : 2;
+  static constexpr int kTmemCols = KB == 64 ? 128 : 256;  // S / P: [0, KB), O: [KB, KB + 64)
+  static constexpr int kQ = kTcQ * 128;                   // 16 KB: [128 queries][64 dims]
+  static constexpr int kK = KB * 128;                     // per stage: [KB keys][64 dims]
+  static constexpr int kV = 64 * KB * 2;                  // per stage: KB / 64 x [64 dims][64 keys]
   static constexpr int kStages = 2;
   static constexpr int kOffQ = 0, kOffK = kQ, kOffV = kQ + kStages * kK;
   static constexpr int kOffBar = kOffV + kStages * kV;
-  static constexpr int kBytes = kOffBar + 256 + 1024;  // barriers + alignment slack
+  static constexpr int kBytes = kOffBar + 256 + 1024;     // barriers + alignment slack
+  // Block-relative key from which blocks every query of the warp sees in full compute their
+  // exponentials on the FMA pipe (exp2_poly2) rather than the special-function unit: the last
+  // eighth of the block (larger shares measured slower: the polynomial costs issue slots).
+  static constexpr int kPolyKey = KB - KB / 8;
+  static_assert(kCtasPerSm * (kBytes + 1024) <= 228 * 1024, "shared memory of the resident CTAs");
+  static_assert(kCtasPerSm * kTmemCols <= 512, "TMEM of the resident CTAs");
 };
-static_assert(kTcCtasPerSm * (TcAttnSmem::kBytes + 1024) <= 228 * 1024, "shared memory of the resident CTAs");
-static_assert(kTcCtasPerSm * kTcTmemCols <= 512, "TMEM of the resident CTAs");
 
-// Softmax helpers for one thread's row of a 64-key block held in registers as two 32-key chunks
-// (raw fp32 scores).  `vis` bit c: chunk c is loaded (some query of the warp sees one of its
-// keys); `full` bit c: every query of the warp sees every key of chunk c (no mask).  Both are
-// warp-uniform; kAll = both chunks visible and full (the common case of global layers), which
+// Softmax helpers for one thread's row of a block held in registers as NC 32-key chunks (raw
+// fp32 scores).  `vis` bit c: chunk c is loaded (some query of the warp sees one of its keys);
+// `full` bit c: every query of the warp sees every key of chunk c (no mask).  Both are
+// warp-uniform; kAll = every chunk visible and full (the common case of global layers), which
 // compiles without a branch.
 //
 // Masks the scores this thread's query may not see to -inf and returns the block maximum.
 // Key ck + i is visible iff (unsigned)(ck + i - lo_key) <= span_keys.
-template <bool kAll>
-__device__ __forceinline__ float tc_block_max(uint32_t (&sx)[2][32], uint32_t vis, uint32_t full, int kb, int lo_key,
+template <bool kAll, int NC>
+__device__ __forceinline__ float tc_block_max(uint32_t (&sx)[NC][32], uint32_t vis, uint32_t full, int kb, int lo_key,
                                               uint32_t span_keys) {
   float mx[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
 #pragma unroll
-  for (int c = 0; c < 2; ++c) {
+  for (int c = 0; c < NC; ++c) {
     if (!kAll && !((vis >> c) & 1)) continue;
     if (!kAll && !((full >> c) & 1)) {
       const int d = kb + 32 * c - lo_key;
@@ -114,26 +124,21 @@ __device__ __forceinline__ float tc_block_max(uint32_t (&sx)[2][32], uint32_t vi
   return mx[0];
 }
 
-// Block-relative key from which blocks every query of the warp sees in full compute their
-// exponentials on the FMA pipe (exp2_poly2) rather than the special-function unit: keys 56..63,
-// an eighth of such a block (larger shares measured slower: the polynomial costs issue slots).
-constexpr int kTcPolyKey = 56;
-
 // P = 2^(s * scale - sub) for the loaded chunks (zeros for the others), stored as 16-bit pairs
 // into TMEM columns p_tmem + 16c; returns the row sum of the fp32 probabilities.
-template <bool kAll, typename T>
-__device__ __forceinline__ float tc_block_probs(const uint32_t (&sx)[2][32], uint32_t vis, float scale, float sub,
+template <bool kAll, typename T, int NC, int kPolyKey>
+__device__ __forceinline__ float tc_block_probs(const uint32_t (&sx)[NC][32], uint32_t vis, float scale, float sub,
                                                 uint32_t p_tmem) {
   float2 sm[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
   const float2 sc = make_float2(scale, scale), ns = make_float2(-sub, -sub);
 #pragma unroll
-  for (int c = 0; c < 2; ++c) {
+  for (int c = 0; c < NC; ++c) {
     uint32_t pk[16];
     if (kAll || ((vis >> c) & 1)) {
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
         const float2 x = fma2(make_float2(__uint_as_float(sx[c][i]), __uint_as_float(sx[c][i + 1])), sc, ns);
-        const float2 p = kAll && 32 * c + i >= kTcPolyKey ? exp2_poly2(x) : make_float2(ex2_approx(x.x), ex2_approx(x.y));
+        const float2 p = kAll && 32 * c + i >= kPolyKey ? exp2_poly2(x) : make_float2(ex2_approx(x.x), ex2_approx(x.y));
         sm[(i >> 1) & 3] = add2(sm[(i >> 1) & 3], p);
         pk[i >> 1] = pack2<T>(p.x, p.y);
       }
@@ -147,10 +152,13 @@ __device__ __forceinline__ float tc_block_probs(const uint32_t (&sx)[2][32], uin
   return t.x + t.y;
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
+// tmK: K rows in boxes of KB rows; tmVt: V^T in boxes of 64 keys x 64 dims.
+template <typename T, int KB>
+__global__ void __launch_bounds__(kTcThreads, TcAttnCfg<KB>::kCtasPerSm)
     tc_attention_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmVt, const TcAttnArgs a) {
+  using Cfg = TcAttnCfg<KB>;
+  constexpr int NC = Cfg::kChunks;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // The tile table, starts and lengths are written by the host before the forward pass, so they
   // are read before waiting on the previous kernel.
@@ -189,22 +197,22 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
     k_lo = max(0, q0 - a.window) & ~15;  // 16-token aligned: the V^T copy's inner coordinate
     k_hi = min(valid, q0 + kTcQ + a.window);
   }
-  const int all_blocks = k_hi > k_lo ? (k_hi - k_lo + kTcKB - 1) / kTcKB : 0;
-  // Key split: this CTA's share of the tile's blocks (k_lo stays 16-aligned: 64-key steps).
+  const int all_blocks = k_hi > k_lo ? (k_hi - k_lo + KB - 1) / KB : 0;
+  // Key split: this CTA's share of the tile's blocks (k_lo stays 16-aligned: KB-key steps).
   const bool split = a.splits > 1;
   const uint32_t rank = split ? cluster_rank() : 0;
   int n_blocks = all_blocks;
   if (split) {
-    const int h = (all_blocks + 1) / 2;
-    n_blocks = rank == 0 ? h : all_blocks - h;
-    if (rank == 1) k_lo += h * kTcKB;
+    const int h = (all_blocks + a.splits - 1) / a.splits;
+    n_blocks = max(0, min(h, all_blocks - (int)rank * h));
+    k_lo += (int)rank * h * KB;
   }
 
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem + TcAttnSmem::kOffQ;
-  uint8_t* sK = smem + TcAttnSmem::kOffK;
-  uint8_t* sV = smem + TcAttnSmem::kOffV;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + TcAttnSmem::kOffBar);
+  uint8_t* sQ = smem + Cfg::kOffQ;
+  uint8_t* sK = smem + Cfg::kOffK;
+  uint8_t* sV = smem + Cfg::kOffV;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
   uint64_t* q_full = bar + 0;
   uint64_t* k_full = bar + 1;   // [2]
   uint64_t* v_full = bar + 3;   // [2]
@@ -230,7 +238,7 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
     tma_prefetch_desc(&tmK);
     tma_prefetch_desc(&tmVt);
   }
-  if (ctl) { tmem_alloc(tmem_slot, kTcTmemCols); tmem_relinquish(); }
+  if (ctl) { tmem_alloc(tmem_slot, Cfg::kTmemCols); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -239,30 +247,32 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
 
   constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
   const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
-  const uint32_t s_tmem = tmem_base + lane_addr, p_tmem = s_tmem, o_tmem = s_tmem + 64;
+  const uint32_t s_tmem = tmem_base + lane_addr, p_tmem = s_tmem, o_tmem = s_tmem + KB;
   const int plane_rows = a.heads * a.M;
   int k_issued = 0, v_issued = 0;  // copies issued (control lane)
   // Copies into stage j & 1 (control lane), issued once the commit covering the MMA that last
   // read the stage has been observed (S_{j-2} for K, P_{j-2} V_{j-2} for V).
   auto load_k = [&](int j) {
     const int st = j & 1;
-    mbar_arrive_expect_tx(k_full + st, TcAttnSmem::kK);
-    tma_load_2d(sK + st * TcAttnSmem::kK, &tmK, k_full + st, 0, plane_rows + head * a.M + first + k_lo + j * kTcKB);
+    mbar_arrive_expect_tx(k_full + st, Cfg::kK);
+    tma_load_2d(sK + st * Cfg::kK, &tmK, k_full + st, 0, plane_rows + head * a.M + first + k_lo + j * KB);
     k_issued = j + 1;
   };
   auto load_v = [&](int j) {
     const int st = j & 1;
-    mbar_arrive_expect_tx(v_full + st, TcAttnSmem::kV);
-    tma_load_2d(sV + st * TcAttnSmem::kV, &tmVt, v_full + st, first + k_lo + j * kTcKB, head * 64);
+    mbar_arrive_expect_tx(v_full + st, Cfg::kV);
+#pragma unroll
+    for (int h = 0; h < KB / 64; ++h)
+      tma_load_2d(sV + st * Cfg::kV + h * 64 * 128, &tmVt, v_full + st, first + k_lo + j * KB + 64 * h, head * 64);
     v_issued = j + 1;
   };
-  // S_j = Q K_j^T into TMEM columns [0, 64) once K_j has landed, then commit s_full (control warp).
+  // S_j = Q K_j^T into TMEM columns [0, KB) once K_j has landed, then commit s_full (control warp).
   auto issue_s = [&](int j) -> bool {
     if (!mbar_wait(k_full + (j & 1), (j >> 1) & 1, a.err, kErrAttnWait, abort_flag, wait_ns)) return false;
     tc_fence_after();
     if (lane == 0) {
-      const uint32_t idesc_s = mma_idesc<bf>(kTcQ, kTcKB);
-      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK + (j & 1) * TcAttnSmem::kK);
+      const uint32_t idesc_s = mma_idesc<bf>(kTcQ, KB);
+      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK + (j & 1) * Cfg::kK);
 #pragma unroll
       for (int k = 0; k < 4; ++k)
         tc_mma_f16(tmem_base, smem_desc_sw128(q_addr + k * 32), smem_desc_sw128(k_addr + k * 32), idesc_s, k > 0);
@@ -271,17 +281,18 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
     __syncwarp();
     return true;
   };
-  // O (+)= P_j V_j, A = P from TMEM columns [0, 32), once V_j has landed (control warp).  Not
+  // O (+)= P_j V_j, A = P from TMEM columns [0, KB / 2), once V_j has landed (control warp).  Not
   // committed: the commit after the next S (or o_full after the last block) covers it.
   auto issue_pv = [&](int j) -> bool {
     if (!mbar_wait(v_full + (j & 1), (j >> 1) & 1, a.err, kErrAttnWait, abort_flag, wait_ns)) return false;
     tc_fence_after();
     if (lane == 0) {
       const uint32_t idesc_o = mma_idesc<bf>(kTcQ, 64);
-      const uint32_t v_addr = smem_u32(sV + (j & 1) * TcAttnSmem::kV);
+      const uint32_t v_addr = smem_u32(sV + (j & 1) * Cfg::kV);
 #pragma unroll
-      for (int k = 0; k < 4; ++k)
-        tc_mma_f16_ts(tmem_base + 64, tmem_base + 8 * k, smem_desc_sw128(v_addr + k * 32), idesc_o, (j | k) != 0);
+      for (int k = 0; k < KB / 16; ++k)
+        tc_mma_f16_ts(tmem_base + KB, tmem_base + 8 * k, smem_desc_sw128(v_addr + (k >> 2) * 64 * 128 + (k & 3) * 32),
+                      idesc_o, (j | k) != 0);
     }
     __syncwarp();
     return true;
@@ -290,7 +301,7 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
   bool ok = true;
   if (ctl && lane == 0 && n_blocks > 0) {
     if (!gathered) {
-      mbar_arrive_expect_tx(q_full, TcAttnSmem::kQ);
+      mbar_arrive_expect_tx(q_full, Cfg::kQ);
       tma_load_2d(sQ, &tmQ, q_full, 0, head * a.M + t0);
     }
     for (int j = 0; j < n_blocks && j < 2; ++j) { load_k(j); load_v(j); }
@@ -333,7 +344,7 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
 
   float m_used = -INFINITY, l = 0.f;
   for (int j = 0; j < n_blocks; ++j) {
-    const int kb = k_lo + j * kTcKB;
+    const int kb = k_lo + j * KB;
     // S_j is ready, and every MMA issued before it (P_{j-1} V_{j-1}) has completed.
     ok = ok && mbar_wait(s_full, j & 1, a.err, kErrAttnWait, abort_flag, wait_ns);
     if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
@@ -348,7 +359,7 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
     // key of the chunk; full bit c: every query of the warp sees every key.  Warp-uniform.
     uint32_t vis = 0, full = 0;
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
+    for (int c = 0; c < NC; ++c) {
       const int ck = kb + 32 * c;
       if (warp_live && ck < valid && (a.window < 0 || (ck + 31 >= qa - a.window && ck <= qa + 31 + a.window)))
         vis |= 1u << c;
@@ -356,16 +367,16 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
         full |= 1u << c;
     }
     full &= vis;
-    uint32_t sx[2][32];
+    uint32_t sx[NC][32];
 #pragma unroll
-    for (int c = 0; c < 2; ++c)
+    for (int c = 0; c < NC; ++c)
       if ((vis >> c) & 1) tmem_ld32_async(s_tmem + 32 * c, sx[c]);
 #pragma unroll
-    for (int c = 0; c < 2; ++c)
+    for (int c = 0; c < NC; ++c)
       if ((vis >> c) & 1) tmem_wait_ld(sx[c]);
-    const bool all = full == 0x3u;
-    const float bmax = all ? tc_block_max<true>(sx, vis, full, kb, lo_key, span_keys)
-                           : tc_block_max<false>(sx, vis, full, kb, lo_key, span_keys);
+    const bool all = full == (1u << NC) - 1;
+    const float bmax = all ? tc_block_max<true, NC>(sx, vis, full, kb, lo_key, span_keys)
+                           : tc_block_max<false, NC>(sx, vis, full, kb, lo_key, span_keys);
     const float m_new = bmax * kScaleLog2;
     float alpha = 1.f;
     bool o_dirty = false;
@@ -375,8 +386,8 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
     }
     const float sub = m_used == -INFINITY ? 0.f : m_used;
     // P_j goes over S_j's first columns, which this warp has read (the loads above completed).
-    const float sum = all ? tc_block_probs<true, T>(sx, vis, kScaleLog2, sub, p_tmem)
-                          : tc_block_probs<false, T>(sx, vis, kScaleLog2, sub, p_tmem);
+    const float sum = all ? tc_block_probs<true, T, NC, Cfg::kPolyKey>(sx, vis, kScaleLog2, sub, p_tmem)
+                          : tc_block_probs<false, T, NC, Cfg::kPolyKey>(sx, vis, kScaleLog2, sub, p_tmem);
     l = l * alpha + sum;
     // Rows whose maximum grew by more than 2^8 rescale O before P_j V_j accumulates into it (O
     // is settled: s_full covered every earlier MMA, and P_j V_j waits for p_full).
@@ -427,44 +438,50 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
     for (int i = 0; i < 32; ++i) { o[0][i] = 0u; o[1][i] = 0u; }
   }
   if (split) {
-    // Every CTA of the cluster reaches both barriers on every path (the early returns above
-    // are taken by both CTAs of a cluster alike).  (1): both CTAs' last MMAs have completed,
-    // so rank 0's Q, K and V buffers are free; rank 1 then writes its row there: 64 O values,
-    // its running maximum (log2 units), its sum and its status.  (2): the rows have landed.
+    // Pairwise merge, step = 1 (and 2 for four ranks).  Every CTA of the cluster reaches both
+    // barriers of every round on every path (the early returns above are taken by all CTAs of a
+    // cluster alike).  (1): every CTA's MMAs have completed, so a receiver's Q, K and V buffers
+    // are free (and, after the first round, its previous round's row has been merged); the
+    // sender writes its row there: 64 O values, its running maximum (log2 units), its sum and
+    // its status.  (2): the rows have landed and the receiver merges them.
     constexpr int kXRow = 68;  // floats per exchanged row (16-byte multiple)
-    static_assert(kTcQ * kXRow * 4 <= TcAttnSmem::kOffBar, "exchange buffer");
+    static_assert(kTcQ * kXRow * 4 <= Cfg::kOffBar, "exchange buffer");
     float* xrow = reinterpret_cast<float*>(sQ) + r * kXRow;
-    cluster_sync();
-    if (rank == 1) {
-      const uint32_t dst = cluster_addr(smem_u32(xrow), 0);
+    for (uint32_t step = 1; step < (uint32_t)a.splits; step *= 2) {
+      const bool sender = rank % (2 * step) == step, receiver = rank % (2 * step) == 0;
+      cluster_sync();
+      if (sender) {
+        const uint32_t dst = cluster_addr(smem_u32(xrow), rank - step);
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int i = 0; i < 32; i += 4)
-          st_cluster_v4(dst + (h * 32 + i) * 4, make_float4(__uint_as_float(o[h][i]), __uint_as_float(o[h][i + 1]),
-                                                            __uint_as_float(o[h][i + 2]), __uint_as_float(o[h][i + 3])));
-      st_cluster_v4(dst + 64 * 4, make_float4(m_used, l, ok ? 1.f : 0.f, 0.f));
-    }
-    cluster_sync();
-    if (rank == 0) {
-      const float4 ml = *reinterpret_cast<const float4*>(xrow + 64);
-      ok = ok && ml.z != 0.f;
-      // Rescale both partial results to the larger maximum (a side that saw no key has
-      // maximum -inf, sum 0 and O 0, and weight 0).
-      const float mx = fmaxf(m_used, ml.x);
-      const float w0 = m_used == -INFINITY ? 0.f : ex2_approx(m_used - mx);
-      const float w1 = ml.x == -INFINITY ? 0.f : ex2_approx(ml.x - mx);
-      l = l * w0 + ml.y * w1;
+          for (int i = 0; i < 32; i += 4)
+            st_cluster_v4(dst + (h * 32 + i) * 4, make_float4(__uint_as_float(o[h][i]), __uint_as_float(o[h][i + 1]),
+                                                              __uint_as_float(o[h][i + 2]), __uint_as_float(o[h][i + 3])));
+        st_cluster_v4(dst + 64 * 4, make_float4(m_used, l, ok ? 1.f : 0.f, 0.f));
+      }
+      cluster_sync();
+      if (receiver) {
+        const float4 ml = *reinterpret_cast<const float4*>(xrow + 64);
+        ok = ok && ml.z != 0.f;
+        // Rescale both partial results to the larger maximum (a side that saw no key has
+        // maximum -inf, sum 0 and O 0, and weight 0).
+        const float mx = fmaxf(m_used, ml.x);
+        const float w0 = m_used == -INFINITY ? 0.f : ex2_approx(m_used - mx);
+        const float w1 = ml.x == -INFINITY ? 0.f : ex2_approx(ml.x - mx);
+        l = l * w0 + ml.y * w1;
+        m_used = mx;
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
+        for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float4 p = *reinterpret_cast<const float4*>(xrow + h * 32 + i);
-          o[h][i] = __float_as_uint(__uint_as_float(o[h][i]) * w0 + p.x * w1);
-          o[h][i + 1] = __float_as_uint(__uint_as_float(o[h][i + 1]) * w0 + p.y * w1);
-          o[h][i + 2] = __float_as_uint(__uint_as_float(o[h][i + 2]) * w0 + p.z * w1);
-          o[h][i + 3] = __float_as_uint(__uint_as_float(o[h][i + 3]) * w0 + p.w * w1);
-        }
+          for (int i = 0; i < 32; i += 4) {
+            const float4 p = *reinterpret_cast<const float4*>(xrow + h * 32 + i);
+            o[h][i] = __float_as_uint(__uint_as_float(o[h][i]) * w0 + p.x * w1);
+            o[h][i + 1] = __float_as_uint(__uint_as_float(o[h][i + 1]) * w0 + p.y * w1);
+            o[h][i + 2] = __float_as_uint(__uint_as_float(o[h][i + 2]) * w0 + p.z * w1);
+            o[h][i + 3] = __float_as_uint(__uint_as_float(o[h][i + 3]) * w0 + p.w * w1);
+          }
+      }
     }
   }
   if (ok && rank == 0) {
@@ -502,7 +519,7 @@ __global__ void __launch_bounds__(kTcThreads, kTcCtasPerSm)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (ctl) tmem_dealloc(tmem_base, kTcTmemCols);
+  if (ctl) tmem_dealloc(tmem_base, Cfg::kTmemCols);
 }
 
 }  // namespace laya

@@ -216,17 +216,18 @@ def packed_case(lengths):
     return starts, np.asarray(lengths, np.int32), M
 
 
-@pytest.mark.parametrize("prec,impl", [("f16", 1), ("bf16", 1), ("f16", 2), ("bf16", 2), ("f16", 3), ("bf16", 3)])
+@pytest.mark.parametrize("prec,impl", [("f16", 1), ("bf16", 1), ("f16", 2), ("bf16", 2), ("f16", 3), ("bf16", 3),
+                                       ("f16", 4), ("bf16", 4)])
 @pytest.mark.parametrize("lengths,window", [([32], -1), ([7, 96], 64), ([128, 1], -1), ([250, 131], 64),
                                             ([256, 219, 145], -1), ([500], 64), ([1024, 333], -1), ([300, 77], 40)])
 def test_packed_attention_matches_oracle(lib, prec, impl, lengths, window):
     """Cases and float64 oracle of tests/test_attention.py:12-56 (h=2, seeded by M), for the
     tcgen05 kernel over 128-query tiles (impl 1: key split chosen as the forward pass does;
-    2: never; 3: always)."""
+    2: never; 3: over 2 CTAs; 4: over 4 CTAs, ranks without a key block included)."""
     check_packed_attention(lib, prec, impl, lengths, window, ramp=False)
 
 
-@pytest.mark.parametrize("prec,impl", [("f16", 1), ("bf16", 1), ("f16", 2), ("bf16", 3)])
+@pytest.mark.parametrize("prec,impl", [("f16", 1), ("bf16", 1), ("f16", 2), ("bf16", 3), ("f16", 4)])
 @pytest.mark.parametrize("lengths,window", [([1024, 333], -1), ([700], 64), ([513, 200], -1)])
 def test_packed_attention_growing_scores(lib, prec, impl, lengths, window):
     """Scores that grow along the row (keys scaled up with position), so the running maximum
