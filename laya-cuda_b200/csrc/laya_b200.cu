@@ -1225,9 +1225,10 @@ void gemm(Engine& e, bool prof, int family, int epi, const CUtensorMap& ta, cons
           int ldo, float* residual, int ldr, const float* bias, int* err, int rope = -1, const int* positions = nullptr) {
   const Tensor& w = W(e, wname);
   const int N = (int)w.shape[0], K = (int)w.shape[1];
-  // The CTA pair wins for the 16-bit output epilogues; the fp32 residual read-modify-write is as
-  // fast or faster on the 1-CTA kernel (measured at 41k rows).
-  const bool pair_ok = epi != EPI_RESIDUAL;
+  // Large classes run every epilogue on the CTA pair (the FFN-down residual GEMM measured 440 ->
+  // 402 ms per throughput step against the 1-CTA kernel: half the weight rows per CTA); small
+  // classes keep residual GEMMs on the 1-CTA kernel, where plan_small may split K.
+  const bool pair_ok = epi != EPI_RESIDUAL || M >= kPairMinRows;
   int bn;
   bool pair;
   if (M < kPairMinRows) {

@@ -88,3 +88,22 @@ def test_static_scratch_rejects_oversized_problems(lib):
     assert b"static scratch" in lib.laya_last_error(None)
     torch.cuda.synchronize()
     assert torch.equal(out, base)
+
+
+def test_static_scratch_rejects_a_misaligned_residual(lib):
+    """The partial sums are added to the residual four floats at a time, so a residual that is
+    not 16-byte aligned is refused on the host (LAYA_ERR_INVALID) before anything is launched,
+    and the residual is left as it was."""
+    x, w, base, bias = case(4, 96, 768, 768)
+    out = torch.zeros(96 * 768 + 4, dtype=torch.float32, device="cuda")
+    out[1:1 + 96 * 768] = base.flatten()
+    shifted = out[1:1 + 96 * 768]                         # 4-byte offset from an aligned buffer
+    assert shifted.data_ptr() % 16 != 0
+    before = out.clone()
+    stream = ct.c_void_p(torch.cuda.current_stream().cuda_stream)
+    code = lib.laya_op_gemm_residual_static(_lib.PRECISION_F16, ptr(x), ptr(w), 96, 768, 768, 3, ptr(shifted),
+                                            ptr(bias), None, stream)
+    assert code == _lib.ERR_INVALID
+    assert b"16-byte aligned" in lib.laya_last_error(None)
+    torch.cuda.synchronize()
+    assert torch.equal(out, before)
