@@ -9,10 +9,16 @@ token counts and answers, so they follow the reference adapter exactly
 import hashlib
 import json
 import math
+import os
 
 import numpy as np
 
 from .models import read_json
+
+# A request holds a few short texts and one state text; handing them to the tokenizer's thread
+# pool costs more than encoding them on the calling thread (a 6-text, 83-word request: ~310 us
+# through the pool, ~55 us without it).  A process that sets the variable keeps its own choice.
+os.environ.setdefault("TOKENIZERS_PARALLELISM", "false")
 
 TYPES = ("choice", "score", "noul")
 NOUL_DEFAULTS = (("false", "no, the statement does not hold"), ("true", "yes, the statement holds"))
@@ -151,11 +157,6 @@ class Laya:
         # calls; the "fast" batch path skips offset tracking, which the contract never reads.
         fast = getattr(self.tokenizer, "encode_batch_fast", None)
         if fast is not None:
-            if len(texts) <= 32:
-                # A one-text batch runs on the calling thread; a multi-text batch hands the texts
-                # to the tokenizer's thread pool, whose dispatch costs more than a request's few
-                # short texts take to encode (~60 vs ~300 us for a 5-text request).
-                return [fast([text], add_special_tokens=False)[0].ids for text in texts]
             return [e.ids for e in fast(texts, add_special_tokens=False)]
         return [e.ids for e in self.tokenizer.encode_batch(texts, add_special_tokens=False)]
 
