@@ -28,6 +28,7 @@ enum DeviceError : int {
   kErrGemmEpilogueWait = 3,
   kErrBadIndex = 4,
   kErrAttnWait = 5,
+  kErrLaunchShape = 6,  // a grid too small for a persistent kernel's work list
 };
 
 __device__ __forceinline__ unsigned long long global_ns() {

@@ -217,22 +217,40 @@ def packed_case(lengths):
 
 
 @pytest.mark.parametrize("prec,impl", [("f16", 1), ("bf16", 1), ("f16", 2), ("bf16", 2), ("f16", 3), ("bf16", 3),
-                                       ("f16", 4), ("bf16", 4)])
+                                       ("f16", 4), ("bf16", 4), ("f16", 5), ("bf16", 5), ("f16", 6), ("bf16", 6),
+                                       ("f16", 7), ("bf16", 7), ("f16", 8), ("bf16", 8)])
 @pytest.mark.parametrize("lengths,window", [([32], -1), ([7, 96], 64), ([128, 1], -1), ([250, 131], 64),
                                             ([256, 219, 145], -1), ([500], 64), ([1024, 333], -1), ([300, 77], 40)])
 def test_packed_attention_matches_oracle(lib, prec, impl, lengths, window):
     """Cases and float64 oracle of tests/test_attention.py:12-56 (h=2, seeded by M), for the
     tcgen05 kernel over 128-query tiles (impl 1: key split chosen as the forward pass does;
-    2: never; 3: over 2 CTAs; 4: over 4 CTAs, ranks without a key block included)."""
+    2: never; 3: over 2 CTAs; 4: over 4 CTAs, ranks without a key block included; 5: one tile
+    per CTA; 6: the persistent kernel on one CTA, which then runs every (tile, head) item,
+    zero-fill and unused table entries included, through one pipeline; 7, 8: the flow kernel
+    (S double-buffered, a control warp) on the resident slots / on one CTA)."""
     check_packed_attention(lib, prec, impl, lengths, window, ramp=False)
 
 
-@pytest.mark.parametrize("prec,impl", [("f16", 1), ("bf16", 1), ("f16", 2), ("bf16", 3), ("f16", 4)])
+@pytest.mark.parametrize("prec,impl", [("f16", 1), ("bf16", 1), ("f16", 2), ("bf16", 3), ("f16", 4), ("f16", 6),
+                                       ("bf16", 6), ("f16", 7), ("f16", 8), ("bf16", 8)])
 @pytest.mark.parametrize("lengths,window", [([1024, 333], -1), ([700], 64), ([513, 200], -1)])
 def test_packed_attention_growing_scores(lib, prec, impl, lengths, window):
     """Scores that grow along the row (keys scaled up with position), so the running maximum
     rises by far more than 2^8 between key blocks: exercises the rescaling of O."""
     check_packed_attention(lib, prec, impl, lengths, window, ramp=True)
+
+
+@pytest.mark.parametrize("prec,impl", [("f16", 1), ("bf16", 1), ("f16", 6), ("f16", 7), ("bf16", 8)])
+@pytest.mark.parametrize("window", [-1, 64])
+def test_packed_attention_large_grid(lib, prec, impl, window):
+    """12 heads over 48 rows of 40-900 tokens: impl 1 runs the persistent kernel on the SMs'
+    resident slots (several items per CTA, longest rows first), impl 6 on its fewest CTAs
+    (up to 128 items each).  Ten rows, the longest and shortest among them, are checked
+    against the float64 oracle; every other real row must be finite and the rest zero."""
+    lengths = [int(v) for v in np.random.default_rng(48).integers(40, 901, 48)]
+    check_packed_attention(lib, prec, impl, lengths, window, ramp=False, h=12,
+                           check_rows=sorted({int(np.argmax(lengths)), int(np.argmin(lengths)), 0, 5, 11, 17, 23,
+                                              31, 40, 47}))
 
 
 # Worst |error| - 16-bit output rounding, by precision: the 16-bit rounding of the
@@ -242,8 +260,7 @@ ATTN_LIMIT = {"bf16": 6e-3, "f16": 1.5e-3}
 ATTN_LIMIT_RAMP = {"bf16": 1e-2, "f16": 1.5e-3}
 
 
-def check_packed_attention(lib, prec, impl, lengths, window, ramp):
-    h = 2
+def check_packed_attention(lib, prec, impl, lengths, window, ramp, h=2, check_rows=None):
     tile_q = 128
     starts, lens, M = packed_case(lengths)
     cap = (M + (tile_q - 16) * len(lengths) + tile_q - 1) // tile_q + 1
@@ -271,8 +288,11 @@ def check_packed_attention(lib, prec, impl, lengths, window, ramp):
     got = out.double().cpu().numpy()
     real = np.zeros(M, bool)
     worst = 0.0
-    for start, n in zip(starts, lens):
+    for row, (start, n) in enumerate(zip(starts, lens)):
         real[start:start + n] = True
+        if check_rows is not None and row not in check_rows:
+            assert np.isfinite(got[start:start + n]).all()
+            continue
         q, k, v = xd[start:start + n].transpose(1, 2, 0, 3)
         s = q @ k.transpose(0, 2, 1) / 8
         if window >= 0:
