@@ -219,8 +219,7 @@ int laya_interleave_geglu(const uint16_t* src, uint16_t* dst, int F, int K);
  * fits 4 CTAs per SM); impl 2: never split; impl 3 / 4: always split over 2 / 4 CTAs.  Unsplit
  * grids larger than the SMs' resident slots (impl 1 and 2) run the persistent kernel, whose CTAs
  * each take a list of (tile, head) items; impl 5: never split, one tile per CTA; impl 6: the
- * persistent kernel with its fewest CTAs (up to 128 items each); impl 7 / 8: the flow kernel (S
- * double-buffered in TMEM, a control warp; 2 CTAs per SM) on the resident slots / its fewest CTAs.
+ * persistent kernel with its fewest CTAs (up to 128 items each).
  * err: device error word. */
 int laya_op_attention(int precision, int impl, const void* qkv, void* out, const int32_t* tiles, int n_tiles,
                       const int32_t* starts, const int32_t* lengths, int M, int heads, int window, int* err,

@@ -494,31 +494,8 @@ void launch_tc_attention_persistent(const AttnMaps& maps, const TcAttnArgs& args
   launch_k(kern, dim3((unsigned)grid), dim3(kTcThreads), TcPersistCfg::kBytes, st, maps.q, maps.k64, maps.vt, a);
 }
 
-// The flow kernel (S double-buffered in TMEM, a control warp): a grid of the SMs' resident CTA
-// slots (2 per SM), or, with `fewest`, of as few CTAs as hold kTcItems work items each.
-template <typename T>
-void launch_tc_attention_flow(const AttnMaps& maps, const TcAttnArgs& args, int n_tiles, cudaStream_t st, int sms,
-                              bool fewest) {
-  static uint64_t configured = 0;  // one bit per device
-  auto kern = tc_attention_flow_kernel<T>;
-  int dev = 0;
-  CK(cudaGetDevice(&dev));
-  if (!(configured & (1ull << dev))) {
-    CK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TcFlowCfg::kBytes));
-    configured |= 1ull << dev;
-  }
-  const int64_t work = (int64_t)args.heads * n_tiles;
-  if (work <= 0) return;
-  const int64_t least = (work + kTcItems - 1) / kTcItems;
-  const int64_t grid = fewest ? least : std::max(least, std::min(work, (int64_t)TcFlowCfg::kCtasPerSm * sms));
-  TcAttnArgs a = args;
-  a.n_tiles = n_tiles;
-  launch_k(kern, dim3((unsigned)grid), dim3(TcFlowCfg::kThreads), TcFlowCfg::kBytes, st, maps.q, maps.k64, maps.vt, a);
-}
-
 // Large grids of whole tiles (no key split, no gathered queries) run the persistent 64-key
-// kernel; `mode` 0 keeps one tile per CTA, 2 forces the persistent kernel with its fewest CTAs,
-// 3 / 4 run the flow kernel on the resident slots / its fewest CTAs.
+// kernel; `mode` 0 keeps one tile per CTA, 2 forces the persistent kernel with its fewest CTAs.
 template <typename T>
 void launch_tc_attention(const AttnMaps& maps, const TcAttnArgs& args, int n_tiles, cudaStream_t st, int sms,
                          int mode = 1) {
@@ -528,10 +505,9 @@ void launch_tc_attention(const AttnMaps& maps, const TcAttnArgs& args, int n_til
   if (n_tiles > 65535) fail(LAYA_ERR_INVALID, "%d attention tiles exceed the grid limit", n_tiles);
   if (a.splits != 1 && a.splits != 2 && a.splits != 4) fail(LAYA_ERR_INVALID, "attention key split %d (1, 2 or 4)", a.splits);
   const bool whole = a.splits == 1 && !a.q_index;
-  if (mode >= 2) {
-    if (!whole) fail(LAYA_ERR_INVALID, "the persistent attention kernels run whole tiles only");
-    if (mode == 2) launch_tc_attention_persistent<T>(maps, a, n_tiles, st, sms, true);
-    else launch_tc_attention_flow<T>(maps, a, n_tiles, st, sms, mode == 4);
+  if (mode == 2) {
+    if (!whole) fail(LAYA_ERR_INVALID, "the persistent attention kernel runs whole tiles only");
+    launch_tc_attention_persistent<T>(maps, a, n_tiles, st, sms, true);
   } else if (attention_block_keys(a.heads, n_tiles, a.splits, sms) == 128) {
     launch_tc_attention_kb<T, 128>(maps, a, n_tiles, st);
   } else if (whole && mode == 1) {
@@ -2073,10 +2049,10 @@ int laya_op_attention(int precision, int impl, const void* qkv, void* out, const
                       const int32_t* starts, const int32_t* lengths, int M, int heads, int window, int* err,
                       void* stream) {
   API_BEGIN
-  if (impl < 1 || impl > 8)
+  if (impl < 1 || impl > 6)
     fail(LAYA_ERR_INVALID,
          "attention impl %d (1: forward-pass rule, 2: no key split, 3: 2-way, 4: 4-way key split, 5: one tile per "
-         "CTA, 6: persistent, fewest CTAs, 7: flow, 8: flow, fewest CTAs)", impl);
+         "CTA, 6: persistent, fewest CTAs)", impl);
   const bool bf = precision == LAYA_PRECISION_BF16;
   const AttnMaps maps = attn_maps(qkv, M, heads, bf);
   TcAttnArgs t{};
@@ -2085,7 +2061,7 @@ int laya_op_attention(int precision, int impl, const void* qkv, void* out, const
   int dev = 0;
   CK(cudaGetDevice(&dev));
   t.splits = impl == 2 || impl >= 5 ? 1 : impl == 3 ? 2 : impl == 4 ? 4 : attention_splits(heads, n_tiles, sm_count(dev), window, M);
-  const int mode = impl == 5 ? 0 : impl == 6 ? 2 : impl == 7 ? 3 : impl == 8 ? 4 : 1;
+  const int mode = impl == 5 ? 0 : impl == 6 ? 2 : 1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (bf) launch_tc_attention<__nv_bfloat16>(maps, t, n_tiles, st, sm_count(dev), mode);
   else launch_tc_attention<__half>(maps, t, n_tiles, st, sm_count(dev), mode);

@@ -895,381 +895,4 @@ __global__ void __launch_bounds__(kTcThreads, TcPersistCfg::kCtasPerSm)
   if (ctl) tmem_dealloc(tmem_base, Cfg::kTmemCols);
 }
 
-// ---------------------------------------------------------------------------------------------
-// Flow form of the persistent kernel: S double-buffered in TMEM, so the tensor core computes
-// S_{g+2} = Q K_{g+2}^T while the softmax warps work on S_g, and a fifth warp that only issues
-// copies and MMAs.  The 4-CTA layout above holds P over S in 128 TMEM columns, so within a CTA
-// the softmax of a block waits for its S product and the next S waits for the softmax: the
-// special-function pipe then idles most of each block.  Here a CTA holds 256 columns (two CTAs
-// per SM):
-//   S buffers   [0, 64) and [64, 128): block g in buffer g & 1; P_g over its first 32 columns
-//   O           [128, 192)
-// Shared memory: two Q tiles (item i in buffer i & 1 of the items with key blocks), three K
-// and three V^T stages (block g in stage g % 3), the item list.
-//
-// Control warp (warp 4, lane 0), per block g:
-//   s_full[g & 1] observed (S_g complete, and with it every MMA issued before, P_{g-2} V_{g-2}
-//     included): K of block g + 3 into stage g % 3, V^T of block g + 1 into stage (g + 1) % 3,
-//     and after an item's last S, the Q tile of the item after next into that item's buffer;
-//   p_full observed (the four softmax warps wrote P_g): O (+)= P_g V_g, commit pv_done; then
-//     S_{g+2} (its item's Q tile and K stage landed), commit s_full[g & 1].
-// Softmax warps: per block wait s_full, softmax, write P, arrive p_full; a rescale of O waits
-// for pv_done of block g - 1 first; after an item's last block, wait pv_done, read O, store.
-// Every barrier is at most one phase ahead of any waiter, so parity waits are exact (S and P
-// have one barrier per S buffer).
-struct TcFlowCfg {
-  static constexpr int KB = 64, kChunks = 2;
-  static constexpr int kCtasPerSm = 2;
-  static constexpr int kThreads = 160;     // 4 softmax warps + the control warp
-  static constexpr int kTmemCols = 256;
-  static constexpr int kColO = 128;
-  static constexpr int kQ = kTcQ * 128, kK = KB * 128, kV = 64 * KB * 2;
-  static constexpr int kQBufs = 2, kKStages = 3, kVStages = 3;
-  static constexpr int kOffQ = 0, kOffK = kQBufs * kQ, kOffV = kOffK + kKStages * kK;
-  static constexpr int kOffBar = kOffV + kVStages * kV;
-  static constexpr int kOffItems = kOffBar + 256;
-  static constexpr int kBytes = kOffItems + kTcItems * 32 + 1024;
-  static constexpr int kPolyKey = KB - KB / 8;
-  static_assert(kCtasPerSm * (kBytes + 1024) <= 228 * 1024, "shared memory of the resident CTAs");
-  static_assert(kCtasPerSm * kTmemCols <= 512, "TMEM of the resident CTAs");
-};
-
-template <typename T>
-__global__ void __launch_bounds__(TcFlowCfg::kThreads, TcFlowCfg::kCtasPerSm)
-    tc_attention_flow_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                             const __grid_constant__ CUtensorMap tmVt, const TcAttnArgs a) {
-  using Cfg = TcFlowCfg;
-  constexpr int KB = Cfg::KB, NC = Cfg::kChunks;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem + Cfg::kOffQ;
-  uint8_t* sK = smem + Cfg::kOffK;
-  uint8_t* sV = smem + Cfg::kOffV;
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + Cfg::kOffBar);
-  uint64_t* q_full = bar + 0;    // [2]
-  uint64_t* k_full = bar + 2;    // [3]
-  uint64_t* v_full = bar + 5;    // [3]
-  uint64_t* s_full = bar + 8;    // [2]: S of the buffer's latest block complete
-  // [2]: the four softmax warps wrote P_g (per buffer: the warps may finish block g + 1 before
-  // the control lane has observed block g, which one barrier would fold into one parity).
-  uint64_t* p_full = bar + 10;
-  uint64_t* pv_done = bar + 12;  // P_g V_g complete
-  uint64_t* drain = bar + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 14);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int4* items = reinterpret_cast<int4*>(smem + Cfg::kOffItems);
-
-  const int n_work = a.n_tiles * a.heads;
-  int n_mine = (int)blockIdx.x < n_work ? (n_work - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  if (n_mine > kTcItems) {  // the host sizes the grid so that this never happens
-    if (threadIdx.x == 0 && a.err) atomicCAS(a.err, 0, kErrLaunchShape);
-    n_mine = kTcItems;
-  }
-  // Item descriptors (t0, t1, first, valid), (k_lo, blocks, head, 0), read before the dependency
-  // wait: the tile table, starts and lengths are written by the host.
-  for (int k = threadIdx.x; k < n_mine; k += Cfg::kThreads) {
-    const int w = blockIdx.x + k * gridDim.x;
-    const int4 tile = a.tiles[w / a.heads];
-    int first = 0, valid = tile.z < 0 ? tile.z : 0, k_lo = 0, blocks = 0;
-    if (tile.z >= 0) {
-      first = a.starts[tile.z];
-      valid = a.lengths[tile.z];
-      const int q0 = tile.x - first;
-      int k_hi = valid;
-      if (a.window >= 0) {
-        k_lo = max(0, q0 - a.window) & ~15;  // 16-token aligned: the V^T copy's inner coordinate
-        k_hi = min(valid, q0 + kTcQ + a.window);
-      }
-      blocks = k_hi > k_lo ? (k_hi - k_lo + KB - 1) / KB : 0;
-    }
-    items[2 * k] = make_int4(tile.x, tile.y, first, valid);
-    items[2 * k + 1] = make_int4(k_lo, blocks, w % a.heads, 0);
-  }
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool ctl = warp == 4;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; ++i) { mbar_init(q_full + i, 1); mbar_init(s_full + i, 1); }
-    for (int i = 0; i < 3; ++i) { mbar_init(k_full + i, 1); mbar_init(v_full + i, 1); }
-    mbar_init(p_full, 4); mbar_init(p_full + 1, 4); mbar_init(pv_done, 1); mbar_init(drain, 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-    tma_prefetch_desc(&tmQ);
-    tma_prefetch_desc(&tmK);
-    tma_prefetch_desc(&tmVt);
-  }
-  if (ctl) { tmem_alloc(tmem_slot, Cfg::kTmemCols); tmem_relinquish(); }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem_base = *tmem_slot;
-  pdl_wait();
-  auto next_item = [&](int k) {  // the first item at or after k that has key blocks
-    while (k < n_mine && items[2 * k + 1].y == 0) ++k;
-    return k;
-  };
-  constexpr bool bf = std::is_same<T, __nv_bfloat16>::value;
-
-  bool ok = true;
-  // Control lane state.  Cursors: the next K / V^T block to load (item, blocks left, coordinate:
-  // K the tile's row in the tensor map, V^T the first key's column), the next S to issue (item,
-  // blocks left, index among the items with key blocks), the next item whose Q tile to load and
-  // the Q tiles loaded.  ph: bit b (K stages 0-2, V stages 3-5, Q buffers 6-7) the parity of the
-  // next copy into that buffer, bit 8 + b set once a copy was issued into it.
-  uint32_t ph = 0;
-  if (ctl) {
-    if (lane == 0) {
-      int k_item = n_mine, k_left = 0, k_at = 0;
-      int v_item = n_mine, v_left = 0, v_at = 0, v_head = 0;
-      int s_item = n_mine, s_left = 0, s_seq = 0;
-      int q_item = next_item(0), q_count = 0;
-      auto issued = [&](int b) {
-        ph ^= 1u << b;
-        ph |= 256u << b;
-      };
-      auto seek_k = [&](int item) {
-        k_item = next_item(item);
-        if (k_item < n_mine) {
-          const int4 d0 = items[2 * k_item], d1 = items[2 * k_item + 1];
-          k_left = d1.y;
-          k_at = (a.heads + d1.z) * a.M + d0.z + d1.x;
-        }
-      };
-      auto seek_v = [&](int item) {
-        v_item = next_item(item);
-        if (v_item < n_mine) {
-          const int4 d0 = items[2 * v_item], d1 = items[2 * v_item + 1];
-          v_left = d1.y;
-          v_at = d0.z + d1.x;
-          v_head = d1.z;
-        }
-      };
-      auto seek_s = [&](int item) {
-        s_item = next_item(item);
-        if (s_item < n_mine) s_left = items[2 * s_item + 1].y;
-      };
-      auto load_k = [&](int block) {  // block: the block counter g of the copy
-        const int st = block % 3;
-        mbar_arrive_expect_tx(k_full + st, Cfg::kK);
-        tma_load_2d(sK + st * Cfg::kK, &tmK, k_full + st, 0, k_at);
-        issued(st);
-        if (--k_left > 0) k_at += KB;
-        else seek_k(k_item + 1);
-      };
-      auto load_v = [&](int block) {
-        const int st = block % 3;
-        mbar_arrive_expect_tx(v_full + st, Cfg::kV);
-        tma_load_2d(sV + st * Cfg::kV, &tmVt, v_full + st, v_at, v_head * 64);
-        issued(3 + st);
-        if (--v_left > 0) v_at += KB;
-        else seek_v(v_item + 1);
-      };
-      auto load_q = [&]() {
-        const int buf = q_count & 1;
-        const int4 d0 = items[2 * q_item], d1 = items[2 * q_item + 1];
-        mbar_arrive_expect_tx(q_full + buf, Cfg::kQ);
-        tma_load_2d(sQ + buf * Cfg::kQ, &tmQ, q_full + buf, 0, d1.z * a.M + d0.x);
-        issued(6 + buf);
-        ++q_count;
-        q_item = next_item(q_item + 1);
-      };
-      // S_block = Q K_block^T into S buffer block & 1, once its item's Q tile and the K stage
-      // have landed; commit s_full of that buffer.
-      auto issue_s = [&](int block) -> bool {
-        const int buf = s_seq & 1;
-        if (!mbar_wait(q_full + buf, (s_seq >> 1) & 1, a.err, kErrAttnWait, abort_flag, wait_limit(a.wait_ns)))
-          return false;
-        if (!mbar_wait(k_full + block % 3, (block / 3) & 1, a.err, kErrAttnWait, abort_flag, wait_limit(a.wait_ns)))
-          return false;
-        tc_fence_after();
-        const uint32_t idesc_s = mma_idesc<bf>(kTcQ, KB);
-        const uint32_t q_addr = smem_u32(sQ + buf * Cfg::kQ), k_addr = smem_u32(sK + (block % 3) * Cfg::kK);
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          tc_mma_f16(tmem_base + 64 * (block & 1), smem_desc_sw128(q_addr + k * 32), smem_desc_sw128(k_addr + k * 32),
-                     idesc_s, k > 0);
-        tc_commit(s_full + (block & 1));
-        if (--s_left == 0) {
-          seek_s(s_item + 1);
-          ++s_seq;
-        }
-        return true;
-      };
-
-      seek_k(0);
-      seek_v(0);
-      seek_s(0);
-      for (int i = 0; i < 2 && q_item < n_mine; ++i) load_q();
-      for (int i = 0; i < 3 && k_item < n_mine; ++i) load_k(i);
-      for (int i = 0; i < 2 && v_item < n_mine; ++i) load_v(i);
-      for (int i = 0; i < 2 && s_item < n_mine && ok; ++i) ok = issue_s(i);
-      int g = 0;
-      for (int k = next_item(0); k < n_mine && ok; k = next_item(k + 1)) {
-        const int n_blocks = items[2 * k + 1].y;
-        for (int j = 0; j < n_blocks; ++j, ++g) {
-          ok = mbar_wait(s_full + (g & 1), (g >> 1) & 1, a.err, kErrAttnWait, abort_flag, wait_limit(a.wait_ns));
-          if (!ok) break;
-          // S_g completed (and every MMA issued before it): its K stage takes block g + 3,
-          // the V^T stage of P_{g-2} V_{g-2} takes block g + 1 (blocks 0-2 and 0-1 were loaded
-          // up front, so the cursors stand at exactly these blocks); after the item's last S
-          // its Q buffer takes the item after next.
-          if (k_item < n_mine) load_k(g + 3);
-          if (g >= 1 && v_item < n_mine) load_v(g + 1);
-          if (j + 1 == n_blocks && q_item < n_mine) load_q();
-          ok = mbar_wait(p_full + (g & 1), (g >> 1) & 1, a.err, kErrAttnWait, abort_flag, wait_limit(a.wait_ns)) &&
-               mbar_wait(v_full + g % 3, (g / 3) & 1, a.err, kErrAttnWait, abort_flag, wait_limit(a.wait_ns));
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t idesc_o = mma_idesc<bf>(kTcQ, 64);
-          const uint32_t v_addr = smem_u32(sV + (g % 3) * Cfg::kV);
-#pragma unroll
-          for (int kk = 0; kk < KB / 16; ++kk)
-            tc_mma_f16_ts(tmem_base + Cfg::kColO, tmem_base + 64 * (g & 1) + 8 * kk,
-                          smem_desc_sw128(v_addr + kk * 32), idesc_o, j > 0 || kk > 0);
-          tc_commit(pv_done);
-          if (s_item < n_mine) ok = issue_s(g + 2);
-        }
-      }
-    }
-    __syncwarp();
-  }
-  else {
-    // Softmax warps 0-3: thread r owns query row r of the tile (TMEM lane r).
-    const int r = threadIdx.x;
-    const uint32_t lane_addr = (uint32_t)(warp * 32) << 16;
-    const uint32_t o_tmem = tmem_base + lane_addr + Cfg::kColO;
-    T* const out = reinterpret_cast<T*>(a.out);
-    constexpr float kScaleLog2 = 0.125f * 1.4426950408889634f;
-    int g = 0;
-    for (int k = 0; k < n_mine && ok; ++k) {
-      const int n_blocks = items[2 * k + 1].y;
-      if (n_blocks == 0) {
-        // Tokens past the last row (or a tile no key reaches): zeros; unused entries: nothing.
-        const int4 d0 = items[2 * k];
-        const int head = items[2 * k + 1].z;
-        if (d0.w != -2)
-          for (int i = threadIdx.x; i < (d0.y - d0.x) * 8; i += kTcThreads) {
-            const int t = d0.x + (i >> 3);
-            *reinterpret_cast<uint4*>(out + (size_t)t * (a.heads * 64) + head * 64 + (i & 7) * 8) =
-                make_uint4(0, 0, 0, 0);
-          }
-        continue;
-      }
-      const int valid = items[2 * k].w, k_lo = items[2 * k + 1].x;
-      const int q = items[2 * k].x - items[2 * k].z + r;  // row-relative index of this thread's query
-      const int qa = q - lane;                            // the warp's first query
-      int lo_key = a.window >= 0 ? q - a.window : 0;
-      const int hi_key = a.window >= 0 ? min(valid - 1, q + a.window) : valid - 1;
-      uint32_t span_keys = (uint32_t)(hi_key - lo_key);
-      if (hi_key < lo_key) { lo_key = 1 << 30; span_keys = 0; }
-      const bool warp_live = qa < valid;
-      float m_used = -INFINITY, l = 0.f;
-      for (int j = 0; j < n_blocks; ++j, ++g) {
-        const int kb = k_lo + j * KB;
-        ok = ok && mbar_wait(s_full + (g & 1), (g >> 1) & 1, a.err, kErrAttnWait, abort_flag, wait_limit(a.wait_ns));
-        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t s_tmem = tmem_base + lane_addr + 64 * (g & 1);
-        uint32_t vis = 0, full = 0;
-#pragma unroll
-        for (int c = 0; c < NC; ++c) {
-          const int ck = kb + 32 * c;
-          if (warp_live && ck < valid && (a.window < 0 || (ck + 31 >= qa - a.window && ck <= qa + 31 + a.window)))
-            vis |= 1u << c;
-          if (ck + 31 < valid && (a.window < 0 || (ck >= qa + 31 - a.window && ck + 31 <= qa + a.window)))
-            full |= 1u << c;
-        }
-        full &= vis;
-        uint32_t sx[NC][32];
-#pragma unroll
-        for (int c = 0; c < NC; ++c)
-          if ((vis >> c) & 1) tmem_ld32_async(s_tmem + 32 * c, sx[c]);
-#pragma unroll
-        for (int c = 0; c < NC; ++c)
-          if ((vis >> c) & 1) tmem_wait_ld(sx[c]);
-        const bool all = full == (1u << NC) - 1;
-        const float bmax = all ? tc_block_max<true, NC>(sx, vis, full, kb, lo_key, span_keys)
-                               : tc_block_max<false, NC>(sx, vis, full, kb, lo_key, span_keys);
-        const float m_new = bmax * kScaleLog2;
-        float alpha = 1.f;
-        bool o_dirty = false;
-        if (m_new > m_used + kTcRescaleLog2) {  // false while every visible key is masked
-          if (m_used != -INFINITY) { alpha = ex2_approx(m_used - m_new); o_dirty = true; }
-          m_used = m_new;
-        }
-        const float sub = m_used == -INFINITY ? 0.f : m_used;
-        // P_g over the first 32 columns of S_g's buffer, which this warp has read.
-        const float sum = all ? tc_block_probs<true, T, NC, Cfg::kPolyKey>(sx, vis, kScaleLog2, sub, s_tmem)
-                              : tc_block_probs<false, T, NC, Cfg::kPolyKey>(sx, vis, kScaleLog2, sub, s_tmem);
-        l = l * alpha + sum;
-        if (__any_sync(0xffffffffu, o_dirty)) {
-          // O must hold P_{g-1} V_{g-1} before it is rescaled (o_dirty needs an earlier block of
-          // this item, so g >= 1); P_g V_g waits for p_full below.
-          ok = mbar_wait(pv_done, (g - 1) & 1, a.err, kErrAttnWait, abort_flag, wait_limit(a.wait_ns));
-          if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-          tc_fence_after();
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
-            uint32_t o[32];
-            tmem_ld32_async(o_tmem + 32 * h, o);
-            tmem_wait_ld(o);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(o_tmem + 32 * h, o);
-          }
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(p_full + (g & 1));
-      }
-      if (!ok) break;
-      // Normalise and store this item's rows (zeros for padding queries) once its last P V
-      // product has completed.
-      ok = mbar_wait(pv_done, (g - 1) & 1, a.err, kErrAttnWait, abort_flag, wait_limit(a.wait_ns));
-      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      tc_fence_after();
-      const int token = items[2 * k].x + r;
-      const bool store = token < items[2 * k].y;
-      const bool live = q < valid && l > 0.f;
-      const float inv = live ? 1.f / l : 0.f;
-      T* dst = out + (size_t)token * (a.heads * 64) + items[2 * k + 1].z * 64;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t o[32];
-        tmem_ld32_async(o_tmem + 32 * h, o);
-        tmem_wait_ld(o);
-        if (store) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            float v[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) v[e] = live ? __uint_as_float(o[i + e]) * inv : 0.f;
-            uint4 w;
-            w.x = pack2<T>(v[0], v[1]); w.y = pack2<T>(v[2], v[3]);
-            w.z = pack2<T>(v[4], v[5]); w.w = pack2<T>(v[6], v[7]);
-            *reinterpret_cast<uint4*>(dst + h * 32 + i) = w;
-          }
-        }
-      }
-    }
-  }
-  if (ctl && lane == 0) {
-    // Every MMA issued completes before the TMEM is released, and every copy lands before the
-    // CTA exits (bounded waits).
-    tc_commit(drain);
-    mbar_drain(drain, 0);
-    if (*abort_flag) {
-      // The last copy into each buffer has the parity before its bit's last toggle.  Buffers
-      // 0-2: k_full, 3-5: v_full, 6-7: q_full (barriers 2-4, 5-7, 0-1).
-      for (int b = 0; b < 8; ++b)
-        if ((ph >> (8 + b)) & 1) mbar_drain(bar + (b < 6 ? b + 2 : b - 6), ((ph >> b) & 1) ^ 1);
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (ctl) tmem_dealloc(tmem_base, Cfg::kTmemCols);
-}
-
 }  // namespace laya

@@ -217,8 +217,7 @@ def packed_case(lengths):
 
 
 @pytest.mark.parametrize("prec,impl", [("f16", 1), ("bf16", 1), ("f16", 2), ("bf16", 2), ("f16", 3), ("bf16", 3),
-                                       ("f16", 4), ("bf16", 4), ("f16", 5), ("bf16", 5), ("f16", 6), ("bf16", 6),
-                                       ("f16", 7), ("bf16", 7), ("f16", 8), ("bf16", 8)])
+                                       ("f16", 4), ("bf16", 4), ("f16", 5), ("bf16", 5), ("f16", 6), ("bf16", 6)])
 @pytest.mark.parametrize("lengths,window", [([32], -1), ([7, 96], 64), ([128, 1], -1), ([250, 131], 64),
                                             ([256, 219, 145], -1), ([500], 64), ([1024, 333], -1), ([300, 77], 40)])
 def test_packed_attention_matches_oracle(lib, prec, impl, lengths, window):
@@ -226,13 +225,12 @@ def test_packed_attention_matches_oracle(lib, prec, impl, lengths, window):
     tcgen05 kernel over 128-query tiles (impl 1: key split chosen as the forward pass does;
     2: never; 3: over 2 CTAs; 4: over 4 CTAs, ranks without a key block included; 5: one tile
     per CTA; 6: the persistent kernel on one CTA, which then runs every (tile, head) item,
-    zero-fill and unused table entries included, through one pipeline; 7, 8: the flow kernel
-    (S double-buffered, a control warp) on the resident slots / on one CTA)."""
+    zero-fill and unused table entries included, through one pipeline)."""
     check_packed_attention(lib, prec, impl, lengths, window, ramp=False)
 
 
 @pytest.mark.parametrize("prec,impl", [("f16", 1), ("bf16", 1), ("f16", 2), ("bf16", 3), ("f16", 4), ("f16", 6),
-                                       ("bf16", 6), ("f16", 7), ("f16", 8), ("bf16", 8)])
+                                       ("bf16", 6)])
 @pytest.mark.parametrize("lengths,window", [([1024, 333], -1), ([700], 64), ([513, 200], -1)])
 def test_packed_attention_growing_scores(lib, prec, impl, lengths, window):
     """Scores that grow along the row (keys scaled up with position), so the running maximum
@@ -240,7 +238,7 @@ def test_packed_attention_growing_scores(lib, prec, impl, lengths, window):
     check_packed_attention(lib, prec, impl, lengths, window, ramp=True)
 
 
-@pytest.mark.parametrize("prec,impl", [("f16", 1), ("bf16", 1), ("f16", 6), ("f16", 7), ("bf16", 8)])
+@pytest.mark.parametrize("prec,impl", [("f16", 1), ("bf16", 1), ("f16", 6), ("bf16", 6)])
 @pytest.mark.parametrize("window", [-1, 64])
 def test_packed_attention_large_grid(lib, prec, impl, window):
     """12 heads over 48 rows of 40-900 tokens: impl 1 runs the persistent kernel on the SMs'
