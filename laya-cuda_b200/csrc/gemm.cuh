@@ -342,12 +342,22 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tba
   }
 }
 
-template <int BN, int EPI, typename T>
+template <int BN, int EPI, typename T, int NI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const GemmArgs args) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
+  // NI > 1: NI threads (lane 0 of warp 1 and of epilogue warps 2..NI) issue the MMAs of a tile,
+  // issuer i taking k-blocks i, i + NI, ... into its own accumulator; the epilogue warps add the
+  // accumulators before the epilogue.  One thread's tcgen05.mma stream runs about one
+  // instruction per ~100 ns whatever N is up to 256, so a tile of N <= 128 leaves most of the
+  // tensor core idle with one issuer; independent streams from several threads run
+  // concurrently.  Only for grids in which every CTA has at most one tile (the host checks), so
+  // the epilogue warps are idle while they issue.  Each stage always goes to the same issuer
+  // (NI divides S), so every issuer sees its stages' phases in order.
+  static_assert(NI == 1 || (S % NI == 0 && NI <= kEpiWarps + 1), "issuers must divide the stages");
+  constexpr int kCols = NI == 1 ? Cfg::kTmemCols : (NI * BN < 32 ? 32 : NI * BN);
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -358,7 +368,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t* tfull = bars + 2 * S;
   uint64_t* tempty = bars + 2 * S + 2;
   uint64_t* drain = bars + 2 * S + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 5);
+  uint64_t* presum = bars + 2 * S + 5;  // NI > 1: every epilogue warp added its share
+  uint64_t* idrain = bars + 2 * S + 6;  // [NI - 1]: drains of the extra issuers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * S + 6 + (NI > 1 ? NI - 1 : 0));
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const unsigned long long wait_ns = wait_limit(args.wait_ns);
 
@@ -374,13 +386,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], 1); mbar_init(&tempty[i], kEpiWarps); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&tfull[i], NI); mbar_init(&tempty[i], kEpiWarps); }
     mbar_init(drain, 1);
+    mbar_init(presum, kEpiWarps);
+    for (int i = 0; i + 1 < NI; ++i) mbar_init(&idrain[i], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) { tma_prefetch_desc(&tmA); tma_prefetch_desc(&tmB); }
-  if (warp == 1) { tmem_alloc(tmem_slot, Cfg::kTmemCols); tmem_relinquish(); }
+  if (warp == 1) { tmem_alloc(tmem_slot, kCols); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -394,6 +408,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int r = t - split * m_blocks * n_blocks;
     mb = r / n_blocks;
     nb = r - mb * n_blocks;
+  };
+
+  // NI > 1 (one tile per CTA): issuer i's share of the tile's k-blocks into accumulator i, then
+  // a commit to tfull.  Bounded waits; the caller drains its own MMAs afterwards.
+  auto issue_share = [&](int i) {
+    const uint32_t idesc = mma_idesc<std::is_same<T, __nv_bfloat16>::value>(kBM, BN);
+    const uint32_t d_tmem = tmem_base + (uint32_t)(i * BN);
+    bool ok = (int)blockIdx.x < tiles;
+    for (int kb = i; kb < k_blocks && ok; kb += NI) {
+      const int stage = kb % S;
+      if (!mbar_wait(&full[stage], (kb / S) & 1, args.err, kErrGemmMmaWait, abort_flag, wait_ns)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t a0 = smem_u32(sA + stage * Cfg::kStageA);
+      const uint32_t b0 = smem_u32(sB + stage * Cfg::kStageB);
+#pragma unroll
+      for (int k = 0; k < kBK / 16; ++k)
+        tc_mma_f16(d_tmem, smem_desc_sw128(a0 + k * 32), smem_desc_sw128(b0 + k * 32), idesc,
+                   (kb > i || k > 0) ? 1u : 0u);
+      tc_commit(&empty[stage]);
+    }
+    if (ok) tc_commit(&tfull[0]);
   };
 
   if (warp == 0) {
@@ -447,7 +482,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1) {
     pdl_wait();
-    if (lane == 0) {
+    if (lane == 0 && NI > 1) {
+      issue_share(0);
+      tc_commit(drain);
+      mbar_drain(drain, 0);
+    } else if (lane == 0) {
       const uint32_t idesc = mma_idesc<std::is_same<T, __nv_bfloat16>::value>(kBM, BN);
       int stage = 0; uint32_t phase = 0;
       int acc = 0; uint32_t acc_phase = 0;
@@ -492,9 +531,44 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       QkvPipe<BN, T> qp;
       if (EPI == EPI_RESIDUAL) rp.start(args, row0, nb * BN, half, lane);
       if (EPI == EPI_QKV) qp.start(args, row0 + lane, nb * BN, half);
+      if (NI > 1 && warp - 1 < NI) {
+        // Extra issuer (one tile per CTA: the loop runs once).
+        if (lane == 0) {
+          issue_share(warp - 1);
+          tc_commit(&idrain[warp - 2]);
+          mbar_drain(&idrain[warp - 2], 0);
+        }
+        __syncwarp();
+      }
       if (!mbar_wait(&tfull[acc], acc_phase, args.err, kErrGemmEpilogueWait, abort_flag, wait_ns)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      if (NI > 1) {
+        // Accumulator 0 += accumulators 1.. (those that received k-blocks): this warp adds the
+        // 32-column chunks h of its lane quarter with h % 2 == half, then every epilogue warp
+        // waits until all shares are in (the epilogue reads columns across the halves).
+        const int used = k_blocks < NI ? k_blocks : NI;
+#pragma unroll 1
+        for (int h = half; h < BN / 32; h += 2) {
+          uint32_t v[32];
+          tmem_ld32_async(tbase + 32 * h, v);
+          tmem_wait_ld(v);
+          for (int i = 1; i < used; ++i) {
+            uint32_t w[32];
+            tmem_ld32_async(tbase + (uint32_t)(i * BN) + 32 * h, w);
+            tmem_wait_ld(w);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) + __uint_as_float(w[e]));
+          }
+          tmem_st32(tbase + 32 * h, v);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(presum);
+        if (!mbar_wait(presum, 0, args.err, kErrGemmEpilogueWait, abort_flag, wait_ns)) break;
+        tc_fence_after();
+      }
       if (EPI == EPI_RESIDUAL) rp.finish(args, tbase, row0, nb * BN, half, lane, stage);
       else if (EPI == EPI_QKV) qp.finish(args, tbase, row0, nb * BN, half, lane, stage);
       else epilogue_tile<BN, EPI, T>(args, tbase, row0, nb * BN, split, half, lane, stage);
@@ -508,7 +582,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  if (warp == 1) tmem_dealloc(tmem_base, kCols);
 }
 
 

@@ -176,10 +176,10 @@ void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cuda
 // ---------------------------------------------------------------------------------------------
 // Kernel dispatch
 // ---------------------------------------------------------------------------------------------
-template <typename T, int BN, int EPI>
-void launch_gemm_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t st) {
+template <typename T, int BN, int EPI, int NI>
+void launch_gemm_ni(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t st) {
   static uint64_t configured = 0;  // one bit per device
-  auto kern = gemm_kernel<BN, EPI, T>;
+  auto kern = gemm_kernel<BN, EPI, T, NI>;
   int dev = 0;
   CK(cudaGetDevice(&dev));
   if (!(configured & (1ull << dev))) {
@@ -187,6 +187,28 @@ void launch_gemm_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmAr
     configured |= 1ull << dev;
   }
   launch_k(kern, dim3(grid), dim3(kGemmThreads), GemmCfg<BN>::kSmemBytes, st, ta, tb, a);
+}
+
+// MMA issuers of a 1-CTA GEMM: one thread's tcgen05.mma stream runs about one instruction per
+// ~100 ns whatever the column tile, so grids in which every CTA has a single tile of 64 or 128
+// columns spread its k-blocks over 4 or 2 issuing threads (independent accumulators added
+// before the epilogue).  Larger grids keep one issuer and double-buffered accumulators.
+int gemm_issuers(int bn, int tiles, int grid, int k_blocks) {
+  if (tiles > grid) return 1;
+  if (bn == 64) return k_blocks >= 4 ? 4 : 1;
+  if (bn == 128) return k_blocks >= 2 ? 2 : 1;
+  return 1;
+}
+
+template <typename T, int BN, int EPI>
+void launch_gemm_inst(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int grid, cudaStream_t st) {
+  const int tiles = ((a.M + kBM - 1) / kBM) * (a.N / BN) * a.splits;
+  const int ni = gemm_issuers(BN, tiles, grid, a.K / kBK / a.splits);
+  constexpr int kMulti = BN == 64 ? 4 : BN == 128 ? 2 : 1;
+  if constexpr (kMulti > 1) {
+    if (ni == kMulti) return launch_gemm_ni<T, BN, EPI, kMulti>(ta, tb, a, grid, st);
+  }
+  launch_gemm_ni<T, BN, EPI, 1>(ta, tb, a, grid, st);
 }
 
 // CTA-pair GEMM: clusters of 2 (cta_group::2), plus programmatic serialisation.
