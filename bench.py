@@ -407,6 +407,29 @@ def stream_latency(path, arch, count=200, seed=2):
             "tokens_per_request_mean": round(float(np.mean(tokens)), 1)}
 
 
+def api_throughput(path, arch, count=1024, seed=5):
+    """Configuration-5-shaped requests as text (states of U[256,1024] words, 3 choice questions x 8
+    options) through the user-facing BatchEngine: tokenisation, batching under 64 questions and
+    64 x 1024 packed tokens, packing, H2D, forward, D2H and decoding into answer dicts, all
+    inside the timed region (first submit to last answer).  The graphs of the shape classes are
+    captured by an untimed pass over the same requests first."""
+    from laya_cuda import BatchEngine
+    from laya_cuda import synthetic as S
+    rng = np.random.default_rng(seed)
+    requests = [S.stream_request_texts(rng, arch["vocab"], lengths=LENGTHS, questions=(QUESTIONS, QUESTIONS),
+                                       options=(OPTIONS, OPTIONS)) for _ in range(count)]
+    with BatchEngine(path, max_batch_size=MICRO, max_batch_tokens=MICRO * 1024, max_pending=count,
+                     max_wait_ms=1, max_cached_shapes=64) as engine:
+        for _ in range(2):
+            t0 = time.perf_counter()
+            futures = [engine.submit(state, questions) for state, questions in requests]
+            answers = [f.result(300) for f in futures]
+            seconds = time.perf_counter() - t0
+    questions = sum(len(a["answers"]) for a in answers)
+    return {"value": round(questions / seconds, 2), "unit": "sequences/s", "requests": count, "sequences": questions,
+            "api": "BatchEngine.submit(text) -> answer dicts (tokenise, batch, pack, H2D, forward, D2H, decode)"}
+
+
 def run_engine(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
@@ -542,6 +565,7 @@ def run_engine(args, rank, world, local_rank):
                 typed = S.architecture("laya-typed-decisions")
                 stream = stream_latency(S.cached_checkpoint(CACHE, "laya-typed-decisions", seed=0), typed)
         loads = cold_loads(["laya", "laya-multilingual"]) if world == 1 and args.latency != "none" else None
+        api_rate = api_throughput(path, arch) if world == 1 and args.latency == "full" else None
         cpu = None
         if world == 1 and args.cpu_budget > 0:
             weights = S.make_weights(arch, seed=0)
@@ -561,7 +585,7 @@ def run_engine(args, rank, world, local_rank):
                            "l2": "inputs larger than L2 (no flush)"},
                 "gpu_launches": launches * args.steps, "kernels": fam,
                 "kernels_note": "per family over one profiled step (event pair around every launch), after the timed steps",
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "api_throughput": api_rate,
                 "clocks": clocks.summary(), "latency_batch1": lat, "stream_config4": stream, "cold_load": loads,
                 "attention_flops_per_step": attention_flops([len(i[0]) for i in items], arch)}
     engine.close()

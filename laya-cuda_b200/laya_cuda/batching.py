@@ -10,7 +10,8 @@ worker releases the GPU.
 Unlike the reference's worker, which runs one synchronous Runtime.predict per batch
 (batching.py:122), this one pipelines through Runtime.submit / collect: batch i+1 is packed and
 launched before batch i is collected and decoded, and requests that arrive while a batch runs
-are tokenised before it is collected, so tokenisation, packing and decoding overlap the device.
+are tokenised before it is collected, and a burst of requests is tokenised batch by batch, so
+tokenisation, packing and decoding overlap the device.
 """
 from concurrent.futures import Future
 from copy import deepcopy
@@ -104,25 +105,28 @@ class BatchEngine:
             taken, self._queue = self._queue, []
             return taken
 
-    def _prepare(self, engine, active, taken):
-        """Tokenises newly taken requests (while a previous batch may still run on the device)."""
-        prepared = []
-        active.extend(taken)
-        for request in taken:
-            if not request[0].set_running_or_notify_cancel():
-                self._finish(request)
-                active.remove(request)
-                continue
-            try:
-                items = engine.adapter.prepare(request[1], request[2])
-                tokens = sum(span(len(item[0])) for item in items)
-                if len(items) > self.max_batch_size or tokens > self.max_batch_tokens:
-                    raise ValueError("Request exceeds batch budget; increase limits or submit fewer questions")
-                prepared.append((request, items, tokens))
-            except Exception as error:
-                active.remove(request)
-                self._finish(request, error=error)
-        return prepared
+    def _prepare(self, engine, active, request):
+        """Tokenises one taken request (already in `active`); returns (request, items, packed
+        tokens), or None when it was cancelled or failed (its future is then resolved)."""
+        if not request[0].set_running_or_notify_cancel():
+            self._finish(request)
+            active.remove(request)
+            return None
+        try:
+            items = engine.adapter.prepare(request[1], request[2])
+            tokens = sum(span(len(item[0])) for item in items)
+            if len(items) > self.max_batch_size or tokens > self.max_batch_tokens:
+                raise ValueError("Request exceeds batch budget; increase limits or submit fewer questions")
+            return request, items, tokens
+        except Exception as error:
+            active.remove(request)
+            self._finish(request, error=error)
+            return None
+
+    def _fills(self, prepared):
+        """Whether the prepared requests reach one batch's question or token budget."""
+        return (sum(len(entry[1]) for entry in prepared) >= self.max_batch_size
+                or sum(entry[2] for entry in prepared) >= self.max_batch_tokens)
 
     def _next_batch(self, prepared):
         """First-fit in arrival order under both budgets (questions and packed 16-token row spans);
@@ -180,11 +184,21 @@ class BatchEngine:
                     self._finish(request, error=error)
             offset += len(rows)
 
-    def _run(self, engine, active, prepared, pending):
-        """Launches the prepared requests batch by batch.  Each batch is launched before the
-        previous one is collected and decoded, so host work overlaps the device (at most two
-        batches in flight).  Returns the last launched batch, still in flight, or None."""
-        while prepared:
+    def _run(self, engine, active, taken, pending):
+        """Tokenises and launches the taken requests batch by batch.  Requests are tokenised only
+        as far as the next batch needs, so a burst's later requests are tokenised while earlier
+        batches run; each batch is launched before the previous one is collected and decoded
+        (at most two batches in flight).  Returns the last launched batch, still in flight, or
+        None."""
+        active.extend(taken)
+        waiting, prepared = list(taken), []
+        while waiting or prepared:
+            while waiting and not self._fills(prepared):
+                entry = self._prepare(engine, active, waiting.pop(0))
+                if entry is not None:
+                    prepared.append(entry)
+            if not prepared:
+                break
             batch, prepared, questions = self._next_batch(prepared)
             launched = self._launch(engine, active, batch, questions)
             if pending is not None:
@@ -207,7 +221,7 @@ class BatchEngine:
                     self._complete(engine, active, *pending)
                     pending = None
                     continue
-                pending = self._run(engine, active, self._prepare(engine, active, taken), pending)
+                pending = self._run(engine, active, taken, pending)
             if pending is not None:
                 self._complete(engine, active, *pending)
         except BaseException as error:
