@@ -200,8 +200,7 @@ struct QkvPipe {
       const int part = n / width;
       const int head = (n - part * width) >> 6;
       float lo[16], hi[16];
-      tmem_ld16(tbase + 64 * c + 16 * half, lo);
-      tmem_ld16(tbase + 64 * c + 32 + 16 * half, hi);
+      tmem_ld16x2(tbase + 64 * c + 16 * half, tbase + 64 * c + 32 + 16 * half, lo, hi);
       if (a.bias) {
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
@@ -274,16 +273,19 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tba
       uint4 p[8];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        float g[32], u[32];
-        tmem_ld32(tbase + c * 128 + h * 32, g);
-        tmem_ld32(tbase + c * 128 + 64 + h * 32, u);
+        // Gate and up columns loaded together, one wait.
+        uint32_t g[32], u[32];
+        tmem_ld32_async(tbase + c * 128 + h * 32, g);
+        tmem_ld32_async(tbase + c * 128 + 64 + h * 32, u);
+        tmem_wait_ld(g);
+        tmem_wait_ld(u);
 #pragma unroll
         for (int i = 0; i < 32; i += 8) {
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float2 y = mul2(gelu_erf2(make_float2(g[i + 2 * e], g[i + 2 * e + 1])),
-                                  make_float2(u[i + 2 * e], u[i + 2 * e + 1]));
+            const float2 y = mul2(gelu_erf2(make_float2(__uint_as_float(g[i + 2 * e]), __uint_as_float(g[i + 2 * e + 1]))),
+                                  make_float2(__uint_as_float(u[i + 2 * e]), __uint_as_float(u[i + 2 * e + 1])));
             w[e] = pack2<T>(y.x, y.y);
           }
           p[h * 4 + i / 8] = make_uint4(w[0], w[1], w[2], w[3]);
