@@ -210,6 +210,31 @@ def test_gemm_residual_and_partials(lib, prec, splits):
     assert np.max(np.abs(partial.sum(0).double().cpu().numpy() - xd @ wd.T)) < 2e-4 * math.sqrt(K)
 
 
+@pytest.mark.parametrize("prec", ["bf16", "f16"])
+@pytest.mark.parametrize("M,N,K,block_n,splits", [(128, 64, 320, 64, 1), (200, 128, 192, 128, 1), (96, 256, 448, 64, 1),
+                                                  (300, 384, 1536, 128, 3), (64, 768, 768, 64, 3)])
+def test_gemm_issuer_shares(lib, prec, M, N, K, block_n, splits):
+    """Grids with one tile per CTA spread a tile's k-blocks over several MMA-issuing threads
+    (4 for 64-column tiles, 2 for 128), each into its own accumulator: shares that do not divide
+    evenly (5 k-blocks over 4 issuers, 3 over 2, 7 over 4), and split-K partials whose split
+    ranges are shared out again, all against float64."""
+    rng = np.random.default_rng(M + N + K + splits)
+    x, xd = rand16((M, K), prec, rng)
+    w, wd = rand16((N, K), prec, rng, 0.05)
+    if splits == 1:
+        bias = torch.from_numpy(rng.normal(0, 0.1, N).astype(np.float32)).cuda()
+        out = torch.full((M, N), float("nan"), dtype=PRECISIONS[prec][1], device="cuda")
+        gemm(lib, prec, 0, x, w, out, N, bias=bias, block_n=block_n)
+        expected = xd @ wd.T + bias.double().cpu().numpy()
+        got = out.double().cpu().numpy()
+        tol = ROUND[prec] * np.abs(expected) + 1e-4 * math.sqrt(K)
+        assert np.all(np.abs(got - expected) <= tol), float(np.max(np.abs(got - expected) - tol))
+    else:
+        partial = torch.zeros((splits, M, N), dtype=torch.float32, device="cuda")
+        gemm(lib, prec, 6, x, w, residual=partial, ldr=N, splits=splits, block_n=block_n)
+        assert np.max(np.abs(partial.sum(0).double().cpu().numpy() - xd @ wd.T)) < 2e-4 * math.sqrt(K)
+
+
 def packed_case(lengths):
     starts = np.cumsum([0] + [span(n) for n in lengths])[:-1].astype(np.int32)
     M = span(sum(span(n) for n in lengths) + 16)  # include tokens past the last row
