@@ -202,7 +202,8 @@ class Laya:
             value = float(value)
         except (TypeError, ValueError):
             return 1.0
-        return float(np.clip(value, .5, 5)) if math.isfinite(value) else 1.0
+        # Scalar clamp: the value np.clip gives a finite float, without its per-call setup.
+        return min(max(value, .5), 5.0) if math.isfinite(value) else 1.0
 
     def decode_plan(self, questions):
         """The parts of decode() that need no model output: per question (id, kind, criteria,
@@ -223,7 +224,7 @@ class Laya:
             prob = softmax(logits[row, :count].astype(np.float32) / np.float32(temp))
             if count > 1:
                 entropy = (prob * np.log(np.maximum(prob, 1e-12))).sum()
-                conf = float(np.clip(1 + entropy / math.log(count), 0, 1))
+                conf = float(min(max(1 + entropy / math.log(count), 0), 1))  # finite: as np.clip
             else:
                 conf = 1.0
             answer = {"type": kind, "confidence": round(conf, 4),
