@@ -65,7 +65,9 @@ struct GemmLnCfg {
   static constexpr int kXBytes = 2 * 2 * C * kBM * 2 * 4;
   static constexpr uint32_t kXTxBytes = C * kEpiWarps * 32 * 8;  // received per CTA per tile
   static constexpr int kOffBar = kOffX + kXBytes;
-  static constexpr int kSmemBytes = kOffBar + 512 + 1024;
+  // The CTA's column block of gamma (fp32), read by the LayerNorm pass.
+  static constexpr int kOffGB = kOffBar + 512;
+  static constexpr int kSmemBytes = kOffGB + BN * 4 + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory of one CTA");
 };
 
@@ -203,6 +205,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_drain(drain, 0);
     }
   } else {
+    // This CTA's columns of gamma (a weight: loaded before the dependency wait) into shared
+    // memory, so the LayerNorm pass reads it as broadcast 16-byte loads; the eight epilogue warps
+    // meet on named barrier 1 before any of them reads the copy.  (beta, absent from the
+    // encoder's norms, is read from global memory when given.)
+    float* s_gamma = reinterpret_cast<float*>(smem + Cfg::kOffGB);
+    for (int i = threadIdx.x - 64; i < BN; i += kEpiWarps * 32) s_gamma[i] = args.gamma[nb * BN + i];
+    asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
     pdl_wait();
     // Epilogue warp: TMEM lane quarter q (tile rows 32q..32q+31, one per lane) and column half h
     // (this CTA's columns [h BN/2, (h+1) BN/2), NCH 32-column chunks).
@@ -352,14 +361,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // block, and a last 32-column block (64 bytes per row) when NCH is odd.
       auto normalise = [&](int j, uint32_t (&v)[32], uint4* p) {
         tmem_wait_ld(v);
-        const int c0 = col0 + 32 * j;
+        const int c0 = half * (BN / 2) + 32 * j;  // column within this CTA's block
 #pragma unroll
         for (int i = 0; i < 32; i += 8) {
+          const float4 g0 = *reinterpret_cast<const float4*>(s_gamma + c0 + i);
+          const float4 g1 = *reinterpret_cast<const float4*>(s_gamma + c0 + i + 4);
+          const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
           float y[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
-            y[e] = (__uint_as_float(v[i + e]) - mean) * rstd * args.gamma[c0 + i + e];
-            if (args.beta) y[e] += args.beta[c0 + i + e];
+            y[e] = (__uint_as_float(v[i + e]) - mean) * rstd * g[e];
+            if (args.beta) y[e] += args.beta[nb * BN + c0 + i + e];
           }
           p[i / 8] = make_uint4(pack2<T>(y[0], y[1]), pack2<T>(y[2], y[3]), pack2<T>(y[4], y[5]), pack2<T>(y[6], y[7]));
         }
