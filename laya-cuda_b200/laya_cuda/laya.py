@@ -188,7 +188,9 @@ class Laya:
                 ids += option
             ids.append(self.sep)
             room = max(0, self.max_len - len(ids) - 1)
-            ids = (ids + state_ids[:room] + [self.sep])[:self.max_len]
+            ids.extend(state_ids[:room])  # in place: ids is this item's own list
+            ids.append(self.sep)
+            del ids[self.max_len:]
             if markers[-1] >= len(ids):
                 raise ValueError(f"Question {qid!r} exceeds the option token budget")
             items.append((ids, markers, TYPES.index(kind)))
@@ -234,7 +236,7 @@ class Laya:
                 answer.update(noul=round(yes, 4), confidence=round(float(max(prob[1], 1 - prob[1])), 4))
             else:
                 keys = list(criteria) if kind == "choice" else [str(i) for i in range(count)]
-                answer["probabilities"] = {key: round(float(p), 4) for key, p in zip(keys, prob)}
+                answer["probabilities"] = {key: round(p, 4) for key, p in zip(keys, prob.tolist())}
                 if kind == "choice":
                     answer["choice"] = keys[int(prob.argmax())]
                 else:
