@@ -200,3 +200,42 @@ def test_next_batch_launches_before_the_previous_is_collected(monkeypatch):
     assert order == [("submit", "a"), ("submit", "b"), ("collect", "a"), ("submit", "c"), ("collect", "b"),
                      ("collect", "c")]
     assert events.index(("decode", "a")) > events.index(("submit", "b"))
+
+
+def test_burst_is_tokenised_batch_by_batch(monkeypatch):
+    """A burst taken in one collection is not tokenised up front: the requests of batch i+1 are
+    prepared after batch i has been launched, so tokenisation overlaps the device, and batches
+    still keep arrival order within both budgets."""
+    events = []
+
+    class Engine:
+        def __init__(self, *args, **kwargs):
+            self.adapter = self
+            self.runtime = self
+
+        def prepare(self, state, questions):
+            events.append(("prepare", state))
+            return [([state] * 20, [0], 0) for _ in questions]
+
+        def submit(self, items):
+            events.append(("submit", tuple(item[0][0] for item in items)))
+            return tuple(item[0][0] for item in items)
+
+        def collect(self, ticket):
+            return list(ticket), [0] * len(ticket), {"gpu_ms": 1}
+
+        def decode(self, logits, acts, questions, items):
+            return dict(zip(questions, logits))
+
+        def close(self):
+            pass
+
+    monkeypatch.setattr(batching, "Engine", Engine)
+    with BatchEngine(max_batch_size=2, max_wait_ms=50) as engine:
+        futures = [engine.submit(s, {"q": 1}) for s in "abcde"]
+        assert [f.result(5) for f in futures] == [{"q": s} for s in "abcde"]
+    submits = [e[1] for e in events if e[0] == "submit"]
+    assert submits == [("a", "b"), ("c", "d"), ("e",)]
+    # Requests c and d are tokenised only after batch (a, b) was launched, e after (c, d).
+    assert events.index(("prepare", "c")) > events.index(("submit", ("a", "b")))
+    assert events.index(("prepare", "e")) > events.index(("submit", ("c", "d")))
