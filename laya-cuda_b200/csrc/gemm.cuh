@@ -245,8 +245,32 @@ struct QkvPipe {
             *reinterpret_cast<uint4*>(out + (size_t)(row0 + r) * 64 + col) =
                 *reinterpret_cast<const uint4*>(stage + stage_off(r, j));
         }
+      } else if (a.M % 8 == 0) {
+        // V transposed, [heads][64][M]: the warp's 32 dims x 32 tokens go through the staging
+        // block transposed (dim d' = 0..31 its 16 low then 16 high dims, 64 bytes of tokens per
+        // dim), then each lane stores four 16-byte runs of 8 tokens.  M a multiple of 8 keeps
+        // every run 16-byte aligned and wholly inside or wholly past the last row.
+        T* vt = reinterpret_cast<T*>(a.out) + ((size_t)2 * a.heads + head) * a.M * 64;
+        __syncwarp();
+        T* st16 = reinterpret_cast<T*>(stage);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          st16[i * 32 + lane] = from_f32<T>(lo[i]);
+          st16[(16 + i) * 32 + lane] = from_f32<T>(hi[i]);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int piece = lane + 32 * k, dd = piece >> 2, sub = piece & 3;
+          const int dim = dd < 16 ? 16 * half + dd : 32 + 16 * half + (dd - 16);
+          const int t0 = row0 + 8 * sub;
+          if (t0 < a.M)
+            *reinterpret_cast<uint4*>(vt + (size_t)dim * a.M + t0) =
+                *reinterpret_cast<const uint4*>(st16 + dd * 32 + 8 * sub);
+        }
       } else if (row < a.M) {
-        // V transposed, [heads][64][M]: each dimension's 32 stores fill one 64-byte run.
+        // Row counts that are not a multiple of 8: one 2-byte store per dim and token (each
+        // dimension's 32 stores fill one 64-byte run).
         T* vt = reinterpret_cast<T*>(a.out) + ((size_t)2 * a.heads + head) * a.M * 64 + row;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
