@@ -576,12 +576,14 @@ void launch_norm(const NormArgs& a, cudaStream_t st) {
   if (a.d % 64 || a.d > 1024) fail(LAYA_ERR_INVALID, "unsupported width %d", a.d);
   const int warps = row_warps(a.rows);
   const int grid = (a.rows + warps - 1) / warps;
-  const bool partials = a.splits > 0;
+  const bool partials = a.splits > 0, fused = a.fused_final != 0;
   switch (a.d / 32) {
-#define LAYA_NORM_CASE(N)                                                                   \
-  case N:                                                                                   \
-    if (partials) launch_k(norm_kernel<N, T, true>, dim3(grid), dim3(warps * 32), 0, st, a); \
-    else launch_k(norm_kernel<N, T, false>, dim3(grid), dim3(warps * 32), 0, st, a);         \
+#define LAYA_NORM_CASE(N)                                                                                  \
+  case N:                                                                                                  \
+    if (fused && partials) launch_k(norm_kernel<N, T, true, true>, dim3(grid), dim3(warps * 32), 0, st, a); \
+    else if (fused) launch_k(norm_kernel<N, T, false, true>, dim3(grid), dim3(warps * 32), 0, st, a);       \
+    else if (partials) launch_k(norm_kernel<N, T, true, false>, dim3(grid), dim3(warps * 32), 0, st, a);    \
+    else launch_k(norm_kernel<N, T, false, false>, dim3(grid), dim3(warps * 32), 0, st, a);                 \
     break;
     LAYA_FOR_EACH_WIDTH(LAYA_NORM_CASE)
 #undef LAYA_NORM_CASE

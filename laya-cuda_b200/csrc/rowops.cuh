@@ -85,6 +85,34 @@ __device__ __forceinline__ void row_layernorm(float (&v)[NPL], const float (&g)[
   for (int i = 0; i < NPL; ++i) v[i] = (v[i] - mean) * inv * g[i] + b[i];
 }
 
+// LayerNorm without a held beta: v = (v - mean) * rsqrt(var + eps) * gamma, then + beta loaded
+// here only when given (the encoder's norms have none), so no beta slice stays live across the
+// reductions.
+template <int NPL>
+__device__ __forceinline__ void row_layernorm_beta_late(float (&v)[NPL], const float (&g)[NPL], const float* beta,
+                                                        int lane, float eps) {
+  constexpr float inv_d = 1.0f / (32 * NPL);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NPL; ++i) s += v[i];
+  const float mean = warp_sum(s) * inv_d;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < NPL; ++i) { const float t = v[i] - mean; q += t * t; }
+  const float inv = rsqrtf(warp_sum(q) * inv_d + eps);
+#pragma unroll
+  for (int i = 0; i < NPL; ++i) v[i] = (v[i] - mean) * inv * g[i];
+  if (beta) {
+    constexpr int CH = RowVec<NPL>::CH;
+#pragma unroll
+    for (int j = 0; j < NPL / CH; ++j) {
+      const int col = j * 32 * CH + lane * CH;
+#pragma unroll
+      for (int c = 0; c < CH; ++c) v[j * CH + c] += beta[col + c];
+    }
+  }
+}
+
 // Loads the lane's slice of an optional [d] vector (zeros when absent).
 template <int NPL>
 __device__ __forceinline__ void row_load_opt(const float* src, int lane, float (&v)[NPL]) {
@@ -136,9 +164,11 @@ struct NormArgs {
 
 // Normal:  residual += sum(partials) + bias; x = LN1(residual).
 // Fused:   residual = LN1(residual + sum(partials) + bias) + type_emb[kind]; x = LN2(residual).
-// PARTIALS selects the split-K variant (only used for small classes), keeping the common
-// variant's register footprint small.  Replaces kernels.cu:20-49 and kernels.cu:155-158.
-template <int NPL, typename T, bool PARTIALS>
+// PARTIALS selects the split-K variant (only used for small classes) and FUSED the final-norm
+// fusion (once per pass, `a.fused_final`), so the common variant holds only gamma and the row in
+// registers (beta, when given, is added after normalising): four 256-thread blocks fit an SM.
+// Replaces kernels.cu:20-49 and kernels.cu:155-158.
+template <int NPL, typename T, bool PARTIALS, bool FUSED>
 __global__ void __launch_bounds__(kRowWarps * 32) norm_kernel(const NormArgs a) {
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   // Every independent load is issued up front, so a row costs about one memory round trip: the
@@ -146,7 +176,7 @@ __global__ void __launch_bounds__(kRowWarps * 32) norm_kernel(const NormArgs a) 
   // the residual row and up to four partial rows together.
   float g1[NPL], b1[NPL], pb[NPL];
   row_load<NPL>(a.gamma1, lane, g1);
-  row_load_opt<NPL>(a.beta1, lane, b1);
+  if (FUSED) row_load_opt<NPL>(a.beta1, lane, b1);
   if (PARTIALS) row_load_opt<NPL>(a.partial_bias, lane, pb);
   pdl_wait();
   if (row >= a.rows) return;
@@ -175,7 +205,7 @@ __global__ void __launch_bounds__(kRowWarps * 32) norm_kernel(const NormArgs a) 
 #pragma unroll
     for (int i = 0; i < NPL; ++i) v[i] += acc[i] + pb[i];
   }
-  if (a.fused_final) {
+  if (FUSED) {
     float g2[NPL], b2[NPL], t[NPL];
     row_load<NPL>(a.gamma2, lane, g2);
     row_load_opt<NPL>(a.beta2, lane, b2);
@@ -187,7 +217,7 @@ __global__ void __launch_bounds__(kRowWarps * 32) norm_kernel(const NormArgs a) 
     row_layernorm<NPL>(v, g2, b2, a.eps2);
   } else {
     if (PARTIALS) row_store<NPL>(r, lane, v);
-    row_layernorm<NPL>(v, g1, b1, a.eps1);
+    row_layernorm_beta_late<NPL>(v, g1, a.beta1, lane, a.eps1);
   }
   if (a.x) row_store_t<NPL, T>(reinterpret_cast<T*>(a.x) + (size_t)row * d, lane, v);
 }

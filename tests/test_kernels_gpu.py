@@ -354,11 +354,12 @@ def test_embed_norm(lib, prec, width):
 
 @pytest.mark.parametrize("prec", ["bf16", "f16"])
 @pytest.mark.parametrize("width", [64, 768, 1024])
-@pytest.mark.parametrize("splits,beta", [(0, False), (2, True)])
-def test_norm_residual_partials(lib, prec, width, splits, beta):
-    """cf. tests/test_gpu.py:68-103: residual accumulation then LayerNorm with/without beta."""
+@pytest.mark.parametrize("splits,beta", [(0, False), (0, True), (2, False), (2, True)])
+@pytest.mark.parametrize("rows", [29, 2371])
+def test_norm_residual_partials(lib, prec, width, splits, beta, rows):
+    """cf. tests/test_gpu.py:68-103: residual accumulation then LayerNorm with/without beta.
+    2,371 rows launch 8-warp blocks with a partly filled last block; 29 rows one-warp blocks."""
     rng = np.random.default_rng(31)
-    rows = 3 * 8 + 5
     source = rng.normal(2, .3, (rows, width)).astype(np.float32)
     parts = rng.normal(0, .1, (max(splits, 1), rows, width)).astype(np.float32)
     gamma = rng.normal(1, .1, width).astype(np.float32)
