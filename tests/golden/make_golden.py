@@ -114,4 +114,6 @@ def generate(reference_root):
 
 
 if __name__ == "__main__":
-    generate(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py /path/to/laya-cuda")
+    generate(sys.argv[1])
