@@ -10,8 +10,10 @@ worker releases the GPU.
 Unlike the reference's worker, which runs one synchronous Runtime.predict per batch
 (batching.py:122), this one pipelines through Runtime.submit / collect: batch i+1 is packed and
 launched before batch i is collected and decoded, and requests that arrive while a batch runs
-are tokenised before it is collected, and a burst of requests is tokenised batch by batch, so
-tokenisation, packing and decoding overlap the device.
+are tokenised before it is collected, and a burst of requests is tokenised batch by batch (a
+batch's requests together, through the adapter's prepare_many, which spreads the tokenizer over
+a few helper threads), so tokenisation, packing and decoding overlap the device.  Every engine
+and adapter call is made on the worker thread.
 """
 from concurrent.futures import Future
 from copy import deepcopy
@@ -105,23 +107,49 @@ class BatchEngine:
             taken, self._queue = self._queue, []
             return taken
 
-    def _prepare(self, engine, active, request):
-        """Tokenises one taken request (already in `active`); returns (request, items, packed
-        tokens), or None when it was cancelled or failed (its future is then resolved)."""
-        if not request[0].set_running_or_notify_cancel():
-            self._finish(request)
-            active.remove(request)
-            return None
-        try:
-            items = engine.adapter.prepare(request[1], request[2])
-            tokens = sum(span(len(item[0])) for item in items)
-            if len(items) > self.max_batch_size or tokens > self.max_batch_tokens:
-                raise ValueError("Request exceeds batch budget; increase limits or submit fewer questions")
-            return request, items, tokens
-        except Exception as error:
-            active.remove(request)
-            self._finish(request, error=error)
-            return None
+    def _prepare(self, engine, active, waiting, prepared):
+        """Tokenises the next taken requests (already in `active`): those whose questions fit
+        what is left of the question budget after `prepared` (at least one; a request has one
+        item per question).  Returns their (request, items, packed tokens) entries; a request
+        that was cancelled or failed is resolved and dropped.  Several requests go to the
+        adapter's prepare_many when it has one (tokenised in parallel, on this thread's call)."""
+        room = self.max_batch_size - sum(len(entry[1]) for entry in prepared)
+        chunk = []
+        while waiting:
+            questions = waiting[0][2]
+            size = len(questions) if isinstance(questions, dict) else 1
+            if chunk and size > room:
+                break
+            request = waiting.pop(0)
+            room -= size
+            if request[0].set_running_or_notify_cancel():
+                chunk.append(request)
+            else:
+                self._finish(request)
+                active.remove(request)
+        many = getattr(engine.adapter, "prepare_many", None)
+        if many is not None and len(chunk) > 1:
+            results = many([(request[1], request[2]) for request in chunk])
+        else:
+            results = []
+            for request in chunk:
+                try:
+                    results.append(engine.adapter.prepare(request[1], request[2]))
+                except Exception as error:
+                    results.append(error)
+        entries = []
+        for request, items in zip(chunk, results):
+            try:
+                if isinstance(items, Exception):
+                    raise items
+                tokens = sum(span(len(item[0])) for item in items)
+                if len(items) > self.max_batch_size or tokens > self.max_batch_tokens:
+                    raise ValueError("Request exceeds batch budget; increase limits or submit fewer questions")
+                entries.append((request, items, tokens))
+            except Exception as error:
+                active.remove(request)
+                self._finish(request, error=error)
+        return entries
 
     def _fills(self, prepared):
         """Whether the prepared requests reach one batch's question or token budget."""
@@ -186,17 +214,15 @@ class BatchEngine:
 
     def _run(self, engine, active, taken, pending):
         """Tokenises and launches the taken requests batch by batch.  Requests are tokenised only
-        as far as the next batch needs, so a burst's later requests are tokenised while earlier
-        batches run; each batch is launched before the previous one is collected and decoded
-        (at most two batches in flight).  Returns the last launched batch, still in flight, or
-        None."""
+        as far as the next batch needs (by their question counts, then by the token budget), so
+        a burst's later requests are tokenised while earlier batches run; each batch is launched
+        before the previous one is collected and decoded (at most two batches in flight).
+        Returns the last launched batch, still in flight, or None."""
         active.extend(taken)
         waiting, prepared = list(taken), []
         while waiting or prepared:
             while waiting and not self._fills(prepared):
-                entry = self._prepare(engine, active, waiting.pop(0))
-                if entry is not None:
-                    prepared.append(entry)
+                prepared.extend(self._prepare(engine, active, waiting, prepared))
             if not prepared:
                 break
             batch, prepared, questions = self._next_batch(prepared)

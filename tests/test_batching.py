@@ -239,3 +239,56 @@ def test_burst_is_tokenised_batch_by_batch(monkeypatch):
     # Requests c and d are tokenised only after batch (a, b) was launched, e after (c, d).
     assert events.index(("prepare", "c")) > events.index(("submit", ("a", "b")))
     assert events.index(("prepare", "e")) > events.index(("submit", ("c", "d")))
+
+
+def test_burst_is_prepared_in_chunks_on_the_worker(monkeypatch):
+    """With an adapter that has prepare_many, a burst's requests are handed over in chunks that
+    fill the next batch's question budget (counted before tokenising), on the worker thread; a
+    request that fails in the chunk fails alone, and a chunk of one goes through prepare."""
+    events, owners = [], set()
+
+    class Engine:
+        def __init__(self, *args, **kwargs):
+            self.adapter = self
+            self.runtime = self
+
+        def prepare(self, state, questions):
+            owners.add(get_ident())
+            events.append(("prepare", state))
+            return [([state] * 20, [0], 0) for _ in questions]
+
+        def prepare_many(self, requests):
+            owners.add(get_ident())
+            events.append(("many", tuple(state for state, _ in requests)))
+            return [ValueError(f"bad {state}") if state == "c" else self.prepare(state, questions)
+                    for state, questions in requests]
+
+        def submit(self, items):
+            owners.add(get_ident())
+            events.append(("submit", tuple(item[0][0] for item in items)))
+            return tuple(item[0][0] for item in items)
+
+        def collect(self, ticket):
+            return list(ticket), [0] * len(ticket), {"gpu_ms": 1}
+
+        def decode(self, logits, acts, questions, items):
+            return dict(zip(questions, logits))
+
+        def close(self):
+            pass
+
+    monkeypatch.setattr(batching, "Engine", Engine)
+    with BatchEngine(max_batch_size=4, max_wait_ms=50) as engine:
+        sizes = {"a": 1, "b": 2, "c": 1, "d": 1, "e": 3, "f": 2}
+        futures = {s: engine.submit(s, {f"q{i}": 1 for i in range(n)}) for s, n in sizes.items()}
+        for s, future in futures.items():
+            if s == "c":
+                with pytest.raises(ValueError, match="bad c"):
+                    future.result(5)
+            else:
+                assert future.result(5) == {f"q{i}": s for i in range(sizes[s])}
+    assert len(owners) == 1 and get_ident() not in owners
+    # a + b + c fill the 4-question budget and go together; after c fails, d alone fills the
+    # room left (one request: prepare); e (3) and f (2) do not fit one batch.
+    assert [e[1] for e in events if e[0] == "many"] == [("a", "b", "c")]
+    assert [tuple(dict.fromkeys(e[1])) for e in events if e[0] == "submit"] == [("a", "b", "d"), ("e",), ("f",)]

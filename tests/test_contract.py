@@ -64,6 +64,30 @@ def test_errors_match_reference(adapter):
         assert type(info.value).__name__ == g["error"] and str(info.value) == g["message"]
 
 
+def test_prepare_many_equals_prepare(adapter):
+    """prepare_many (BatchEngine's path for several requests: each request's texts encoded on a
+    helper thread) gives every request exactly prepare()'s items, and every failing request the
+    error prepare() raises for it, whether parsing (before encoding) or the option budget (after)
+    fails, without disturbing its neighbours."""
+    requests = [(g["state"], {n: QUESTIONS[n] for n in g["questions"]}) for g in GOLDEN["prepare"]]
+    many_options = {"type": "choice", "instructions": "i", "criteria": [f"option number {i}" for i in range(400)]}
+    requests[1:1] = [("x", {}), ("x", {"q": {"type": "rank", "instructions": "i"}}), ("x", {"q": many_options})]
+    results = adapter.prepare_many(requests)
+    assert len(results) == len(requests)
+    failed = 0
+    for request, result in zip(requests, results):
+        try:
+            want = adapter.prepare(*request)
+        except Exception as error:
+            failed += 1
+            assert type(result) is type(error) and str(result) == str(error)
+        else:
+            assert result == want
+    assert failed == 3
+    assert adapter.prepare_many([]) == []
+    assert adapter.prepare_many(requests[:1]) == [adapter.prepare(*requests[0])]
+
+
 def test_import_is_light():
     """tests/test_contract.py:11-17: importing the package pulls in no heavy libraries."""
     root = HERE.parent
