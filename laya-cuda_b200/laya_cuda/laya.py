@@ -27,14 +27,16 @@ os.environ.setdefault("TOKENIZERS_PARALLELISM", "false")
 # config-5-shaped request of ~640 words: ~710 us on one thread, ~230 us each with four).  Only
 # the tokenizer runs there; the calling thread parses the questions and builds the items.
 TOKENIZE_THREADS = max(2, min(4, (os.cpu_count() or 2) // 2))
-_helpers, _helpers_lock = None, Lock()
+_helpers, _helpers_pid, _helpers_lock = None, None, Lock()
 
 
 def _tokenize_helpers():
-    global _helpers
+    """The process's helper threads (a forked child makes its own: it inherits none)."""
+    global _helpers, _helpers_pid
     with _helpers_lock:
-        if _helpers is None:
+        if _helpers is None or _helpers_pid != os.getpid():
             _helpers = ThreadPoolExecutor(TOKENIZE_THREADS, thread_name_prefix="laya-tokenize")
+            _helpers_pid = os.getpid()
         return _helpers
 
 TYPES = ("choice", "score", "noul")

@@ -200,3 +200,24 @@ def test_fingerprint_equals_compact_json_digest(adapter):
             items.append(item if rng.random() < 0.5 else list(item))
         want = hashlib.sha256(json.dumps(items, separators=(",", ":")).encode()).hexdigest()
         assert adapter.fingerprint(items) == want
+
+
+@pytest.mark.skipif(not hasattr(__import__("os"), "fork"), reason="needs fork")
+@pytest.mark.filterwarnings("ignore:This process .* is multi-threaded:DeprecationWarning")
+def test_prepare_many_in_a_forked_child(adapter):
+    """A child forked after prepare_many has run gets its own helper threads (the parent's do not
+    exist in the child), so its prepare_many completes with the same items."""
+    import multiprocessing
+    requests = [(g["state"], {n: QUESTIONS[n] for n in g["questions"]}) for g in GOLDEN["prepare"][:4]]
+    want = adapter.prepare_many(requests)
+    ctx = multiprocessing.get_context("fork")
+    queue = ctx.Queue()
+    child = ctx.Process(target=lambda: queue.put(adapter.prepare_many(requests)))
+    child.start()
+    try:
+        got = queue.get(timeout=60)
+    finally:
+        child.join(60)
+        if child.is_alive():
+            child.kill()
+    assert child.exitcode == 0 and got == want
