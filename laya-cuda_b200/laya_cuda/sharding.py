@@ -84,7 +84,8 @@ class ShardedEngine:
         with ShardedEngine("laya", devices=["cuda:0", "cuda:1"]) as engine:
             answers = engine.predict_batch([(state, questions), ...])
 
-    `predict_batch` prepares every request on the calling thread, partitions them with `shard`
+    `predict_batch` prepares every request (tokenised in parallel by the adapter's
+    prepare_many, called on the calling thread), partitions them with `shard`
     by modelled work, and has each device's thread run its share as micro-batches of at most
     `micro_batch` packed sequences (two in flight per device), then decode.  Answers come back
     in request order; `last_metrics` reports each device's requests, sequences, tokens, GPU time
@@ -129,7 +130,7 @@ class ShardedEngine:
         if any(engine is None or engine.closed for engine in self.engines):
             raise RuntimeError("Engine is closed")
         started = time.perf_counter()
-        prepared = [self.adapter.prepare(state, questions) for state, questions in requests]
+        prepared = self._prepare(requests)
         costs = [request_cost(items, **self.geometry) for items in prepared]
         parts = shard(costs, len(self.engines))
         answers, per_device, errors = [None] * len(requests), [None] * len(self.engines), []
@@ -163,6 +164,18 @@ class ShardedEngine:
         self.last_metrics = {"devices": per_device, "imbalance": imbalance(costs, parts),
                              "api_ms": (time.perf_counter() - started) * 1000}
         return answers
+
+    def _prepare(self, requests):
+        """Every request's items (the first failing request's error is raised, as a loop over
+        prepare() would); the adapter's prepare_many encodes them in parallel when it has one."""
+        many = getattr(self.adapter, "prepare_many", None)
+        if many is None or len(requests) < 2:
+            return [self.adapter.prepare(state, questions) for state, questions in requests]
+        prepared = many(list(requests))
+        for items in prepared:
+            if isinstance(items, Exception):
+                raise items
+        return prepared
 
     def close(self):
         for engine in self.engines:

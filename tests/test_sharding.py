@@ -107,3 +107,31 @@ def test_sharded_engine_routes_requests_and_keeps_order(monkeypatch):
     for rank, c in enumerate(calls):
         assert c and c[0][0] == f"laya-device-{rank}" and max(c[0][1]) <= 8
     assert all(e.closed for e in engine.engines)
+
+
+def test_sharded_engine_prepares_through_prepare_many(monkeypatch):
+    """With an adapter that has prepare_many, a batch of requests is prepared in one call (the
+    tokenizer runs in parallel there); the first failing request's error is raised, as a loop
+    over prepare() would raise it."""
+    import laya_cuda.engine
+    calls = []
+
+    class ManyAdapter(FakeAdapter):
+        def prepare_many(self, requests):
+            calls.append(len(requests))
+            return [ValueError(f"bad {i}") if state == "bad" else self.prepare(state, q)
+                    for i, (state, q) in enumerate(requests)]
+
+    class ManyEngine(FakeEngine):
+        def __init__(self, model, device, **options):
+            super().__init__(model, device, **options)
+            self.adapter = ManyAdapter()
+
+    monkeypatch.setattr(laya_cuda.engine, "Engine", ManyEngine)
+    requests = [("x" * (100 + i), 1 + i % 3) for i in range(10)]
+    with sharding.ShardedEngine("m", devices=["cuda:0", "cuda:1"]) as engine:
+        answers = engine.predict_batch(requests)
+        assert calls == [10]
+        assert [a["tokens"] for a in answers] == [[len(s) + i for i in range(q)] for s, q in requests]
+        with pytest.raises(ValueError, match="bad 3"):
+            engine.predict_batch(requests[:3] + [("bad", 1), ("bad", 1)])
