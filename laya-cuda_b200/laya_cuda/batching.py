@@ -30,6 +30,28 @@ class _Prediction(Future):
     metrics: dict
 
 
+def _copy_json(value):
+    t = type(value)
+    if t is str or t is int or t is float or t is bool or value is None:
+        return value
+    if t is dict:
+        return {key: _copy_json(item) for key, item in value.items()}
+    if t is list:
+        return [_copy_json(item) for item in value]
+    return deepcopy(value)
+
+
+def snapshot(value):
+    """A copy of a submitted state or question mapping, so later changes by the caller do not
+    reach the request (the reference deep-copies both).  Plain dicts, lists and scalars, what
+    JSON-like requests hold, are copied directly (a few times faster than deepcopy); anything
+    else, and structures too deep or cyclic for that, goes through deepcopy."""
+    try:
+        return _copy_json(value)
+    except RecursionError:
+        return deepcopy(value)
+
+
 class BatchEngine:
     def __init__(self, model="laya", *, max_batch_size=16, max_batch_tokens=4096, max_pending=128, max_wait_ms=1,
                  **engine_options):
@@ -58,7 +80,7 @@ class BatchEngine:
                 raise Full("BatchEngine pending request limit reached")
             future = _Prediction()
             future.metrics = {}
-            self._queue.append((future, deepcopy(state), deepcopy(questions), started))
+            self._queue.append((future, snapshot(state), snapshot(questions), started))
             self._pending += 1
             self._cv.notify()
         return future

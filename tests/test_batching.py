@@ -292,3 +292,39 @@ def test_burst_is_prepared_in_chunks_on_the_worker(monkeypatch):
     # room left (one request: prepare); e (3) and f (2) do not fit one batch.
     assert [e[1] for e in events if e[0] == "many"] == [("a", "b", "c")]
     assert [tuple(dict.fromkeys(e[1])) for e in events if e[0] == "submit"] == [("a", "b", "d"), ("e",), ("f",)]
+
+
+def test_snapshot_copies_like_deepcopy():
+    """submit's snapshot: equal values and no shared mutable part for JSON-like requests (nested
+    dicts and lists of scalars); other types and cycles go through deepcopy, so every input is
+    copied as the reference's deepcopy copies it, and nesting too deep for deepcopy fails the
+    same way."""
+    from collections import OrderedDict
+    from copy import deepcopy
+    from laya_cuda.batching import snapshot
+    questions = {"q": {"type": "choice", "instructions": {"ask": ["a", 1, 2.5, None, True]}, "criteria": ["x", "y"]}}
+    copy = snapshot(questions)
+    assert copy == deepcopy(questions)
+    questions["q"]["criteria"].append("z")
+    questions["q"]["instructions"]["ask"].clear()
+    assert copy["q"]["criteria"] == ["x", "y"] and copy["q"]["instructions"]["ask"] == ["a", 1, 2.5, None, True]
+    ordered = OrderedDict(a=[1])
+    assert type(snapshot(ordered)) is OrderedDict and snapshot(ordered)["a"] is not ordered["a"]
+    pair = ([1], "s")
+    assert snapshot(pair) == pair and snapshot(pair)[0] is not pair[0]
+    cyclic = {"a": []}
+    cyclic["a"].append(cyclic)
+    copied = snapshot(cyclic)
+    assert copied["a"][0] is copied and copied is not cyclic
+    def nested(depth):
+        outer = value = []
+        for _ in range(depth):
+            value.append([])
+            value = value[0]
+        return outer
+    assert snapshot(nested(300)) == nested(300)
+    too_deep = nested(5000)
+    with pytest.raises(RecursionError):
+        deepcopy(too_deep)
+    with pytest.raises(RecursionError):
+        snapshot(too_deep)
