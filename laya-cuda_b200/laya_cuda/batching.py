@@ -138,8 +138,7 @@ class BatchEngine:
         room = self.max_batch_size - sum(len(entry[1]) for entry in prepared)
         chunk = []
         while waiting:
-            questions = waiting[0][2]
-            size = len(questions) if isinstance(questions, dict) else 1
+            size = self._questions(waiting[0])
             if chunk and size > room:
                 break
             request = waiting.pop(0)
@@ -173,9 +172,19 @@ class BatchEngine:
                 self._finish(request, error=error)
         return entries
 
-    def _fills(self, prepared):
-        """Whether the prepared requests reach one batch's question or token budget."""
-        return (sum(len(entry[1]) for entry in prepared) >= self.max_batch_size
+    @staticmethod
+    def _questions(request):
+        """Items a taken request will have (one per question), known before tokenising."""
+        questions = request[2]
+        return len(questions) if isinstance(questions, dict) else 1
+
+    def _fills(self, prepared, upcoming):
+        """Whether the prepared requests reach one batch's question or token budget, or leave
+        too little question room for the next waiting request, which then starts the next batch
+        (first-fit would leave it out of this one anyway)."""
+        questions = sum(len(entry[1]) for entry in prepared)
+        return (questions >= self.max_batch_size
+                or (prepared and questions + self._questions(upcoming) > self.max_batch_size)
                 or sum(entry[2] for entry in prepared) >= self.max_batch_tokens)
 
     def _next_batch(self, prepared):
@@ -243,7 +252,7 @@ class BatchEngine:
         active.extend(taken)
         waiting, prepared = list(taken), []
         while waiting or prepared:
-            while waiting and not self._fills(prepared):
+            while waiting and not self._fills(prepared, waiting[0]):
                 prepared.extend(self._prepare(engine, active, waiting, prepared))
             if not prepared:
                 break

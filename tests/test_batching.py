@@ -328,3 +328,43 @@ def test_snapshot_copies_like_deepcopy():
         deepcopy(too_deep)
     with pytest.raises(RecursionError):
         snapshot(too_deep)
+
+
+def test_request_that_cannot_fit_starts_the_next_chunk(monkeypatch):
+    """A waiting request whose questions exceed the room the prepared ones leave is not
+    tokenised alone: the batch launches, and that request opens the next chunk."""
+    events = []
+
+    class Engine:
+        def __init__(self, *args, **kwargs):
+            self.adapter = self
+            self.runtime = self
+
+        def prepare(self, state, questions):
+            events.append(("prepare", state))
+            return [([state] * 20, [0], 0) for _ in questions]
+
+        def prepare_many(self, requests):
+            events.append(("many", tuple(state for state, _ in requests)))
+            return [[([state] * 20, [0], 0) for _ in questions] for state, questions in requests]
+
+        def submit(self, items):
+            events.append(("submit", tuple(dict.fromkeys(item[0][0] for item in items))))
+            return tuple(item[0][0] for item in items)
+
+        def collect(self, ticket):
+            return list(ticket), [0] * len(ticket), {"gpu_ms": 1}
+
+        def decode(self, logits, acts, questions, items):
+            return dict(zip(questions, logits))
+
+        def close(self):
+            pass
+
+    monkeypatch.setattr(batching, "Engine", Engine)
+    with BatchEngine(max_batch_size=4, max_wait_ms=50) as engine:
+        sizes = {"a": 1, "b": 2, "c": 2, "d": 1}
+        futures = [engine.submit(s, {f"q{i}": 1 for i in range(n)}) for s, n in sizes.items()]
+        for future in futures:
+            future.result(5)
+    assert events == [("many", ("a", "b")), ("submit", ("a", "b")), ("many", ("c", "d")), ("submit", ("c", "d"))]
